@@ -1,0 +1,384 @@
+"""Benchmark of the B200 GDN kernels (one JSON line on rank 0).
+
+Headline (value): GDN decode on BASELINE config 1 -- B=256 sequences per GPU,
+one token each, fp32 k-last state [256, 8, 128, 128] -- reported as the
+state-stream HBM throughput in GB/s summed over GPUs (weak scaling: every GPU
+owns its own 256 sequences; sequences are independent, so there is no
+collective in the timed region).  Per-step microseconds are in
+``ms_per_step``/``decode_us_per_step``.  Prefill tokens/s (configs 2 and 3 on
+one GPU; a config-4b shard of 8 x 8192 tokens per GPU for N > 1) ride along
+in ``prefill``.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...     (N > 1)
+
+Timing: W untimed warm-up steps, then exactly K steps between a barrier and
+a device synchronize, each step timed on its stream with CUDA events; an L2
+flush (a 256 MiB write) runs between steps outside the events; the reported
+time is the max over ranks.  ``--impl reference`` times the reference's own
+algorithm on the host CPU (the oracle port in oracle/, all host threads).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+import __graft_entry__  # noqa: E402
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+DECODE_BATCH = 256
+STATE_BYTES_PER_SEQ = 8 * 128 * 128 * 4
+# algorithmic bytes of one decode step per sequence: state read + write,
+# q, k, v, a, b, output (bf16), plus A_log/dt_bias once per launch
+DECODE_BYTES_PER_SEQ = 2 * STATE_BYTES_PER_SEQ + 1024 + 1024 + 2048 + 16 + 16 + 2048
+DECODE_BYTES_FIXED = 64
+L2_FLUSH_BYTES = 256 << 20
+
+
+def load_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {k: d[k] for k in ("hbm_gbs", "bf16_tflops", "bf16_tflops_sustained")}, "measured"
+    return dict(PEAKS_FALLBACK), "fallback"
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks/throttle reasons while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def max_over_ranks(x: float, ws: int, device) -> float:
+    if ws == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(ws: int):
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def time_steps(step, steps: int, warmup: int, ws: int, device, flush: torch.Tensor | None):
+    """Runs warmup+steps calls of ``step``; returns (per-step device ms list, wall s)."""
+    for _ in range(warmup):
+        if flush is not None:
+            flush.add_(1)
+        step()
+    torch.cuda.synchronize(device)
+    barrier(ws)
+    torch.cuda.synchronize(device)
+    stream = torch.cuda.current_stream(device)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    t0 = time.perf_counter()
+    for i in range(steps):
+        if flush is not None:
+            flush.add_(1)  # evict L2 (256 MiB write) outside the timed events
+        evs[i][0].record(stream)
+        step()
+        evs[i][1].record(stream)
+    torch.cuda.synchronize(device)
+    wall = time.perf_counter() - t0
+    barrier(ws)
+    return [s.elapsed_time(e) for s, e in evs], wall
+
+
+def cpu_threads() -> int:
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+
+
+def cpu_decode_baseline(pkg, budget_s: float):
+    """The reference algorithm (oracle port, C + OpenMP) on the host, decode B=256."""
+    from oracle import oracle
+
+    inp = pkg.inputs.make_decode_inputs(DECODE_BATCH, seed=0)
+    threads = cpu_threads()
+    oracle.decode(*inp.args(), threads=threads)  # warm
+    n, t0 = 0, time.perf_counter()
+    while True:
+        oracle.decode(*inp.args(), threads=threads)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or n >= 200:
+            break
+    sec = el / n
+    return {"value": DECODE_BATCH * STATE_BYTES_PER_SEQ * 2 / sec / 1e9, "unit": "GB/s",
+            "us_per_step": sec * 1e6, "cores": threads, "kind": "port",
+            "sample": f"{n} full decode steps of config 1 (B=256) through oracle/gdn_oracle.c"}
+
+
+def cpu_prefill_baseline(pkg, budget_s: float):
+    from oracle import oracle
+
+    threads = cpu_threads()
+    inp = pkg.inputs.make_prefill_inputs([512] * 8, seed=0, with_state=True)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        oracle.prefill(*inp.args(), threads=threads)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or n >= 50:
+            break
+    return {"tokens_per_s": n * inp.total_tokens / el, "cores": threads, "kind": "port",
+            "sample": f"{n} x prefill of 8 sequences x 512 tokens through oracle/gdn_oracle.c"}
+
+
+def bench_prefill(pkg, device, lengths, seed, steps, warmup, ws, flush, with_state=True):
+    inp = pkg.inputs.make_prefill_inputs(lengths, seed=seed, with_state=with_state).to(device)
+    T, N = inp.total_tokens, inp.num_seqs
+    out = torch.empty((T, 8, 128), dtype=torch.bfloat16, device=device)
+    ns = torch.empty((N, 8, 128, 128), dtype=torch.float32, device=device)
+    ws_bytes = pkg.prefill.workspace_bytes(T, N)
+    wsb = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=device)
+
+    def step():
+        pkg.prefill.launch_gdn(*inp.args(), output=out, new_state=ns, workspace=wsb)
+
+    times, _ = time_steps(step, steps, warmup, ws, device, flush)
+    ms = max_over_ranks(sum(times) / len(times), ws, device)
+    flops_per_tok = 1452715.0  # fixed chunked-WY count at C=64, 8 heads
+    bytes_ = 6176 * T + 524288 * N * (2 if with_state else 1)
+    return {"tokens": T, "seqs": N, "ms": ms, "tokens_per_s": T * ws / (ms * 1e-3),
+            "algo_bytes": bytes_, "algo_flops": flops_per_tok * T,
+            "hbm_gbs": bytes_ / (ms * 1e-3) / 1e9, "tflops": flops_per_tok * T / (ms * 1e-3) / 1e12}
+
+
+def run_ours(args):
+    ws, rank, local = dist_env()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=device)
+    pkg = __graft_entry__.load_package()
+    peaks, peaks_kind = load_peaks()
+    B = DECODE_BATCH
+    inp = pkg.inputs.make_decode_inputs(B, seed=1000 + rank).to(device)
+    out = torch.empty((B, 8, 128), dtype=torch.bfloat16, device=device)
+    st = [inp.state, torch.empty_like(inp.state)]
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+    flip = [0]
+    launches = [0]
+
+    def step():
+        s_in, s_out = st[flip[0]], st[1 - flip[0]]
+        pkg.decode.launch_gdn(inp.q, inp.k, inp.v, s_in, inp.A_log, inp.a, inp.dt_bias, inp.b,
+                              inp.scale, out, s_out)
+        flip[0] ^= 1
+        launches[0] += 1
+
+    with ClockSampler(device.index) as clk:
+        times, wall = time_steps(step, args.steps, args.warmup, ws, device, flush)
+    clocks = clk.summary()
+    n_launch_timed = args.steps  # one decode kernel per step
+    ms_local = sum(times) / len(times)
+    ms = max_over_ranks(ms_local, ws, device)
+    state_bytes = B * STATE_BYTES_PER_SEQ * 2
+    value = ws * state_bytes / (ms * 1e-3) / 1e9
+    algo_bytes = DECODE_BYTES_PER_SEQ * B + DECODE_BYTES_FIXED
+    achieved = algo_bytes / (ms_local * 1e-3) / 1e9
+
+    # e2e: same step through the public host-buffer API, PCIe copies inside
+    stager = pkg.decode.HostStager(B, device)
+    h_in = [t.cpu().pin_memory() for t in (inp.q, inp.k, inp.v, inp.state, inp.A_log, inp.a,
+                                            inp.dt_bias, inp.b)]
+    h_out = torch.empty((B, 8, 128), dtype=torch.bfloat16).pin_memory()
+    h_ns = torch.empty_like(h_in[3]).pin_memory()
+
+    def e2e_step():
+        q, k, v, s, A_log, a, dtb, b = h_in
+        stager(q, k, v, s, A_log, a, dtb, b, inp.scale, h_out, h_ns)
+
+    e2e_steps = max(3, min(args.steps, 10))
+    e2e_times, _ = time_steps(e2e_step, e2e_steps, 2, ws, device, None)
+    e2e_ms = max_over_ranks(sum(e2e_times) / len(e2e_times), ws, device)
+    h2d, d2h = stager.bytes_per_step()
+
+    # prefill side numbers
+    if ws == 1:
+        pf = {"config2_T4096_N1": bench_prefill(pkg, device, [4096], 0, max(3, args.steps // 2),
+                                                 args.warmup, ws, flush, with_state=False),
+              "config3_32seq": bench_prefill(pkg, device, pkg.inputs.config3_lengths(0), 0,
+                                             max(3, args.steps // 2), args.warmup, ws, flush)}
+    else:
+        pf = {"config4b_shard_8x8192": bench_prefill(pkg, device, [8192] * 8, 2000 + rank, 3,
+                                                      min(args.warmup, 3), ws, flush)}
+
+    line = {
+        "metric": "gdn decode state-stream HBM GB/s (config 1: B=256 per GPU, fp32 k-last state)",
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": ws,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 5),
+        "decode_us_per_step": round(ms * 1e3, 2),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp32 state / bf16 io",
+        "data": "synthetic (seeded; BASELINE config 1 distributions)",
+        "config": {"workload": "config1_decode_B256_per_gpu", "batch_per_gpu": B,
+                   "global_batch": B * ws, "seq_len": 1, "parallelism": f"sequence-shard x{ws}",
+                   "l2": "flushed between steps (256 MiB write)"},
+        "gpu_launches": n_launch_timed,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     "peak_source": f"{peaks_kind} (MEASURED_PEAKS.json hbm_gbs)" if peaks_kind == "measured"
+                     else "fallback 6650 GB/s", "traffic": None,
+                     "algo_bytes_per_launch": algo_bytes, "kernel": "gdn_decode_kernel<16>"},
+        "e2e": {"value": round(ws * state_bytes / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
+                "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "api": "decode.HostStager -> launch_gdn (pinned host buffers, PCIe copies timed)"},
+        "clocks": clocks,
+        "wall_s_timed_region": round(wall, 4),
+        "prefill": pf,
+    }
+    if rank == 0 and ws == 1:
+        line["cpu_baseline"] = cpu_decode_baseline(pkg, args.cpu_budget)
+        line["cpu_baseline_prefill"] = cpu_prefill_baseline(pkg, args.cpu_budget)
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_reference(args):
+    """The reference's own algorithm on the host CPU (oracle port), rank 0 only."""
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return
+    pkg = __graft_entry__.load_package()
+    from oracle import oracle
+
+    threads = cpu_threads()
+    B = DECODE_BATCH
+    inp = pkg.inputs.make_decode_inputs(B, seed=1000)
+    for _ in range(max(1, min(args.warmup, 3))):
+        oracle.decode(*inp.args(), threads=threads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        oracle.decode(*inp.args(), threads=threads)
+        times.append(time.perf_counter() - t0)
+    sec = sum(times) / len(times)
+    value = B * STATE_BYTES_PER_SEQ * 2 / sec / 1e9
+    line = {
+        "impl": "reference",
+        "metric": "gdn decode state-stream HBM GB/s (config 1: B=256 per GPU, fp32 k-last state)",
+        "value": round(value, 4), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (seeded; BASELINE config 1 distributions)",
+        "config": {"workload": "config1_decode_B256_per_gpu", "batch_per_gpu": B, "global_batch": B,
+                   "seq_len": 1, "parallelism": "host CPU"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} full decode steps of config 1 (B=256) through "
+                                   "oracle/gdn_oracle.c (restatement of reference_torch_impl.py)"},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds per CPU-baseline sample")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,149 @@
+/*
+ * gdn_b200.h -- C ABI of the B200 (sm_100a) Gated Delta Network kernels.
+ *
+ * Two destination-passing entry points replace the two reference plugins of
+ * romitjain/kachua-mlsys:
+ *
+ *   gdn_decode_launch   replaces gdn_decode_qk4_v8_d128_k_last/solution/cuda/kernel.cu:982-1064
+ *                       (launch_gdn, bound to Python at kernel.cu:1066-1068 and
+ *                       loaded by solution/cuda/binding.py:20-51)
+ *   gdn_prefill_launch  replaces gdn_prefill_qk4_v8_d128_k_last/solution/triton/kernel.py:56-262
+ *                       (launch_gdn, registered as "flashinfer.kernel")
+ *
+ * Problem constants are those of both definitions: 4 q/k heads, 8 v heads,
+ * head dim 128, k-last fp32 state [.., 8, 128 (V), 128 (K)].
+ *
+ * Conventions
+ *   - Every pointer is a device pointer of the current CUDA device, except
+ *     the argument structs themselves (host memory).
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default
+ *     stream).  Launches are asynchronous; nothing here synchronises.
+ *   - The caller owns every buffer and must fully pre-allocate `output` and
+ *     `new_state` (destination-passing style, as the reference harness does).
+ *   - `scale == 0` selects 1/sqrt(128), as the reference's `scale is None or
+ *     scale == 0.0` (decode reference_torch_impl.py:32-33).
+ *   - Functions return a gdn_status_t; nothing is launched unless GDN_OK.
+ *     Kernels that detect bad device-side data (cu_seqlens out of range, a
+ *     bounded wait that gave up) record it in a per-device status word read
+ *     by gdn_read_device_status().
+ */
+#ifndef GDN_B200_H_
+#define GDN_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GDN_NUM_QK_HEADS 4
+#define GDN_NUM_V_HEADS 8
+#define GDN_HEAD_DIM 128
+
+typedef enum gdn_status_t {
+    GDN_OK = 0,
+    GDN_ERR_NULL_POINTER = 1,      /* a required pointer is NULL */
+    GDN_ERR_BAD_SIZE = 2,          /* negative or inconsistent sizes */
+    GDN_ERR_MISALIGNED = 3,        /* a pointer violates its alignment rule */
+    GDN_ERR_WORKSPACE = 4,         /* workspace missing or too small */
+    GDN_ERR_CUDA = 5,              /* a CUDA runtime call failed */
+    GDN_ERR_BAD_DTYPE = 6,         /* unsupported cu_seqlens dtype code */
+    GDN_ERR_NO_DEVICE = 7,         /* no usable sm_100 device is current */
+    GDN_ERR_DEVICE_BAD_SEQLENS = 16,  /* device status bit: cu_seqlens not monotone / out of range */
+    GDN_ERR_DEVICE_TIMEOUT = 32       /* device status bit: a bounded wait expired */
+} gdn_status_t;
+
+/* ---------------------------------------------------------------- decode -- */
+
+/* One decode step (one token per sequence).  Shapes (row-major, contiguous):
+ *   q, k      bf16 [B, 1, 4, 128]     (8-byte aligned)
+ *   v         bf16 [B, 1, 8, 128]
+ *   state     fp32 [B, 8, 128, 128]   k-last, 16-byte aligned; may alias new_state
+ *   A_log     fp32 [8]
+ *   a, b      bf16 [B, 1, 8]
+ *   dt_bias   fp32 [8]
+ *   output    bf16 [B, 8, 128]        (identical bytes to [B, 1, 8, 128])
+ *   new_state fp32 [B, 8, 128, 128]   16-byte aligned
+ * Reference: gdn_decode_qk4_v8_d128_k_last/solution/cuda/kernel.cu:982-994. */
+typedef struct GdnDecodeArgs {
+    const void* q;
+    const void* k;
+    const void* v;
+    const float* state;
+    const float* A_log;
+    const void* a;
+    const float* dt_bias;
+    const void* b;
+    void* output;
+    float* new_state;
+    int64_t batch;
+    float scale;
+} GdnDecodeArgs;
+
+int gdn_decode_launch(const GdnDecodeArgs* args, void* stream);
+
+/* --------------------------------------------------------------- prefill -- */
+
+#define GDN_SEQLENS_INT32 0
+#define GDN_SEQLENS_INT64 1
+
+/* Variable-length prefill over packed sequences.  Shapes:
+ *   q, k       bf16 [T, 4, 128]        16-byte aligned
+ *   v          bf16 [T, 8, 128]        16-byte aligned
+ *   state      fp32 [N, 8, 128, 128]   or NULL (zero initial state)
+ *   A_log      fp32 [8];  dt_bias fp32 [8]
+ *   a, b       bf16 [T, 8]
+ *   cu_seqlens int32 or int64 [N + 1], non-decreasing, cu[0] = 0, cu[N] <= T
+ *   output     bf16 [T, 8, 128]        16-byte aligned
+ *   new_state  fp32 [N, 8, 128, 128]   16-byte aligned; must not alias state
+ * Empty sequences get a zero new_state row, as the reference oracle
+ * (prefill reference_torch_impl.py:53-55).  Output rows of tokens that belong
+ * to no sequence are written as zeros.
+ * Reference: gdn_prefill_qk4_v8_d128_k_last/solution/triton/kernel.py:56-57. */
+typedef struct GdnPrefillArgs {
+    const void* q;
+    const void* k;
+    const void* v;
+    const float* state;
+    const float* A_log;
+    const void* a;
+    const float* dt_bias;
+    const void* b;
+    const void* cu_seqlens;
+    int32_t cu_seqlens_dtype;
+    int32_t reserved0;
+    int64_t total_tokens;
+    int64_t num_seqs;
+    float scale;
+    void* output;
+    float* new_state;
+} GdnPrefillArgs;
+
+/* Bytes of device workspace gdn_prefill_launch needs for these sizes
+ * (256-byte aligned base).  Replaces the torch.empty scratch tensors the
+ * reference allocates per call (triton/kernel.py:136-168, :196-218). */
+size_t gdn_prefill_workspace_size(int64_t total_tokens, int64_t num_seqs);
+
+int gdn_prefill_launch(const GdnPrefillArgs* args, void* workspace, size_t workspace_bytes,
+                       void* stream);
+
+/* ---------------------------------------------------------------- status -- */
+
+/* Human-readable name of a gdn_status_t (static string). */
+const char* gdn_status_string(int status);
+
+/* Synchronises `stream`, then stores the current device's status word (OR of
+ * GDN_ERR_DEVICE_* bits recorded by kernels since the last clear) in *out.
+ * When `clear` is non-zero the word is reset to 0.  No reference counterpart:
+ * the reference performs no error checking (kernel.cu:982-1064). */
+int gdn_read_device_status(int* out, int clear, void* stream);
+
+/* ABI version of this header (bumped on any struct or signature change). */
+int gdn_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDN_B200_H_ */

@@ -1,0 +1,146 @@
+// gdn_capi.cu -- the extern "C" boundary (include/gdn_b200.h).
+//
+// The library is built as one translation unit: this file includes every
+// kernel source, so the per-device status word needs no relocatable device
+// code.  Every entry point validates pointers, sizes and alignment on the
+// host and returns a gdn_status_t before anything is launched; the reference
+// plugin did no checking at all (kernel.cu:982-1064).
+#include "gdn_b200.h"
+
+#include "gdn_common.cuh"
+#include "gdn_decode.cu"
+#include "gdn_prefill_recurrent.cu"
+#include "gdn_prefill_chunked.cu"
+
+#include <math.h>
+
+namespace gdn {
+static bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// The current device must be an sm_100 part (the cubin is sm_100a only).
+static int check_device() {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) return GDN_ERR_NO_DEVICE;
+    static int cached[64];  // 0 = unknown, 1 = ok, 2 = bad
+    if (dev >= 0 && dev < 64 && cached[dev] != 0) return cached[dev] == 1 ? GDN_OK : GDN_ERR_NO_DEVICE;
+    int major = 0, minor = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
+        return GDN_ERR_NO_DEVICE;
+    const bool ok = (major == 10 && minor == 0);
+    if (dev >= 0 && dev < 64) cached[dev] = ok ? 1 : 2;
+    return ok ? GDN_OK : GDN_ERR_NO_DEVICE;
+}
+
+static float resolve_scale(float s) { return s == 0.0f ? 1.0f / sqrtf((float)kD) : s; }
+}  // namespace gdn
+
+using namespace gdn;
+
+extern "C" int gdn_abi_version(void) { return 1; }
+
+extern "C" const char* gdn_status_string(int status) {
+    switch (status) {
+        case GDN_OK: return "ok";
+        case GDN_ERR_NULL_POINTER: return "a required pointer is NULL";
+        case GDN_ERR_BAD_SIZE: return "negative or inconsistent sizes";
+        case GDN_ERR_MISALIGNED: return "a pointer violates its alignment rule";
+        case GDN_ERR_WORKSPACE: return "workspace missing or too small";
+        case GDN_ERR_CUDA: return "a CUDA runtime call failed";
+        case GDN_ERR_BAD_DTYPE: return "unsupported cu_seqlens dtype code";
+        case GDN_ERR_NO_DEVICE: return "no usable sm_100 device is current";
+        case GDN_ERR_DEVICE_BAD_SEQLENS: return "device: cu_seqlens not monotone or out of range";
+        case GDN_ERR_DEVICE_TIMEOUT: return "device: a bounded wait expired";
+        default: return "unknown status";
+    }
+}
+
+extern "C" int gdn_decode_launch(const GdnDecodeArgs* a, void* stream) {
+    if (a == nullptr) return GDN_ERR_NULL_POINTER;
+    if (a->batch < 0) return GDN_ERR_BAD_SIZE;
+    if (a->batch == 0) return GDN_OK;
+    if (!a->q || !a->k || !a->v || !a->state || !a->A_log || !a->a || !a->dt_bias || !a->b ||
+        !a->output || !a->new_state)
+        return GDN_ERR_NULL_POINTER;
+    if (!aligned(a->q, 8) || !aligned(a->k, 8) || !aligned(a->state, 16) || !aligned(a->new_state, 16) ||
+        !aligned(a->v, 2) || !aligned(a->a, 2) || !aligned(a->b, 2) || !aligned(a->output, 2) ||
+        !aligned(a->A_log, 4) || !aligned(a->dt_bias, 4))
+        return GDN_ERR_MISALIGNED;
+    if (int rc = check_device()) return rc;
+    DecodeParams p;
+    p.q = static_cast<const uint16_t*>(a->q);
+    p.k = static_cast<const uint16_t*>(a->k);
+    p.v = static_cast<const uint16_t*>(a->v);
+    p.state = a->state;
+    p.A_log = a->A_log;
+    p.a = static_cast<const uint16_t*>(a->a);
+    p.dt_bias = a->dt_bias;
+    p.b = static_cast<const uint16_t*>(a->b);
+    p.out = static_cast<uint16_t*>(a->output);
+    p.new_state = a->new_state;
+    p.batch = a->batch;
+    p.scale = resolve_scale(a->scale);
+    return launch_decode(p, static_cast<cudaStream_t>(stream)) == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
+}
+
+extern "C" size_t gdn_prefill_workspace_size(int64_t total_tokens, int64_t num_seqs) {
+    if (total_tokens < 0 || num_seqs < 0) return 0;
+    return chunked_workspace_bytes(total_tokens, num_seqs);
+}
+
+extern "C" int gdn_prefill_launch(const GdnPrefillArgs* a, void* workspace, size_t workspace_bytes,
+                                  void* stream) {
+    if (a == nullptr) return GDN_ERR_NULL_POINTER;
+    if (a->total_tokens < 0 || a->num_seqs < 0) return GDN_ERR_BAD_SIZE;
+    if (a->cu_seqlens_dtype != GDN_SEQLENS_INT32 && a->cu_seqlens_dtype != GDN_SEQLENS_INT64)
+        return GDN_ERR_BAD_DTYPE;
+    if (!a->cu_seqlens || !a->A_log || !a->dt_bias) return GDN_ERR_NULL_POINTER;
+    if (a->total_tokens > 0 &&
+        (!a->q || !a->k || !a->v || !a->a || !a->b || !a->output))
+        return GDN_ERR_NULL_POINTER;
+    if (a->num_seqs > 0 && !a->new_state) return GDN_ERR_NULL_POINTER;
+    if (!aligned(a->q, 16) || !aligned(a->k, 16) || !aligned(a->v, 16) || !aligned(a->output, 16) ||
+        !aligned(a->new_state, 16) || !aligned(a->state, 16) || !aligned(a->a, 2) || !aligned(a->b, 2) ||
+        !aligned(a->cu_seqlens, a->cu_seqlens_dtype == GDN_SEQLENS_INT64 ? 8 : 4))
+        return GDN_ERR_MISALIGNED;
+    if (a->state != nullptr && a->num_seqs > 0 && a->state == a->new_state) return GDN_ERR_BAD_SIZE;
+    if (int rc = check_device()) return rc;
+    const size_t need = chunked_workspace_bytes(a->total_tokens, a->num_seqs);
+    if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 256)))
+        return GDN_ERR_WORKSPACE;
+
+    PrefillParams p;
+    p.q = static_cast<const uint16_t*>(a->q);
+    p.k = static_cast<const uint16_t*>(a->k);
+    p.v = static_cast<const uint16_t*>(a->v);
+    p.state = a->state;
+    p.A_log = a->A_log;
+    p.a = static_cast<const uint16_t*>(a->a);
+    p.dt_bias = a->dt_bias;
+    p.b = static_cast<const uint16_t*>(a->b);
+    p.cu_seqlens = a->cu_seqlens;
+    p.cu_is_int64 = a->cu_seqlens_dtype == GDN_SEQLENS_INT64;
+    p.total_tokens = a->total_tokens;
+    p.num_seqs = a->num_seqs;
+    p.scale = resolve_scale(a->scale);
+    p.out = static_cast<uint16_t*>(a->output);
+    p.new_state = a->new_state;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (a->total_tokens > 0 && launch_prefill_zero_uncovered(p, s) != cudaSuccess) return GDN_ERR_CUDA;
+    if (a->num_seqs == 0) return GDN_OK;
+    const cudaError_t e = launch_prefill(p, workspace, workspace_bytes, s);
+    return e == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
+}
+
+extern "C" int gdn_read_device_status(int* out, int clear, void* stream) {
+    if (out == nullptr) return GDN_ERR_NULL_POINTER;
+    if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess) return GDN_ERR_CUDA;
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_status, sizeof(int)) != cudaSuccess) return GDN_ERR_CUDA;
+    *out = v;
+    if (clear) {
+        const int z = 0;
+        if (cudaMemcpyToSymbol(g_status, &z, sizeof(int)) != cudaSuccess) return GDN_ERR_CUDA;
+    }
+    return GDN_OK;
+}

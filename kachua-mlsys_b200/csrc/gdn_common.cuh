@@ -1,0 +1,74 @@
+// gdn_common.cuh -- shared constants and device helpers for the GDN kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gdn {
+
+constexpr int kHQK = 4;        // q/k heads
+constexpr int kHV = 8;         // v heads
+constexpr int kGva = kHV / kHQK;
+constexpr int kD = 128;        // head dim (K and V)
+constexpr int kSmCount = 148;  // B200
+
+// Per-device status word (OR of GDN_ERR_DEVICE_* bits); one copy per device
+// that loads the library.  The library is a single translation unit
+// (gdn_capi.cu includes every kernel file), so this is its only definition.
+__device__ int g_status = 0;
+
+__device__ __forceinline__ void record_status(int bits) { atomicOr(&g_status, bits); }
+
+__device__ __forceinline__ float bf16_bits_to_float(uint16_t h) {
+    return __uint_as_float(static_cast<uint32_t>(h) << 16);
+}
+
+// 4 packed bf16 (8 bytes) -> 4 floats
+__device__ __forceinline__ float4 bf16x4_to_float4(uint2 u) {
+    float4 r;
+    r.x = __uint_as_float(u.x << 16);
+    r.y = __uint_as_float(u.x & 0xffff0000u);
+    r.z = __uint_as_float(u.y << 16);
+    r.w = __uint_as_float(u.y & 0xffff0000u);
+    return r;
+}
+
+// torch.nn.functional.softplus(x) with beta=1, threshold=20.
+__device__ __forceinline__ float softplus_f(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+
+// Decay g = exp(-exp(A_log) * softplus(a + dt_bias)) and beta = sigmoid(b),
+// as decode reference_torch_impl.py:35-38 / prefill :34-36.
+__device__ __forceinline__ void gdn_gates(float A_log, float dt_bias, float a, float b, float& g,
+                                          float& beta) {
+    const float x = a + dt_bias;
+    g = expf(-expf(A_log) * softplus_f(x));
+    beta = 1.0f / (1.0f + expf(-b));
+}
+
+// log2 of the decay, for the chunked path: log2 g = -exp(A_log) * softplus(x) / ln 2.
+__device__ __forceinline__ float gdn_log2_decay(float A_log, float dt_bias, float a) {
+    return -expf(A_log) * softplus_f(a + dt_bias) * 1.4426950408889634f;
+}
+
+// Streaming 16-byte load that bypasses L1.  Coherent (no .nc), so it stays
+// correct when the state is updated in place (state == new_state).
+__device__ __forceinline__ float4 ld_stream_f4(const float* p) {
+    float4 r;
+    asm volatile("ld.global.L1::no_allocate.L2::256B.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ void st_stream_f4(float* p, float4 v) {
+    asm volatile("st.global.cs.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z),
+                 "f"(v.w)
+                 : "memory");
+}
+
+__device__ __forceinline__ uint2 ld_u2(const void* p) {
+    return *reinterpret_cast<const uint2*>(p);
+}
+
+}  // namespace gdn

@@ -1,0 +1,91 @@
+"""Decode kernel parity against the CPU oracle (decode reference_torch_impl.py:12-72).
+
+Bars (from the north star): bf16 output within atol/rtol 1e-2 of the oracle's
+fp32 output; fp32 new state within 1e-3 norm-wise relative error
+(max|got-ref| / max|ref|).
+"""
+import numpy as np
+import pytest
+import torch
+
+from tests.conftest import state_rel_err
+from tests.golden.cases import CASES, build_inputs
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(pkg, inp, dev, **kw):
+    g = inp.to(dev)
+    out, ns = pkg.decode.launch_gdn(*g.args(), **kw)
+    torch.cuda.synchronize()
+    return out.cpu(), ns.cpu()
+
+
+@pytest.mark.parametrize("batch", [1, 2, 3, 5, 8, 17, 64, 256])
+def test_decode_matches_oracle(pkg, orc, cuda_dev, batch):
+    inp = pkg.inputs.make_decode_inputs(batch, seed=100 + batch)
+    ro, rs = orc.decode(*inp.args())
+    out, ns = _run(pkg, inp, cuda_dev)
+    assert out.dtype == torch.bfloat16 and out.shape == (batch, 8, 128)
+    torch.testing.assert_close(out.float(), ro, atol=1e-2, rtol=1e-2)
+    assert state_rel_err(ns, rs) < 1e-3
+    # the streaming update is fp32 throughout: far inside the bar
+    assert state_rel_err(ns, rs) < 1e-5
+
+
+@pytest.mark.parametrize("name", ["decode_b2", "decode_b1_scale"])
+def test_decode_matches_reference_vectors(pkg, cuda_dev, name):
+    """GPU output against the vectors produced by the reference itself."""
+    from pathlib import Path
+
+    case = CASES[name]
+    inp = build_inputs(case)
+    z = np.load(Path(__file__).parent / "golden" / f"{name}.npz")
+    out, ns = _run(pkg, inp, cuda_dev)
+    torch.testing.assert_close(out.float(), torch.from_numpy(z["output"]), atol=1e-2, rtol=1e-2)
+    assert state_rel_err(ns, torch.from_numpy(z["new_state"])) < 1e-5
+
+
+def test_decode_in_place(pkg, orc, cuda_dev):
+    inp = pkg.inputs.make_decode_inputs(33, seed=7)
+    ro, rs = orc.decode(*inp.args())
+    g = inp.to(cuda_dev)
+    out = torch.empty(33, 1, 8, 128, dtype=torch.bfloat16, device=cuda_dev)  # [B,1,8,128] form
+    pkg.decode.launch_gdn(g.q, g.k, g.v, g.state, g.A_log, g.a, g.dt_bias, g.b, g.scale, out, g.state)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(out.view(33, 8, 128).float().cpu(), ro, atol=1e-2, rtol=1e-2)
+    assert state_rel_err(g.state, rs) < 1e-5
+
+
+@pytest.mark.parametrize("scale", [None, 0.0, 0.05, -0.3])
+def test_decode_scale(pkg, orc, cuda_dev, scale):
+    inp = pkg.inputs.make_decode_inputs(4, seed=3)
+    inp.scale = scale
+    ro, rs = orc.decode(*inp.args())
+    out, ns = _run(pkg, inp, cuda_dev)
+    torch.testing.assert_close(out.float(), ro, atol=1e-2, rtol=1e-2)
+
+
+def test_decode_deterministic(pkg, cuda_dev):
+    inp = pkg.inputs.make_decode_inputs(40, seed=8)
+    o1, s1 = _run(pkg, inp, cuda_dev)
+    o2, s2 = _run(pkg, inp, cuda_dev)
+    assert torch.equal(o1, o2) and torch.equal(s1, s2)
+
+
+def test_decode_empty_batch(pkg, cuda_dev):
+    inp = pkg.inputs.make_decode_inputs(0, seed=0)
+    out, ns = _run(pkg, inp, cuda_dev)
+    assert out.shape == (0, 8, 128) and ns.shape == (0, 8, 128, 128)
+
+
+def test_decode_large_values_finite(pkg, orc, cuda_dev):
+    """Extreme gates: softplus threshold (a > 20) and saturated beta."""
+    inp = pkg.inputs.make_decode_inputs(6, seed=21)
+    inp.a = (inp.a.float() * 30).to(torch.bfloat16)
+    inp.b = (inp.b.float() * 30).to(torch.bfloat16)
+    ro, rs = orc.decode(*inp.args())
+    out, ns = _run(pkg, inp, cuda_dev)
+    assert torch.isfinite(out.float()).all() and torch.isfinite(ns).all()
+    torch.testing.assert_close(out.float(), ro, atol=1e-2, rtol=1e-2)
+    assert state_rel_err(ns, rs) < 1e-3
