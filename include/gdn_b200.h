@@ -88,6 +88,15 @@ int gdn_decode_launch(const GdnDecodeArgs* args, void* stream);
 #define GDN_SEQLENS_INT32 0
 #define GDN_SEQLENS_INT64 1
 
+/* Prefill algorithm selector (GdnPrefillArgs.path).  AUTO sends batches of
+ * short sequences (mean length <= 48) to the token-recurrent kernel and the
+ * rest to the chunked tensor-core kernels.  No reference counterpart: the
+ * reference's host dispatch chose among its Triton paths internally
+ * (triton/kernel.py:93-129). */
+#define GDN_PREFILL_PATH_AUTO 0
+#define GDN_PREFILL_PATH_RECURRENT 1
+#define GDN_PREFILL_PATH_CHUNKED 2
+
 /* Variable-length prefill over packed sequences.  Shapes:
  *   q, k       bf16 [T, 4, 128]        16-byte aligned
  *   v          bf16 [T, 8, 128]        16-byte aligned
@@ -112,7 +121,7 @@ typedef struct GdnPrefillArgs {
     const void* b;
     const void* cu_seqlens;
     int32_t cu_seqlens_dtype;
-    int32_t reserved0;
+    int32_t path;            /* GDN_PREFILL_PATH_*; 0 = automatic choice */
     int64_t total_tokens;
     int64_t num_seqs;
     float scale;
@@ -141,6 +150,19 @@ int gdn_read_device_status(int* out, int clear, void* stream);
 
 /* ABI version of this header (bumped on any struct or signature change). */
 int gdn_abi_version(void);
+
+/* ------------------------------------------------------------ diagnostics -- */
+
+#define GDN_MMA_KIND_BF16 1
+#define GDN_MMA_KIND_TF32 2
+
+/* D[M x N] = A[M x K] . B[N x K]^T on one CTA through the same shared-memory
+ * operand images, tcgen05 descriptors and TMEM read-back the prefill kernels
+ * use.  A, B row-major (bf16 for BF16, fp32 for TF32 -- rounded to tf32);
+ * D fp32 row-major.  M in {64, 128}; N a multiple of 16 in [16, 256];
+ * K in {64, 128}.  No reference counterpart: a self-test of the tensor-core
+ * layer. */
+int gdn_mma_selftest(int kind, int M, int N, int K, const void* A, const void* B, float* D, void* stream);
 
 #ifdef __cplusplus
 }

@@ -27,8 +27,11 @@ EXPORTED_SYMBOLS = (
     "gdn_status_string",
     "gdn_read_device_status",
     "gdn_abi_version",
+    "gdn_mma_selftest",
 )
-ABI_VERSION = 1
+ABI_VERSION = 2
+PATH_AUTO, PATH_RECURRENT, PATH_CHUNKED = 0, 1, 2
+MMA_KIND_BF16, MMA_KIND_TF32 = 1, 2
 
 
 class GdnDecodeArgs(ctypes.Structure):
@@ -60,7 +63,7 @@ class GdnPrefillArgs(ctypes.Structure):
         ("b", ctypes.c_void_p),
         ("cu_seqlens", ctypes.c_void_p),
         ("cu_seqlens_dtype", ctypes.c_int32),
-        ("reserved0", ctypes.c_int32),
+        ("path", ctypes.c_int32),
         ("total_tokens", ctypes.c_int64),
         ("num_seqs", ctypes.c_int64),
         ("scale", ctypes.c_float),
@@ -105,6 +108,8 @@ def load(build_if_needed: bool = True) -> ctypes.CDLL:
         lib.gdn_read_device_status.restype = ctypes.c_int
         lib.gdn_abi_version.argtypes = []
         lib.gdn_abi_version.restype = ctypes.c_int
+        lib.gdn_mma_selftest.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, P, P]
+        lib.gdn_mma_selftest.restype = ctypes.c_int
         if lib.gdn_abi_version() != ABI_VERSION:
             raise RuntimeError("libgdn_b200.so ABI version mismatch; rebuild it")
         _lib = lib

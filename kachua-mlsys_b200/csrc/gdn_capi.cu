@@ -37,7 +37,7 @@ static float resolve_scale(float s) { return s == 0.0f ? 1.0f / sqrtf((float)kD)
 
 using namespace gdn;
 
-extern "C" int gdn_abi_version(void) { return 1; }
+extern "C" int gdn_abi_version(void) { return 2; }
 
 extern "C" const char* gdn_status_string(int status) {
     switch (status) {
@@ -94,6 +94,7 @@ extern "C" int gdn_prefill_launch(const GdnPrefillArgs* a, void* workspace, size
     if (a->total_tokens < 0 || a->num_seqs < 0) return GDN_ERR_BAD_SIZE;
     if (a->cu_seqlens_dtype != GDN_SEQLENS_INT32 && a->cu_seqlens_dtype != GDN_SEQLENS_INT64)
         return GDN_ERR_BAD_DTYPE;
+    if (a->path < GDN_PREFILL_PATH_AUTO || a->path > GDN_PREFILL_PATH_CHUNKED) return GDN_ERR_BAD_SIZE;
     if (!a->cu_seqlens || !a->A_log || !a->dt_bias) return GDN_ERR_NULL_POINTER;
     if (a->total_tokens > 0 &&
         (!a->q || !a->k || !a->v || !a->a || !a->b || !a->output))
@@ -128,7 +129,7 @@ extern "C" int gdn_prefill_launch(const GdnPrefillArgs* a, void* workspace, size
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (a->total_tokens > 0 && launch_prefill_zero_uncovered(p, s) != cudaSuccess) return GDN_ERR_CUDA;
     if (a->num_seqs == 0) return GDN_OK;
-    const cudaError_t e = launch_prefill(p, workspace, workspace_bytes, s);
+    const cudaError_t e = launch_prefill(p, a->path, workspace, workspace_bytes, s);
     return e == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
 }
 
@@ -143,4 +144,16 @@ extern "C" int gdn_read_device_status(int* out, int clear, void* stream) {
         if (cudaMemcpyToSymbol(g_status, &z, sizeof(int)) != cudaSuccess) return GDN_ERR_CUDA;
     }
     return GDN_OK;
+}
+
+extern "C" int gdn_mma_selftest(int kind, int M, int N, int K, const void* A, const void* B, float* D,
+                                void* stream) {
+    if (!A || !B || !D) return GDN_ERR_NULL_POINTER;
+    if ((kind != GDN_MMA_KIND_BF16 && kind != GDN_MMA_KIND_TF32) || (M != 64 && M != 128) || N < 16 ||
+        N > 256 || N % 16 != 0 || (K != 64 && K != 128))
+        return GDN_ERR_BAD_SIZE;
+    if (int rc = check_device()) return rc;
+    return launch_mma_selftest(kind, M, N, K, A, B, D, static_cast<cudaStream_t>(stream)) == cudaSuccess
+               ? GDN_OK
+               : GDN_ERR_CUDA;
 }

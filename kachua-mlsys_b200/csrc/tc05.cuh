@@ -1,0 +1,216 @@
+// tc05.cuh -- thin inline-PTX layer over the sm_100a async units used here:
+// tcgen05 (tensor-core MMA with TMEM accumulators), TMA bulk copies
+// (cp.async.bulk, no tensor map, never multicast) and mbarriers.
+//
+// Operand images.  Every MMA operand lives in shared memory as a K-major
+// "SW128" image: rows of 128 bytes grouped 8 per 1024-byte atom, the 16-byte
+// chunks of row r XOR-swizzled by (r & 7).  An operand with more than 128
+// bytes of K per row is split into K-blocks, each a separate [rows][128 B]
+// image placed back to back.  Element (r, c) of a fp32 image lives in K-block
+// c / 32 at byte (c % 32) * 4 of row r; of a bf16 image in K-block c / 64 at
+// byte (c % 64) * 2.  Image bases are 1024-byte aligned.  The same byte
+// layout is used for operand images stored in global memory, so they move
+// with one bulk copy.
+//
+// Accumulators.  cta_group::1 MMAs with M = 128 put row m in TMEM lane m; with
+// M = 64 row m sits in lane (m % 16) + 32 * (m / 16), i.e. lanes 0-15 of each
+// warp's 32-lane sub-partition.  Column n of the tile is TMEM column base + n.
+#pragma once
+
+#include <stdint.h>
+
+namespace gdn {
+namespace tc05 {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Byte offset of element (row, byte-in-row) in a SW128 image whose K-blocks
+// hold `rows` rows each.
+__device__ __forceinline__ uint32_t sw128_off(int row, int byte_in_kblock_row, int kblock, int rows) {
+    return static_cast<uint32_t>(kblock * rows * 128 + row * 128 +
+                                 ((((byte_in_kblock_row >> 4) ^ (row & 7)) << 4) | (byte_in_kblock_row & 15)));
+}
+__device__ __forceinline__ uint32_t sw128_f32(int row, int col, int rows) {
+    return sw128_off(row, (col & 31) * 4, col >> 5, rows);
+}
+__device__ __forceinline__ uint32_t sw128_bf16(int row, int col, int rows) {
+    return sw128_off(row, (col & 63) * 2, col >> 6, rows);
+}
+
+// ---------------------------------------------------------------- mbarrier --
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait: gives up after `limit` polls (each poll may itself block for a
+// hardware-defined slice) and returns false; callers record a status bit and
+// unwind instead of hanging the GPU.
+constexpr uint32_t kWaitLimit = 1u << 24;
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    for (uint32_t i = 0; i < kWaitLimit; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+
+// ------------------------------------------------------------ bulk copies --
+__device__ __forceinline__ void bulk_g2s(uint32_t dst_smem, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst_smem),
+        "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void bulk_s2g(void* dst, uint32_t src_smem, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src_smem), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_all() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Generic-proxy shared-memory writes -> visible to the async proxy (MMA, bulk copy).
+__device__ __forceinline__ void fence_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ------------------------------------------------------------------- TMEM --
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// 32 lanes x 32 consecutive columns -> 32 registers per thread.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&r)[32]) {
+    uint32_t u[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]), "=r"(u[7]),
+          "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]), "=r"(u[14]), "=r"(u[15]),
+          "=r"(u[16]), "=r"(u[17]), "=r"(u[18]), "=r"(u[19]), "=r"(u[20]), "=r"(u[21]), "=r"(u[22]), "=r"(u[23]),
+          "=r"(u[24]), "=r"(u[25]), "=r"(u[26]), "=r"(u[27]), "=r"(u[28]), "=r"(u[29]), "=r"(u[30]), "=r"(u[31])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 32; ++i) r[i] = __uint_as_float(u[i]);
+}
+// 32 lanes x 16 consecutive columns.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&r)[16]) {
+    uint32_t u[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]), "=r"(u[7]),
+          "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]), "=r"(u[14]), "=r"(u[15])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 16; ++i) r[i] = __uint_as_float(u[i]);
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// TMEM address of (lane, column) relative to an allocation base.
+__device__ __forceinline__ uint32_t taddr(uint32_t base, uint32_t lane, uint32_t col) {
+    return base + (lane << 16) + col;
+}
+
+// ---------------------------------------------------------------- the MMA --
+// Shared-memory matrix descriptor of a K-major SW128 image (sm_100 format:
+// start >> 4 at [0,14), LBO >> 4 at [16,30) (unused for swizzled K-major,
+// set to 1), SBO >> 4 at [32,46) = 1024 B between 8-row groups, version 1 at
+// [46,48), base offset 0, layout SWIZZLE_128B (2) at [61,64)).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
+    return (static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu)) | (1ull << 16) | (64ull << 32) | (1ull << 46) |
+           (2ull << 61);
+}
+
+enum Kind : uint32_t { kBF16 = 1, kTF32 = 2 };
+
+// Instruction descriptor (kind::f16 / kind::tf32): fp32 accumulator, A and B
+// of the same format, both K-major, no negation, dense.
+__host__ __device__ constexpr uint32_t idesc(Kind k, int M, int N) {
+    return (1u << 4) | (static_cast<uint32_t>(k) << 7) | (static_cast<uint32_t>(k) << 10) |
+           (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(id), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(id), "r"(acc)
+        : "memory");
+}
+// Arrives once on `bar` when every tcgen05 op this thread issued so far is done.
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+// D[M x N] (+)= A[M x Kdim] . B[N x Kdim]^T over whole K-blocks of SW128
+// images; `a_rows` / `b_rows` are the rows per K-block of each image (the
+// K-block stride is rows * 128 bytes).  Issued by one thread.
+template <Kind KIND>
+__device__ __forceinline__ void mma_tile(uint32_t d_tmem, uint32_t a_smem, int a_rows, uint32_t b_smem, int b_rows,
+                                         int kdim, int M, int N, bool accumulate) {
+    const uint32_t id = idesc(KIND, M, N);
+    constexpr int kElemBytes = KIND == kBF16 ? 2 : 4;
+    constexpr int kStepBytes = 32;  // K = 16 (bf16) or 8 (tf32) per instruction
+    const int steps = kdim * kElemBytes / kStepBytes;
+#pragma unroll 1
+    for (int s = 0; s < steps; ++s) {
+        const int kb = (s * kStepBytes) >> 7;
+        const int in = (s * kStepBytes) & 127;
+        const uint64_t ad = sw128_desc(a_smem + kb * a_rows * 128 + in);
+        const uint64_t bd = sw128_desc(b_smem + kb * b_rows * 128 + in);
+        if (KIND == kBF16)
+            mma_bf16(d_tmem, ad, bd, id, (accumulate || s > 0) ? 1u : 0u);
+        else
+            mma_tf32(d_tmem, ad, bd, id, (accumulate || s > 0) ? 1u : 0u);
+    }
+}
+
+// fp32 -> tf32 with round-to-nearest (ties away); low 13 bits cleared.
+__device__ __forceinline__ float to_tf32(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+}  // namespace tc05
+}  // namespace gdn

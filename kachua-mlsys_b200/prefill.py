@@ -87,9 +87,20 @@ def _ptr(t):
     return ctypes.c_void_p(None if t is None else t.data_ptr())
 
 
+PATHS = {"auto": 0, "recurrent": 1, "chunked": 2}
+
+
 def launch_gdn(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None, output=None,
-               new_state=None, workspace: torch.Tensor | None = None, check_seqlens: bool = False):
-    """Varlen GDN prefill (destination-passing); returns ``(output, new_state)``."""
+               new_state=None, workspace: torch.Tensor | None = None, check_seqlens: bool = False,
+               path: str = "auto"):
+    """Varlen GDN prefill (destination-passing); returns ``(output, new_state)``.
+
+    ``path`` selects the algorithm: ``"auto"`` (token-recurrent kernel for
+    batches of short sequences, chunked tensor-core kernels otherwise),
+    ``"recurrent"`` or ``"chunked"``.  ``workspace`` may be passed to reuse a
+    device buffer of at least ``workspace_bytes(T, N)`` bytes.
+    """
+    _need(path in PATHS, f"path must be one of {sorted(PATHS)}")
     _need(isinstance(q, torch.Tensor), "q must be a torch.Tensor")
     if isinstance(cu_seqlens, torch.Tensor) and cu_seqlens.device != q.device:
         cu_seqlens = cu_seqlens.to(q.device)
@@ -107,8 +118,8 @@ def launch_gdn(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None, out
     args = _capi.GdnPrefillArgs(
         _ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a), _ptr(dt_bias), _ptr(b),
         _ptr(cu_seqlens),
-        _capi.GDN_SEQLENS_INT64 if cu_seqlens.dtype == torch.int64 else _capi.GDN_SEQLENS_INT32, 0,
-        T, N, 0.0 if scale is None else float(scale), _ptr(output), _ptr(new_state))
+        _capi.GDN_SEQLENS_INT64 if cu_seqlens.dtype == torch.int64 else _capi.GDN_SEQLENS_INT32,
+        PATHS[path], T, N, 0.0 if scale is None else float(scale), _ptr(output), _ptr(new_state))
     ws_ptr = _ptr(workspace) if need > 0 else ctypes.c_void_p(None)
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream

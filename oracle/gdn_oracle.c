@@ -104,13 +104,13 @@ static void load_bf16_vec(const uint16_t* src, float* dst) {
 /*
  * Decode: q,k bf16 [B,1,4,128]; v bf16 [B,1,8,128]; state fp32 [B,8,128,128];
  * A_log, dt_bias fp32 [8]; a, b bf16 [B,1,8]; output fp32 [B,8,128];
- * new_state fp32 [B,8,128,128].  scale <= 0 selects 1/sqrt(128).
+ * new_state fp32 [B,8,128,128].  scale == 0 selects 1/sqrt(128) (None maps to 0).
  */
 int oracle_gdn_decode(const uint16_t* q, const uint16_t* k, const uint16_t* v,
                       const float* state, const float* A_log, const uint16_t* a,
                       const float* dt_bias, const uint16_t* b, float scale,
                       int64_t batch, float* output, float* new_state, int num_threads) {
-    if (scale <= 0.0f) scale = 1.0f / sqrtf((float)ORC_D);
+    if (scale == 0.0f) scale = 1.0f / sqrtf((float)ORC_D); /* `scale is None or scale == 0.0` */
     const int64_t units = batch * ORC_HV;
 #pragma omp parallel for schedule(dynamic, 4) num_threads(num_threads)
     for (int64_t u = 0; u < units; ++u) {
@@ -144,7 +144,7 @@ int oracle_gdn_prefill(const uint16_t* q, const uint16_t* k, const uint16_t* v,
                        const float* dt_bias, const uint16_t* b,
                        const int64_t* cu_seqlens, int64_t num_seqs, int64_t total_tokens,
                        float scale, uint16_t* output, float* new_state, int num_threads) {
-    if (scale <= 0.0f) scale = 1.0f / sqrtf((float)ORC_D);
+    if (scale == 0.0f) scale = 1.0f / sqrtf((float)ORC_D); /* `scale is None or scale == 0.0` */
     memset(output, 0, sizeof(uint16_t) * (size_t)total_tokens * ORC_HV * ORC_D);
     const int64_t units = num_seqs * ORC_HV;
 #pragma omp parallel for schedule(dynamic, 1) num_threads(num_threads)

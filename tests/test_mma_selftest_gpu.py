@@ -1,0 +1,57 @@
+"""The tcgen05 layer (SW128 operand images, smem/instruction descriptors,
+M=64 / M=128 TMEM layouts, bf16 and tf32 kinds) against torch matmul, for
+every shape the prefill kernels issue."""
+import ctypes
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [  # (kind, M, N, K): the prepare and carry kernels' MMAs, plus neighbours
+    ("bf16", 128, 64, 128),   # [K;Q] K^T
+    ("tf32", 64, 64, 64),     # Neumann products
+    ("tf32", 64, 256, 64),    # [W | U]
+    ("tf32", 64, 16, 128),    # W S^T, BV=16
+    ("tf32", 64, 32, 128),    # W S^T, BV=32
+    ("bf16", 64, 16, 128),    # Q S^T
+    ("bf16", 64, 32, 128),
+    ("tf32", 128, 16, 64),    # (tail K)^T Delta
+    ("tf32", 128, 32, 64),
+    ("bf16", 64, 16, 64),     # P Delta
+    ("bf16", 64, 32, 64),
+    ("tf32", 128, 128, 128),
+    ("bf16", 128, 256, 128),
+]
+
+
+def _tf32(x):
+    """Round-to-nearest (ties away) to tf32, as cvt.rna.tf32.f32."""
+    xi = x.contiguous().view(torch.int32)
+    return ((xi + 0x1000) & ~0x1FFF).view(torch.float32)
+
+
+@pytest.mark.parametrize("kind,M,N,K", SHAPES)
+def test_mma_selftest(pkg, cuda_dev, kind, M, N, K):
+    C = pkg._capi
+    lib = C.load()
+    g = torch.Generator().manual_seed(M * 1000 + N + K)
+    A = torch.randn(M, K, generator=g)
+    B = torch.randn(N, K, generator=g)
+    if kind == "bf16":
+        A, B = A.to(torch.bfloat16), B.to(torch.bfloat16)
+        ref = A.double() @ B.double().T
+        code = C.MMA_KIND_BF16
+    else:
+        ref = _tf32(A).double() @ _tf32(B).double().T
+        code = C.MMA_KIND_TF32
+    dA, dB = A.to(cuda_dev), B.to(cuda_dev)
+    D = torch.full((M, N), float("nan"), device=cuda_dev)
+    rc = lib.gdn_mma_selftest(code, M, N, K, ctypes.c_void_p(dA.data_ptr()), ctypes.c_void_p(dB.data_ptr()),
+                              ctypes.c_void_p(D.data_ptr()),
+                              ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0, C.status_string(rc)
+    torch.cuda.synchronize()
+    assert pkg.prefill.device_status(cuda_dev) == 0
+    err = (D.double().cpu() - ref).abs().max().item()
+    assert err < 1e-3 * max(1.0, ref.abs().max().item()), f"max err {err}"

@@ -19,6 +19,11 @@ pytestmark = pytest.mark.gpu
 OUT_TOL = dict(atol=1e-2, rtol=1e-2)
 
 
+@pytest.fixture(params=["recurrent", "chunked"])
+def path(request):
+    return request.param
+
+
 def _run(pkg, inp, dev, **kw):
     g = inp.to(dev)
     out, ns = pkg.prefill.launch_gdn(*g.args(), **kw)
@@ -37,43 +42,43 @@ def _check(pkg, orc, inp, dev, **kw):
 
 @pytest.mark.parametrize("lengths", [[1], [15], [16], [17], [63], [64], [65], [127], [128], [129],
                                      [200], [1, 1, 1], [64, 64], [5, 0, 70], [0], [0, 0, 3]])
-def test_prefill_lengths(pkg, orc, cuda_dev, lengths):
+def test_prefill_lengths(pkg, orc, cuda_dev, lengths, path):
     _check(pkg, orc, pkg.inputs.make_prefill_inputs(lengths, seed=sum(lengths) + 1, with_state=True),
-           cuda_dev)
+           cuda_dev, path=path)
 
 
 @pytest.mark.parametrize("lengths", [[33], [300, 7]])
-def test_prefill_state_none(pkg, orc, cuda_dev, lengths):
-    _check(pkg, orc, pkg.inputs.make_prefill_inputs(lengths, seed=41, with_state=False), cuda_dev)
+def test_prefill_state_none(pkg, orc, cuda_dev, lengths, path):
+    _check(pkg, orc, pkg.inputs.make_prefill_inputs(lengths, seed=41, with_state=False), cuda_dev, path=path)
 
 
-def test_prefill_int32_cu_seqlens(pkg, orc, cuda_dev):
+def test_prefill_int32_cu_seqlens(pkg, orc, cuda_dev, path):
     inp = pkg.inputs.make_prefill_inputs([70, 3, 140], seed=42, with_state=True)
     ro, rs = orc.prefill(*inp.args())
     inp.cu_seqlens = inp.cu_seqlens.to(torch.int32)
-    out, ns = _run(pkg, inp, cuda_dev)
+    out, ns = _run(pkg, inp, cuda_dev, path=path)
     torch.testing.assert_close(out.float(), ro.float(), **OUT_TOL)
     assert state_rel_err(ns, rs) < 1e-3
 
 
-def test_prefill_uncovered_tokens_zero(pkg, orc, cuda_dev):
+def test_prefill_uncovered_tokens_zero(pkg, orc, cuda_dev, path):
     """Tokens past cu_seqlens[-1] get zero output, as the reference's torch.zeros."""
     inp = pkg.inputs.make_prefill_inputs([20, 30], seed=43, with_state=True)
     inp.cu_seqlens = torch.tensor([0, 20, 40], dtype=torch.int64)  # last 10 tokens uncovered
     ro, rs = orc.prefill(*inp.args())
     g = inp.to(cuda_dev)
     out = torch.full((50, 8, 128), 7.0, dtype=torch.bfloat16, device=cuda_dev)
-    pkg.prefill.launch_gdn(*g.args(), output=out)
+    pkg.prefill.launch_gdn(*g.args(), output=out, path=path)
     torch.cuda.synchronize()
     assert torch.count_nonzero(out[40:]) == 0
     torch.testing.assert_close(out.float().cpu(), ro.float(), **OUT_TOL)
 
 
 @pytest.mark.parametrize("name", ["prefill_varlen", "prefill_nostate"])
-def test_prefill_matches_reference_vectors(pkg, cuda_dev, name):
+def test_prefill_matches_reference_vectors(pkg, cuda_dev, name, path):
     inp = build_inputs(CASES[name])
     z = np.load(Path(__file__).parent / "golden" / f"{name}.npz")
-    out, ns = _run(pkg, inp, cuda_dev)
+    out, ns = _run(pkg, inp, cuda_dev, path=path)
     ref_out = torch.from_numpy(z["output"]).view(torch.bfloat16).float()
     torch.testing.assert_close(out.float(), ref_out, **OUT_TOL)
     assert state_rel_err(ns, torch.from_numpy(z["new_state"])) < 1e-3
@@ -94,28 +99,37 @@ def test_decode_equals_prefill_t1(pkg, cuda_dev):
     assert state_rel_err(ns_p, ns_d) < 1e-5
 
 
-def test_prefill_bad_seqlens_reported(pkg, cuda_dev):
+def test_prefill_bad_seqlens_reported(pkg, cuda_dev, path):
     """cu_seqlens past T is caught on the device: status bit set, no fault."""
     inp = pkg.inputs.make_prefill_inputs([10, 10], seed=45, with_state=True)
     g = inp.to(cuda_dev)
     g.cu_seqlens = torch.tensor([0, 10, 25], dtype=torch.int64, device=cuda_dev)
-    pkg.prefill.launch_gdn(*g.args())
+    pkg.prefill.launch_gdn(*g.args(), path=path)
     assert pkg.prefill.device_status(cuda_dev) & 16
     assert pkg.prefill.device_status(cuda_dev) == 0  # cleared by the read
 
 
-def test_prefill_config2(pkg, orc, cuda_dev):
+def test_prefill_config2(pkg, orc, cuda_dev, path):
     """one sequence of 4096 tokens, zero initial state."""
-    _check(pkg, orc, pkg.inputs.config2(with_state=False), cuda_dev)
+    _check(pkg, orc, pkg.inputs.config2(with_state=False), cuda_dev, path=path)
 
 
-def test_prefill_config3(pkg, orc, cuda_dev):
+def test_prefill_config3(pkg, orc, cuda_dev, path):
     """32 ragged sequences (~33k tokens), non-zero state."""
-    _check(pkg, orc, pkg.inputs.config3(), cuda_dev)
+    _check(pkg, orc, pkg.inputs.config3(), cuda_dev, path=path)
 
 
-def test_prefill_deterministic(pkg, cuda_dev):
+def test_prefill_deterministic(pkg, cuda_dev, path):
     inp = pkg.inputs.make_prefill_inputs([300, 77], seed=46, with_state=True)
-    o1, s1 = _run(pkg, inp, cuda_dev)
-    o2, s2 = _run(pkg, inp, cuda_dev)
+    o1, s1 = _run(pkg, inp, cuda_dev, path=path)
+    o2, s2 = _run(pkg, inp, cuda_dev, path=path)
     assert torch.equal(o1, o2) and torch.equal(s1, s2)
+
+
+def test_chunked_matches_recurrent(pkg, cuda_dev):
+    """The two CUDA paths agree with each other on a multi-chunk varlen batch."""
+    inp = pkg.inputs.make_prefill_inputs([257, 64, 130, 1], seed=47, with_state=True)
+    o_r, s_r = _run(pkg, inp, cuda_dev, path="recurrent")
+    o_c, s_c = _run(pkg, inp, cuda_dev, path="chunked")
+    torch.testing.assert_close(o_c.float(), o_r.float(), **OUT_TOL)
+    assert state_rel_err(s_c, s_r) < 1e-3
