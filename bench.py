@@ -45,6 +45,10 @@ STATE_BYTES_PER_SEQ = 8 * 128 * 128 * 4
 DECODE_BYTES_PER_SEQ = 2 * STATE_BYTES_PER_SEQ + 1024 + 1024 + 2048 + 16 + 16 + 2048
 DECODE_BYTES_FIXED = 64
 L2_FLUSH_BYTES = 256 << 20
+SLEEP_CYCLES = 200_000  # ~100 us GPU spin before each timed step (outside the events)
+# dram__bytes_read.sum + dram__bytes_write.sum of one gdn_decode_kernel launch at
+# B=256, from one ncu capture (profiles/gdn_decode_kernel_B256.md)
+DECODE_NCU_TRAFFIC = 214475264
 
 
 def load_peaks():
@@ -151,6 +155,9 @@ def time_steps(step, steps: int, warmup: int, ws: int, device, flush: torch.Tens
     for i in range(steps):
         if flush is not None:
             flush.add_(1)  # evict L2 (256 MiB write) outside the timed events
+        # keep the GPU busy while the host enqueues the step, so the start event
+        # is not timing host-side launch latency
+        torch.cuda._sleep(SLEEP_CYCLES)
         evs[i][0].record(stream)
         step()
         evs[i][1].record(stream)
@@ -220,6 +227,72 @@ def bench_prefill(pkg, device, lengths, seed, steps, warmup, ws, flush, with_sta
             "hbm_gbs": bytes_ / (ms * 1e-3) / 1e9, "tflops": flops_per_tok * T / (ms * 1e-3) / 1e12}
 
 
+def soak(step, seconds: float, device, flush):
+    """Untimed repeats of ``step`` so the clock sampler sees the GPU under this load."""
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        for _ in range(20):
+            if flush is not None:
+                flush.add_(1)
+            step()
+        torch.cuda.synchronize(device)
+
+
+def bench_decode(pkg, args, device, ws, rank, flush, peaks, peaks_kind):
+    B = DECODE_BATCH
+    inp = pkg.inputs.make_decode_inputs(B, seed=1000 + rank).to(device)
+    out = torch.empty((B, 8, 128), dtype=torch.bfloat16, device=device)
+    st = [inp.state, torch.empty_like(inp.state)]
+    flip = [0]
+
+    def step():
+        s_in, s_out = st[flip[0]], st[1 - flip[0]]
+        pkg.decode.launch_gdn(inp.q, inp.k, inp.v, s_in, inp.A_log, inp.a, inp.dt_bias, inp.b,
+                              inp.scale, out, s_out)
+        flip[0] ^= 1
+
+    with ClockSampler(device.index) as clk:
+        if args.soak > 0:
+            soak(step, args.soak, device, flush)
+        times, wall = time_steps(step, args.steps, args.warmup, ws, device, flush)
+    ms_local = sum(times) / len(times)
+    ms = max_over_ranks(ms_local, ws, device)
+    state_bytes = B * STATE_BYTES_PER_SEQ * 2
+    algo_bytes = DECODE_BYTES_PER_SEQ * B + DECODE_BYTES_FIXED
+    res = {
+        "ms": ms, "ms_local": ms_local, "wall": wall, "clocks": clk.summary(),
+        "value": ws * state_bytes / (ms * 1e-3) / 1e9,
+        "roofline": {"bound": "hbm", "achieved": round(algo_bytes / (ms_local * 1e-3) / 1e9, 1),
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(algo_bytes / (ms_local * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+                     "peak_source": ("measured: MEASURED_PEAKS.json hbm_gbs" if peaks_kind == "measured"
+                                     else "fallback 6650 GB/s"),
+                     "traffic": DECODE_NCU_TRAFFIC, "algo_bytes_per_launch": algo_bytes,
+                     "kernel": "gdn_decode_kernel<16>",
+                     "traffic_source": "profiles/gdn_decode_kernel_B256.md (ncu dram bytes, one launch)"},
+    }
+    if not args.skip_e2e:
+        stager = pkg.decode.HostStager(B, device)
+        h_in = [t.cpu().pin_memory() for t in (inp.q, inp.k, inp.v, inp.state, inp.A_log, inp.a,
+                                                inp.dt_bias, inp.b)]
+        h_out = torch.empty((B, 8, 128), dtype=torch.bfloat16).pin_memory()
+        h_ns = torch.empty_like(h_in[3]).pin_memory()
+
+        def e2e_step():
+            q, k, v, s_, A_log, a, dtb, b = h_in
+            stager(q, k, v, s_, A_log, a, dtb, b, inp.scale, h_out, h_ns)
+
+        e2e_steps = max(3, min(args.steps, 10))
+        e2e_times, _ = time_steps(e2e_step, e2e_steps, 3, ws, device, None)
+        e2e_ms = max_over_ranks(sum(e2e_times) / len(e2e_times), ws, device)
+        h2d, d2h = stager.bytes_per_step()
+        res["e2e"] = {"value": round(ws * state_bytes / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
+                      "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d,
+                      "d2h_bytes_per_step": d2h,
+                      "api": "decode.HostStager -> launch_gdn (pinned host buffers, PCIe copies timed)"}
+    return res
+
+
 def run_ours(args):
     ws, rank, local = dist_env()
     device = torch.device("cuda", local)
@@ -233,89 +306,51 @@ def run_ours(args):
                                 device_id=device)
     pkg = __graft_entry__.load_package()
     peaks, peaks_kind = load_peaks()
-    B = DECODE_BATCH
-    inp = pkg.inputs.make_decode_inputs(B, seed=1000 + rank).to(device)
-    out = torch.empty((B, 8, 128), dtype=torch.bfloat16, device=device)
-    st = [inp.state, torch.empty_like(inp.state)]
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
-    flip = [0]
-    launches = [0]
-
-    def step():
-        s_in, s_out = st[flip[0]], st[1 - flip[0]]
-        pkg.decode.launch_gdn(inp.q, inp.k, inp.v, s_in, inp.A_log, inp.a, inp.dt_bias, inp.b,
-                              inp.scale, out, s_out)
-        flip[0] ^= 1
-        launches[0] += 1
-
-    with ClockSampler(device.index) as clk:
-        times, wall = time_steps(step, args.steps, args.warmup, ws, device, flush)
-    clocks = clk.summary()
-    n_launch_timed = args.steps  # one decode kernel per step
-    ms_local = sum(times) / len(times)
-    ms = max_over_ranks(ms_local, ws, device)
-    state_bytes = B * STATE_BYTES_PER_SEQ * 2
-    value = ws * state_bytes / (ms * 1e-3) / 1e9
-    algo_bytes = DECODE_BYTES_PER_SEQ * B + DECODE_BYTES_FIXED
-    achieved = algo_bytes / (ms_local * 1e-3) / 1e9
-
-    # e2e: same step through the public host-buffer API, PCIe copies inside
-    stager = pkg.decode.HostStager(B, device)
-    h_in = [t.cpu().pin_memory() for t in (inp.q, inp.k, inp.v, inp.state, inp.A_log, inp.a,
-                                            inp.dt_bias, inp.b)]
-    h_out = torch.empty((B, 8, 128), dtype=torch.bfloat16).pin_memory()
-    h_ns = torch.empty_like(h_in[3]).pin_memory()
-
-    def e2e_step():
-        q, k, v, s, A_log, a, dtb, b = h_in
-        stager(q, k, v, s, A_log, a, dtb, b, inp.scale, h_out, h_ns)
-
-    e2e_steps = max(3, min(args.steps, 10))
-    e2e_times, _ = time_steps(e2e_step, e2e_steps, 2, ws, device, None)
-    e2e_ms = max_over_ranks(sum(e2e_times) / len(e2e_times), ws, device)
-    h2d, d2h = stager.bytes_per_step()
-
-    # prefill side numbers
+    wl = args.workload
+    line = {}
+    if wl in ("all", "decode"):
+        d = bench_decode(pkg, args, device, ws, rank, flush, peaks, peaks_kind)
+        line = {
+            "metric": "gdn decode state-stream HBM GB/s (config 1: B=256 per GPU, fp32 k-last state)",
+            "value": round(d["value"], 2),
+            "unit": "GB/s",
+            "n_gpus": ws,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(d["ms"], 5),
+            "decode_us_per_step": round(d["ms"] * 1e3, 2),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "fp32 state / bf16 io",
+            "data": "synthetic (seeded; BASELINE config 1 distributions)",
+            "config": {"workload": "config1_decode_B256_per_gpu", "batch_per_gpu": DECODE_BATCH,
+                       "global_batch": DECODE_BATCH * ws, "seq_len": 1,
+                       "parallelism": f"sequence-shard x{ws}",
+                       "l2": "flushed between steps (256 MiB write)"},
+            "gpu_launches": args.steps,  # one decode kernel per timed step
+            "roofline": d["roofline"],
+            "clocks": d["clocks"],
+            "wall_s_timed_region": round(d["wall"], 4),
+        }
+        if "e2e" in d:
+            line["e2e"] = d["e2e"]
+    pf = {}
+    psteps = max(3, args.steps // 2)
     if ws == 1:
-        pf = {"config2_T4096_N1": bench_prefill(pkg, device, [4096], 0, max(3, args.steps // 2),
-                                                 args.warmup, ws, flush, with_state=False),
-              "config3_32seq": bench_prefill(pkg, device, pkg.inputs.config3_lengths(0), 0,
-                                             max(3, args.steps // 2), args.warmup, ws, flush)}
-    else:
-        pf = {"config4b_shard_8x8192": bench_prefill(pkg, device, [8192] * 8, 2000 + rank, 3,
-                                                      min(args.warmup, 3), ws, flush)}
-
-    line = {
-        "metric": "gdn decode state-stream HBM GB/s (config 1: B=256 per GPU, fp32 k-last state)",
-        "value": round(value, 2),
-        "unit": "GB/s",
-        "n_gpus": ws,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": round(ms, 5),
-        "decode_us_per_step": round(ms * 1e3, 2),
-        "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": None,
-        "dtype": "fp32 state / bf16 io",
-        "data": "synthetic (seeded; BASELINE config 1 distributions)",
-        "config": {"workload": "config1_decode_B256_per_gpu", "batch_per_gpu": B,
-                   "global_batch": B * ws, "seq_len": 1, "parallelism": f"sequence-shard x{ws}",
-                   "l2": "flushed between steps (256 MiB write)"},
-        "gpu_launches": n_launch_timed,
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
-                     "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                     "peak_source": f"{peaks_kind} (MEASURED_PEAKS.json hbm_gbs)" if peaks_kind == "measured"
-                     else "fallback 6650 GB/s", "traffic": None,
-                     "algo_bytes_per_launch": algo_bytes, "kernel": "gdn_decode_kernel<16>"},
-        "e2e": {"value": round(ws * state_bytes / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
-                "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "api": "decode.HostStager -> launch_gdn (pinned host buffers, PCIe copies timed)"},
-        "clocks": clocks,
-        "wall_s_timed_region": round(wall, 4),
-        "prefill": pf,
-    }
-    if rank == 0 and ws == 1:
+        if wl in ("all", "prefill2"):
+            pf["config2_T4096_N1"] = bench_prefill(pkg, device, [4096], 0, psteps, args.warmup, ws, flush,
+                                                   with_state=False)
+        if wl in ("all", "prefill3"):
+            pf["config3_32seq"] = bench_prefill(pkg, device, pkg.inputs.config3_lengths(0), 0, psteps,
+                                                args.warmup, ws, flush)
+    if wl in ("all", "prefill4b") and (ws > 1 or wl == "prefill4b"):
+        pf["config4b_shard_8x8192"] = bench_prefill(pkg, device, [8192] * 8, 2000 + rank, 3,
+                                                    min(args.warmup, 3), ws, flush)
+    if pf:
+        line["prefill"] = pf
+    if rank == 0 and ws == 1 and not args.skip_cpu and wl == "all":
         line["cpu_baseline"] = cpu_decode_baseline(pkg, args.cpu_budget)
         line["cpu_baseline_prefill"] = cpu_prefill_baseline(pkg, args.cpu_budget)
     if ws > 1:
@@ -371,6 +406,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds per CPU-baseline sample")
+    ap.add_argument("--workload", default="all",
+                    choices=["all", "decode", "prefill2", "prefill3", "prefill4b"],
+                    help="all = the JSON line the driver reads; the others time one workload")
+    ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline (profiling runs)")
+    ap.add_argument("--skip-e2e", action="store_true", help="omit the host-buffer e2e leg")
+    ap.add_argument("--soak", type=float, default=1.0,
+                    help="seconds of untimed steps under the clock sampler before timing")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
