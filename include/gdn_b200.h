@@ -137,6 +137,27 @@ size_t gdn_prefill_workspace_size(int64_t total_tokens, int64_t num_seqs);
 int gdn_prefill_launch(const GdnPrefillArgs* args, void* workspace, size_t workspace_bytes,
                        void* stream);
 
+/* Size of the fixed scratch array behind gdn_prefill_launch_noalloc. */
+#define GDN_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/* gdn_prefill_launch for callers that cannot allocate device memory -- a
+ * plugin host or server that owns all device memory and gives extensions no
+ * allocator, or a step where cudaMalloc is not allowed (it may synchronise the
+ * device and is illegal during stream capture).  No counterpart in the
+ * reference, whose plugin allocated its scratch with torch.empty on every call.
+ *
+ * Same arguments and results as gdn_prefill_launch, but the scratch is a
+ * fixed array of GDN_NOALLOC_SCRATCH_BYTES inside this library, held on every
+ * GPU that loads the library until the process exits; nothing is allocated.
+ * Limit: unless args->path is GDN_PREFILL_PATH_RECURRENT, problems with
+ * gdn_prefill_workspace_size(T, N) > GDN_NOALLOC_SCRATCH_BYTES are rejected
+ * with GDN_ERR_WORKSPACE before anything runs (about 2,200 tokens for one
+ * sequence with the current workspace layout).  The first call on each device
+ * looks up the array's device address; make it before any stream capture.
+ * All calls on a device share the array: calls whose kernels overlap on the
+ * GPU (different streams or host threads) race and must be serialised. */
+int gdn_prefill_launch_noalloc(const GdnPrefillArgs* args, void* stream);
+
 /* ---------------------------------------------------------------- status -- */
 
 /* Human-readable name of a gdn_status_t (static string). */

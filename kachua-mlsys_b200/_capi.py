@@ -28,6 +28,7 @@ EXPORTED_SYMBOLS = (
     "gdn_read_device_status",
     "gdn_abi_version",
     "gdn_mma_selftest",
+    "gdn_prefill_launch_noalloc",
 )
 ABI_VERSION = 2
 PATH_AUTO, PATH_RECURRENT, PATH_CHUNKED = 0, 1, 2

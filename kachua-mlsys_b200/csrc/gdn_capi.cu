@@ -157,3 +157,6 @@ extern "C" int gdn_mma_selftest(int kind, int M, int N, int K, const void* A, co
                ? GDN_OK
                : GDN_ERR_CUDA;
 }
+
+// Allocation-free prefill entry point (fixed scratch array in this library).
+#include "gdn_prefill_noalloc.cu"
