@@ -13,9 +13,11 @@ in ``prefill``.
     torchrun --nproc-per-node N bench.py --gpus N ...     (N > 1)
 
 Timing: W untimed warm-up steps, then exactly K steps between a barrier and
-a device synchronize, each step timed on its stream with CUDA events; an L2
-flush (a 256 MiB write) runs between steps outside the events; the reported
-time is the max over ranks.  ``--impl reference`` times the reference's own
+a device synchronize, timed with CUDA events on the launching stream; the
+reported time is the max over ranks.  Decode steps run back to back over three
+rotating 128 MiB state buffers (inputs larger than L2, each step pays for its
+own write-backs).  Prefill steps are timed one by one with an L2 flush (a
+256 MiB read) between them, outside the events.  ``--impl reference`` times the reference's own
 algorithm on the host CPU (the oracle port in oracle/, all host threads).
 """
 from __future__ import annotations
@@ -140,11 +142,19 @@ def barrier(ws: int):
         dist.barrier()
 
 
+def flush_l2(buf: torch.Tensor) -> None:
+    """Evicts L2 by READING a 256 MiB buffer: the L2 ends up full of clean lines,
+    so the next timed kernel neither hits its inputs in L2 nor pays for writing
+    back someone else's dirty lines (a write-based flush would charge the
+    timed kernel ~126 MB of write-backs)."""
+    torch.sum(buf, dtype=torch.float32)
+
+
 def time_steps(step, steps: int, warmup: int, ws: int, device, flush: torch.Tensor | None):
     """Runs warmup+steps calls of ``step``; returns (per-step device ms list, wall s)."""
     for _ in range(warmup):
         if flush is not None:
-            flush.add_(1)
+            flush_l2(flush)
         step()
     torch.cuda.synchronize(device)
     barrier(ws)
@@ -154,7 +164,7 @@ def time_steps(step, steps: int, warmup: int, ws: int, device, flush: torch.Tens
     t0 = time.perf_counter()
     for i in range(steps):
         if flush is not None:
-            flush.add_(1)  # evict L2 (256 MiB write) outside the timed events
+            flush_l2(flush)  # outside the timed events
         # keep the GPU busy while the host enqueues the step, so the start event
         # is not timing host-side launch latency
         torch.cuda._sleep(SLEEP_CYCLES)
@@ -222,9 +232,32 @@ def bench_prefill(pkg, device, lengths, seed, steps, warmup, ws, flush, with_sta
     ms = max_over_ranks(sum(times) / len(times), ws, device)
     flops_per_tok = 1452715.0  # fixed chunked-WY count at C=64, 8 heads
     bytes_ = 6176 * T + 524288 * N * (2 if with_state else 1)
-    return {"tokens": T, "seqs": N, "ms": ms, "tokens_per_s": T * ws / (ms * 1e-3),
-            "algo_bytes": bytes_, "algo_flops": flops_per_tok * T,
-            "hbm_gbs": bytes_ / (ms * 1e-3) / 1e9, "tflops": flops_per_tok * T / (ms * 1e-3) / 1e12}
+    res = {"tokens": T, "seqs": N, "ms": ms, "tokens_per_s": T * ws / (ms * 1e-3),
+           "algo_bytes": bytes_, "algo_flops": flops_per_tok * T,
+           "hbm_gbs": bytes_ / (ms * 1e-3) / 1e9, "tflops": flops_per_tok * T / (ms * 1e-3) / 1e12}
+    if ws > 1:
+        res.update(time_gather(pkg, out, ns, ws, device))
+        res["tokens_per_s_with_gather"] = T * ws / ((ms + res["gather_ms"]) * 1e-3)
+    return res
+
+
+def time_gather(pkg, out, ns, ws, device):
+    """The final gather of every rank's outputs and states to rank 0 (NCCL
+    point-to-point over NVLink), timed on the device, max over ranks."""
+    rank = int(os.environ.get("RANK", "0"))
+    shapes = [[tuple(out.shape), tuple(ns.shape)]] * ws  # equal shards in this bench
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    pkg.shard.gather_to_rank0([out, ns], shapes, rank, ws)  # warm the P2P paths
+    torch.cuda.synchronize(device)
+    barrier(ws)
+    e0.record(stream)
+    pkg.shard.gather_to_rank0([out, ns], shapes, rank, ws)
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    ms = max_over_ranks(e0.elapsed_time(e1), ws, device)
+    moved = (ws - 1) * (out.numel() * 2 + ns.numel() * 4)
+    return {"gather_ms": ms, "gather_bytes": moved, "gather_gbs_into_rank0": moved / (ms * 1e-3) / 1e9}
 
 
 def soak(step, seconds: float, device, flush):
@@ -233,29 +266,52 @@ def soak(step, seconds: float, device, flush):
     while time.perf_counter() - t0 < seconds:
         for _ in range(20):
             if flush is not None:
-                flush.add_(1)
+                flush_l2(flush)
             step()
         torch.cuda.synchronize(device)
 
 
+def time_back_to_back(step, steps: int, warmup: int, ws: int, device):
+    """K steps issued back to back between one event pair (steady state)."""
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(device)
+    barrier(ws)
+    torch.cuda.synchronize(device)
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(SLEEP_CYCLES)  # the queue fills while the GPU spins
+    t0 = time.perf_counter()
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    wall = time.perf_counter() - t0
+    barrier(ws)
+    return e0.elapsed_time(e1) / steps, wall
+
+
 def bench_decode(pkg, args, device, ws, rank, flush, peaks, peaks_kind):
+    """Config 1 decode, steady state: three rotating 128 MiB state buffers (step
+    i reads buffer i%3 and writes (i+1)%3), so every state read misses L2 and
+    every step pays for its own write-backs; K steps back to back."""
     B = DECODE_BATCH
     inp = pkg.inputs.make_decode_inputs(B, seed=1000 + rank).to(device)
     out = torch.empty((B, 8, 128), dtype=torch.bfloat16, device=device)
-    st = [inp.state, torch.empty_like(inp.state)]
-    flip = [0]
+    st = [inp.state, torch.empty_like(inp.state), torch.empty_like(inp.state)]
+    launches = [pkg.decode.PreparedLaunch(inp.q, inp.k, inp.v, st[i], inp.A_log, inp.a, inp.dt_bias,
+                                          inp.b, inp.scale, out, st[(i + 1) % 3]) for i in range(3)]
+    it = [0]
 
     def step():
-        s_in, s_out = st[flip[0]], st[1 - flip[0]]
-        pkg.decode.launch_gdn(inp.q, inp.k, inp.v, s_in, inp.A_log, inp.a, inp.dt_bias, inp.b,
-                              inp.scale, out, s_out)
-        flip[0] ^= 1
+        launches[it[0] % 3]()
+        it[0] += 1
 
     with ClockSampler(device.index) as clk:
         if args.soak > 0:
-            soak(step, args.soak, device, flush)
-        times, wall = time_steps(step, args.steps, args.warmup, ws, device, flush)
-    ms_local = sum(times) / len(times)
+            soak(step, args.soak, device, None)
+        ms_local, wall = time_back_to_back(step, args.steps, args.warmup, ws, device)
     ms = max_over_ranks(ms_local, ws, device)
     state_bytes = B * STATE_BYTES_PER_SEQ * 2
     algo_bytes = DECODE_BYTES_PER_SEQ * B + DECODE_BYTES_FIXED
@@ -328,7 +384,7 @@ def run_ours(args):
             "config": {"workload": "config1_decode_B256_per_gpu", "batch_per_gpu": DECODE_BATCH,
                        "global_batch": DECODE_BATCH * ws, "seq_len": 1,
                        "parallelism": f"sequence-shard x{ws}",
-                       "l2": "flushed between steps (256 MiB write)"},
+                       "l2": "inputs larger than L2: 3 rotating 128 MiB state buffers, steps back to back"},
             "gpu_launches": args.steps,  # one decode kernel per timed step
             "roofline": d["roofline"],
             "clocks": d["clocks"],

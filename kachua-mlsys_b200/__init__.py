@@ -12,7 +12,7 @@ romitjain/kachua-mlsys):
 * ``inputs``             -- seeded synthetic inputs of the benchmark configs
 * ``shard``              -- sequence sharding across GPUs and the final gather
 """
-from . import _build, _capi, decode, inputs, prefill  # noqa: F401
+from . import _build, _capi, decode, inputs, prefill, shard  # noqa: F401
 
 __all__ = ["decode", "prefill", "inputs", "build"]
 

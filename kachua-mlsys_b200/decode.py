@@ -90,6 +90,34 @@ def launch_gdn(q, k, v, state, A_log, a, dt_bias, b, scale=None, output=None, ne
     return output, new_state
 
 
+class PreparedLaunch:
+    """A validated decode call that can be re-issued with ~one ctypes call.
+
+    For serving loops that call the same buffers every step (and for CUDA
+    graph capture): arguments are checked once here; ``__call__`` launches on
+    the current stream of the tensors' device.
+    """
+
+    def __init__(self, q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state):
+        B = validate(q, k, v, state, A_log, a, dt_bias, b, output, new_state)
+        self._keep = (q, k, v, state, A_log, a, dt_bias, b, output, new_state)
+        self.device = q.device
+        self.lib = _capi.load()
+        self.args = _capi.GdnDecodeArgs(
+            _ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a), _ptr(dt_bias), _ptr(b),
+            _ptr(output), _ptr(new_state), B, 0.0 if scale is None else float(scale))
+        self._ref = ctypes.byref(self.args)
+
+    def __call__(self) -> None:
+        if torch.cuda.current_device() != self.device.index:
+            raise RuntimeError(f"PreparedLaunch for {self.device} called with cuda:"
+                               f"{torch.cuda.current_device()} current")
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        rc = self.lib.gdn_decode_launch(self._ref, ctypes.c_void_p(stream))
+        if rc:
+            _capi.check(rc, "gdn_decode_launch")
+
+
 def kernel(q, k, v, state, A_log, a, dt_bias, b, scale=None):
     """Value-returning form of the reference binding (binding.py:34-51)."""
     return launch_gdn(q, k, v, state, A_log, a, dt_bias, b, scale)

@@ -1,0 +1,126 @@
+"""Sequence sharding and the final gather (host logic, CPU only).
+
+Per-shard results come from the CPU oracle, so these tests need no GPU; the
+multi-process tests run world_size-2 gloo groups on 127.0.0.1.
+"""
+import datetime
+import multiprocessing as mp
+import os
+import socket
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+REPO = Path(__file__).resolve().parents[1]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_plan_prefill_lpt(pkg):
+    plan = pkg.shard.plan_prefill([100, 5, 70, 70, 30, 0], 2)
+    assert sorted(sum(plan, [])) == list(range(6))
+    loads = [sum([100, 5, 70, 70, 30, 0][s] for s in p) for p in plan]
+    assert max(loads) - min(loads) <= 30
+    assert plan == pkg.shard.plan_prefill([100, 5, 70, 70, 30, 0], 2)  # deterministic
+    assert pkg.shard.plan_prefill([3, 4], 4)[2:] == [[], []]  # idle ranks allowed
+
+
+def test_decode_slices_cover(pkg):
+    for B, W in ((256, 8), (7, 3), (1, 2)):
+        sl = [pkg.shard.decode_slice(B, W, r) for r in range(W)]
+        assert sl[0][0] == 0 and sl[-1][1] == B
+        assert all(sl[i][1] == sl[i + 1][0] for i in range(W - 1))
+
+
+@pytest.mark.parametrize("world", [1, 2, 3])
+def test_prefill_shard_merge_equals_unsharded(pkg, orc, world):
+    inp = pkg.inputs.make_prefill_inputs([40, 0, 17, 65, 3], seed=71, with_state=True)
+    ref_out, ref_ns = orc.prefill(*inp.args())
+    shards = pkg.shard.plan_prefill_shards(inp.cu_seqlens, world)
+    outs, states = [], []
+    for sh in shards:
+        o, s = orc.prefill(*pkg.shard.shard_prefill_inputs(inp, sh).args())
+        outs.append(o)
+        states.append(s)
+    out, ns = pkg.shard.merge_prefill(shards, outs, states, inp.total_tokens, inp.num_seqs)
+    assert torch.equal(out, ref_out) and torch.equal(ns, ref_ns)
+
+
+def test_decode_shard_equals_unsharded(pkg, orc):
+    inp = pkg.inputs.make_decode_inputs(5, seed=72)
+    ref_out, ref_ns = orc.decode(*inp.args())
+    outs, states = [], []
+    for r in range(2):
+        o, s = orc.decode(*pkg.shard.shard_decode_inputs(inp, 2, r).args())
+        outs.append(o)
+        states.append(s)
+    assert torch.equal(torch.cat(outs), ref_out) and torch.equal(torch.cat(states), ref_ns)
+
+
+def _worker(rank, world, port, mode, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    sys.path.insert(0, str(REPO))
+    import torch.distributed as dist
+
+    import __graft_entry__
+    from oracle import oracle
+
+    pkg = __graft_entry__.load_package()
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=4))
+    try:
+        inp = pkg.inputs.make_prefill_inputs([33, 70, 1, 0, 20], seed=73, with_state=True)
+        shards = pkg.shard.plan_prefill_shards(inp.cu_seqlens, world)
+        mine = shards[rank]
+        if mode == "dead" and rank == 1:
+            return  # this rank leaves before the gather: rank 0 must see an error
+        o, s = oracle.prefill(*pkg.shard.shard_prefill_inputs(inp, mine).args(), threads=1)
+        shapes = [[(sh.tokens, 8, 128), (len(sh.seqs), 8, 128, 128)] for sh in shards]
+        got = pkg.shard.gather_to_rank0([o.view(torch.int16), s], shapes, rank, world)
+        if rank == 0:
+            outs = [g[0].view(torch.bfloat16) for g in got]
+            states = [g[1] for g in got]
+            out, ns = pkg.shard.merge_prefill(shards, outs, states, inp.total_tokens, inp.num_seqs)
+            ref_out, ref_ns = oracle.prefill(*inp.args(), threads=1)
+            q.put(("ok", bool(torch.equal(out, ref_out) and torch.equal(ns, ref_ns))))
+    except Exception as e:  # reported to the test through the queue
+        q.put(("error", f"{type(e).__name__}: {e}"))
+    finally:
+        if not (mode == "dead" and rank == 1):
+            try:
+                dist.destroy_process_group()
+            except Exception:
+                pass
+
+
+def _run_world(mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=90)
+        if p.is_alive():
+            p.kill()
+            pytest.fail("worker did not finish")
+    return [q.get(timeout=5) for _ in range(q.qsize())] if not q.empty() else []
+
+
+def test_gloo_gather_world2_matches_unsharded():
+    res = _run_world("ok")
+    assert ("ok", True) in res, res
+
+
+def test_gloo_dead_rank_is_detected():
+    """A rank that leaves before the gather: rank 0's receive fails within the
+    process-group timeout instead of hanging."""
+    res = _run_world("dead")
+    assert any(kind == "error" for kind, _ in res), res
