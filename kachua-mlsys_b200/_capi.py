@@ -30,9 +30,10 @@ EXPORTED_SYMBOLS = (
     "gdn_mma_selftest",
     "gdn_prefill_launch_noalloc",
 )
-ABI_VERSION = 2
+ABI_VERSION = 3
 PATH_AUTO, PATH_RECURRENT, PATH_CHUNKED = 0, 1, 2
 MMA_KIND_BF16, MMA_KIND_TF32 = 1, 2
+MMA_A_MN, MMA_B_MN, MMA_D_LANE16 = 1, 2, 4
 
 
 class GdnDecodeArgs(ctypes.Structure):
@@ -109,7 +110,7 @@ def load(build_if_needed: bool = True) -> ctypes.CDLL:
         lib.gdn_read_device_status.restype = ctypes.c_int
         lib.gdn_abi_version.argtypes = []
         lib.gdn_abi_version.restype = ctypes.c_int
-        lib.gdn_mma_selftest.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, P, P]
+        lib.gdn_mma_selftest.argtypes = [ctypes.c_int] * 5 + [P, P, P, P]
         lib.gdn_mma_selftest.restype = ctypes.c_int
         if lib.gdn_abi_version() != ABI_VERSION:
             raise RuntimeError("libgdn_b200.so ABI version mismatch; rebuild it")

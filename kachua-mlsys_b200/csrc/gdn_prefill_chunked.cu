@@ -746,31 +746,50 @@ cudaError_t launch_prefill(const PrefillParams& p, int path, void* workspace, si
 
 // ------------------------------------------------------------- self-test --
 // D[M x N] = A[M x K] . B[N x K]^T through the same image writers,
-// descriptors and TMEM read-back as the kernels above (one CTA).
+// descriptors and TMEM read-back as the kernels above (one CTA).  flags:
+// bit 0 A MN-major, bit 1 B MN-major, bit 2 accumulator at TMEM lane 16
+// (the second M=64 tile of a lane-packed pair; M = 64 only).
+template <Kind KIND>
+__device__ __forceinline__ void selftest_issue(int flags, uint32_t d, uint32_t a, uint32_t b, int M, int N, int K) {
+    const int ar = (flags & 1) ? K : M, br = (flags & 2) ? K : N;
+    switch (flags & 3) {
+        case 0: mma_tile<KIND, false, false>(d, a, ar, b, br, K, M, N, false); break;
+        case 1: mma_tile<KIND, true, false>(d, a, ar, b, br, K, M, N, false); break;
+        case 2: mma_tile<KIND, false, true>(d, a, ar, b, br, K, M, N, false); break;
+        default: mma_tile<KIND, true, true>(d, a, ar, b, br, K, M, N, false); break;
+    }
+}
+
 __global__ void __launch_bounds__(128, 1)
-    gdn_mma_selftest_kernel(int kind, int M, int N, int K, const void* A, const void* B, float* D) {
+    gdn_mma_selftest_kernel(int kind, int flags, int M, int N, int K, const void* A, const void* B, float* D) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = align1024(smem_raw);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int eb = kind == kBF16 ? 2 : 4;
     const int kblocks = K * eb / 128;
+    const bool a_mn = flags & 1, b_mn = flags & 2, lane16 = flags & 4;
     uint8_t* sA = sm;
-    uint8_t* sB = sm + kblocks * M * 128;
-    uint64_t* bar = reinterpret_cast<uint64_t*>(sB + kblocks * N * 128);
+    uint8_t* sB = sm + M * K * eb;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(sB + N * K * eb);
     uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
+    (void)kblocks;
     for (int idx = tid; idx < M * K; idx += 128) {
-        const int r = idx / K, c = idx % K;
+        const int r = idx / K, c = idx % K;  // A[r][c]: row m = r, k = c
+        const int row = a_mn ? c : r, col = a_mn ? r : c, rows = a_mn ? K : M;
         if (kind == kBF16)
-            *reinterpret_cast<uint16_t*>(sA + sw128_bf16(r, c, M)) = static_cast<const uint16_t*>(A)[idx];
+            *reinterpret_cast<uint16_t*>(sA + sw128_bf16(row, col, rows)) = static_cast<const uint16_t*>(A)[idx];
         else
-            st_f32(sA, sw128_f32(r, c, M), to_tf32(static_cast<const float*>(A)[idx]));
+            st_f32(sA, a_mn ? mn32_f32(row, col, rows) : sw128_f32(row, col, rows),
+                   to_tf32(static_cast<const float*>(A)[idx]));
     }
     for (int idx = tid; idx < N * K; idx += 128) {
-        const int r = idx / K, c = idx % K;
+        const int r = idx / K, c = idx % K;  // B[r][c]: n = r, k = c
+        const int row = b_mn ? c : r, col = b_mn ? r : c, rows = b_mn ? K : N;
         if (kind == kBF16)
-            *reinterpret_cast<uint16_t*>(sB + sw128_bf16(r, c, N)) = static_cast<const uint16_t*>(B)[idx];
+            *reinterpret_cast<uint16_t*>(sB + sw128_bf16(row, col, rows)) = static_cast<const uint16_t*>(B)[idx];
         else
-            st_f32(sB, sw128_f32(r, c, N), to_tf32(static_cast<const float*>(B)[idx]));
+            st_f32(sB, b_mn ? mn32_f32(row, col, rows) : sw128_f32(row, col, rows),
+                   to_tf32(static_cast<const float*>(B)[idx]));
     }
     int ncols = 32;
     while (ncols < N) ncols <<= 1;
@@ -787,17 +806,26 @@ __global__ void __launch_bounds__(128, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tm = *tslot;
+    const uint32_t d = lane16 ? taddr(tm, 16, 0) : tm;
     if (tid == 0) {
         if (kind == kBF16)
-            mma_tile<kBF16>(tm, smem_u32(sA), M, smem_u32(sB), N, K, M, N, false);
+            selftest_issue<kBF16>(flags, d, smem_u32(sA), smem_u32(sB), M, N, K);
         else
-            mma_tile<kTF32>(tm, smem_u32(sA), M, smem_u32(sB), N, K, M, N, false);
+            selftest_issue<kTF32>(flags, d, smem_u32(sA), smem_u32(sB), M, N, K);
         mma_commit(smem_u32(bar));
     }
     const bool ok = mbar_wait(smem_u32(bar), 0);
     tc_fence_after();
-    const int row = M == 128 ? tid : 16 * warp + lane;
-    const bool has_row = M == 128 || lane < 16;
+    // M=128: row = lane of the whole CTA; M=64: lanes 0-15 (or 16-31) of each warp
+    int row;
+    bool has_row;
+    if (M == 128) {
+        row = tid;
+        has_row = true;
+    } else {
+        row = 16 * warp + (lane & 15);
+        has_row = lane16 ? lane >= 16 : lane < 16;
+    }
     for (int c = 0; c < N; c += 16) {
         float r16[16];
         tmem_ld16(taddr(tm, 32 * warp, c), r16);
@@ -814,13 +842,13 @@ __global__ void __launch_bounds__(128, 1)
     }
 }
 
-cudaError_t launch_mma_selftest(int kind, int M, int N, int K, const void* A, const void* B, float* D,
+cudaError_t launch_mma_selftest(int kind, int flags, int M, int N, int K, const void* A, const void* B, float* D,
                                 cudaStream_t stream) {
-    const int eb = kind == kBF16 ? 2 : 4;
-    const int smem = (K * eb / 128) * (M + N) * 128 + 64 + 1024;
+    // the whole opt-in shared memory, so even a misread descriptor stride stays inside the CTA's window
+    const int smem = 227 * 1024;
     cudaError_t e = set_smem(gdn_mma_selftest_kernel, smem);
     if (e != cudaSuccess) return e;
-    gdn_mma_selftest_kernel<<<1, 128, smem, stream>>>(kind, M, N, K, A, B, D);
+    gdn_mma_selftest_kernel<<<1, 128, smem, stream>>>(kind, flags, M, N, K, A, B, D);
     return cudaGetLastError();
 }
 

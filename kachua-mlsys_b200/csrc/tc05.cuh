@@ -39,6 +39,15 @@ __device__ __forceinline__ uint32_t sw128_bf16(int row, int col, int rows) {
     return sw128_off(row, (col & 63) * 2, col >> 6, rows);
 }
 
+// MN-major 32-bit (tf32) operand image, layout SWIZZLE_128B_BASE32B: rows =
+// K index, 128-byte rows of 32 consecutive M (or N) elements, 4-row atoms of
+// 512 B in which the 32-byte chunks of row k are XOR-swizzled by (k & 3);
+// MN blocks of 32 elements are `krows * 128` bytes apart.
+__device__ __forceinline__ uint32_t mn32_f32(int k, int mn, int krows) {
+    const int b = (mn & 31) * 4;
+    return static_cast<uint32_t>((mn >> 5) * krows * 128 + k * 128 + ((((b >> 5) ^ (k & 3)) << 5) | (b & 31)));
+}
+
 // ---------------------------------------------------------------- mbarrier --
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
@@ -153,12 +162,30 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
            (2ull << 61);
 }
 
+// Descriptor of an MN-major 16-bit (bf16) SW128 image: the same byte layout
+// with rows = K index and the 128-byte row holding consecutive M (or N)
+// elements; 8-row K groups 1024 B apart (SBO), MN blocks `lbo` bytes apart
+// (LBO = K rows of the image x 128).
+__device__ __forceinline__ uint64_t sw128_desc_mn(uint32_t smem_addr, uint32_t lbo) {
+    return (static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu)) |
+           (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Descriptor of an MN-major 32-bit image (mn32_f32 layout): layout type
+// SWIZZLE_128B_BASE32B (1), 4-row K groups 512 B apart (SBO), MN blocks
+// `lbo` bytes apart.
+__device__ __forceinline__ uint64_t mn32_desc(uint32_t smem_addr, uint32_t lbo) {
+    return (static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu)) |
+           (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) | (32ull << 32) | (1ull << 46) | (1ull << 61);
+}
+
 enum Kind : uint32_t { kBF16 = 1, kTF32 = 2 };
 
 // Instruction descriptor (kind::f16 / kind::tf32): fp32 accumulator, A and B
-// of the same format, both K-major, no negation, dense.
-__host__ __device__ constexpr uint32_t idesc(Kind k, int M, int N) {
+// of the same format, no negation, dense; a_mn / b_mn select MN-major operands.
+__host__ __device__ constexpr uint32_t idesc(Kind k, int M, int N, bool a_mn = false, bool b_mn = false) {
     return (1u << 4) | (static_cast<uint32_t>(k) << 7) | (static_cast<uint32_t>(k) << 10) |
+           (static_cast<uint32_t>(a_mn) << 15) | (static_cast<uint32_t>(b_mn) << 16) |
            (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
@@ -182,22 +209,36 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
                  : "memory");
 }
 
-// D[M x N] (+)= A[M x Kdim] . B[N x Kdim]^T over whole K-blocks of SW128
-// images; `a_rows` / `b_rows` are the rows per K-block of each image (the
-// K-block stride is rows * 128 bytes).  Issued by one thread.
-template <Kind KIND>
+// D[M x N] (+)= A[M x Kdim] . B[N x Kdim]^T, issued by one thread.
+// A K-major operand image has rows = M (or N) with `x_rows` rows per K-block
+// (K-block stride x_rows * 128 B); an MN-major image has rows = K with
+// `x_rows` = its K rows (MN-block stride x_rows * 128 B) -- SW128 for bf16,
+// the mn32_f32 layout for tf32.  One instruction takes 32 bytes of K: 16 bf16
+// or 8 tf32 elements, i.e. 16 or 8 rows of an MN-major image.
+template <Kind KIND, bool A_MN = false, bool B_MN = false>
 __device__ __forceinline__ void mma_tile(uint32_t d_tmem, uint32_t a_smem, int a_rows, uint32_t b_smem, int b_rows,
                                          int kdim, int M, int N, bool accumulate) {
-    const uint32_t id = idesc(KIND, M, N);
+    const uint32_t id = idesc(KIND, M, N, A_MN, B_MN);
     constexpr int kElemBytes = KIND == kBF16 ? 2 : 4;
-    constexpr int kStepBytes = 32;  // K = 16 (bf16) or 8 (tf32) per instruction
-    const int steps = kdim * kElemBytes / kStepBytes;
+    constexpr int kStepK = 32 / kElemBytes;  // K elements per instruction
+    const int steps = kdim / kStepK;
 #pragma unroll 1
     for (int s = 0; s < steps; ++s) {
-        const int kb = (s * kStepBytes) >> 7;
-        const int in = (s * kStepBytes) & 127;
-        const uint64_t ad = sw128_desc(a_smem + kb * a_rows * 128 + in);
-        const uint64_t bd = sw128_desc(b_smem + kb * b_rows * 128 + in);
+        uint64_t ad, bd;
+        if (A_MN) {
+            ad = KIND == kBF16 ? sw128_desc_mn(a_smem + s * kStepK * 128, a_rows * 128)
+                               : mn32_desc(a_smem + s * kStepK * 128, a_rows * 128);
+        } else {
+            const int kb = (s * 32) >> 7, in = (s * 32) & 127;
+            ad = sw128_desc(a_smem + kb * a_rows * 128 + in);
+        }
+        if (B_MN) {
+            bd = KIND == kBF16 ? sw128_desc_mn(b_smem + s * kStepK * 128, b_rows * 128)
+                               : mn32_desc(b_smem + s * kStepK * 128, b_rows * 128);
+        } else {
+            const int kb = (s * 32) >> 7, in = (s * 32) & 127;
+            bd = sw128_desc(b_smem + kb * b_rows * 128 + in);
+        }
         if (KIND == kBF16)
             mma_bf16(d_tmem, ad, bd, id, (accumulate || s > 0) ? 1u : 0u);
         else

@@ -22,6 +22,21 @@ SHAPES = [  # (kind, M, N, K): the prepare and carry kernels' MMAs, plus neighbo
     ("bf16", 64, 32, 64),
     ("tf32", 128, 128, 128),
     ("bf16", 128, 256, 128),
+    # MN-major operands and the lane-16 accumulator of a packed M=64 pair
+    ("tf32", 64, 64, 64, 2),
+    ("tf32", 64, 64, 64, 1),
+    ("tf32", 64, 64, 64, 3),
+    ("tf32", 128, 32, 64, 2),
+    ("tf32", 128, 16, 64, 1),
+    ("tf32", 128, 128, 64, 3),
+    ("bf16", 64, 128, 64, 2),
+    ("bf16", 128, 64, 64, 1),
+    ("bf16", 128, 256, 64, 3),
+    ("tf32", 64, 64, 64, 4),
+    ("tf32", 64, 256, 64, 6),
+    ("bf16", 64, 128, 64, 7),
+    ("tf32", 128, 32, 128, 2),
+    ("bf16", 64, 64, 128, 2),
 ]
 
 
@@ -31,8 +46,10 @@ def _tf32(x):
     return ((xi + 0x1000) & ~0x1FFF).view(torch.float32)
 
 
-@pytest.mark.parametrize("kind,M,N,K", SHAPES)
-def test_mma_selftest(pkg, cuda_dev, kind, M, N, K):
+@pytest.mark.parametrize("case", SHAPES, ids=lambda c: "-".join(map(str, c)))
+def test_mma_selftest(pkg, cuda_dev, case):
+    kind, M, N, K = case[:4]
+    flags = case[4] if len(case) > 4 else 0
     C = pkg._capi
     lib = C.load()
     g = torch.Generator().manual_seed(M * 1000 + N + K)
@@ -47,7 +64,7 @@ def test_mma_selftest(pkg, cuda_dev, kind, M, N, K):
         code = C.MMA_KIND_TF32
     dA, dB = A.to(cuda_dev), B.to(cuda_dev)
     D = torch.full((M, N), float("nan"), device=cuda_dev)
-    rc = lib.gdn_mma_selftest(code, M, N, K, ctypes.c_void_p(dA.data_ptr()), ctypes.c_void_p(dB.data_ptr()),
+    rc = lib.gdn_mma_selftest(code, flags, M, N, K, ctypes.c_void_p(dA.data_ptr()), ctypes.c_void_p(dB.data_ptr()),
                               ctypes.c_void_p(D.data_ptr()),
                               ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert rc == 0, C.status_string(rc)
@@ -55,3 +72,11 @@ def test_mma_selftest(pkg, cuda_dev, kind, M, N, K):
     assert pkg.prefill.device_status(cuda_dev) == 0
     err = (D.double().cpu() - ref).abs().max().item()
     assert err < 1e-3 * max(1.0, ref.abs().max().item()), f"max err {err}"
+
+
+def test_mma_selftest_rejects_partial_mn_rows(pkg, cuda_dev):
+    """MN-major images must fill whole 128-byte rows (bf16 N=32 would not)."""
+    lib = pkg._capi.load()
+    buf = torch.zeros(64 * 128, device=cuda_dev)
+    p = ctypes.c_void_p(buf.data_ptr())
+    assert lib.gdn_mma_selftest(pkg._capi.MMA_KIND_BF16, 2, 64, 32, 128, p, p, p, None) == 2
