@@ -146,15 +146,19 @@ __global__ void __launch_bounds__(1024) gdn_chunk_table_kernel(const PrefillPara
 }
 
 // ---------------------------------------------------------------- prepare --
-// Shared memory of the prepare kernel (offsets from a 1024-aligned base).
-constexpr int kPrepKQ = 0;                         // bf16 [K;Q] image, 2 kblocks x 128 rows     32 KiB
-constexpr int kPrepX = kPrepKQ + 2 * 128 * 128;    // fp32 X (Neumann iterate, then Ainv) [64][64] 16 KiB
-constexpr int kPrepP = kPrepX + 2 * 64 * 128;      // fp32 power P [64][64]                     16 KiB
-constexpr int kPrepPT = kPrepP + 2 * 64 * 128;     // fp32 P^T                                  16 KiB
-constexpr int kPrepRHS = kPrepPT + 2 * 64 * 128;   // fp32 [(beta G K)^T ; (beta V)^T] [256][64] 64 KiB
-constexpr int kPrepPout = kPrepRHS + 2 * 256 * 128;  // bf16 P (output-side) [64][64]             8 KiB
-constexpr int kPrepSmall = kPrepPout + 64 * 128;
-constexpr int kPrepSmem = kPrepSmall + 2048 + 1024;  // + gates/bars, + alignment slack
+// One CTA (128 threads) per chunk record and q/k head; the two v-heads of the
+// q/k head share every M=64 accumulator, head 0 in TMEM lanes 0-15 and head 1
+// in lanes 16-31 of each warp's sub-partition, so in the packed epilogues
+// thread (warp w, lane l) owns row 16w + (l & 15) of head l >> 4.  Every
+// operand image is written as whole 16-byte vectors of one row; B operands
+// are MN-major images, so no transposed copy is ever made.
+constexpr int kPrepKQ = 0;          // bf16 [K;Q] K-major, 2 kblocks x 128 rows            32 KiB
+constexpr int kPrepX = 32768;       // tf32 X_h (Neumann iterate -> A^-1) K-major, 2 heads  2 x 16 KiB
+constexpr int kPrepPA = 65536;      // tf32 P_h (power of N) K-major                         2 x 16 KiB
+constexpr int kPrepPB = 98304;      // tf32 P_h MN-major (B operand)                          2 x 16 KiB
+constexpr int kPrepRHS = kPrepPA;   // tf32 [beta G K | beta V] MN-major, 64 x 256, over PA+PB  64 KiB
+constexpr int kPrepSmall = 131072;
+constexpr int kPrepSmem = kPrepSmall + 2048 + 1024;
 constexpr int kPrepTmemCols = 256;
 
 struct PrepSmall {
@@ -163,7 +167,6 @@ struct PrepSmall {
     float beta[2][kC];
     uint64_t bar_mma;
     uint32_t tmem_base;
-    int abort_flag;
 };
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
@@ -174,17 +177,28 @@ __device__ __forceinline__ void st_f32(uint8_t* img, uint32_t off, float v) {
     *reinterpret_cast<float*>(img + off) = v;
 }
 
+__device__ __forceinline__ float4 tf32x4(float a, float b, float c, float d) {
+    return make_float4(to_tf32(a), to_tf32(b), to_tf32(c), to_tf32(d));
+}
+
+// 8 bf16 (one 16-byte chunk) -> 8 floats
+__device__ __forceinline__ void bf16x8_to_f32(uint4 u, float (&f)[8]) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        f[2 * e] = __uint_as_float(w[e] << 16);
+        f[2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+    }
+}
+
 __global__ void __launch_bounds__(128, 1)
     gdn_chunk_prepare_kernel(const PrefillParams p, uint8_t* __restrict__ ws, const WsLayout L) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = align1024(smem_raw);
     uint8_t* sKQ = sm + kPrepKQ;
-    uint8_t* sX = sm + kPrepX;
-    uint8_t* sP = sm + kPrepP;
-    uint8_t* sPT = sm + kPrepPT;
-    uint8_t* sRHS = sm + kPrepRHS;
-    uint8_t* sPout = sm + kPrepPout;
     PrepSmall& sml = *reinterpret_cast<PrepSmall*>(sm + kPrepSmall);
+    const uint32_t aKQ = smem_u32(sKQ), aX = smem_u32(sm + kPrepX), aPA = smem_u32(sm + kPrepPA),
+                   aPB = smem_u32(sm + kPrepPB), aRHS = smem_u32(sm + kPrepRHS);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t rec = blockIdx.x;
@@ -199,7 +213,6 @@ __global__ void __launch_bounds__(128, 1)
     if (tid == 0) {
         mbar_init(bar, 1);
         fence_mbar_init();
-        sml.abort_flag = 0;
     }
     if (warp == 0) {
         tmem_alloc(smem_u32(&sml.tmem_base), kPrepTmemCols);
@@ -207,15 +220,13 @@ __global__ void __launch_bounds__(128, 1)
     }
 
     // 1. K and Q tiles -> [K;Q] bf16 image (rows >= n zero); gates of both v-heads
+#pragma unroll 4
     for (int idx = tid; idx < 2 * kC * 16; idx += 128) {
         const int m = idx >> 10;  // 0: K, 1: Q
         const int row = (idx >> 4) & 63;
         const int ch = idx & 15;  // 16-byte chunk of the 256-byte row
         uint4 val = make_uint4(0, 0, 0, 0);
-        if (row < n) {
-            const uint16_t* src = (m ? p.q : p.k) + ((t0 + row) * kHQK + hq) * kD + ch * 8;
-            val = *reinterpret_cast<const uint4*>(src);
-        }
+        if (row < n) val = *reinterpret_cast<const uint4*>((m ? p.q : p.k) + ((t0 + row) * kHQK + hq) * kD + ch * 8);
         const int r = 64 * m + row;
         *reinterpret_cast<uint4*>(sKQ + (ch >> 3) * (128 * 128) + r * 128 + (((ch & 7) ^ (r & 7)) << 4)) = val;
     }
@@ -240,210 +251,194 @@ __global__ void __launch_bounds__(128, 1)
 
     // 2. Gram: rows 0-63 K K^T, rows 64-127 Q K^T (bf16, M=128, N=64, K=128)
     if (tid == 0) {
-        mma_tile<kBF16>(tm, smem_u32(sKQ), 128, smem_u32(sKQ), 128, kD, 128, 64, false);
+        mma_ct<kBF16, false, false, kD, 128, 128, 128, 64>(tm, aKQ, aKQ, false);
         mma_commit(bar);
+        // the chunk's Q image leaves for the carry kernel (rows 64-127 of each K-block)
+        uint8_t* gq = ws + L.off_q + (rec * kHQK + hq) * kQImg;
+        bulk_s2g(gq, aKQ + 64 * 128, 64 * 128);
+        bulk_s2g(gq + 64 * 128, aKQ + 128 * 128 + 64 * 128, 64 * 128);
+        bulk_commit();
     }
-    {  // prefix sums of log2 g (64 sequential adds per thread; deterministic)
+    {  // inclusive prefix of log2 g (64 sequential adds; deterministic)
         const int hl = tid >> 6, i = tid & 63;
         float acc = 0.f;
         for (int m = 0; m <= i; ++m) acc += sml.lg[hl][m];
         sml.LG[hl][i] = acc;
     }
+    __syncthreads();
     ok = mbar_wait(bar, phase);
     phase ^= 1;
     tc_fence_after();
-    float gram[64];
     {
-        float t32[32];
-        tmem_ld32(taddr(tm, 32 * warp, 0), t32);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) gram[j] = t32[j];
-        tmem_ld32(taddr(tm, 32 * warp, 32), t32);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) gram[32 + j] = t32[j];
-        tmem_wait_ld();
-    }
-    tc_fence_before();
-    if (__syncthreads_or(!ok)) {
-                aborted = true;
-                goto done;
-            }
-
-    // 3. the Q image of this chunk and q/k head (rows 64-127 of each K-block)
-    if (tid == 0) {
-        uint8_t* gq = ws + L.off_q + (rec * kHQK + hq) * kQImg;
-        bulk_s2g(gq, smem_u32(sKQ + 64 * 128), 64 * 128);
-        bulk_s2g(gq + 64 * 128, smem_u32(sKQ + 128 * 128 + 64 * 128), 64 * 128);
-        bulk_commit();
-    }
-
-    for (int hl = 0; hl < 2; ++hl) {
-        const int h = 2 * hq + hl;
-        const int64_t rh = rec * kHV + h;
-        if (tid == 0) bulk_wait_read_all();  // staging buffers of the previous head are free
-        __syncthreads();
-        // a. N (strictly lower) -> P, P^T, X = I - N (threads 0-63 own K K^T rows);
-        //    output-side P_out (threads 64-127 own Q K^T rows)
+        // 3. Gram epilogue (M=128 rows: thread = row).  Rows 0-63 build N, P and
+        //    X = I - N of both heads; rows 64-127 build the output-side P.
+        float gram[64];
         {
-            const int i = tid & 63;
-            const float LGi = sml.LG[hl][i];
-            if (tid < 64) {
-                const float bi = sml.beta[hl][i];
+            float t32[32];
+            tmem_ld32(taddr(tm, 32 * warp, 0), t32);
 #pragma unroll
-                for (int j = 0; j < 64; ++j) {
-                    const float nij = (j < i) ? bi * exp2f(LGi - sml.LG[hl][j]) * gram[j] : 0.f;
-                    const float tn = to_tf32(nij);
-                    st_f32(sP, sw128_f32(i, j, 64), tn);
-                    st_f32(sPT, sw128_f32(j, i, 64), tn);
-                    st_f32(sX, sw128_f32(i, j, 64), to_tf32((j == i ? 1.f : 0.f) - nij));
+            for (int j = 0; j < 32; ++j) gram[j] = t32[j];
+            tmem_ld32(taddr(tm, 32 * warp, 32), t32);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) gram[32 + j] = t32[j];
+            tmem_wait_ld();
+        }
+        const int i = tid & 63;
+        if (tid < 64) {
+#pragma unroll 1
+            for (int hl = 0; hl < 2; ++hl) {
+                const float LGi = sml.LG[hl][i], bi = sml.beta[hl][i];
+                const uint32_t xa = aX + hl * 16384, pa = aPA + hl * 16384, pb = aPB + hl * 16384;
+#pragma unroll
+                for (int j0 = 0; j0 < 64; j0 += 4) {
+                    float nv[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int j = j0 + e;
+                        nv[e] = (j < i) ? bi * exp2f(LGi - sml.LG[hl][j]) * gram[j] : 0.f;
+                    }
+                    const float4 t = tf32x4(nv[0], nv[1], nv[2], nv[3]);
+                    st_shared_v4(pa + sw128_f32(i, j0, 64), t);
+                    st_shared_v4(pb + mn32_f32(i, j0, 64), t);
+                    st_shared_v4(xa + sw128_f32(i, j0, 64),
+                                 tf32x4((j0 == i) - nv[0], (j0 + 1 == i) - nv[1], (j0 + 2 == i) - nv[2],
+                                        (j0 + 3 == i) - nv[3]));
                 }
-            } else {
+            }
+        } else {
+#pragma unroll 1
+            for (int hl = 0; hl < 2; ++hl) {
+                const float LGi = sml.LG[hl][i];
+                uint8_t* gp = ws + L.off_p + (rec * kHV + 2 * hq + hl) * kPImg;
 #pragma unroll
-                for (int j = 0; j < 64; j += 2) {
-                    const float p0 = (j <= i) ? exp2f(LGi - sml.LG[hl][j]) * gram[j] : 0.f;
-                    const float p1 = (j + 1 <= i) ? exp2f(LGi - sml.LG[hl][j + 1]) * gram[j + 1] : 0.f;
-                    __nv_bfloat162 v2 = __floats2bfloat162_rn(p0, p1);
-                    *reinterpret_cast<__nv_bfloat162*>(sPout + sw128_bf16(i, j, 64)) = v2;
+                for (int c = 0; c < 8; ++c) {
+                    uint32_t w[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int j = 8 * c + 2 * e;
+                        const float a0 = (j <= i) ? exp2f(LGi - sml.LG[hl][j]) * gram[j] : 0.f;
+                        const float a1 = (j + 1 <= i) ? exp2f(LGi - sml.LG[hl][j + 1]) * gram[j + 1] : 0.f;
+                        const __nv_bfloat162 v2 = __floats2bfloat162_rn(a0, a1);
+                        w[e] = *reinterpret_cast<const uint32_t*>(&v2);
+                    }
+                    *reinterpret_cast<uint4*>(gp + i * 128 + ((c ^ (i & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+                }
+            }
+        }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {  // Neumann round 0: N_h^2 for both heads (lanes 16 h, columns 64-127)
+        tc_fence_after();
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+            mma_ct<kTF32, false, true, 64, 64, 64, 64, 64>(taddr(tm, 16 * h, 64), aPA + h * 16384, aPB + h * 16384,
+                                                          false);
+        mma_commit(bar);
+    }
+    // 4. Neumann doubling, both heads packed: epilogue e updates X (e >= 1) and P (e <= 4)
+    const int hl = lane >> 4;
+    const int row = 16 * warp + (lane & 15);
+    for (int e = 0; e <= 5; ++e) {
+        ok = mbar_wait(bar, phase);
+        phase ^= 1;
+        tc_fence_after();
+        if (e >= 1) {
+            const uint32_t xa = aX + hl * 16384;
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                float xp[32];
+                tmem_ld32(taddr(tm, 32 * warp, 32 * half), xp);
+                tmem_wait_ld();
+#pragma unroll
+                for (int j0 = 0; j0 < 32; j0 += 4) {
+                    const uint32_t off = xa + sw128_f32(row, 32 * half + j0, 64);
+                    const float4 x = ld_shared_v4(off);
+                    st_shared_v4(off, tf32x4(x.x + xp[j0], x.y + xp[j0 + 1], x.z + xp[j0 + 2], x.w + xp[j0 + 3]));
+                }
+            }
+        }
+        if (e <= 4) {
+            const uint32_t pa = aPA + hl * 16384, pb = aPB + hl * 16384;
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                float pp[32];
+                tmem_ld32(taddr(tm, 32 * warp, 64 + 32 * half), pp);
+                tmem_wait_ld();
+#pragma unroll
+                for (int j0 = 0; j0 < 32; j0 += 4) {
+                    const float4 t = tf32x4(pp[j0], pp[j0 + 1], pp[j0 + 2], pp[j0 + 3]);
+                    st_shared_v4(pa + sw128_f32(row, 32 * half + j0, 64), t);
+                    st_shared_v4(pb + mn32_f32(row, 32 * half + j0, 64), t);
                 }
             }
         }
         fence_async_smem();
         tc_fence_before();
-        __syncthreads();
-        if (tid == 0) {
-            bulk_s2g(ws + L.off_p + rh * kPImg, smem_u32(sPout), kPImg);
-            bulk_commit();
+        if (__syncthreads_or(!ok)) {
+            aborted = true;
+            goto done;
+        }
+        if (tid == 0 && e <= 4) {
             tc_fence_after();
-            mma_tile<kTF32>(tm + 64, smem_u32(sP), 64, smem_u32(sPT), 64, 64, 64, 64, false);  // N^2
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                mma_ct<kTF32, false, true, 64, 64, 64, 64, 64>(taddr(tm, 16 * h, 0), aX + h * 16384,
+                                                              aPB + h * 16384, false);  // X P
+                if (e <= 3)
+                    mma_ct<kTF32, false, true, 64, 64, 64, 64, 64>(taddr(tm, 16 * h, 64), aPA + h * 16384,
+                                                                  aPB + h * 16384, false);  // P P
+            }
             mma_commit(bar);
         }
-        // b. Neumann rounds: epilogue e updates X (e >= 1) and P (e <= 4)
-        for (int e = 0; e <= 5; ++e) {
-            ok = mbar_wait(bar, phase);
-            phase ^= 1;
-            tc_fence_after();
-            const int i = 16 * warp + lane;  // M=64 row of this lane (lanes < 16)
-            if (e >= 1) {
-#pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    float xp[32];
-                    tmem_ld32(taddr(tm, 32 * warp, 32 * half), xp);
-                    tmem_wait_ld();
-                    if (lane < 16) {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const uint32_t off = sw128_f32(i, 32 * half + j, 64);
-                            const float x = *reinterpret_cast<const float*>(sX + off);
-                            st_f32(sX, off, to_tf32(x + xp[j]));
-                        }
-                    }
-                }
-            }
-            if (e <= 4) {
-#pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    float pp[32];
-                    tmem_ld32(taddr(tm, 32 * warp, 64 + 32 * half), pp);
-                    tmem_wait_ld();
-                    if (lane < 16) {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const float v = to_tf32(pp[j]);
-                            st_f32(sP, sw128_f32(i, 32 * half + j, 64), v);
-                            st_f32(sPT, sw128_f32(32 * half + j, i, 64), v);
-                        }
-                    }
-                }
-            }
-            fence_async_smem();
-            tc_fence_before();
-            if (__syncthreads_or(!ok)) {
-                aborted = true;
-                goto done;
-            }
-            if (tid == 0 && e <= 4) {
-                tc_fence_after();
-                mma_tile<kTF32>(tm, smem_u32(sX), 64, smem_u32(sPT), 64, 64, 64, 64, false);  // X P
-                if (e <= 3) mma_tile<kTF32>(tm + 64, smem_u32(sP), 64, smem_u32(sPT), 64, 64, 64, 64, false);
-                mma_commit(bar);
-            }
-        }
-        // c. right-hand sides, K-bar^T image (into the free P/P^T space) and the gate vector
+    }
+    // 5. per head: [beta G K | beta V] (MN-major, over the dead P images), the
+    //    K-bar image and gate vector to global, then [W | U] = A^-1 [..]
+#pragma unroll 1
+    for (int h2 = 0; h2 < 2; ++h2) {
+        const int h = 2 * hq + h2;
+        const int64_t rh = rec * kHV + h;
         {
             const int j = tid & 63, part = tid >> 6;
-            const float LGj = sml.LG[hl][j];
-            const float LGc = sml.LG[hl][63];
-            const float bj = sml.beta[hl][j];
-            const float Gj = exp2f(LGj);
-            const float tail = exp2f(LGc - LGj);
-            uint8_t* sKT = sP;  // [128 rows k][64 cols j] fp32, 32 KiB over sP + sPT
+            const float LGj = sml.LG[h2][j], bj = sml.beta[h2][j];
+            const float Gj = exp2f(LGj), tail = exp2f(sml.LG[h2][63] - LGj);
+            uint8_t* gkb = ws + L.off_kt + rh * kKTImg;
+            // part 0: columns 0-127 (beta G K) and K-bar columns 0-63; part 1: beta V and K-bar 64-127
             if (part == 0) {
 #pragma unroll 4
-                for (int k = 0; k < kD; ++k) {
-                    const float kv =
-                        __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(sKQ + sw128_bf16(j, k, 128)));
-                    st_f32(sRHS, sw128_f32(k, j, 256), to_tf32(bj * Gj * kv));
-                    if (k < 64) st_f32(sKT, sw128_f32(k, j, 128), to_tf32(tail * kv));
+                for (int d0 = 0; d0 < kD; d0 += 8) {
+                    float f[8];
+                    bf16x8_to_f32(*reinterpret_cast<const uint4*>(sKQ + sw128_bf16(j, d0, 128)), f);
+                    const float s = bj * Gj;
+                    st_shared_v4(aRHS + mn32_f32(j, d0, 64), tf32x4(s * f[0], s * f[1], s * f[2], s * f[3]));
+                    st_shared_v4(aRHS + mn32_f32(j, d0 + 4, 64), tf32x4(s * f[4], s * f[5], s * f[6], s * f[7]));
+                    if (d0 < 64) {
+                        *reinterpret_cast<float4*>(gkb + mn32_f32(j, d0, 64)) =
+                            tf32x4(tail * f[0], tail * f[1], tail * f[2], tail * f[3]);
+                        *reinterpret_cast<float4*>(gkb + mn32_f32(j, d0 + 4, 64)) =
+                            tf32x4(tail * f[4], tail * f[5], tail * f[6], tail * f[7]);
+                    }
                 }
+                float* gvec = reinterpret_cast<float*>(ws + L.off_vec + rh * kVecBytes);
+                gvec[j] = Gj;
+                if (j == 0) gvec[64] = exp2f(sml.LG[h2][63]);
             } else {
                 const bool act = j < n;
                 const uint16_t* vsrc = p.v + ((t0 + j) * kHV + h) * kD;
 #pragma unroll 4
-                for (int d0 = 0; d0 < kD; d0 += 4) {
-                    float4 v4 = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (act) v4 = bf16x4_to_float4(ld_u2(vsrc + d0));
-                    st_f32(sRHS, sw128_f32(128 + d0 + 0, j, 256), to_tf32(bj * v4.x));
-                    st_f32(sRHS, sw128_f32(128 + d0 + 1, j, 256), to_tf32(bj * v4.y));
-                    st_f32(sRHS, sw128_f32(128 + d0 + 2, j, 256), to_tf32(bj * v4.z));
-                    st_f32(sRHS, sw128_f32(128 + d0 + 3, j, 256), to_tf32(bj * v4.w));
-                }
-#pragma unroll 4
-                for (int k = 64; k < kD; ++k) {
-                    const float kv =
-                        __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(sKQ + sw128_bf16(j, k, 128)));
-                    st_f32(sKT, sw128_f32(k, j, 128), to_tf32(tail * kv));
-                }
-                float* gvec = reinterpret_cast<float*>(ws + L.off_vec + rh * kVecBytes);
-                gvec[j] = Gj;
-                if (j == 0) gvec[64] = exp2f(LGc);
-            }
-        }
-        fence_async_smem();
-        tc_fence_before();
-        __syncthreads();
-        if (tid == 0) {
-            bulk_s2g(ws + L.off_kt + rh * kKTImg, smem_u32(sP), kKTImg);
-            bulk_commit();
-            tc_fence_after();
-            mma_tile<kTF32>(tm, smem_u32(sX), 64, smem_u32(sRHS), 256, 64, 64, 256, false);  // [W | U]
-            mma_commit(bar);
-        }
-        ok = mbar_wait(bar, phase);
-        phase ^= 1;
-        tc_fence_after();
-        if (__syncthreads_or(!ok)) {
-                aborted = true;
-                goto done;
-            }
-        // d. W (tf32 image) and U (plain fp32) rows -> staging (the RHS space) -> global
-        {
-            const int i = 16 * warp + lane;
-            uint8_t* sW = sRHS;
-            float* sU = reinterpret_cast<float*>(sRHS + kWImg);
-#pragma unroll 1
-            for (int c = 0; c < 8; ++c) {
-                float acc[32];
-                tmem_ld32(taddr(tm, 32 * warp, 32 * c), acc);
-                tmem_wait_ld();
-                if (lane < 16) {
-                    if (c < 4) {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) st_f32(sW, sw128_f32(i, 32 * c + j, 64), to_tf32(acc[j]));
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; j += 4)
-                            *reinterpret_cast<float4*>(sU + i * kD + 32 * (c - 4) + j) =
-                                make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+                for (int d0 = 0; d0 < kD; d0 += 8) {
+                    float f[8];
+                    bf16x8_to_f32(act ? *reinterpret_cast<const uint4*>(vsrc + d0) : make_uint4(0, 0, 0, 0), f);
+                    st_shared_v4(aRHS + mn32_f32(j, 128 + d0, 64), tf32x4(bj * f[0], bj * f[1], bj * f[2], bj * f[3]));
+                    st_shared_v4(aRHS + mn32_f32(j, 132 + d0, 64), tf32x4(bj * f[4], bj * f[5], bj * f[6], bj * f[7]));
+                    if (d0 >= 64) {
+                        float g[8];
+                        bf16x8_to_f32(*reinterpret_cast<const uint4*>(sKQ + sw128_bf16(j, d0, 128)), g);
+                        *reinterpret_cast<float4*>(gkb + mn32_f32(j, d0, 64)) =
+                            tf32x4(tail * g[0], tail * g[1], tail * g[2], tail * g[3]);
+                        *reinterpret_cast<float4*>(gkb + mn32_f32(j, d0 + 4, 64)) =
+                            tf32x4(tail * g[4], tail * g[5], tail * g[6], tail * g[7]);
                     }
                 }
             }
@@ -452,9 +447,39 @@ __global__ void __launch_bounds__(128, 1)
         tc_fence_before();
         __syncthreads();
         if (tid == 0) {
-            bulk_s2g(ws + L.off_w + rh * kWImg, smem_u32(sRHS), kWImg);
-            bulk_s2g(ws + L.off_u + rh * kUBytes, smem_u32(sRHS + kWImg), kUBytes);
-            bulk_commit();
+            tc_fence_after();
+            mma_ct<kTF32, false, true, 64, 64, 64, 64, 256>(taddr(tm, 16 * h2, 0), aX + h2 * 16384, aRHS, false);
+            mma_commit(bar);
+        }
+        ok = mbar_wait(bar, phase);  // also frees the RHS image for the next head
+        phase ^= 1;
+        tc_fence_after();
+        if (__syncthreads_or(!ok)) {
+            aborted = true;
+            goto done;
+        }
+    }
+    {   // 6. [W | U] rows of both heads (packed): W as the carry's tf32 A image, U plain
+        const int h = 2 * hq + hl;
+        const int64_t rh = rec * kHV + h;
+        uint8_t* gw = ws + L.off_w + rh * kWImg;
+        float* gu = reinterpret_cast<float*>(ws + L.off_u + rh * kUBytes) + row * kD;
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) {
+            float acc[32];
+            tmem_ld32(taddr(tm, 32 * warp, 32 * c), acc);
+            tmem_wait_ld();
+            if (c < 4) {
+#pragma unroll
+                for (int j0 = 0; j0 < 32; j0 += 4)
+                    *reinterpret_cast<float4*>(gw + sw128_f32(row, 32 * c + j0, 64)) =
+                        tf32x4(acc[j0], acc[j0 + 1], acc[j0 + 2], acc[j0 + 3]);
+            } else {
+#pragma unroll
+                for (int j0 = 0; j0 < 32; j0 += 4)
+                    *reinterpret_cast<float4*>(gu + 32 * (c - 4) + j0) =
+                        make_float4(acc[j0], acc[j0 + 1], acc[j0 + 2], acc[j0 + 3]);
+            }
         }
     }
 done:
@@ -471,6 +496,13 @@ done:
 }
 
 // ------------------------------------------------------------------ carry --
+// One CTA (128 threads) per sequence x v-head x BV value rows.  Per chunk:
+//   MMA1  W S0^T (tf32, B = S MN-major)  and  Q S0^T (bf16)      -> rows = tokens
+//   epi A Delta = U - W S0^T  -> Delta images (tf32 MN-major, bf16 K-major)
+//   MMA2  (tail K)^T Delta (tf32, both operands MN-major)  and  P Delta (bf16)
+//   epi B S1 = G_C S0 + (tail K)^T Delta (thread k owns state column k),
+//         O = scale (G (.) Q S0^T + P Delta) for the chunk's tokens
+// The next chunk's operand images are bulk-copied into the other slot meanwhile.
 constexpr int kSlotQ = 0;
 constexpr int kSlotW = kSlotQ + kQImg;
 constexpr int kSlotKT = kSlotW + kWImg;
@@ -481,11 +513,11 @@ constexpr uint32_t kSlotTx = kQImg + kWImg + kKTImg + kPImg + kVecBytes;
 
 template <int BV>
 struct CarrySmem {
-    static constexpr int kSlots = 0;                               // 2 operand slots
-    static constexpr int kS32 = kSlots + 2 * kSlotBytes;           // fp32 S image [BV][128], 4 kblocks
-    static constexpr int kS16 = kS32 + BV * 512;                   // bf16 S image [BV][128], 2 kblocks
-    static constexpr int kD32 = kS16 + BV * 256;                   // fp32 Delta^T image [BV][64], 2 kblocks
-    static constexpr int kD16 = kD32 + BV * 256;                   // bf16 Delta^T image [BV][64], 1 kblock
+    static constexpr int kSlots = 0;                      // 2 operand slots
+    static constexpr int kS32 = kSlots + 2 * kSlotBytes;  // tf32 S MN-major [128 k][BV]
+    static constexpr int kS16 = kS32 + BV * 512;          // bf16 S K-major [BV v][128 k]
+    static constexpr int kD32 = kS16 + BV * 256;          // tf32 Delta MN-major [64 j][BV]
+    static constexpr int kD16 = kD32 + BV * 256;          // bf16 Delta K-major [BV v][64 j]
     static constexpr int kSmall = kD16 + BV * 128;
     static constexpr int kTotal = kSmall + 128 + 1024;
     static constexpr int kTmemCols = 4 * BV < 32 ? 32 : 4 * BV;
@@ -495,13 +527,11 @@ template <int BV>
 __global__ void __launch_bounds__(128, 1)
     gdn_chunk_carry_kernel(const PrefillParams p, const uint8_t* __restrict__ ws, const WsLayout L) {
     using SM = CarrySmem<BV>;
-    static_assert(BV == 16 || BV == 32, "value-row tile");
+    static_assert(BV == 32 || BV == 64, "value-row tile (MN-major tf32 images need 32-wide rows)");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = align1024(smem_raw);
-    uint8_t* sS32 = sm + SM::kS32;
-    uint8_t* sS16 = sm + SM::kS16;
-    uint8_t* sD32 = sm + SM::kD32;
-    uint8_t* sD16 = sm + SM::kD16;
+    const uint32_t aS32 = smem_u32(sm + SM::kS32), aS16 = smem_u32(sm + SM::kS16), aD32 = smem_u32(sm + SM::kD32),
+                   aD16 = smem_u32(sm + SM::kD16);
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + SM::kSmall);  // full[2], mma1, mma2
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + SM::kSmall + 64);
 
@@ -516,8 +546,7 @@ __global__ void __launch_bounds__(128, 1)
     int64_t t0, t1;
     seq_bounds(p, s, t0, t1);
     const int nch = static_cast<int>((t1 - t0 + kC - 1) / kC);
-    const int* wbase = reinterpret_cast<const int*>(ws + L.off_base);
-    const int rec0 = wbase[s];
+    const int rec0 = reinterpret_cast<const int*>(ws + L.off_base)[s];
     float* ns_col = p.new_state + (unit * kD + v0) * kD + tid;  // column k = tid of rows v0..
     if (nch == 0 || rec0 + nch > L.R) {
         if (nch != 0) record_status(16);
@@ -536,11 +565,16 @@ __global__ void __launch_bounds__(128, 1)
 #pragma unroll
         for (int v = 0; v < BV; ++v) S[v] = 0.f;
     }
+    auto write_state_images = [&]() {
 #pragma unroll
-    for (int v = 0; v < BV; ++v) {
-        st_f32(sS32, sw128_f32(v, tid, BV), to_tf32(S[v]));
-        *reinterpret_cast<__nv_bfloat16*>(sS16 + sw128_bf16(v, tid, BV)) = __float2bfloat16_rn(S[v]);
-    }
+        for (int v = 0; v < BV; v += 4) {
+            st_shared_v4(aS32 + mn32_f32(tid, v, kD), tf32x4(S[v], S[v + 1], S[v + 2], S[v + 3]));
+        }
+#pragma unroll
+        for (int v = 0; v < BV; ++v)
+            *reinterpret_cast<__nv_bfloat16*>(sm + SM::kS16 + sw128_bf16(v, tid, BV)) = __float2bfloat16_rn(S[v]);
+    };
+    write_state_images();
 
     const uint32_t full0 = smem_u32(&bars[0]), mma1 = smem_u32(&bars[2]), mma2 = smem_u32(&bars[3]);
     if (tid == 0) {
@@ -557,14 +591,14 @@ __global__ void __launch_bounds__(128, 1)
     auto issue_loads = [&](int c) {
         const int64_t r = rec0 + c;
         const int64_t rh = r * kHV + h;
-        uint8_t* slot = sm + SM::kSlots + (c & 1) * kSlotBytes;
+        const uint32_t slot = smem_u32(sm + SM::kSlots + (c & 1) * kSlotBytes);
         const uint32_t fb = full0 + 8 * (c & 1);
         mbar_expect_tx(fb, kSlotTx);
-        bulk_g2s(smem_u32(slot + kSlotQ), ws + L.off_q + (r * kHQK + h / kGva) * kQImg, kQImg, fb);
-        bulk_g2s(smem_u32(slot + kSlotW), ws + L.off_w + rh * kWImg, kWImg, fb);
-        bulk_g2s(smem_u32(slot + kSlotKT), ws + L.off_kt + rh * kKTImg, kKTImg, fb);
-        bulk_g2s(smem_u32(slot + kSlotP), ws + L.off_p + rh * kPImg, kPImg, fb);
-        bulk_g2s(smem_u32(slot + kSlotVec), ws + L.off_vec + rh * kVecBytes, kVecBytes, fb);
+        bulk_g2s(slot + kSlotQ, ws + L.off_q + (r * kHQK + h / kGva) * kQImg, kQImg, fb);
+        bulk_g2s(slot + kSlotW, ws + L.off_w + rh * kWImg, kWImg, fb);
+        bulk_g2s(slot + kSlotKT, ws + L.off_kt + rh * kKTImg, kKTImg, fb);
+        bulk_g2s(slot + kSlotP, ws + L.off_p + rh * kPImg, kPImg, fb);
+        bulk_g2s(slot + kSlotVec, ws + L.off_vec + rh * kVecBytes, kVecBytes, fb);
     };
     fence_async_smem();
     tc_fence_before();
@@ -581,6 +615,7 @@ __global__ void __launch_bounds__(128, 1)
     for (int c = 0; c < nch; ++c) {
         const int slot = c & 1;
         const uint8_t* sl = sm + SM::kSlots + slot * kSlotBytes;
+        const uint32_t asl = smem_u32(sl);
         const int64_t r = rec0 + c;
         const int64_t rh = r * kHV + h;
         if (c + 1 < nch) {
@@ -591,16 +626,16 @@ __global__ void __launch_bounds__(128, 1)
         if (ok) last_landed = c;
         if (tid == 0 && ok) {
             tc_fence_after();
-            mma_tile<kTF32>(t_ws, smem_u32(sl + kSlotW), 64, smem_u32(sS32), BV, kD, 64, BV, false);
-            mma_tile<kBF16>(t_qs, smem_u32(sl + kSlotQ), 64, smem_u32(sS16), BV, kD, 64, BV, false);
+            mma_ct<kTF32, false, true, kD, 64, kD, 64, BV>(t_ws, asl + kSlotW, aS32, false);
+            mma_ct<kBF16, false, false, kD, 64, BV, 64, BV>(t_qs, asl + kSlotQ, aS16, false);
             mma_commit(mma1);
         }
         const int tok = 64 * c + row;
         const bool act = lane < 16 && tok < t1 - t0;
         float u[BV];
-        if (lane < 16) {
+        {
             const float4* up = reinterpret_cast<const float4*>(
-                reinterpret_cast<const float*>(ws + L.off_u + rh * kUBytes) + row * kD + v0);
+                reinterpret_cast<const float*>(ws + L.off_u + rh * kUBytes) + (row & 63) * kD + v0);
 #pragma unroll
             for (int v = 0; v < BV; v += 4) {
                 const float4 x = up[v / 4];
@@ -615,20 +650,31 @@ __global__ void __launch_bounds__(128, 1)
         const float gi = vec[row & 63];
         ok = ok && mbar_wait(mma1, c & 1);
         tc_fence_after();
-        {  // Delta = U - W S0^T  -> Delta^T images (B operand of the next two MMAs)
-            float ws_row[BV];
-            if constexpr (BV == 16) {
-                tmem_ld16(taddr(t_ws, 32 * warp, 0), ws_row);
+        {  // Delta = U - W S0^T -> Delta images (B operands of the next two MMAs)
+            float wsr[BV];
+            if constexpr (BV == 32) {
+                tmem_ld32(taddr(t_ws, 32 * warp, 0), wsr);
             } else {
-                tmem_ld32(taddr(t_ws, 32 * warp, 0), ws_row);
+                float a[32], b[32];
+                tmem_ld32(taddr(t_ws, 32 * warp, 0), a);
+                tmem_ld32(taddr(t_ws, 32 * warp, 32), b);
+#pragma unroll
+                for (int v = 0; v < 32; ++v) wsr[v] = a[v], wsr[32 + v] = b[v];
             }
             tmem_wait_ld();
             if (lane < 16) {
 #pragma unroll
-                for (int v = 0; v < BV; ++v) {
-                    const float d = u[v] - ws_row[v];
-                    st_f32(sD32, sw128_f32(v, row, BV), to_tf32(d));
-                    *reinterpret_cast<__nv_bfloat16*>(sD16 + sw128_bf16(v, row, BV)) = __float2bfloat16_rn(d);
+                for (int v = 0; v < BV; v += 4) {
+                    const float d0 = u[v] - wsr[v], d1 = u[v + 1] - wsr[v + 1], d2 = u[v + 2] - wsr[v + 2],
+                                d3 = u[v + 3] - wsr[v + 3];
+                    st_shared_v4(aD32 + mn32_f32(row, v, 64), tf32x4(d0, d1, d2, d3));
+                    *reinterpret_cast<__nv_bfloat16*>(sm + SM::kD16 + sw128_bf16(v, row, BV)) = __float2bfloat16_rn(d0);
+                    *reinterpret_cast<__nv_bfloat16*>(sm + SM::kD16 + sw128_bf16(v + 1, row, BV)) =
+                        __float2bfloat16_rn(d1);
+                    *reinterpret_cast<__nv_bfloat16*>(sm + SM::kD16 + sw128_bf16(v + 2, row, BV)) =
+                        __float2bfloat16_rn(d2);
+                    *reinterpret_cast<__nv_bfloat16*>(sm + SM::kD16 + sw128_bf16(v + 3, row, BV)) =
+                        __float2bfloat16_rn(d3);
                 }
             }
         }
@@ -640,30 +686,37 @@ __global__ void __launch_bounds__(128, 1)
         }
         if (tid == 0) {
             tc_fence_after();
-            mma_tile<kTF32>(t_up, smem_u32(sl + kSlotKT), 128, smem_u32(sD32), BV, 64, 128, BV, false);
-            mma_tile<kBF16>(t_pd, smem_u32(sl + kSlotP), 64, smem_u32(sD16), BV, 64, 64, BV, false);
+            mma_ct<kTF32, true, true, 64, 64, 64, 128, BV>(t_up, asl + kSlotKT, aD32, false);
+            mma_ct<kBF16, false, false, 64, 64, BV, 64, BV>(t_pd, asl + kSlotP, aD16, false);
             mma_commit(mma2);
         }
         ok = mbar_wait(mma2, c & 1);
         tc_fence_after();
         {  // S1 = G_C S0 + (tail K)^T Delta ; O = scale (G (.) Q S0^T + P Delta)
             float up[BV], qs[BV], pd[BV];
-            if constexpr (BV == 16) {
-                tmem_ld16(taddr(t_up, 32 * warp, 0), up);
-                tmem_ld16(taddr(t_qs, 32 * warp, 0), qs);
-                tmem_ld16(taddr(t_pd, 32 * warp, 0), pd);
-            } else {
+            if constexpr (BV == 32) {
                 tmem_ld32(taddr(t_up, 32 * warp, 0), up);
                 tmem_ld32(taddr(t_qs, 32 * warp, 0), qs);
                 tmem_ld32(taddr(t_pd, 32 * warp, 0), pd);
+            } else {
+                float a[32];
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    tmem_ld32(taddr(t_up, 32 * warp, 32 * hh), a);
+#pragma unroll
+                    for (int v = 0; v < 32; ++v) up[32 * hh + v] = a[v];
+                    tmem_ld32(taddr(t_qs, 32 * warp, 32 * hh), a);
+#pragma unroll
+                    for (int v = 0; v < 32; ++v) qs[32 * hh + v] = a[v];
+                    tmem_ld32(taddr(t_pd, 32 * warp, 32 * hh), a);
+#pragma unroll
+                    for (int v = 0; v < 32; ++v) pd[32 * hh + v] = a[v];
+                }
             }
             tmem_wait_ld();
 #pragma unroll
-            for (int v = 0; v < BV; ++v) {
-                S[v] = fmaf(gc, S[v], up[v]);
-                st_f32(sS32, sw128_f32(v, tid, BV), to_tf32(S[v]));
-                *reinterpret_cast<__nv_bfloat16*>(sS16 + sw128_bf16(v, tid, BV)) = __float2bfloat16_rn(S[v]);
-            }
+            for (int v = 0; v < BV; ++v) S[v] = fmaf(gc, S[v], up[v]);
+            write_state_images();
             if (act) {
                 __nv_bfloat16* o = out + ((t0 + tok) * kHV + h) * kD + v0;
 #pragma unroll
@@ -719,18 +772,11 @@ cudaError_t launch_prefill_chunked(const PrefillParams& p, void* workspace, cuda
     if (L.R > 0x7fffffffLL) return cudaErrorInvalidValue;
     gdn_chunk_prepare_kernel<<<dim3(static_cast<unsigned>(L.R), kHQK), 128, kPrepSmem, stream>>>(p, ws, L);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    const bool wide = p.num_seqs * kHV * (kD / 32) >= kSmCount;
-    if (wide) {
-        using SM = CarrySmem<32>;
-        if ((e = set_smem(gdn_chunk_carry_kernel<32>, SM::kTotal)) != cudaSuccess) return e;
-        const int64_t grid = p.num_seqs * kHV * (kD / 32);
-        gdn_chunk_carry_kernel<32><<<static_cast<unsigned>(grid), 128, SM::kTotal, stream>>>(p, ws, L);
-    } else {
-        using SM = CarrySmem<16>;
-        if ((e = set_smem(gdn_chunk_carry_kernel<16>, SM::kTotal)) != cudaSuccess) return e;
-        const int64_t grid = p.num_seqs * kHV * (kD / 16);
-        gdn_chunk_carry_kernel<16><<<static_cast<unsigned>(grid), 128, SM::kTotal, stream>>>(p, ws, L);
-    }
+    using SM = CarrySmem<32>;
+    if ((e = set_smem(gdn_chunk_carry_kernel<32>, SM::kTotal)) != cudaSuccess) return e;
+    const int64_t grid = p.num_seqs * kHV * (kD / 32);
+    if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
+    gdn_chunk_carry_kernel<32><<<static_cast<unsigned>(grid), 128, SM::kTotal, stream>>>(p, ws, L);
     return cudaGetLastError();
 }
 

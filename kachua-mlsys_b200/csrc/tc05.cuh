@@ -246,6 +246,45 @@ __device__ __forceinline__ void mma_tile(uint32_t d_tmem, uint32_t a_smem, int a
     }
 }
 
+// mma_tile with every shape known at compile time: the two base descriptors
+// are built once and each K step only adds a constant to the start-address
+// field (no carry out of its 14 bits: shared addresses stay below 256 KB).
+template <Kind KIND, bool A_MN, bool B_MN, int KDIM, int AROWS, int BROWS, int M, int N>
+__device__ __forceinline__ void mma_ct(uint32_t d_tmem, uint32_t a_smem, uint32_t b_smem, bool accumulate) {
+    constexpr uint32_t id = idesc(KIND, M, N, A_MN, B_MN);
+    constexpr int kElemBytes = KIND == kBF16 ? 2 : 4;
+    constexpr int kStepK = 32 / kElemBytes;
+    constexpr int kSteps = KDIM / kStepK;
+    static_assert(KDIM % kStepK == 0, "K must be a whole number of instructions");
+    const uint64_t a0 = A_MN ? (KIND == kBF16 ? sw128_desc_mn(a_smem, AROWS * 128) : mn32_desc(a_smem, AROWS * 128))
+                             : sw128_desc(a_smem);
+    const uint64_t b0 = B_MN ? (KIND == kBF16 ? sw128_desc_mn(b_smem, BROWS * 128) : mn32_desc(b_smem, BROWS * 128))
+                             : sw128_desc(b_smem);
+#pragma unroll
+    for (int s = 0; s < kSteps; ++s) {
+        const uint32_t a_off = A_MN ? s * kStepK * 128 : ((s * 32) >> 7) * AROWS * 128 + ((s * 32) & 127);
+        const uint32_t b_off = B_MN ? s * kStepK * 128 : ((s * 32) >> 7) * BROWS * 128 + ((s * 32) & 127);
+        const uint64_t ad = a0 + (a_off >> 4);
+        const uint64_t bd = b0 + (b_off >> 4);
+        const uint32_t acc = (accumulate || s > 0) ? 1u : 0u;
+        if (KIND == kBF16)
+            mma_bf16(d_tmem, ad, bd, id, acc);
+        else
+            mma_tf32(d_tmem, ad, bd, id, acc);
+    }
+}
+
+// Vector stores of 4 fp32 into shared memory / 16 bytes anywhere.
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, float4 v) {
+    asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+__device__ __forceinline__ float4 ld_shared_v4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+    return v;
+}
+
 // fp32 -> tf32 with round-to-nearest (ties away); low 13 bits cleared.
 __device__ __forceinline__ float to_tf32(float x) {
     uint32_t r;
