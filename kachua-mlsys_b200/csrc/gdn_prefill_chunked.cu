@@ -37,13 +37,12 @@ namespace gdn {
 using namespace tc05;
 
 constexpr int kC = 64;
-constexpr int kQImg = kC * kD * 2;        // bf16 [64][128]        16 KiB
 constexpr int kWImg = kC * kD * 4;        // fp32 [64][128]        32 KiB
 constexpr int kKTImg = kD * kC * 4;       // fp32 [128][64]        32 KiB
-constexpr int kPImg = kC * kC * 2;        // bf16 [64][64]          8 KiB
+constexpr int kPImg = kC * kC * 4;        // tf32 [64][64]         16 KiB
 constexpr int kUBytes = kC * kD * 4;      // fp32 [64][128] plain  32 KiB
 constexpr int kVecBytes = 512;            // G[64], G_C
-constexpr int kRecordBytes = kHQK * kQImg + kHV * (kWImg + kKTImg + kPImg + kUBytes + kVecBytes);
+constexpr int kRecordBytes = kHV * (kWImg + kKTImg + kPImg + kUBytes + kVecBytes);
 
 __host__ __device__ inline int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
 
@@ -51,7 +50,7 @@ __host__ __device__ inline int64_t align_up(int64_t x, int64_t a) { return (x + 
 // per-record operand arrays (every array 1024-byte aligned).
 struct WsLayout {
     int64_t R;  // record capacity: ceil(T / 64) + N bounds sum_s ceil(len_s / 64)
-    int64_t off_hdr, off_base, off_table, off_q, off_w, off_kt, off_p, off_u, off_vec, total;
+    int64_t off_hdr, off_base, off_table, off_w, off_kt, off_p, off_u, off_vec, total;
 };
 
 __host__ __device__ inline WsLayout ws_layout(int64_t T, int64_t N) {
@@ -64,8 +63,6 @@ __host__ __device__ inline WsLayout ws_layout(int64_t T, int64_t N) {
     o = align_up(o + 4 * (N + 1), 1024);
     L.off_table = o;
     o = align_up(o + 16 * L.R, 1024);
-    L.off_q = o;
-    o += L.R * kHQK * kQImg;
     L.off_w = o;
     o += L.R * kHV * kWImg;
     L.off_kt = o;
@@ -152,12 +149,15 @@ __global__ void __launch_bounds__(1024) gdn_chunk_table_kernel(const PrefillPara
 // thread (warp w, lane l) owns row 16w + (l & 15) of head l >> 4.  Every
 // operand image is written as whole 16-byte vectors of one row; B operands
 // are MN-major images, so no transposed copy is ever made.
+// Shared memory, 99 KB so that two CTAs share an SM: the X images reuse the
+// [K;Q] tile once the Gram MMA and the Q-image store have read it, and the
+// right-hand sides reuse the P images once the Neumann rounds are done.
 constexpr int kPrepKQ = 0;          // bf16 [K;Q] K-major, 2 kblocks x 128 rows            32 KiB
-constexpr int kPrepX = 32768;       // tf32 X_h (Neumann iterate -> A^-1) K-major, 2 heads  2 x 16 KiB
-constexpr int kPrepPA = 65536;      // tf32 P_h (power of N) K-major                         2 x 16 KiB
-constexpr int kPrepPB = 98304;      // tf32 P_h MN-major (B operand)                          2 x 16 KiB
+constexpr int kPrepX = 0;           // tf32 X_h (Neumann iterate -> A^-1) K-major, 2 heads  2 x 16 KiB (over KQ)
+constexpr int kPrepPA = 32768;      // tf32 P_h (power of N) K-major                         2 x 16 KiB
+constexpr int kPrepPB = 65536;      // tf32 P_h MN-major (B operand)                          2 x 16 KiB
 constexpr int kPrepRHS = kPrepPA;   // tf32 [beta G K | beta V] MN-major, 64 x 256, over PA+PB  64 KiB
-constexpr int kPrepSmall = 131072;
+constexpr int kPrepSmall = 98304;
 constexpr int kPrepSmem = kPrepSmall + 2048 + 1024;
 constexpr int kPrepTmemCols = 256;
 
@@ -177,6 +177,13 @@ __device__ __forceinline__ void st_f32(uint8_t* img, uint32_t off, float v) {
     *reinterpret_cast<float*>(img + off) = v;
 }
 
+// 2^x on the SFU (ex2.approx: a couple of ulp); x <= 0 here, so no overflow.
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 __device__ __forceinline__ float4 tf32x4(float a, float b, float c, float d) {
     return make_float4(to_tf32(a), to_tf32(b), to_tf32(c), to_tf32(d));
 }
@@ -191,7 +198,7 @@ __device__ __forceinline__ void bf16x8_to_f32(uint4 u, float (&f)[8]) {
     }
 }
 
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(128, 2)
     gdn_chunk_prepare_kernel(const PrefillParams p, uint8_t* __restrict__ ws, const WsLayout L) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = align1024(smem_raw);
@@ -253,11 +260,6 @@ __global__ void __launch_bounds__(128, 1)
     if (tid == 0) {
         mma_ct<kBF16, false, false, kD, 128, 128, 128, 64>(tm, aKQ, aKQ, false);
         mma_commit(bar);
-        // the chunk's Q image leaves for the carry kernel (rows 64-127 of each K-block)
-        uint8_t* gq = ws + L.off_q + (rec * kHQK + hq) * kQImg;
-        bulk_s2g(gq, aKQ + 64 * 128, 64 * 128);
-        bulk_s2g(gq + 64 * 128, aKQ + 128 * 128 + 64 * 128, 64 * 128);
-        bulk_commit();
     }
     {  // inclusive prefix of log2 g (64 sequential adds; deterministic)
         const int hl = tid >> 6, i = tid & 63;
@@ -269,6 +271,7 @@ __global__ void __launch_bounds__(128, 1)
     ok = mbar_wait(bar, phase);
     phase ^= 1;
     tc_fence_after();
+    __syncthreads();  // every thread is past the Gram MMA before X overwrites [K;Q]
     {
         // 3. Gram epilogue (M=128 rows: thread = row).  Rows 0-63 build N, P and
         //    X = I - N of both heads; rows 64-127 build the output-side P.
@@ -295,7 +298,7 @@ __global__ void __launch_bounds__(128, 1)
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                         const int j = j0 + e;
-                        nv[e] = (j < i) ? bi * exp2f(LGi - sml.LG[hl][j]) * gram[j] : 0.f;
+                        nv[e] = (j < i) ? bi * fast_exp2(LGi - sml.LG[hl][j]) * gram[j] : 0.f;
                     }
                     const float4 t = tf32x4(nv[0], nv[1], nv[2], nv[3]);
                     st_shared_v4(pa + sw128_f32(i, j0, 64), t);
@@ -311,17 +314,14 @@ __global__ void __launch_bounds__(128, 1)
                 const float LGi = sml.LG[hl][i];
                 uint8_t* gp = ws + L.off_p + (rec * kHV + 2 * hq + hl) * kPImg;
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    uint32_t w[4];
+                for (int j0 = 0; j0 < 64; j0 += 4) {
+                    float pv[4];
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        const int j = 8 * c + 2 * e;
-                        const float a0 = (j <= i) ? exp2f(LGi - sml.LG[hl][j]) * gram[j] : 0.f;
-                        const float a1 = (j + 1 <= i) ? exp2f(LGi - sml.LG[hl][j + 1]) * gram[j + 1] : 0.f;
-                        const __nv_bfloat162 v2 = __floats2bfloat162_rn(a0, a1);
-                        w[e] = *reinterpret_cast<const uint32_t*>(&v2);
+                        const int j = j0 + e;
+                        pv[e] = (j <= i) ? fast_exp2(LGi - sml.LG[hl][j]) * gram[j] : 0.f;
                     }
-                    *reinterpret_cast<uint4*>(gp + i * 128 + ((c ^ (i & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+                    *reinterpret_cast<float4*>(gp + sw128_f32(i, j0, 64)) = tf32x4(pv[0], pv[1], pv[2], pv[3]);
                 }
             }
         }
@@ -405,11 +405,13 @@ __global__ void __launch_bounds__(128, 1)
             const float Gj = exp2f(LGj), tail = exp2f(sml.LG[h2][63] - LGj);
             uint8_t* gkb = ws + L.off_kt + rh * kKTImg;
             // part 0: columns 0-127 (beta G K) and K-bar columns 0-63; part 1: beta V and K-bar 64-127
+            const bool act = j < n;
+            const uint16_t* ksrc = p.k + ((t0 + j) * kHQK + hq) * kD;  // K row j (L2-resident)
             if (part == 0) {
 #pragma unroll 4
                 for (int d0 = 0; d0 < kD; d0 += 8) {
                     float f[8];
-                    bf16x8_to_f32(*reinterpret_cast<const uint4*>(sKQ + sw128_bf16(j, d0, 128)), f);
+                    bf16x8_to_f32(act ? *reinterpret_cast<const uint4*>(ksrc + d0) : make_uint4(0, 0, 0, 0), f);
                     const float s = bj * Gj;
                     st_shared_v4(aRHS + mn32_f32(j, d0, 64), tf32x4(s * f[0], s * f[1], s * f[2], s * f[3]));
                     st_shared_v4(aRHS + mn32_f32(j, d0 + 4, 64), tf32x4(s * f[4], s * f[5], s * f[6], s * f[7]));
@@ -424,7 +426,6 @@ __global__ void __launch_bounds__(128, 1)
                 gvec[j] = Gj;
                 if (j == 0) gvec[64] = exp2f(sml.LG[h2][63]);
             } else {
-                const bool act = j < n;
                 const uint16_t* vsrc = p.v + ((t0 + j) * kHV + h) * kD;
 #pragma unroll 4
                 for (int d0 = 0; d0 < kD; d0 += 8) {
@@ -434,7 +435,7 @@ __global__ void __launch_bounds__(128, 1)
                     st_shared_v4(aRHS + mn32_f32(j, 132 + d0, 64), tf32x4(bj * f[4], bj * f[5], bj * f[6], bj * f[7]));
                     if (d0 >= 64) {
                         float g[8];
-                        bf16x8_to_f32(*reinterpret_cast<const uint4*>(sKQ + sw128_bf16(j, d0, 128)), g);
+                        bf16x8_to_f32(act ? *reinterpret_cast<const uint4*>(ksrc + d0) : make_uint4(0, 0, 0, 0), g);
                         *reinterpret_cast<float4*>(gkb + mn32_f32(j, d0, 64)) =
                             tf32x4(tail * g[0], tail * g[1], tail * g[2], tail * g[3]);
                         *reinterpret_cast<float4*>(gkb + mn32_f32(j, d0 + 4, 64)) =
@@ -497,31 +498,32 @@ done:
 
 // ------------------------------------------------------------------ carry --
 // One CTA (128 threads) per sequence x v-head x BV value rows.  Per chunk:
-//   MMA1  W S0^T (tf32, B = S MN-major)  and  Q S0^T (bf16)      -> rows = tokens
-//   epi A Delta = U - W S0^T  -> Delta images (tf32 MN-major, bf16 K-major)
-//   MMA2  (tail K)^T Delta (tf32, both operands MN-major)  and  P Delta (bf16)
-//   epi B S1 = G_C S0 + (tail K)^T Delta (thread k owns state column k),
-//         O = scale (G (.) Q S0^T + P Delta) for the chunk's tokens
-// The next chunk's operand images are bulk-copied into the other slot meanwhile.
-constexpr int kSlotQ = 0;
-constexpr int kSlotW = kSlotQ + kQImg;
-constexpr int kSlotKT = kSlotW + kWImg;
-constexpr int kSlotP = kSlotKT + kKTImg;
-constexpr int kSlotVec = kSlotP + kPImg;
-constexpr int kSlotBytes = kSlotVec + 1024;
-constexpr uint32_t kSlotTx = kQImg + kWImg + kKTImg + kPImg + kVecBytes;
-
+//   MMA1  [W ; G(.)Q] S0^T  (tf32, M=128): TMEM lanes 0-63 hold W S0^T,
+//         lanes 64-127 G(.)Q S0^T (one row per token in both halves)
+//   epi A warps 0-1: Delta = U - W S0^T -> Delta image (tf32, MN-major)
+//   MMA2  (tail K)^T Delta (M=128, rows = state columns k) and [0 ; P] Delta
+//         accumulated onto lanes 64-127, which then hold the chunk's output
+//   epi B every thread: S1 = G_C S0 + (tail K)^T Delta for its column k;
+//         warps 2-3 store O = scale (G(.)Q S0^T + P Delta)
+// Operands arrive by bulk copy; each is reloaded for the next chunk as soon
+// as the MMA reading it completes (W after MMA1; tail K, P, G after MMA2), and
+// warps 2-3 build the next chunk's G(.)Q rows from the raw q input while MMA2
+// runs, so one buffer per operand suffices.  All operands feeding the state
+// are tf32 (round-to-nearest); the state itself stays fp32 in registers.
 template <int BV>
 struct CarrySmem {
-    static constexpr int kSlots = 0;                      // 2 operand slots
-    static constexpr int kS32 = kSlots + 2 * kSlotBytes;  // tf32 S MN-major [128 k][BV]
-    static constexpr int kS16 = kS32 + BV * 512;          // bf16 S K-major [BV v][128 k]
-    static constexpr int kD32 = kS16 + BV * 256;          // tf32 Delta MN-major [64 j][BV]
-    static constexpr int kD16 = kD32 + BV * 256;          // bf16 Delta K-major [BV v][64 j]
-    static constexpr int kSmall = kD16 + BV * 128;
+    static constexpr int kA1 = 0;                 // tf32 [W ; G Q] K-major, 4 kblocks x 128 rows   64 KiB
+    static constexpr int kA2 = kA1 + 65536;       // tf32 [0 ; P]   K-major, 2 kblocks x 128 rows   32 KiB
+    static constexpr int kKB = kA2 + 32768;       // tf32 tail K MN-major [64 j][128 k]             32 KiB
+    static constexpr int kVec = kKB + 32768;      // two gate vectors G[64], G_C (by chunk parity)
+    static constexpr int kS32 = kVec + 1024;      // tf32 S MN-major [128 k][BV]
+    static constexpr int kD32 = kS32 + BV * 512;  // tf32 Delta MN-major [64 j][BV]
+    static constexpr int kSmall = kD32 + BV * 256;
     static constexpr int kTotal = kSmall + 128 + 1024;
-    static constexpr int kTmemCols = 4 * BV < 32 ? 32 : 4 * BV;
+    static constexpr int kTmemCols = 2 * BV < 32 ? 32 : 2 * BV;
 };
+constexpr uint32_t kCarryTxA = kWImg;
+constexpr uint32_t kCarryTxB = kKTImg + kPImg + kVecBytes;
 
 template <int BV>
 __global__ void __launch_bounds__(128, 1)
@@ -530,22 +532,24 @@ __global__ void __launch_bounds__(128, 1)
     static_assert(BV == 32 || BV == 64, "value-row tile (MN-major tf32 images need 32-wide rows)");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = align1024(smem_raw);
-    const uint32_t aS32 = smem_u32(sm + SM::kS32), aS16 = smem_u32(sm + SM::kS16), aD32 = smem_u32(sm + SM::kD32),
-                   aD16 = smem_u32(sm + SM::kD16);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + SM::kSmall);  // full[2], mma1, mma2
+    const uint32_t aA1 = smem_u32(sm + SM::kA1), aA2 = smem_u32(sm + SM::kA2), aKB = smem_u32(sm + SM::kKB),
+                   aVec = smem_u32(sm + SM::kVec), aS32 = smem_u32(sm + SM::kS32), aD32 = smem_u32(sm + SM::kD32);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + SM::kSmall);  // fullA, fullB, mma1, mma2
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + SM::kSmall + 64);
 
     constexpr int kTiles = kD / BV;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tid = threadIdx.x, warp = tid >> 5;
     const int64_t unit = blockIdx.x / kTiles;
     const int vt = static_cast<int>(blockIdx.x - unit * kTiles);
     const int64_t s = unit / kHV;
     const int h = static_cast<int>(unit - s * kHV);
+    const int hq = h / kGva;
     const int v0 = vt * BV;
 
     int64_t t0, t1;
     seq_bounds(p, s, t0, t1);
-    const int nch = static_cast<int>((t1 - t0 + kC - 1) / kC);
+    const int len = static_cast<int>(t1 - t0);
+    const int nch = (len + kC - 1) / kC;
     const int rec0 = reinterpret_cast<const int*>(ws + L.off_base)[s];
     float* ns_col = p.new_state + (unit * kD + v0) * kD + tid;  // column k = tid of rows v0..
     if (nch == 0 || rec0 + nch > L.R) {
@@ -555,7 +559,7 @@ __global__ void __launch_bounds__(128, 1)
         return;
     }
 
-    // state rows v0..v0+BV, column k = tid, in registers; images for the MMAs
+    // state rows v0..v0+BV, column k = tid, in registers; MN-major image for the MMAs
     float S[BV];
     if (p.state != nullptr) {
         const float* st = p.state + (unit * kD + v0) * kD + tid;
@@ -565,118 +569,121 @@ __global__ void __launch_bounds__(128, 1)
 #pragma unroll
         for (int v = 0; v < BV; ++v) S[v] = 0.f;
     }
-    auto write_state_images = [&]() {
+    auto write_state_image = [&]() {
 #pragma unroll
-        for (int v = 0; v < BV; v += 4) {
+        for (int v = 0; v < BV; v += 4)
             st_shared_v4(aS32 + mn32_f32(tid, v, kD), tf32x4(S[v], S[v + 1], S[v + 2], S[v + 3]));
-        }
-#pragma unroll
-        for (int v = 0; v < BV; ++v)
-            *reinterpret_cast<__nv_bfloat16*>(sm + SM::kS16 + sw128_bf16(v, tid, BV)) = __float2bfloat16_rn(S[v]);
     };
-    write_state_images();
+    write_state_image();
+    {  // the zero upper half of [0 ; P] (rows 0-63 of both K-blocks), written once
+        const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const int idx = tid * 8 + e;  // 1024 chunks of 16 B
+            st_shared_v4(aA2 + (idx >> 9) * 16384 + (idx & 511) * 16, z);
+        }
+    }
+    auto gvec = [&](int c) {
+        return reinterpret_cast<const float*>(ws + L.off_vec + ((int64_t)(rec0 + c) * kHV + h) * kVecBytes);
+    };
+    // G (.) Q rows of chunk c into rows 64-127 of [W ; G Q] (warps 2-3: token i = tid - 64)
+    auto build_gq = [&](int c) {
+        const int i = tid - 64;
+        const int tok = kC * c + i;
+        const bool act = tok < len;
+        const float gi = act ? gvec(c)[i] : 0.f;
+        const uint16_t* qrow = p.q + ((t0 + tok) * kHQK + hq) * kD;
+#pragma unroll 4
+        for (int k0 = 0; k0 < kD; k0 += 8) {
+            float f[8];
+            bf16x8_to_f32(act ? *reinterpret_cast<const uint4*>(qrow + k0) : make_uint4(0, 0, 0, 0), f);
+            st_shared_v4(aA1 + sw128_f32(64 + i, k0, 128), tf32x4(gi * f[0], gi * f[1], gi * f[2], gi * f[3]));
+            st_shared_v4(aA1 + sw128_f32(64 + i, k0 + 4, 128), tf32x4(gi * f[4], gi * f[5], gi * f[6], gi * f[7]));
+        }
+    };
+    if (warp >= 2) build_gq(0);
 
-    const uint32_t full0 = smem_u32(&bars[0]), mma1 = smem_u32(&bars[2]), mma2 = smem_u32(&bars[3]);
+    const uint32_t fullA = smem_u32(&bars[0]), fullB = smem_u32(&bars[1]), mma1 = smem_u32(&bars[2]),
+                   mma2 = smem_u32(&bars[3]);
+    auto issue_A = [&](int c) {  // W of chunk c -> rows 0-63 of each K-block of [W ; G Q]
+        const uint8_t* gw = ws + L.off_w + ((int64_t)(rec0 + c) * kHV + h) * kWImg;
+        mbar_expect_tx(fullA, kCarryTxA);
+#pragma unroll
+        for (int kb = 0; kb < 4; ++kb) bulk_g2s(aA1 + kb * 16384, gw + kb * 8192, 8192, fullA);
+    };
+    auto issue_B = [&](int c) {  // tail K, P (rows 64-127 of [0 ; P]) and G of chunk c
+        const int64_t rh = (int64_t)(rec0 + c) * kHV + h;
+        const uint8_t* gp = ws + L.off_p + rh * kPImg;
+        mbar_expect_tx(fullB, kCarryTxB);
+        bulk_g2s(aKB, ws + L.off_kt + rh * kKTImg, kKTImg, fullB);
+        bulk_g2s(aA2 + 8192, gp, 8192, fullB);
+        bulk_g2s(aA2 + 16384 + 8192, gp + 8192, 8192, fullB);
+        bulk_g2s(aVec + (c & 1) * 512, ws + L.off_vec + rh * kVecBytes, kVecBytes, fullB);
+    };
     if (tid == 0) {
-        mbar_init(full0, 1);
-        mbar_init(full0 + 8, 1);
+        mbar_init(fullA, 1);
+        mbar_init(fullB, 1);
         mbar_init(mma1, 1);
         mbar_init(mma2, 1);
         fence_mbar_init();
+        issue_A(0);
+        issue_B(0);
     }
     if (warp == 0) {
         tmem_alloc(smem_u32(tmem_slot), SM::kTmemCols);
         tmem_relinquish();
     }
-    auto issue_loads = [&](int c) {
-        const int64_t r = rec0 + c;
-        const int64_t rh = r * kHV + h;
-        const uint32_t slot = smem_u32(sm + SM::kSlots + (c & 1) * kSlotBytes);
-        const uint32_t fb = full0 + 8 * (c & 1);
-        mbar_expect_tx(fb, kSlotTx);
-        bulk_g2s(slot + kSlotQ, ws + L.off_q + (r * kHQK + h / kGva) * kQImg, kQImg, fb);
-        bulk_g2s(slot + kSlotW, ws + L.off_w + rh * kWImg, kWImg, fb);
-        bulk_g2s(slot + kSlotKT, ws + L.off_kt + rh * kKTImg, kKTImg, fb);
-        bulk_g2s(slot + kSlotP, ws + L.off_p + rh * kPImg, kPImg, fb);
-        bulk_g2s(slot + kSlotVec, ws + L.off_vec + rh * kVecBytes, kVecBytes, fb);
-    };
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tm = *tmem_slot;
-    const uint32_t t_ws = tm, t_qs = tm + BV, t_up = tm + 2 * BV, t_pd = tm + 3 * BV;
-    if (tid == 0) issue_loads(0);
+    const uint32_t t_acc = tm, t_up = tm + BV;
 
-    const int row = 16 * warp + lane;  // token row of M=64 tiles (lanes < 16)
     __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
     bool ok = true, aborted = false;
-    int last_issued = 0, last_landed = -1;  // chunk indices of the operand loads
+    int a_issued = 0, a_landed = -1, b_issued = 0, b_landed = -1;
     for (int c = 0; c < nch; ++c) {
-        const int slot = c & 1;
-        const uint8_t* sl = sm + SM::kSlots + slot * kSlotBytes;
-        const uint32_t asl = smem_u32(sl);
-        const int64_t r = rec0 + c;
-        const int64_t rh = r * kHV + h;
-        if (c + 1 < nch) {
-            if (tid == 0) issue_loads(c + 1);
-            last_issued = c + 1;
+        const int64_t rh = (int64_t)(rec0 + c) * kHV + h;
+        // MMA1 as soon as W of this chunk has landed
+        if (tid == 0) {
+            ok = mbar_wait(fullA, c & 1);
+            if (ok) {
+                a_landed = c;
+                tc_fence_after();
+                mma_ct<kTF32, false, true, kD, 128, kD, 128, BV>(t_acc, aA1, aS32, false);
+                mma_commit(mma1);
+            }
         }
-        ok = mbar_wait(full0 + 8 * slot, (c >> 1) & 1);
-        if (ok) last_landed = c;
-        if (tid == 0 && ok) {
-            tc_fence_after();
-            mma_ct<kTF32, false, true, kD, 64, kD, 64, BV>(t_ws, asl + kSlotW, aS32, false);
-            mma_ct<kBF16, false, false, kD, 64, BV, 64, BV>(t_qs, asl + kSlotQ, aS16, false);
-            mma_commit(mma1);
-        }
-        const int tok = 64 * c + row;
-        const bool act = lane < 16 && tok < t1 - t0;
         float u[BV];
-        {
-            const float4* up = reinterpret_cast<const float4*>(
-                reinterpret_cast<const float*>(ws + L.off_u + rh * kUBytes) + (row & 63) * kD + v0);
+        if (warp < 2) {  // U row of token j = tid, while MMA1 runs
+            const float4* up =
+                reinterpret_cast<const float4*>(reinterpret_cast<const float*>(ws + L.off_u + rh * kUBytes) +
+                                                tid * kD + v0);
 #pragma unroll
             for (int v = 0; v < BV; v += 4) {
                 const float4 x = up[v / 4];
-                u[v] = x.x;
-                u[v + 1] = x.y;
-                u[v + 2] = x.z;
-                u[v + 3] = x.w;
+                u[v] = x.x, u[v + 1] = x.y, u[v + 2] = x.z, u[v + 3] = x.w;
             }
         }
-        const float* vec = reinterpret_cast<const float*>(sl + kSlotVec);
-        const float gc = vec[64];
-        const float gi = vec[row & 63];
-        ok = ok && mbar_wait(mma1, c & 1);
+        ok = __syncthreads_and(ok) && mbar_wait(mma1, c & 1);
         tc_fence_after();
-        {  // Delta = U - W S0^T -> Delta images (B operands of the next two MMAs)
+        if (tid == 0 && c + 1 < nch) issue_A(c + 1);  // W's rows of [W ; G Q] are free again
+        if (c + 1 < nch) a_issued = c + 1;
+        if (warp < 2) {  // epi A: Delta row j = tid
             float wsr[BV];
-            if constexpr (BV == 32) {
-                tmem_ld32(taddr(t_ws, 32 * warp, 0), wsr);
-            } else {
-                float a[32], b[32];
-                tmem_ld32(taddr(t_ws, 32 * warp, 0), a);
-                tmem_ld32(taddr(t_ws, 32 * warp, 32), b);
 #pragma unroll
-                for (int v = 0; v < 32; ++v) wsr[v] = a[v], wsr[32 + v] = b[v];
-            }
-            tmem_wait_ld();
-            if (lane < 16) {
+            for (int c0 = 0; c0 < BV; c0 += 32) {
+                float a[32];
+                tmem_ld32(taddr(t_acc, 32 * warp, c0), a);
+                tmem_wait_ld();
 #pragma unroll
-                for (int v = 0; v < BV; v += 4) {
-                    const float d0 = u[v] - wsr[v], d1 = u[v + 1] - wsr[v + 1], d2 = u[v + 2] - wsr[v + 2],
-                                d3 = u[v + 3] - wsr[v + 3];
-                    st_shared_v4(aD32 + mn32_f32(row, v, 64), tf32x4(d0, d1, d2, d3));
-                    *reinterpret_cast<__nv_bfloat16*>(sm + SM::kD16 + sw128_bf16(v, row, BV)) = __float2bfloat16_rn(d0);
-                    *reinterpret_cast<__nv_bfloat16*>(sm + SM::kD16 + sw128_bf16(v + 1, row, BV)) =
-                        __float2bfloat16_rn(d1);
-                    *reinterpret_cast<__nv_bfloat16*>(sm + SM::kD16 + sw128_bf16(v + 2, row, BV)) =
-                        __float2bfloat16_rn(d2);
-                    *reinterpret_cast<__nv_bfloat16*>(sm + SM::kD16 + sw128_bf16(v + 3, row, BV)) =
-                        __float2bfloat16_rn(d3);
-                }
+                for (int v = 0; v < 32; ++v) wsr[c0 + v] = a[v];
             }
+#pragma unroll
+            for (int v = 0; v < BV; v += 4)
+                st_shared_v4(aD32 + mn32_f32(tid, v, kC),
+                             tf32x4(u[v] - wsr[v], u[v + 1] - wsr[v + 1], u[v + 2] - wsr[v + 2], u[v + 3] - wsr[v + 3]));
         }
         fence_async_smem();
         tc_fence_before();
@@ -685,48 +692,50 @@ __global__ void __launch_bounds__(128, 1)
             break;
         }
         if (tid == 0) {
-            tc_fence_after();
-            mma_ct<kTF32, true, true, 64, 64, 64, 128, BV>(t_up, asl + kSlotKT, aD32, false);
-            mma_ct<kBF16, false, false, 64, 64, BV, 64, BV>(t_pd, asl + kSlotP, aD16, false);
-            mma_commit(mma2);
-        }
-        ok = mbar_wait(mma2, c & 1);
-        tc_fence_after();
-        {  // S1 = G_C S0 + (tail K)^T Delta ; O = scale (G (.) Q S0^T + P Delta)
-            float up[BV], qs[BV], pd[BV];
-            if constexpr (BV == 32) {
-                tmem_ld32(taddr(t_up, 32 * warp, 0), up);
-                tmem_ld32(taddr(t_qs, 32 * warp, 0), qs);
-                tmem_ld32(taddr(t_pd, 32 * warp, 0), pd);
-            } else {
-                float a[32];
-#pragma unroll
-                for (int hh = 0; hh < 2; ++hh) {
-                    tmem_ld32(taddr(t_up, 32 * warp, 32 * hh), a);
-#pragma unroll
-                    for (int v = 0; v < 32; ++v) up[32 * hh + v] = a[v];
-                    tmem_ld32(taddr(t_qs, 32 * warp, 32 * hh), a);
-#pragma unroll
-                    for (int v = 0; v < 32; ++v) qs[32 * hh + v] = a[v];
-                    tmem_ld32(taddr(t_pd, 32 * warp, 32 * hh), a);
-#pragma unroll
-                    for (int v = 0; v < 32; ++v) pd[32 * hh + v] = a[v];
-                }
+            ok = mbar_wait(fullB, c & 1);
+            if (ok) {
+                b_landed = c;
+                tc_fence_after();
+                mma_ct<kTF32, true, true, kC, kC, kC, 128, BV>(t_up, aKB, aD32, false);     // (tail K)^T Delta
+                mma_ct<kTF32, false, true, kC, 128, kC, 128, BV>(t_acc, aA2, aD32, true);   // += [0 ; P] Delta
+                mma_commit(mma2);
             }
-            tmem_wait_ld();
+        }
+        if (warp >= 2 && c + 1 < nch) build_gq(c + 1);  // rows 64-127 of [W ; G Q] are free since MMA1
+        ok = __syncthreads_and(ok) && mbar_wait(fullB, c & 1) && mbar_wait(mma2, c & 1);
+        tc_fence_after();
+        const float gc = *reinterpret_cast<const float*>(sm + SM::kVec + (c & 1) * 512 + 64 * 4);
+        if (tid == 0 && c + 1 < nch) issue_B(c + 1);  // tail K and P are free again; G goes to the other half
+        if (c + 1 < nch) b_issued = c + 1;
+        {  // epi B: state column k = tid; warps 2-3 also store the outputs of token tid - 64
 #pragma unroll
-            for (int v = 0; v < BV; ++v) S[v] = fmaf(gc, S[v], up[v]);
-            write_state_images();
-            if (act) {
-                __nv_bfloat16* o = out + ((t0 + tok) * kHV + h) * kD + v0;
+            for (int c0 = 0; c0 < BV; c0 += 32) {
+                float a[32];
+                tmem_ld32(taddr(t_up, 32 * warp, c0), a);
+                tmem_wait_ld();
 #pragma unroll
-                for (int v = 0; v < BV; v += 8) {
-                    __nv_bfloat162 w[4];
+                for (int v = 0; v < 32; ++v) S[c0 + v] = fmaf(gc, S[c0 + v], a[v]);
+            }
+            write_state_image();
+            if (warp >= 2) {
+                const int i = tid - 64;
+                const int tok = kC * c + i;
 #pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        w[e] = __floats2bfloat162_rn(p.scale * fmaf(gi, qs[v + 2 * e], pd[v + 2 * e]),
-                                                     p.scale * fmaf(gi, qs[v + 2 * e + 1], pd[v + 2 * e + 1]));
-                    *reinterpret_cast<uint4*>(o + v) = *reinterpret_cast<uint4*>(w);
+                for (int c0 = 0; c0 < BV; c0 += 32) {
+                    float o[32];
+                    tmem_ld32(taddr(t_acc, 32 * warp, c0), o);
+                    tmem_wait_ld();
+                    if (tok < len) {
+                        __nv_bfloat16* dst = out + ((t0 + tok) * kHV + h) * kD + v0 + c0;
+#pragma unroll
+                        for (int v = 0; v < 32; v += 8) {
+                            __nv_bfloat162 w[4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e)
+                                w[e] = __floats2bfloat162_rn(p.scale * o[v + 2 * e], p.scale * o[v + 2 * e + 1]);
+                            *reinterpret_cast<uint4*>(dst + v) = *reinterpret_cast<uint4*>(w);
+                        }
+                    }
                 }
             }
         }
@@ -739,8 +748,9 @@ __global__ void __launch_bounds__(128, 1)
     }
     if (aborted && tid == 0) {
         record_status(32 /* GDN_ERR_DEVICE_TIMEOUT */);
-        // drain the operand loads still in flight (at most two) before the CTA exits
-        for (int cc = last_landed + 1; cc <= last_issued; ++cc) mbar_wait(full0 + 8 * (cc & 1), (cc >> 1) & 1);
+        // drain the operand loads still in flight before the CTA exits
+        for (int cc = a_landed + 1; cc <= a_issued; ++cc) mbar_wait(fullA, cc & 1);
+        for (int cc = b_landed + 1; cc <= b_issued; ++cc) mbar_wait(fullB, cc & 1);
     }
 #pragma unroll
     for (int v = 0; v < BV; ++v) ns_col[v * kD] = S[v];
@@ -772,11 +782,20 @@ cudaError_t launch_prefill_chunked(const PrefillParams& p, void* workspace, cuda
     if (L.R > 0x7fffffffLL) return cudaErrorInvalidValue;
     gdn_chunk_prepare_kernel<<<dim3(static_cast<unsigned>(L.R), kHQK), 128, kPrepSmem, stream>>>(p, ws, L);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    using SM = CarrySmem<32>;
-    if ((e = set_smem(gdn_chunk_carry_kernel<32>, SM::kTotal)) != cudaSuccess) return e;
-    const int64_t grid = p.num_seqs * kHV * (kD / 32);
-    if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
-    gdn_chunk_carry_kernel<32><<<static_cast<unsigned>(grid), 128, SM::kTotal, stream>>>(p, ws, L);
+    // value-row tile: 64 rows (two CTAs per head) once that still fills the SMs, else 32
+    if (p.num_seqs * kHV * (kD / 64) >= kSmCount) {
+        using SM = CarrySmem<64>;
+        if ((e = set_smem(gdn_chunk_carry_kernel<64>, SM::kTotal)) != cudaSuccess) return e;
+        const int64_t grid = p.num_seqs * kHV * (kD / 64);
+        if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
+        gdn_chunk_carry_kernel<64><<<static_cast<unsigned>(grid), 128, SM::kTotal, stream>>>(p, ws, L);
+    } else {
+        using SM = CarrySmem<32>;
+        if ((e = set_smem(gdn_chunk_carry_kernel<32>, SM::kTotal)) != cudaSuccess) return e;
+        const int64_t grid = p.num_seqs * kHV * (kD / 32);
+        if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
+        gdn_chunk_carry_kernel<32><<<static_cast<unsigned>(grid), 128, SM::kTotal, stream>>>(p, ws, L);
+    }
     return cudaGetLastError();
 }
 
