@@ -176,6 +176,7 @@ int gdn_abi_version(void);
 
 #define GDN_MMA_KIND_BF16 1
 #define GDN_MMA_KIND_TF32 2
+#define GDN_MMA_KIND_F16 3
 
 #define GDN_MMA_A_MN_MAJOR 1  /* A operand image stored MN-major */
 #define GDN_MMA_B_MN_MAJOR 2  /* B operand image stored MN-major */
@@ -184,8 +185,8 @@ int gdn_abi_version(void);
 /* D[M x N] = A[M x K] . B[N x K]^T on one CTA through the same shared-memory
  * operand images, tcgen05 descriptors and TMEM read-back the prefill kernels
  * use; `flags` selects the operand majors and accumulator placement.  A, B
- * row-major in global memory (bf16 for BF16, fp32 for TF32 -- rounded to
- * tf32); D fp32 row-major.  M in {64, 128}; N a multiple of 16 in [16, 256];
+ * row-major in global memory (bf16 for BF16, fp16 for F16, fp32 for TF32 --
+ * rounded to tf32); D fp32 row-major.  M in {64, 128}; N a multiple of 16 in [16, 256];
  * K in {64, 128}; an MN-major operand's M (or N) must fill whole 128-byte
  * rows (multiples of 64 bf16 / 32 tf32).  No reference counterpart: a
  * self-test of the tensor-core layer. */

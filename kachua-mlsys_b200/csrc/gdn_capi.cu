@@ -149,14 +149,16 @@ extern "C" int gdn_read_device_status(int* out, int clear, void* stream) {
 extern "C" int gdn_mma_selftest(int kind, int flags, int M, int N, int K, const void* A, const void* B, float* D,
                                 void* stream) {
     if (!A || !B || !D) return GDN_ERR_NULL_POINTER;
-    if ((kind != GDN_MMA_KIND_BF16 && kind != GDN_MMA_KIND_TF32) || (M != 64 && M != 128) || N < 16 ||
+    if ((kind != GDN_MMA_KIND_BF16 && kind != GDN_MMA_KIND_TF32 && kind != GDN_MMA_KIND_F16) || (M != 64 && M != 128) ||
+        N < 16 ||
         N > 256 || N % 16 != 0 || (K != 64 && K != 128) || (flags & ~7) != 0 || ((flags & 4) && M != 64))
         return GDN_ERR_BAD_SIZE;
     // an MN-major image fills whole 128-byte rows: its M (or N) extent must be too
-    const int row_elems = kind == GDN_MMA_KIND_BF16 ? 64 : 32;
+    const int row_elems = kind == GDN_MMA_KIND_TF32 ? 32 : 64;
     if (((flags & 1) && M % row_elems != 0) || ((flags & 2) && N % row_elems != 0)) return GDN_ERR_BAD_SIZE;
     if (int rc = check_device()) return rc;
-    return launch_mma_selftest(kind, flags, M, N, K, A, B, D, static_cast<cudaStream_t>(stream)) == cudaSuccess
+    const int k = kind == GDN_MMA_KIND_F16 ? (int)kF16 : kind == GDN_MMA_KIND_BF16 ? (int)kBF16 : (int)kTF32;
+    return launch_mma_selftest(k, flags, M, N, K, A, B, D, static_cast<cudaStream_t>(stream)) == cudaSuccess
                ? GDN_OK
                : GDN_ERR_CUDA;
 }

@@ -830,7 +830,7 @@ __global__ void __launch_bounds__(128, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = align1024(smem_raw);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int eb = kind == kBF16 ? 2 : 4;
+    const int eb = kind == kTF32 ? 4 : 2;
     const int kblocks = K * eb / 128;
     const bool a_mn = flags & 1, b_mn = flags & 2, lane16 = flags & 4;
     uint8_t* sA = sm;
@@ -841,7 +841,7 @@ __global__ void __launch_bounds__(128, 1)
     for (int idx = tid; idx < M * K; idx += 128) {
         const int r = idx / K, c = idx % K;  // A[r][c]: row m = r, k = c
         const int row = a_mn ? c : r, col = a_mn ? r : c, rows = a_mn ? K : M;
-        if (kind == kBF16)
+        if (kind != kTF32)
             *reinterpret_cast<uint16_t*>(sA + sw128_bf16(row, col, rows)) = static_cast<const uint16_t*>(A)[idx];
         else
             st_f32(sA, a_mn ? mn32_f32(row, col, rows) : sw128_f32(row, col, rows),
@@ -850,7 +850,7 @@ __global__ void __launch_bounds__(128, 1)
     for (int idx = tid; idx < N * K; idx += 128) {
         const int r = idx / K, c = idx % K;  // B[r][c]: n = r, k = c
         const int row = b_mn ? c : r, col = b_mn ? r : c, rows = b_mn ? K : N;
-        if (kind == kBF16)
+        if (kind != kTF32)
             *reinterpret_cast<uint16_t*>(sB + sw128_bf16(row, col, rows)) = static_cast<const uint16_t*>(B)[idx];
         else
             st_f32(sB, b_mn ? mn32_f32(row, col, rows) : sw128_f32(row, col, rows),
@@ -875,6 +875,8 @@ __global__ void __launch_bounds__(128, 1)
     if (tid == 0) {
         if (kind == kBF16)
             selftest_issue<kBF16>(flags, d, smem_u32(sA), smem_u32(sB), M, N, K);
+        else if (kind == kF16)
+            selftest_issue<kF16>(flags, d, smem_u32(sA), smem_u32(sB), M, N, K);
         else
             selftest_issue<kTF32>(flags, d, smem_u32(sA), smem_u32(sB), M, N, K);
         mma_commit(smem_u32(bar));

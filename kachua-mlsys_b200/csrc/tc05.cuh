@@ -179,7 +179,9 @@ __device__ __forceinline__ uint64_t mn32_desc(uint32_t smem_addr, uint32_t lbo) 
            (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) | (32ull << 32) | (1ull << 46) | (1ull << 61);
 }
 
-enum Kind : uint32_t { kBF16 = 1, kTF32 = 2 };
+// Operand formats: kind::f16 takes kF16 or kBF16, kind::tf32 takes kTF32; the value is
+// the instruction descriptor's format code.
+enum Kind : uint32_t { kF16 = 0, kBF16 = 1, kTF32 = 2 };
 
 // Instruction descriptor (kind::f16 / kind::tf32): fp32 accumulator, A and B
 // of the same format, no negation, dense; a_mn / b_mn select MN-major operands.
@@ -189,6 +191,7 @@ __host__ __device__ constexpr uint32_t idesc(Kind k, int M, int N, bool a_mn = f
            (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// kind::f16: fp16 or bf16 operands, as the instruction descriptor says
 __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
@@ -219,27 +222,27 @@ template <Kind KIND, bool A_MN = false, bool B_MN = false>
 __device__ __forceinline__ void mma_tile(uint32_t d_tmem, uint32_t a_smem, int a_rows, uint32_t b_smem, int b_rows,
                                          int kdim, int M, int N, bool accumulate) {
     const uint32_t id = idesc(KIND, M, N, A_MN, B_MN);
-    constexpr int kElemBytes = KIND == kBF16 ? 2 : 4;
+    constexpr int kElemBytes = KIND == kTF32 ? 4 : 2;
     constexpr int kStepK = 32 / kElemBytes;  // K elements per instruction
     const int steps = kdim / kStepK;
 #pragma unroll 1
     for (int s = 0; s < steps; ++s) {
         uint64_t ad, bd;
         if (A_MN) {
-            ad = KIND == kBF16 ? sw128_desc_mn(a_smem + s * kStepK * 128, a_rows * 128)
+            ad = KIND != kTF32 ? sw128_desc_mn(a_smem + s * kStepK * 128, a_rows * 128)
                                : mn32_desc(a_smem + s * kStepK * 128, a_rows * 128);
         } else {
             const int kb = (s * 32) >> 7, in = (s * 32) & 127;
             ad = sw128_desc(a_smem + kb * a_rows * 128 + in);
         }
         if (B_MN) {
-            bd = KIND == kBF16 ? sw128_desc_mn(b_smem + s * kStepK * 128, b_rows * 128)
+            bd = KIND != kTF32 ? sw128_desc_mn(b_smem + s * kStepK * 128, b_rows * 128)
                                : mn32_desc(b_smem + s * kStepK * 128, b_rows * 128);
         } else {
             const int kb = (s * 32) >> 7, in = (s * 32) & 127;
             bd = sw128_desc(b_smem + kb * b_rows * 128 + in);
         }
-        if (KIND == kBF16)
+        if (KIND != kTF32)
             mma_bf16(d_tmem, ad, bd, id, (accumulate || s > 0) ? 1u : 0u);
         else
             mma_tf32(d_tmem, ad, bd, id, (accumulate || s > 0) ? 1u : 0u);
@@ -252,13 +255,13 @@ __device__ __forceinline__ void mma_tile(uint32_t d_tmem, uint32_t a_smem, int a
 template <Kind KIND, bool A_MN, bool B_MN, int KDIM, int AROWS, int BROWS, int M, int N>
 __device__ __forceinline__ void mma_ct(uint32_t d_tmem, uint32_t a_smem, uint32_t b_smem, bool accumulate) {
     constexpr uint32_t id = idesc(KIND, M, N, A_MN, B_MN);
-    constexpr int kElemBytes = KIND == kBF16 ? 2 : 4;
+    constexpr int kElemBytes = KIND == kTF32 ? 4 : 2;
     constexpr int kStepK = 32 / kElemBytes;
     constexpr int kSteps = KDIM / kStepK;
     static_assert(KDIM % kStepK == 0, "K must be a whole number of instructions");
-    const uint64_t a0 = A_MN ? (KIND == kBF16 ? sw128_desc_mn(a_smem, AROWS * 128) : mn32_desc(a_smem, AROWS * 128))
+    const uint64_t a0 = A_MN ? (KIND != kTF32 ? sw128_desc_mn(a_smem, AROWS * 128) : mn32_desc(a_smem, AROWS * 128))
                              : sw128_desc(a_smem);
-    const uint64_t b0 = B_MN ? (KIND == kBF16 ? sw128_desc_mn(b_smem, BROWS * 128) : mn32_desc(b_smem, BROWS * 128))
+    const uint64_t b0 = B_MN ? (KIND != kTF32 ? sw128_desc_mn(b_smem, BROWS * 128) : mn32_desc(b_smem, BROWS * 128))
                              : sw128_desc(b_smem);
 #pragma unroll
     for (int s = 0; s < kSteps; ++s) {
@@ -267,7 +270,7 @@ __device__ __forceinline__ void mma_ct(uint32_t d_tmem, uint32_t a_smem, uint32_
         const uint64_t ad = a0 + (a_off >> 4);
         const uint64_t bd = b0 + (b_off >> 4);
         const uint32_t acc = (accumulate || s > 0) ? 1u : 0u;
-        if (KIND == kBF16)
+        if (KIND != kTF32)
             mma_bf16(d_tmem, ad, bd, id, acc);
         else
             mma_tf32(d_tmem, ad, bd, id, acc);

@@ -37,6 +37,12 @@ SHAPES = [  # (kind, M, N, K): the prepare and carry kernels' MMAs, plus neighbo
     ("bf16", 64, 128, 64, 7),
     ("tf32", 128, 32, 128, 2),
     ("bf16", 64, 64, 128, 2),
+    # fp16 operands (kind::f16 with format F16)
+    ("f16", 128, 64, 128),
+    ("f16", 64, 64, 64, 2),
+    ("f16", 128, 128, 64, 3),
+    ("f16", 64, 256, 64, 6),
+    ("f16", 128, 64, 128, 2),
 ]
 
 
@@ -55,10 +61,11 @@ def test_mma_selftest(pkg, cuda_dev, case):
     g = torch.Generator().manual_seed(M * 1000 + N + K)
     A = torch.randn(M, K, generator=g)
     B = torch.randn(N, K, generator=g)
-    if kind == "bf16":
-        A, B = A.to(torch.bfloat16), B.to(torch.bfloat16)
+    if kind in ("bf16", "f16"):
+        dt = torch.bfloat16 if kind == "bf16" else torch.float16
+        A, B = A.to(dt), B.to(dt)
         ref = A.double() @ B.double().T
-        code = C.MMA_KIND_BF16
+        code = C.MMA_KIND_BF16 if kind == "bf16" else C.MMA_KIND_F16
     else:
         ref = _tf32(A).double() @ _tf32(B).double().T
         code = C.MMA_KIND_TF32
