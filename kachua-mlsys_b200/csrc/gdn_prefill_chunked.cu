@@ -17,19 +17,27 @@
 // :497-540).  Every ratio is formed as exp2 of a non-positive log2 difference,
 // never as a division by G (the beta/G form overflows, experiment_log.md:1027-1050).
 //
+// Affine form used by the kernels (K' = tail (.) K):
+//   S1 = S0 M^T + D^T,   M = G_C I - K'^T W   [k][k'],   D = K'^T U   [k][v]
+//   O  = scale (Qt S0^T + Ut),   Qt = G (.) Q - P W,     Ut = P U
+// -- the same identities with Delta expanded, so the chunk-to-chunk chain is
+// one matrix product and everything else is per-chunk, parallel work.
+//
 // Kernel 1, gdn_chunk_prepare (one CTA per chunk x q/k head, both v-heads):
 //   [K;Q] K^T on bf16 tcgen05 (M=128, N=64, K=128); per v-head the gates,
-//   N and P; Ainv by six rounds of 64x64x64 tf32 tcgen05 products; W|U as one
-//   M=64, N=256, K=64 tf32 MMA.  Results leave as SW128 operand images
-//   (the carry's shared-memory layout) through bulk stores.
-// Kernel 2, gdn_chunk_carry (one CTA per sequence x v-head x BV value rows):
-//   walks the chunks in order with the fp32 state rows in registers; per chunk
-//   four MMAs -- W S0^T (tf32), Q S0^T (bf16), (tail K)^T Delta (tf32),
-//   P Delta (bf16) -- with the next chunk's operands bulk-copied into the other
-//   half of a double buffer meanwhile.
-// Precision: every operand that feeds the state (W, S, Delta, tail K, Ainv,
-// the Neumann powers) is rounded fp32 -> tf32 with round-to-nearest; operands
-// that only feed the bf16 output (Q S0^T, P Delta) run in bf16.
+//   N and P; Ainv by Neumann doubling on fp16 tcgen05 64x64x64 products (both
+//   v-heads packed into one M=64 accumulator pair); [W | U] = Ainv [bGK | bV]
+//   (M=64, N=256); then P [W | U] and K'^T [W | U] (M=128, N=256), whose
+//   epilogues write Qt, Ut, M and D to the workspace.
+// Kernel 2, gdn_chunk_carry (one CTA per sequence x v-head x 64 value rows):
+//   four state warps keep the fp32 state in registers and run the chain
+//   S <- S M^T + D^T with one M=128, N=64, K=128 fp16 MMA per chunk; four
+//   output warps finish O = scale (Qt S^T + Ut) from a second MMA on the same
+//   state image, overlapped with the next chunk.  Operands arrive by bulk
+//   copies issued two chunks ahead.
+// Precision: tensor-core operands are fp16 (round-to-nearest, 11-bit
+// significand like tf32) with fp32 accumulation; the state and D stay fp32
+// between chunks, and only the MMA's copy of the state is rounded.
 #include "gdn_common.cuh"
 #include "tc05.cuh"
 
@@ -37,20 +45,19 @@ namespace gdn {
 using namespace tc05;
 
 constexpr int kC = 64;
-constexpr int kWImg = kC * kD * 4;        // fp32 [64][128]        32 KiB
-constexpr int kKTImg = kD * kC * 4;       // fp32 [128][64]        32 KiB
-constexpr int kPImg = kC * kC * 4;        // tf32 [64][64]         16 KiB
-constexpr int kUBytes = kC * kD * 4;      // fp32 [64][128] plain  32 KiB
-constexpr int kVecBytes = 512;            // G[64], G_C
-constexpr int kRecordBytes = kHV * (kWImg + kKTImg + kPImg + kUBytes + kVecBytes);
+constexpr int kMImg = kD * kD * 2;        // f16 M K-major [128 k][128 k']        32 KiB
+constexpr int kDBytes = kD * kD * 4;       // fp32 D rows [128 k][128 v]            64 KiB
+constexpr int kQtImg = kC * kD * 2;        // f16 Qt K-major [64 i][128 k]           16 KiB
+constexpr int kUtBytes = kC * kD * 2;      // f16 Ut [2 halves][64 i][64 v]          16 KiB
+constexpr int kRecordBytes = kHV * (kMImg + kDBytes + kQtImg + kUtBytes);
 
 __host__ __device__ inline int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
 
 // Workspace: header, per-sequence record bases, the chunk table and the
-// per-record operand arrays (every array 1024-byte aligned).
+// per-record, per-head operand arrays (every array 1024-byte aligned).
 struct WsLayout {
     int64_t R;  // record capacity: ceil(T / 64) + N bounds sum_s ceil(len_s / 64)
-    int64_t off_hdr, off_base, off_table, off_w, off_kt, off_p, off_u, off_vec, total;
+    int64_t off_hdr, off_base, off_table, off_m, off_d, off_qt, off_ut, total;
 };
 
 __host__ __device__ inline WsLayout ws_layout(int64_t T, int64_t N) {
@@ -63,16 +70,14 @@ __host__ __device__ inline WsLayout ws_layout(int64_t T, int64_t N) {
     o = align_up(o + 4 * (N + 1), 1024);
     L.off_table = o;
     o = align_up(o + 16 * L.R, 1024);
-    L.off_w = o;
-    o += L.R * kHV * kWImg;
-    L.off_kt = o;
-    o += L.R * kHV * kKTImg;
-    L.off_p = o;
-    o += L.R * kHV * kPImg;
-    L.off_u = o;
-    o += L.R * kHV * kUBytes;
-    L.off_vec = o;
-    o += L.R * kHV * kVecBytes;
+    L.off_m = o;
+    o += L.R * kHV * kMImg;
+    L.off_d = o;
+    o += L.R * kHV * kDBytes;
+    L.off_qt = o;
+    o += L.R * kHV * kQtImg;
+    L.off_ut = o;
+    o += L.R * kHV * kUtBytes;
     L.total = align_up(o, 1024);
     return L;
 }
@@ -143,20 +148,24 @@ __global__ void __launch_bounds__(1024) gdn_chunk_table_kernel(const PrefillPara
 }
 
 // ---------------------------------------------------------------- prepare --
-// One CTA (128 threads) per chunk record and q/k head; the two v-heads of the
-// q/k head share every M=64 accumulator, head 0 in TMEM lanes 0-15 and head 1
-// in lanes 16-31 of each warp's sub-partition, so in the packed epilogues
-// thread (warp w, lane l) owns row 16w + (l & 15) of head l >> 4.  Every
-// operand image is written as whole 16-byte vectors of one row; B operands
-// are MN-major images, so no transposed copy is ever made.
-// Shared memory, 99 KB so that two CTAs share an SM: the X images reuse the
-// [K;Q] tile once the Gram MMA and the Q-image store have read it, and the
-// right-hand sides reuse the P images once the Neumann rounds are done.
-constexpr int kPrepKQ = 0;          // bf16 [K;Q] K-major, 2 kblocks x 128 rows            32 KiB
-constexpr int kPrepX = 0;           // tf32 X_h (Neumann iterate -> A^-1) K-major, 2 heads  2 x 16 KiB (over KQ)
-constexpr int kPrepPA = 32768;      // tf32 P_h (power of N) K-major                         2 x 16 KiB
-constexpr int kPrepPB = 65536;      // tf32 P_h MN-major (B operand)                          2 x 16 KiB
-constexpr int kPrepRHS = kPrepPA;   // tf32 [beta G K | beta V] MN-major, 64 x 256, over PA+PB  64 KiB
+// One CTA (128 threads) per chunk record and q/k head.  Everything the carry
+// kernel's state chain does not need is finished here, in fp16 operand images
+// (round-to-nearest; fp32 accumulation), per v-head h:
+//   M  = G_C I - (tail K)^T W          [k][k']  fp16 K-major  (the carry's A operand)
+//   D  = (tail K)^T U                  [k][v]   fp32 rows
+//   Qt = G (.) Q - P W                 [i][k]   fp16 K-major  (the output MMA's A operand)
+//   Ut = P U                           [i][v]   fp16, two 64-column halves
+// so that one chunk of the carry is S1 = S0 M^T + D and O = scale (Qt S0^T + Ut).
+// The two v-heads of the q/k head share every M=64 accumulator (head 0 in TMEM
+// lanes 0-15, head 1 in lanes 16-31 of each warp's sub-partition); in those
+// epilogues thread (warp w, lane l) owns row 16w + (l & 15) of head l >> 4.
+constexpr int kPrepKQ = 0;          // bf16 [K;Q] K-major, 2 kblocks x 128 rows                 32 KiB
+constexpr int kPrepX = 0;           // f16 X_h K-major [64][64] (Neumann iterate -> A^-1), over KQ  2 x 8 KiB
+constexpr int kPrepPA = 16384;      // f16 power P_h K-major [64][64]                              2 x 8 KiB
+constexpr int kPrepPB = 32768;      // f16 power P_h MN-major                                      2 x 8 KiB
+constexpr int kPrepPO = 49152;      // f16 output-side P_h K-major [64 i][64 j]                    2 x 8 KiB
+constexpr int kPrepRHS = 65536;     // f16 [beta G K | beta V] MN-major [64 j][256] -> then [W | U]  32 KiB
+constexpr int kPrepKB = 16384;      // f16 tail K MN-major [64 j][128 k] over PA/PB (after Neumann) 16 KiB
 constexpr int kPrepSmall = 98304;
 constexpr int kPrepSmem = kPrepSmall + 2048 + 1024;
 constexpr int kPrepTmemCols = 256;
@@ -177,15 +186,15 @@ __device__ __forceinline__ void st_f32(uint8_t* img, uint32_t off, float v) {
     *reinterpret_cast<float*>(img + off) = v;
 }
 
+__device__ __forceinline__ float4 tf32x4(float a, float b, float c, float d) {
+    return make_float4(to_tf32(a), to_tf32(b), to_tf32(c), to_tf32(d));
+}
+
 // 2^x on the SFU (ex2.approx: a couple of ulp); x <= 0 here, so no overflow.
 __device__ __forceinline__ float fast_exp2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
-}
-
-__device__ __forceinline__ float4 tf32x4(float a, float b, float c, float d) {
-    return make_float4(to_tf32(a), to_tf32(b), to_tf32(c), to_tf32(d));
 }
 
 // 8 bf16 (one 16-byte chunk) -> 8 floats
@@ -198,6 +207,41 @@ __device__ __forceinline__ void bf16x8_to_f32(uint4 u, float (&f)[8]) {
     }
 }
 
+// 8 floats -> 8 fp16 (round-to-nearest) in one 16-byte chunk
+__device__ __forceinline__ uint4 f16x8(const float* f) {
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const __half2 h2 = __floats2half2_rn(f[2 * e], f[2 * e + 1]);
+        w[e] = *reinterpret_cast<const uint32_t*>(&h2);
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__device__ __forceinline__ void st_shared_u4(uint32_t addr, uint4 v) {
+    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+__device__ __forceinline__ uint4 ld_shared_u4(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ void h16x8_to_f32(uint4 u, float (&f)[8]) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const float2 p = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+        f[2 * e] = p.x;
+        f[2 * e + 1] = p.y;
+    }
+}
+
+// Offset of element (row, col) in a 16-bit SW128 image with `rows` rows per
+// 128-byte column block; the same formula serves K-major (row = M/N index)
+// and MN-major (row = K index) images.
+__device__ __forceinline__ uint32_t h16(int row, int col, int rows) { return sw128_bf16(row, col, rows); }
+
 __global__ void __launch_bounds__(128, 2)
     gdn_chunk_prepare_kernel(const PrefillParams p, uint8_t* __restrict__ ws, const WsLayout L) {
     extern __shared__ uint8_t smem_raw[];
@@ -205,7 +249,8 @@ __global__ void __launch_bounds__(128, 2)
     uint8_t* sKQ = sm + kPrepKQ;
     PrepSmall& sml = *reinterpret_cast<PrepSmall*>(sm + kPrepSmall);
     const uint32_t aKQ = smem_u32(sKQ), aX = smem_u32(sm + kPrepX), aPA = smem_u32(sm + kPrepPA),
-                   aPB = smem_u32(sm + kPrepPB), aRHS = smem_u32(sm + kPrepRHS);
+                   aPB = smem_u32(sm + kPrepPB), aPO = smem_u32(sm + kPrepPO), aRHS = smem_u32(sm + kPrepRHS),
+                   aKB = smem_u32(sm + kPrepKB);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t rec = blockIdx.x;
@@ -255,6 +300,8 @@ __global__ void __launch_bounds__(128, 2)
     const uint32_t tm = sml.tmem_base;
     uint32_t phase = 0;
     bool ok = true, aborted = false;
+    const int hl = lane >> 4;               // head of this thread in packed M=64 epilogues
+    const int row = 16 * warp + (lane & 15);  // its row there
 
     // 2. Gram: rows 0-63 K K^T, rows 64-127 Q K^T (bf16, M=128, N=64, K=128)
     if (tid == 0) {
@@ -262,10 +309,10 @@ __global__ void __launch_bounds__(128, 2)
         mma_commit(bar);
     }
     {  // inclusive prefix of log2 g (64 sequential adds; deterministic)
-        const int hl = tid >> 6, i = tid & 63;
+        const int h2 = tid >> 6, i = tid & 63;
         float acc = 0.f;
-        for (int m = 0; m <= i; ++m) acc += sml.lg[hl][m];
-        sml.LG[hl][i] = acc;
+        for (int m = 0; m <= i; ++m) acc += sml.lg[h2][m];
+        sml.LG[h2][i] = acc;
     }
     __syncthreads();
     ok = mbar_wait(bar, phase);
@@ -273,8 +320,9 @@ __global__ void __launch_bounds__(128, 2)
     tc_fence_after();
     __syncthreads();  // every thread is past the Gram MMA before X overwrites [K;Q]
     {
-        // 3. Gram epilogue (M=128 rows: thread = row).  Rows 0-63 build N, P and
-        //    X = I - N of both heads; rows 64-127 build the output-side P.
+        // 3. Gram epilogue (M=128 rows: thread = row).  Rows 0-63 build N, its
+        //    two operand copies and X = I - N of both heads; rows 64-127 the
+        //    output-side P = Gam (.) Q K^T (j <= i).
         float gram[64];
         {
             float t32[32];
@@ -287,41 +335,35 @@ __global__ void __launch_bounds__(128, 2)
             tmem_wait_ld();
         }
         const int i = tid & 63;
-        if (tid < 64) {
 #pragma unroll 1
-            for (int hl = 0; hl < 2; ++hl) {
-                const float LGi = sml.LG[hl][i], bi = sml.beta[hl][i];
-                const uint32_t xa = aX + hl * 16384, pa = aPA + hl * 16384, pb = aPB + hl * 16384;
+        for (int h2 = 0; h2 < 2; ++h2) {
+            const float LGi = sml.LG[h2][i];
+            if (tid < 64) {
+                const float bi = sml.beta[h2][i];
 #pragma unroll
-                for (int j0 = 0; j0 < 64; j0 += 4) {
-                    float nv[4];
+                for (int j0 = 0; j0 < 64; j0 += 8) {
+                    float nv[8], xv[8];
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
+                    for (int e = 0; e < 8; ++e) {
                         const int j = j0 + e;
-                        nv[e] = (j < i) ? bi * fast_exp2(LGi - sml.LG[hl][j]) * gram[j] : 0.f;
+                        nv[e] = (j < i) ? bi * fast_exp2(LGi - sml.LG[h2][j]) * gram[j] : 0.f;
+                        xv[e] = (j == i ? 1.f : 0.f) - nv[e];
                     }
-                    const float4 t = tf32x4(nv[0], nv[1], nv[2], nv[3]);
-                    st_shared_v4(pa + sw128_f32(i, j0, 64), t);
-                    st_shared_v4(pb + mn32_f32(i, j0, 64), t);
-                    st_shared_v4(xa + sw128_f32(i, j0, 64),
-                                 tf32x4((j0 == i) - nv[0], (j0 + 1 == i) - nv[1], (j0 + 2 == i) - nv[2],
-                                        (j0 + 3 == i) - nv[3]));
+                    const uint4 nh = f16x8(nv);
+                    st_shared_u4(aPA + h2 * 8192 + h16(i, j0, 64), nh);
+                    st_shared_u4(aPB + h2 * 8192 + h16(i, j0, 64), nh);
+                    st_shared_u4(aX + h2 * 8192 + h16(i, j0, 64), f16x8(xv));
                 }
-            }
-        } else {
-#pragma unroll 1
-            for (int hl = 0; hl < 2; ++hl) {
-                const float LGi = sml.LG[hl][i];
-                uint8_t* gp = ws + L.off_p + (rec * kHV + 2 * hq + hl) * kPImg;
+            } else {
 #pragma unroll
-                for (int j0 = 0; j0 < 64; j0 += 4) {
-                    float pv[4];
+                for (int j0 = 0; j0 < 64; j0 += 8) {
+                    float pv[8];
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
+                    for (int e = 0; e < 8; ++e) {
                         const int j = j0 + e;
-                        pv[e] = (j <= i) ? fast_exp2(LGi - sml.LG[hl][j]) * gram[j] : 0.f;
+                        pv[e] = (j <= i) ? fast_exp2(LGi - sml.LG[h2][j]) * gram[j] : 0.f;
                     }
-                    *reinterpret_cast<float4*>(gp + sw128_f32(i, j0, 64)) = tf32x4(pv[0], pv[1], pv[2], pv[3]);
+                    st_shared_u4(aPO + h2 * 8192 + h16(i, j0, 64), f16x8(pv));
                 }
             }
         }
@@ -333,44 +375,44 @@ __global__ void __launch_bounds__(128, 2)
         tc_fence_after();
 #pragma unroll
         for (int h = 0; h < 2; ++h)
-            mma_ct<kTF32, false, true, 64, 64, 64, 64, 64>(taddr(tm, 16 * h, 64), aPA + h * 16384, aPB + h * 16384,
-                                                          false);
+            mma_ct<kF16, false, true, 64, 64, 64, 64, 64>(taddr(tm, 16 * h, 64), aPA + h * 8192, aPB + h * 8192,
+                                                         false);
         mma_commit(bar);
     }
     // 4. Neumann doubling, both heads packed: epilogue e updates X (e >= 1) and P (e <= 4)
-    const int hl = lane >> 4;
-    const int row = 16 * warp + (lane & 15);
     for (int e = 0; e <= 5; ++e) {
         ok = mbar_wait(bar, phase);
         phase ^= 1;
         tc_fence_after();
         if (e >= 1) {
-            const uint32_t xa = aX + hl * 16384;
+            const uint32_t xa = aX + hl * 8192;
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
                 float xp[32];
                 tmem_ld32(taddr(tm, 32 * warp, 32 * half), xp);
                 tmem_wait_ld();
 #pragma unroll
-                for (int j0 = 0; j0 < 32; j0 += 4) {
-                    const uint32_t off = xa + sw128_f32(row, 32 * half + j0, 64);
-                    const float4 x = ld_shared_v4(off);
-                    st_shared_v4(off, tf32x4(x.x + xp[j0], x.y + xp[j0 + 1], x.z + xp[j0 + 2], x.w + xp[j0 + 3]));
+                for (int j0 = 0; j0 < 32; j0 += 8) {
+                    const uint32_t off = xa + h16(row, 32 * half + j0, 64);
+                    float x[8];
+                    h16x8_to_f32(ld_shared_u4(off), x);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) x[q] += xp[j0 + q];
+                    st_shared_u4(off, f16x8(x));
                 }
             }
         }
         if (e <= 4) {
-            const uint32_t pa = aPA + hl * 16384, pb = aPB + hl * 16384;
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
                 float pp[32];
                 tmem_ld32(taddr(tm, 32 * warp, 64 + 32 * half), pp);
                 tmem_wait_ld();
 #pragma unroll
-                for (int j0 = 0; j0 < 32; j0 += 4) {
-                    const float4 t = tf32x4(pp[j0], pp[j0 + 1], pp[j0 + 2], pp[j0 + 3]);
-                    st_shared_v4(pa + sw128_f32(row, 32 * half + j0, 64), t);
-                    st_shared_v4(pb + mn32_f32(row, 32 * half + j0, 64), t);
+                for (int j0 = 0; j0 < 32; j0 += 8) {
+                    const uint4 t = f16x8(pp + j0);
+                    st_shared_u4(aPA + hl * 8192 + h16(row, 32 * half + j0, 64), t);
+                    st_shared_u4(aPB + hl * 8192 + h16(row, 32 * half + j0, 64), t);
                 }
             }
         }
@@ -384,17 +426,17 @@ __global__ void __launch_bounds__(128, 2)
             tc_fence_after();
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-                mma_ct<kTF32, false, true, 64, 64, 64, 64, 64>(taddr(tm, 16 * h, 0), aX + h * 16384,
-                                                              aPB + h * 16384, false);  // X P
+                mma_ct<kF16, false, true, 64, 64, 64, 64, 64>(taddr(tm, 16 * h, 0), aX + h * 8192, aPB + h * 8192,
+                                                             false);  // X P
                 if (e <= 3)
-                    mma_ct<kTF32, false, true, 64, 64, 64, 64, 64>(taddr(tm, 16 * h, 64), aPA + h * 16384,
-                                                                  aPB + h * 16384, false);  // P P
+                    mma_ct<kF16, false, true, 64, 64, 64, 64, 64>(taddr(tm, 16 * h, 64), aPA + h * 8192,
+                                                                 aPB + h * 8192, false);  // P P
             }
             mma_commit(bar);
         }
     }
-    // 5. per head: [beta G K | beta V] (MN-major, over the dead P images), the
-    //    K-bar image and gate vector to global, then [W | U] = A^-1 [..]
+    // 5. per head: [beta G K | beta V] and tail K, then [W | U] = A^-1 [..], then
+    //    P [W | U] and (tail K)^T [W | U]; results straight to the workspace
 #pragma unroll 1
     for (int h2 = 0; h2 < 2; ++h2) {
         const int h = 2 * hq + h2;
@@ -403,44 +445,28 @@ __global__ void __launch_bounds__(128, 2)
             const int j = tid & 63, part = tid >> 6;
             const float LGj = sml.LG[h2][j], bj = sml.beta[h2][j];
             const float Gj = exp2f(LGj), tail = exp2f(sml.LG[h2][63] - LGj);
-            uint8_t* gkb = ws + L.off_kt + rh * kKTImg;
-            // part 0: columns 0-127 (beta G K) and K-bar columns 0-63; part 1: beta V and K-bar 64-127
             const bool act = j < n;
-            const uint16_t* ksrc = p.k + ((t0 + j) * kHQK + hq) * kD;  // K row j (L2-resident)
-            if (part == 0) {
+            if (part == 0) {  // K row j: beta G K -> RHS columns 0-127, tail K -> K-bar
+                const uint16_t* ksrc = p.k + ((t0 + j) * kHQK + hq) * kD;
+                const float s = bj * Gj;
 #pragma unroll 4
                 for (int d0 = 0; d0 < kD; d0 += 8) {
-                    float f[8];
+                    float f[8], a[8], b[8];
                     bf16x8_to_f32(act ? *reinterpret_cast<const uint4*>(ksrc + d0) : make_uint4(0, 0, 0, 0), f);
-                    const float s = bj * Gj;
-                    st_shared_v4(aRHS + mn32_f32(j, d0, 64), tf32x4(s * f[0], s * f[1], s * f[2], s * f[3]));
-                    st_shared_v4(aRHS + mn32_f32(j, d0 + 4, 64), tf32x4(s * f[4], s * f[5], s * f[6], s * f[7]));
-                    if (d0 < 64) {
-                        *reinterpret_cast<float4*>(gkb + mn32_f32(j, d0, 64)) =
-                            tf32x4(tail * f[0], tail * f[1], tail * f[2], tail * f[3]);
-                        *reinterpret_cast<float4*>(gkb + mn32_f32(j, d0 + 4, 64)) =
-                            tf32x4(tail * f[4], tail * f[5], tail * f[6], tail * f[7]);
-                    }
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) a[q] = s * f[q], b[q] = tail * f[q];
+                    st_shared_u4(aRHS + h16(j, d0, 64), f16x8(a));
+                    st_shared_u4(aKB + h16(j, d0, 64), f16x8(b));
                 }
-                float* gvec = reinterpret_cast<float*>(ws + L.off_vec + rh * kVecBytes);
-                gvec[j] = Gj;
-                if (j == 0) gvec[64] = exp2f(sml.LG[h2][63]);
-            } else {
+            } else {  // V row j: beta V -> RHS columns 128-255
                 const uint16_t* vsrc = p.v + ((t0 + j) * kHV + h) * kD;
 #pragma unroll 4
                 for (int d0 = 0; d0 < kD; d0 += 8) {
-                    float f[8];
+                    float f[8], a[8];
                     bf16x8_to_f32(act ? *reinterpret_cast<const uint4*>(vsrc + d0) : make_uint4(0, 0, 0, 0), f);
-                    st_shared_v4(aRHS + mn32_f32(j, 128 + d0, 64), tf32x4(bj * f[0], bj * f[1], bj * f[2], bj * f[3]));
-                    st_shared_v4(aRHS + mn32_f32(j, 132 + d0, 64), tf32x4(bj * f[4], bj * f[5], bj * f[6], bj * f[7]));
-                    if (d0 >= 64) {
-                        float g[8];
-                        bf16x8_to_f32(act ? *reinterpret_cast<const uint4*>(ksrc + d0) : make_uint4(0, 0, 0, 0), g);
-                        *reinterpret_cast<float4*>(gkb + mn32_f32(j, d0, 64)) =
-                            tf32x4(tail * g[0], tail * g[1], tail * g[2], tail * g[3]);
-                        *reinterpret_cast<float4*>(gkb + mn32_f32(j, d0 + 4, 64)) =
-                            tf32x4(tail * g[4], tail * g[5], tail * g[6], tail * g[7]);
-                    }
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) a[q] = bj * f[q];
+                    st_shared_u4(aRHS + h16(j, 128 + d0, 64), f16x8(a));
                 }
             }
         }
@@ -449,45 +475,114 @@ __global__ void __launch_bounds__(128, 2)
         __syncthreads();
         if (tid == 0) {
             tc_fence_after();
-            mma_ct<kTF32, false, true, 64, 64, 64, 64, 256>(taddr(tm, 16 * h2, 0), aX + h2 * 16384, aRHS, false);
+            mma_ct<kF16, false, true, 64, 64, 64, 64, 256>(tm, aX + h2 * 8192, aRHS, false);  // [W | U], lanes 0-15
             mma_commit(bar);
         }
-        ok = mbar_wait(bar, phase);  // also frees the RHS image for the next head
+        ok = mbar_wait(bar, phase);
         phase ^= 1;
         tc_fence_after();
-        if (__syncthreads_or(!ok)) {
-            aborted = true;
-            goto done;
-        }
-    }
-    {   // 6. [W | U] rows of both heads (packed): W as the carry's tf32 A image, U plain
-        const int h = 2 * hq + hl;
-        const int64_t rh = rec * kHV + h;
-        uint8_t* gw = ws + L.off_w + rh * kWImg;
-        float* gu = reinterpret_cast<float*>(ws + L.off_u + rh * kUBytes) + row * kD;
+        // [W | U] rows (lanes 0-15: this head) -> fp16 MN-major B image over the RHS;
+        // every lane takes part in the (warp-collective) TMEM loads
 #pragma unroll 1
         for (int c = 0; c < 8; ++c) {
             float acc[32];
             tmem_ld32(taddr(tm, 32 * warp, 32 * c), acc);
             tmem_wait_ld();
-            if (c < 4) {
+            if ((lane & 16) == 0) {
 #pragma unroll
-                for (int j0 = 0; j0 < 32; j0 += 4)
-                    *reinterpret_cast<float4*>(gw + sw128_f32(row, 32 * c + j0, 64)) =
-                        tf32x4(acc[j0], acc[j0 + 1], acc[j0 + 2], acc[j0 + 3]);
-            } else {
-#pragma unroll
-                for (int j0 = 0; j0 < 32; j0 += 4)
-                    *reinterpret_cast<float4*>(gu + 32 * (c - 4) + j0) =
-                        make_float4(acc[j0], acc[j0 + 1], acc[j0 + 2], acc[j0 + 3]);
+                for (int j0 = 0; j0 < 32; j0 += 8) st_shared_u4(aRHS + h16(row, 32 * c + j0, 64), f16x8(acc + j0));
             }
+        }
+        fence_async_smem();
+        tc_fence_before();
+        if (__syncthreads_or(!ok)) {
+            aborted = true;
+            goto done;
+        }
+        if (tid == 0) {  // P [W | U] (M=64, lanes 0-15, columns 0-255)
+            tc_fence_after();
+            mma_ct<kF16, false, true, 64, 64, 64, 64, 256>(tm, aPO + h2 * 8192, aRHS, false);
+            mma_commit(bar);
+        }
+        ok = mbar_wait(bar, phase);
+        phase ^= 1;
+        tc_fence_after();
+        {  // Qt = G (.) Q - P W and Ut = P U (rows i = row, lanes 0-15)
+            const float Gi = exp2f(sml.LG[h2][row & 63]);
+            const bool act = (row & 63) < n;
+            const uint16_t* qsrc = p.q + ((t0 + (row & 63)) * kHQK + hq) * kD;
+            uint8_t* gqt = ws + L.off_qt + rh * kQtImg;
+            uint16_t* gut = reinterpret_cast<uint16_t*>(ws + L.off_ut + rh * kUtBytes);
+#pragma unroll 1
+            for (int c = 0; c < 8; ++c) {
+                float acc[32];
+                tmem_ld32(taddr(tm, 32 * warp, 32 * c), acc);
+                tmem_wait_ld();
+                if ((lane & 16) == 0) {
+                    if (c < 4) {
+#pragma unroll
+                        for (int j0 = 0; j0 < 32; j0 += 8) {
+                            float f[8];
+                            bf16x8_to_f32(act ? *reinterpret_cast<const uint4*>(qsrc + 32 * c + j0)
+                                              : make_uint4(0, 0, 0, 0),
+                                          f);
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) f[q] = Gi * f[q] - acc[j0 + q];
+                            *reinterpret_cast<uint4*>(gqt + h16(row, 32 * c + j0, 64)) = f16x8(f);
+                        }
+                    } else {  // Ut: [half][i][64] with half = value column / 64
+                        const int v = 32 * (c - 4);
+#pragma unroll
+                        for (int j0 = 0; j0 < 32; j0 += 8)
+                            *reinterpret_cast<uint4*>(gut + ((v + j0) >> 6) * (kC * 64) + row * 64 + ((v + j0) & 63)) =
+                                f16x8(acc + j0);
+                    }
+                }
+            }
+        }
+        tc_fence_before();
+        __syncthreads();
+        if (tid == 0) {  // (tail K)^T [W | U] (M=128: rows = state column k)
+            tc_fence_after();
+            mma_ct<kF16, true, true, 64, 64, 64, 128, 256>(tm, aKB, aRHS, false);
+            mma_commit(bar);
+        }
+        ok = mbar_wait(bar, phase);
+        phase ^= 1;
+        tc_fence_after();
+        {  // M = G_C I - (tail K)^T W (row k = tid, fp16 K-major) and D = (tail K)^T U (fp32 rows)
+            const float Gc = exp2f(sml.LG[h2][63]);
+            uint8_t* gm = ws + L.off_m + rh * kMImg;
+            float* gd = reinterpret_cast<float*>(ws + L.off_d + rh * kDBytes) + tid * kD;
+#pragma unroll 1
+            for (int c = 0; c < 8; ++c) {
+                float acc[32];
+                tmem_ld32(taddr(tm, 32 * warp, 32 * c), acc);
+                tmem_wait_ld();
+                if (c < 4) {
+#pragma unroll
+                    for (int j0 = 0; j0 < 32; j0 += 8) {
+                        float f[8];
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) f[q] = (32 * c + j0 + q == tid ? Gc : 0.f) - acc[j0 + q];
+                        *reinterpret_cast<uint4*>(gm + h16(tid, 32 * c + j0, 128)) = f16x8(f);
+                    }
+                } else {
+#pragma unroll
+                    for (int j0 = 0; j0 < 32; j0 += 4)
+                        *reinterpret_cast<float4*>(gd + 32 * (c - 4) + j0) =
+                            make_float4(acc[j0], acc[j0 + 1], acc[j0 + 2], acc[j0 + 3]);
+                }
+            }
+        }
+        tc_fence_before();
+        if (__syncthreads_or(!ok)) {
+            aborted = true;
+            goto done;
         }
     }
 done:
-    if (tid == 0) {
-        bulk_wait_all();
-        if (aborted) record_status(32 /* GDN_ERR_DEVICE_TIMEOUT */);
-    }
+    if (tid == 0 && aborted) record_status(32 /* GDN_ERR_DEVICE_TIMEOUT */);
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
@@ -497,53 +592,66 @@ done:
 }
 
 // ------------------------------------------------------------------ carry --
-// One CTA (128 threads) per sequence x v-head x BV value rows.  Per chunk:
-//   MMA1  [W ; G(.)Q] S0^T  (tf32, M=128): TMEM lanes 0-63 hold W S0^T,
-//         lanes 64-127 G(.)Q S0^T (one row per token in both halves)
-//   epi A warps 0-1: Delta = U - W S0^T -> Delta image (tf32, MN-major)
-//   MMA2  (tail K)^T Delta (M=128, rows = state columns k) and [0 ; P] Delta
-//         accumulated onto lanes 64-127, which then hold the chunk's output
-//   epi B every thread: S1 = G_C S0 + (tail K)^T Delta for its column k;
-//         warps 2-3 store O = scale (G(.)Q S0^T + P Delta)
-// Operands arrive by bulk copy; each is reloaded for the next chunk as soon
-// as the MMA reading it completes (W after MMA1; tail K, P, G after MMA2), and
-// warps 2-3 build the next chunk's G(.)Q rows from the raw q input while MMA2
-// runs, so one buffer per operand suffices.  All operands feeding the state
-// are tf32 (round-to-nearest); the state itself stays fp32 in registers.
-template <int BV>
-struct CarrySmem {
-    static constexpr int kA1 = 0;                 // tf32 [W ; G Q] K-major, 4 kblocks x 128 rows   64 KiB
-    static constexpr int kA2 = kA1 + 65536;       // tf32 [0 ; P]   K-major, 2 kblocks x 128 rows   32 KiB
-    static constexpr int kKB = kA2 + 32768;       // tf32 tail K MN-major [64 j][128 k]             32 KiB
-    static constexpr int kVec = kKB + 32768;      // two gate vectors G[64], G_C (by chunk parity)
-    static constexpr int kS32 = kVec + 1024;      // tf32 S MN-major [128 k][BV]
-    static constexpr int kD32 = kS32 + BV * 512;  // tf32 Delta MN-major [64 j][BV]
-    static constexpr int kSmall = kD32 + BV * 256;
-    static constexpr int kTotal = kSmall + 128 + 1024;
-    static constexpr int kTmemCols = 2 * BV < 32 ? 32 : 2 * BV;
-};
-constexpr uint32_t kCarryTxA = kWImg;
-constexpr uint32_t kCarryTxB = kKTImg + kPImg + kVecBytes;
+// One CTA (256 threads) per sequence x v-head x 64 value rows.  The state
+// chain needs one tensor-core MMA per chunk:
+//   S_{c+1}^T = M_c S_c^T + D_c^T      (M fp16 K-major, S fp16 MN-major, fp32 accumulate)
+// Warps 0-3 own the state (thread k = column k of the 64 rows, fp32 registers):
+// they add D_c (prefetched one chunk ahead) to the accumulator and write the
+// next fp16 state image.  Warps 4-7 finish the outputs off the critical path:
+//   O_c = scale (Qt_c S_c^T + Ut_c)    (Qt fp16 K-major; the MMA reads the same state image)
+// Thread 0 issues every MMA and bulk copy.  M is double-buffered and
+// [Qt | Ut] triple-buffered, each refilled as soon as its readers are done,
+// so the copies run a chunk or more ahead of use.
+constexpr int kCarryBV = 64;
+constexpr int kCarryThreads = 256;
+constexpr int kCarMI = 0;                         // f16 M K-major [128 k][128 k'], 2 x 32 KiB
+constexpr int kCarQU = 65536;                     // 3 x (Qt f16 K-major [64 i][128 k] 16 KiB + Ut [64 i][64 v] f16 8 KiB)
+constexpr int kCarQUBytes = 24576;
+constexpr int kCarSI = kCarQU + 3 * kCarQUBytes;  // f16 S MN-major [128 k][64 v], 2 x 16 KiB
+constexpr int kCarSmall = kCarSI + 2 * 16384;
+constexpr int kCarSmem = kCarSmall + 256 + 1024;
+constexpr int kCarTmemCols = 256;                 // accS [0,64), accO x 2 [64,192)
 
-template <int BV>
-__global__ void __launch_bounds__(128, 1)
+// bar.red.or on named barrier `id` among `count` threads
+__device__ __forceinline__ bool named_sync_or(int id, int count, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "barrier.red.or.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "r"(id), "r"(count)
+        : "memory");
+    return r != 0;
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__global__ void __launch_bounds__(kCarryThreads, 1)
     gdn_chunk_carry_kernel(const PrefillParams p, const uint8_t* __restrict__ ws, const WsLayout L) {
-    using SM = CarrySmem<BV>;
-    static_assert(BV == 32 || BV == 64, "value-row tile (MN-major tf32 images need 32-wide rows)");
+    constexpr int BV = kCarryBV;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = align1024(smem_raw);
-    const uint32_t aA1 = smem_u32(sm + SM::kA1), aA2 = smem_u32(sm + SM::kA2), aKB = smem_u32(sm + SM::kKB),
-                   aVec = smem_u32(sm + SM::kVec), aS32 = smem_u32(sm + SM::kS32), aD32 = smem_u32(sm + SM::kD32);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + SM::kSmall);  // fullA, fullB, mma1, mma2
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + SM::kSmall + 64);
+    const uint32_t aMI = smem_u32(sm + kCarMI), aQU = smem_u32(sm + kCarQU), aSI = smem_u32(sm + kCarSI);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kCarSmall);
+    // fullM[2], fullQ[3], mmaS, mmaO[2], oFree[2], quFree[3]
+    const uint32_t bar0 = smem_u32(bars);
+    auto fullM = [&](int b) { return bar0 + 8 * b; };
+    auto fullQ = [&](int b) { return bar0 + 16 + 8 * b; };
+    const uint32_t mmaS = bar0 + 40;
+    auto mmaO = [&](int b) { return bar0 + 48 + 8 * b; };
+    auto oFree = [&](int b) { return bar0 + 64 + 8 * b; };
+    auto quFree = [&](int b) { return bar0 + 80 + 8 * b; };
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kCarSmall + 128);
 
     constexpr int kTiles = kD / BV;
-    const int tid = threadIdx.x, warp = tid >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t unit = blockIdx.x / kTiles;
     const int vt = static_cast<int>(blockIdx.x - unit * kTiles);
     const int64_t s = unit / kHV;
     const int h = static_cast<int>(unit - s * kHV);
-    const int hq = h / kGva;
     const int v0 = vt * BV;
 
     int64_t t0, t1;
@@ -551,86 +659,71 @@ __global__ void __launch_bounds__(128, 1)
     const int len = static_cast<int>(t1 - t0);
     const int nch = (len + kC - 1) / kC;
     const int rec0 = reinterpret_cast<const int*>(ws + L.off_base)[s];
-    float* ns_col = p.new_state + (unit * kD + v0) * kD + tid;  // column k = tid of rows v0..
+    const bool state_warp = warp < 4;
+    const int k = tid;  // state column owned by state threads
     if (nch == 0 || rec0 + nch > L.R) {
-        if (nch != 0) record_status(16);
-#pragma unroll
-        for (int v = 0; v < BV; ++v) ns_col[v * kD] = 0.f;  // empty sequence: zero state row
+        if (nch != 0 && tid == 0) record_status(16);
+        if (state_warp) {  // empty sequence: zero state rows (oracle prefill :53-55)
+            float* ns_col = p.new_state + (unit * kD + v0) * kD + k;
+#pragma unroll 8
+            for (int v = 0; v < BV; ++v) ns_col[v * kD] = 0.f;
+        }
         return;
     }
+    auto rhead = [&](int c) { return (int64_t)(rec0 + c) * kHV + h; };
 
-    // state rows v0..v0+BV, column k = tid, in registers; MN-major image for the MMAs
     float S[BV];
-    if (p.state != nullptr) {
-        const float* st = p.state + (unit * kD + v0) * kD + tid;
+    float Dn[BV];  // D of the next chunk to apply
+    auto load_D = [&](int c) {
+        const float4* src = reinterpret_cast<const float4*>(
+            reinterpret_cast<const float*>(ws + L.off_d + rhead(c) * kDBytes) + k * kD + v0);
 #pragma unroll
-        for (int v = 0; v < BV; ++v) S[v] = st[v * kD];
-    } else {
-#pragma unroll
-        for (int v = 0; v < BV; ++v) S[v] = 0.f;
-    }
-    auto write_state_image = [&]() {
-#pragma unroll
-        for (int v = 0; v < BV; v += 4)
-            st_shared_v4(aS32 + mn32_f32(tid, v, kD), tf32x4(S[v], S[v + 1], S[v + 2], S[v + 3]));
-    };
-    write_state_image();
-    {  // the zero upper half of [0 ; P] (rows 0-63 of both K-blocks), written once
-        const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            const int idx = tid * 8 + e;  // 1024 chunks of 16 B
-            st_shared_v4(aA2 + (idx >> 9) * 16384 + (idx & 511) * 16, z);
-        }
-    }
-    auto gvec = [&](int c) {
-        return reinterpret_cast<const float*>(ws + L.off_vec + ((int64_t)(rec0 + c) * kHV + h) * kVecBytes);
-    };
-    // G (.) Q rows of chunk c into rows 64-127 of [W ; G Q] (warps 2-3: token i = tid - 64)
-    auto build_gq = [&](int c) {
-        const int i = tid - 64;
-        const int tok = kC * c + i;
-        const bool act = tok < len;
-        const float gi = act ? gvec(c)[i] : 0.f;
-        const uint16_t* qrow = p.q + ((t0 + tok) * kHQK + hq) * kD;
-#pragma unroll 4
-        for (int k0 = 0; k0 < kD; k0 += 8) {
-            float f[8];
-            bf16x8_to_f32(act ? *reinterpret_cast<const uint4*>(qrow + k0) : make_uint4(0, 0, 0, 0), f);
-            st_shared_v4(aA1 + sw128_f32(64 + i, k0, 128), tf32x4(gi * f[0], gi * f[1], gi * f[2], gi * f[3]));
-            st_shared_v4(aA1 + sw128_f32(64 + i, k0 + 4, 128), tf32x4(gi * f[4], gi * f[5], gi * f[6], gi * f[7]));
+        for (int v = 0; v < BV; v += 4) {
+            const float4 x = src[v / 4];
+            Dn[v] = x.x, Dn[v + 1] = x.y, Dn[v + 2] = x.z, Dn[v + 3] = x.w;
         }
     };
-    if (warp >= 2) build_gq(0);
-
-    const uint32_t fullA = smem_u32(&bars[0]), fullB = smem_u32(&bars[1]), mma1 = smem_u32(&bars[2]),
-                   mma2 = smem_u32(&bars[3]);
-    auto issue_A = [&](int c) {  // W of chunk c -> rows 0-63 of each K-block of [W ; G Q]
-        const uint8_t* gw = ws + L.off_w + ((int64_t)(rec0 + c) * kHV + h) * kWImg;
-        mbar_expect_tx(fullA, kCarryTxA);
+    auto write_state_image = [&](int b) {
 #pragma unroll
-        for (int kb = 0; kb < 4; ++kb) bulk_g2s(aA1 + kb * 16384, gw + kb * 8192, 8192, fullA);
+        for (int v = 0; v < BV; v += 8) st_shared_u4(aSI + b * 16384 + h16(k, v, kD), f16x8(S + v));
     };
-    auto issue_B = [&](int c) {  // tail K, P (rows 64-127 of [0 ; P]) and G of chunk c
-        const int64_t rh = (int64_t)(rec0 + c) * kHV + h;
-        const uint8_t* gp = ws + L.off_p + rh * kPImg;
-        mbar_expect_tx(fullB, kCarryTxB);
-        bulk_g2s(aKB, ws + L.off_kt + rh * kKTImg, kKTImg, fullB);
-        bulk_g2s(aA2 + 8192, gp, 8192, fullB);
-        bulk_g2s(aA2 + 16384 + 8192, gp + 8192, 8192, fullB);
-        bulk_g2s(aVec + (c & 1) * 512, ws + L.off_vec + rh * kVecBytes, kVecBytes, fullB);
+    if (state_warp) {
+        if (p.state != nullptr) {
+            const float* st = p.state + (unit * kD + v0) * kD + k;
+#pragma unroll
+            for (int v = 0; v < BV; ++v) S[v] = st[v * kD];
+        } else {
+#pragma unroll
+            for (int v = 0; v < BV; ++v) S[v] = 0.f;
+        }
+        write_state_image(0);
+        load_D(0);
+    }
+    auto issue_M = [&](int c) {
+        mbar_expect_tx(fullM(c & 1), kMImg);
+        bulk_g2s(aMI + (c & 1) * kMImg, ws + L.off_m + rhead(c) * kMImg, kMImg, fullM(c & 1));
     };
+    auto issue_QU = [&](int c) {
+        const int b = c % 3;
+        mbar_expect_tx(fullQ(b), kQtImg + kCarQUBytes - kQtImg);
+        bulk_g2s(aQU + b * kCarQUBytes, ws + L.off_qt + rhead(c) * kQtImg, kQtImg, fullQ(b));
+        bulk_g2s(aQU + b * kCarQUBytes + kQtImg, ws + L.off_ut + rhead(c) * kUtBytes + vt * (kC * 64 * 2),
+                 kC * 64 * 2, fullQ(b));
+    };
+    int m_issued = -1, m_waited = -1, q_issued = -1, q_waited = -1;  // thread 0's copy bookkeeping
     if (tid == 0) {
-        mbar_init(fullA, 1);
-        mbar_init(fullB, 1);
-        mbar_init(mma1, 1);
-        mbar_init(mma2, 1);
+        for (int b = 0; b < 2; ++b) mbar_init(fullM(b), 1);
+        for (int b = 0; b < 3; ++b) mbar_init(fullQ(b), 1);
+        mbar_init(mmaS, 1);
+        for (int b = 0; b < 2; ++b) mbar_init(mmaO(b), 1);
+        for (int b = 0; b < 2; ++b) mbar_init(oFree(b), 4);
+        for (int b = 0; b < 3; ++b) mbar_init(quFree(b), 4);
         fence_mbar_init();
-        issue_A(0);
-        issue_B(0);
+        for (int c = 0; c < 2 && c < nch; ++c) issue_M(c), m_issued = c;
+        for (int c = 0; c < 2 && c < nch; ++c) issue_QU(c), q_issued = c;  // chunk 2 is issued at c = 0
     }
     if (warp == 0) {
-        tmem_alloc(smem_u32(tmem_slot), SM::kTmemCols);
+        tmem_alloc(smem_u32(tmem_slot), kCarTmemCols);
         tmem_relinquish();
     }
     fence_async_smem();
@@ -638,127 +731,125 @@ __global__ void __launch_bounds__(128, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tm = *tmem_slot;
-    const uint32_t t_acc = tm, t_up = tm + BV;
-
-    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
+    const uint32_t t_accS = tm;
+    auto t_accO = [&](int b) { return tm + 64 + 64 * b; };
     bool ok = true, aborted = false;
-    int a_issued = 0, a_landed = -1, b_issued = 0, b_landed = -1;
-    for (int c = 0; c < nch; ++c) {
-        const int64_t rh = (int64_t)(rec0 + c) * kHV + h;
-        // MMA1 as soon as W of this chunk has landed
-        if (tid == 0) {
-            ok = mbar_wait(fullA, c & 1);
-            if (ok) {
-                a_landed = c;
-                tc_fence_after();
-                mma_ct<kTF32, false, true, kD, 128, kD, 128, BV>(t_acc, aA1, aS32, false);
-                mma_commit(mma1);
+
+    if (state_warp) {
+        for (int c = 0; c < nch; ++c) {
+            if (tid == 0) {
+                ok = ok && mbar_wait(fullM(c & 1), (c >> 1) & 1);  // ok is false after a failed refill wait
+                if (ok) m_waited = c;
+                ok = ok && mbar_wait(fullQ(c % 3), (c / 3) & 1);
+                if (ok) q_waited = c;
+                ok = ok && (c < 2 || mbar_wait(oFree(c & 1), ((c - 2) >> 1) & 1));
+                if (ok) {
+                    tc_fence_after();
+                    mma_ct<kF16, false, true, kD, 128, kD, 128, BV>(t_accS, aMI + (c & 1) * kMImg,
+                                                                   aSI + (c & 1) * 16384, false);
+                    mma_commit(mmaS);
+                    mma_ct<kF16, false, true, kD, 64, kD, 64, BV>(t_accO(c & 1), aQU + (c % 3) * kCarQUBytes,
+                                                                 aSI + (c & 1) * 16384, false);
+                    mma_commit(mmaO(c & 1));
+                }
             }
-        }
-        float u[BV];
-        if (warp < 2) {  // U row of token j = tid, while MMA1 runs
-            const float4* up =
-                reinterpret_cast<const float4*>(reinterpret_cast<const float*>(ws + L.off_u + rh * kUBytes) +
-                                                tid * kD + v0);
-#pragma unroll
-            for (int v = 0; v < BV; v += 4) {
-                const float4 x = up[v / 4];
-                u[v] = x.x, u[v + 1] = x.y, u[v + 2] = x.z, u[v + 3] = x.w;
+            if (named_sync_or(1, 128, !ok)) {
+                aborted = true;
+                break;
             }
-        }
-        ok = __syncthreads_and(ok) && mbar_wait(mma1, c & 1);
-        tc_fence_after();
-        if (tid == 0 && c + 1 < nch) issue_A(c + 1);  // W's rows of [W ; G Q] are free again
-        if (c + 1 < nch) a_issued = c + 1;
-        if (warp < 2) {  // epi A: Delta row j = tid
-            float wsr[BV];
-#pragma unroll
-            for (int c0 = 0; c0 < BV; c0 += 32) {
+            ok = mbar_wait(mmaS, c & 1);
+            tc_fence_after();
+            {
                 float a[32];
-                tmem_ld32(taddr(t_acc, 32 * warp, c0), a);
-                tmem_wait_ld();
-#pragma unroll
-                for (int v = 0; v < 32; ++v) wsr[c0 + v] = a[v];
-            }
-#pragma unroll
-            for (int v = 0; v < BV; v += 4)
-                st_shared_v4(aD32 + mn32_f32(tid, v, kC),
-                             tf32x4(u[v] - wsr[v], u[v + 1] - wsr[v + 1], u[v + 2] - wsr[v + 2], u[v + 3] - wsr[v + 3]));
-        }
-        fence_async_smem();
-        tc_fence_before();
-        if (__syncthreads_or(!ok)) {
-            aborted = true;
-            break;
-        }
-        if (tid == 0) {
-            ok = mbar_wait(fullB, c & 1);
-            if (ok) {
-                b_landed = c;
-                tc_fence_after();
-                mma_ct<kTF32, true, true, kC, kC, kC, 128, BV>(t_up, aKB, aD32, false);     // (tail K)^T Delta
-                mma_ct<kTF32, false, true, kC, 128, kC, 128, BV>(t_acc, aA2, aD32, true);   // += [0 ; P] Delta
-                mma_commit(mma2);
-            }
-        }
-        if (warp >= 2 && c + 1 < nch) build_gq(c + 1);  // rows 64-127 of [W ; G Q] are free since MMA1
-        ok = __syncthreads_and(ok) && mbar_wait(fullB, c & 1) && mbar_wait(mma2, c & 1);
-        tc_fence_after();
-        const float gc = *reinterpret_cast<const float*>(sm + SM::kVec + (c & 1) * 512 + 64 * 4);
-        if (tid == 0 && c + 1 < nch) issue_B(c + 1);  // tail K and P are free again; G goes to the other half
-        if (c + 1 < nch) b_issued = c + 1;
-        {  // epi B: state column k = tid; warps 2-3 also store the outputs of token tid - 64
-#pragma unroll
-            for (int c0 = 0; c0 < BV; c0 += 32) {
-                float a[32];
-                tmem_ld32(taddr(t_up, 32 * warp, c0), a);
-                tmem_wait_ld();
-#pragma unroll
-                for (int v = 0; v < 32; ++v) S[c0 + v] = fmaf(gc, S[c0 + v], a[v]);
-            }
-            write_state_image();
-            if (warp >= 2) {
-                const int i = tid - 64;
-                const int tok = kC * c + i;
 #pragma unroll
                 for (int c0 = 0; c0 < BV; c0 += 32) {
-                    float o[32];
-                    tmem_ld32(taddr(t_acc, 32 * warp, c0), o);
+                    tmem_ld32(taddr(t_accS, 32 * warp, c0), a);
                     tmem_wait_ld();
-                    if (tok < len) {
-                        __nv_bfloat16* dst = out + ((t0 + tok) * kHV + h) * kD + v0 + c0;
 #pragma unroll
-                        for (int v = 0; v < 32; v += 8) {
-                            __nv_bfloat162 w[4];
-#pragma unroll
-                            for (int e = 0; e < 4; ++e)
-                                w[e] = __floats2bfloat162_rn(p.scale * o[v + 2 * e], p.scale * o[v + 2 * e + 1]);
-                            *reinterpret_cast<uint4*>(dst + v) = *reinterpret_cast<uint4*>(w);
-                        }
+                    for (int v = 0; v < 32; ++v) S[c0 + v] = a[v] + Dn[c0 + v];
+                }
+            }
+            if (c + 1 < nch) {
+                write_state_image((c + 1) & 1);
+                load_D(c + 1);
+            }
+            fence_async_smem();
+            tc_fence_before();
+            if (named_sync_or(1, 128, !ok)) {
+                aborted = true;
+                break;
+            }
+            if (tid == 0) {  // refill: M of chunk c+2 (MMA_S(c) done), [Qt | Ut] of chunk c+2
+                tc_fence_after();
+                if (c + 2 < nch) {
+                    issue_M(c + 2);
+                    m_issued = c + 2;
+                    if (c >= 1 && !mbar_wait(quFree((c + 2) % 3), ((c - 1) / 3) & 1)) {
+                        ok = false;  // caught by the next chunk's barrier
+                    } else {
+                        issue_QU(c + 2);
+                        q_issued = c + 2;
                     }
                 }
             }
         }
-        fence_async_smem();
-        tc_fence_before();
-        if (__syncthreads_or(!ok)) {
-            aborted = true;
-            break;
+        if (tid == 0) {
+            if (aborted) {
+                record_status(32 /* GDN_ERR_DEVICE_TIMEOUT */);
+                for (int cc = m_waited + 1; cc <= m_issued; ++cc) mbar_wait(fullM(cc & 1), (cc >> 1) & 1);
+                for (int cc = q_waited + 1; cc <= q_issued; ++cc) mbar_wait(fullQ(cc % 3), (cc / 3) & 1);
+            }
+        }
+        float* ns_col = p.new_state + (unit * kD + v0) * kD + k;
+#pragma unroll
+        for (int v = 0; v < BV; ++v) ns_col[v * kD] = S[v];
+    } else {
+        // output warps: token i = 16 (warp - 4) + lane (lanes 0-15) of each chunk
+        const int ow = warp - 4;
+        const int i = 16 * ow + (lane & 15);
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
+        for (int c = 0; c < nch; ++c) {
+            bool okc = mbar_wait(mmaO(c & 1), (c >> 1) & 1) && mbar_wait(fullQ(c % 3), (c / 3) & 1);
+            tc_fence_after();
+            const int tok = kC * c + i;
+            const uint32_t ut = aQU + (c % 3) * kCarQUBytes + kQtImg + (i & 63) * 128;
+#pragma unroll
+            for (int c0 = 0; c0 < BV; c0 += 32) {
+                float o[32];
+                tmem_ld32(taddr(t_accO(c & 1), 32 * ow, c0), o);
+                tmem_wait_ld();
+                if (okc && lane < 16 && tok < len) {
+                    __nv_bfloat16* dst = out + ((t0 + tok) * kHV + h) * kD + v0 + c0;
+#pragma unroll
+                    for (int v = 0; v < 32; v += 8) {
+                        float u[8];
+                        h16x8_to_f32(ld_shared_u4(ut + (c0 + v) * 2), u);
+                        __nv_bfloat162 w[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            w[e] = __floats2bfloat162_rn(p.scale * (o[v + 2 * e] + u[2 * e]),
+                                                         p.scale * (o[v + 2 * e + 1] + u[2 * e + 1]));
+                        *reinterpret_cast<uint4*>(dst + v) = *reinterpret_cast<uint4*>(w);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(oFree(c & 1));
+                mbar_arrive(quFree(c % 3));
+            }
+            if (!okc) {
+                if (lane == 0) record_status(32);
+                break;
+            }
         }
     }
-    if (aborted && tid == 0) {
-        record_status(32 /* GDN_ERR_DEVICE_TIMEOUT */);
-        // drain the operand loads still in flight before the CTA exits
-        for (int cc = a_landed + 1; cc <= a_issued; ++cc) mbar_wait(fullA, cc & 1);
-        for (int cc = b_landed + 1; cc <= b_issued; ++cc) mbar_wait(fullB, cc & 1);
-    }
-#pragma unroll
-    for (int v = 0; v < BV; ++v) ns_col[v * kD] = S[v];
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tm, SM::kTmemCols);
+        tmem_dealloc(tm, kCarTmemCols);
     }
 }
 
@@ -782,20 +873,10 @@ cudaError_t launch_prefill_chunked(const PrefillParams& p, void* workspace, cuda
     if (L.R > 0x7fffffffLL) return cudaErrorInvalidValue;
     gdn_chunk_prepare_kernel<<<dim3(static_cast<unsigned>(L.R), kHQK), 128, kPrepSmem, stream>>>(p, ws, L);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    // value-row tile: 64 rows (two CTAs per head) once that still fills the SMs, else 32
-    if (p.num_seqs * kHV * (kD / 64) >= kSmCount) {
-        using SM = CarrySmem<64>;
-        if ((e = set_smem(gdn_chunk_carry_kernel<64>, SM::kTotal)) != cudaSuccess) return e;
-        const int64_t grid = p.num_seqs * kHV * (kD / 64);
-        if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
-        gdn_chunk_carry_kernel<64><<<static_cast<unsigned>(grid), 128, SM::kTotal, stream>>>(p, ws, L);
-    } else {
-        using SM = CarrySmem<32>;
-        if ((e = set_smem(gdn_chunk_carry_kernel<32>, SM::kTotal)) != cudaSuccess) return e;
-        const int64_t grid = p.num_seqs * kHV * (kD / 32);
-        if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
-        gdn_chunk_carry_kernel<32><<<static_cast<unsigned>(grid), 128, SM::kTotal, stream>>>(p, ws, L);
-    }
+    if ((e = set_smem(gdn_chunk_carry_kernel, kCarSmem)) != cudaSuccess) return e;
+    const int64_t grid = p.num_seqs * kHV * (kD / kCarryBV);
+    if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
+    gdn_chunk_carry_kernel<<<static_cast<unsigned>(grid), kCarryThreads, kCarSmem, stream>>>(p, ws, L);
     return cudaGetLastError();
 }
 
