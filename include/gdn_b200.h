@@ -151,7 +151,7 @@ int gdn_prefill_launch(const GdnPrefillArgs* args, void* workspace, size_t works
  * GPU that loads the library until the process exits; nothing is allocated.
  * Limit: unless args->path is GDN_PREFILL_PATH_RECURRENT, problems with
  * gdn_prefill_workspace_size(T, N) > GDN_NOALLOC_SCRATCH_BYTES are rejected
- * with GDN_ERR_WORKSPACE before anything runs (about 1,900 tokens for one
+ * with GDN_ERR_WORKSPACE before anything runs (about 2,600 tokens for one
  * sequence with the current workspace layout).  The first call on each device
  * looks up the array's device address; make it before any stream capture.
  * All calls on a device share the array: calls whose kernels overlap on the

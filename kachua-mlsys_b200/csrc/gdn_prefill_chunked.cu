@@ -38,6 +38,9 @@
 // Precision: tensor-core operands are fp16 (round-to-nearest, 11-bit
 // significand like tf32) with fp32 accumulation; the state and D stay fp32
 // between chunks, and only the MMA's copy of the state is rounded.
+#include <cudaTypedefs.h>  // PFN_cuTensorMapEncodeTiled
+#include <string.h>
+
 #include "gdn_common.cuh"
 #include "tc05.cuh"
 
@@ -45,11 +48,14 @@ namespace gdn {
 using namespace tc05;
 
 constexpr int kC = 64;
-constexpr int kMImg = kD * kD * 2;        // f16 M K-major [128 k][128 k']        32 KiB
-constexpr int kDBytes = kD * kD * 4;       // fp32 D rows [128 k][128 v]            64 KiB
-constexpr int kQtImg = kC * kD * 2;        // f16 Qt K-major [64 i][128 k]           16 KiB
-constexpr int kUtBytes = kC * kD * 2;      // f16 Ut [2 halves][64 i][64 v]          16 KiB
-constexpr int kRecordBytes = kHV * (kMImg + kDBytes + kQtImg + kUtBytes);
+// Per (chunk record, v-head) the prepare kernel leaves 96 KiB of f16 operand
+// images for the carry, at these offsets:
+constexpr int kRecM = 0;          // M = G_C I - K'^T W   [128 k][128 k']  K-major SW128        32 KiB
+constexpr int kRecKb = 32768;     // K' = tail (.) K      [64 j][128 k]    MN-major (2 kblocks) 16 KiB
+constexpr int kRecU = 49152;      // U                    [64 j][128 v]    MN-major (2 blocks)  16 KiB
+constexpr int kRecQt = 65536;     // Qt = G (.) Q - P W   [64 i][128 k]    K-major              16 KiB
+constexpr int kRecUt = 81920;     // Ut = P U             [64 i][128 v]    SW128 rows (2 blocks) 16 KiB
+constexpr int kHeadRecBytes = 98304;
 
 __host__ __device__ inline int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
 
@@ -57,7 +63,7 @@ __host__ __device__ inline int64_t align_up(int64_t x, int64_t a) { return (x + 
 // per-record, per-head operand arrays (every array 1024-byte aligned).
 struct WsLayout {
     int64_t R;  // record capacity: ceil(T / 64) + N bounds sum_s ceil(len_s / 64)
-    int64_t off_hdr, off_base, off_table, off_m, off_d, off_qt, off_ut, total;
+    int64_t off_hdr, off_base, off_table, off_rec, total;
 };
 
 __host__ __device__ inline WsLayout ws_layout(int64_t T, int64_t N) {
@@ -70,14 +76,8 @@ __host__ __device__ inline WsLayout ws_layout(int64_t T, int64_t N) {
     o = align_up(o + 4 * (N + 1), 1024);
     L.off_table = o;
     o = align_up(o + 16 * L.R, 1024);
-    L.off_m = o;
-    o += L.R * kHV * kMImg;
-    L.off_d = o;
-    o += L.R * kHV * kDBytes;
-    L.off_qt = o;
-    o += L.R * kHV * kQtImg;
-    L.off_ut = o;
-    o += L.R * kHV * kUtBytes;
+    L.off_rec = o;
+    o += L.R * kHV * kHeadRecBytes;
     L.total = align_up(o, 1024);
     return L;
 }
@@ -148,32 +148,34 @@ __global__ void __launch_bounds__(1024) gdn_chunk_table_kernel(const PrefillPara
 }
 
 // ---------------------------------------------------------------- prepare --
-// One CTA (128 threads) per chunk record and q/k head.  Everything the carry
-// kernel's state chain does not need is finished here, in fp16 operand images
-// (round-to-nearest; fp32 accumulation), per v-head h:
-//   M  = G_C I - (tail K)^T W          [k][k']  fp16 K-major  (the carry's A operand)
-//   D  = (tail K)^T U                  [k][v]   fp32 rows
-//   Qt = G (.) Q - P W                 [i][k]   fp16 K-major  (the output MMA's A operand)
-//   Ut = P U                           [i][v]   fp16, two 64-column halves
-// so that one chunk of the carry is S1 = S0 M^T + D and O = scale (Qt S0^T + Ut).
-// The two v-heads of the q/k head share every M=64 accumulator (head 0 in TMEM
-// lanes 0-15, head 1 in lanes 16-31 of each warp's sub-partition); in those
-// epilogues thread (warp w, lane l) owns row 16w + (l & 15) of head l >> 4.
-constexpr int kPrepKQ = 0;          // bf16 [K;Q] K-major, 2 kblocks x 128 rows                 32 KiB
-constexpr int kPrepX = 0;           // f16 X_h K-major [64][64] (Neumann iterate -> A^-1), over KQ  2 x 8 KiB
-constexpr int kPrepPA = 16384;      // f16 power P_h K-major [64][64]                              2 x 8 KiB
-constexpr int kPrepPB = 32768;      // f16 power P_h MN-major                                      2 x 8 KiB
-constexpr int kPrepPO = 49152;      // f16 output-side P_h K-major [64 i][64 j]                    2 x 8 KiB
-constexpr int kPrepRHS = 65536;     // f16 [beta G K | beta V] MN-major [64 j][256] -> then [W | U]  32 KiB
-constexpr int kPrepKB = 16384;      // f16 tail K MN-major [64 j][128 k] over PA/PB (after Neumann) 16 KiB
-constexpr int kPrepSmall = 98304;
-constexpr int kPrepSmem = kPrepSmall + 2048 + 1024;
-constexpr int kPrepTmemCols = 256;
+// One CTA (128 threads) per chunk record and v-head: everything the carry's
+// chain does not need, finished per chunk in fp16 operand images (fp32
+// accumulation) and bulk-stored to the workspace:
+//   M   = G_C I - K'^T W    [k][k']   K-major        (A of the state MMA)
+//   K'  = tail (.) K        [j][k]    MN-major       (A of the carry's D = K'^T U)
+//   U                       [j][v]    MN-major, two 64-column blocks
+//   Qt  = G (.) Q - P W     [i][k]    K-major        (A of the output MMA)
+//   Ut  = P U               [i][v]    SW128 rows, two 64-column blocks
+// K, Q and V arrive by tiled TMA loads straight into SW128 images (rows past
+// the chunk hold the next tokens or zeros; every use masks them).  A^-1 comes
+// from an fp32 forward substitution ((I + N) x = e_j, one column per thread);
+// W | U = A^-1 [bGK | bV] and the products with P and K' run on tcgen05 with
+// two M=64 results packed into TMEM lanes 0-15 / 16-31.
+constexpr int kPrepThreads = 128;
+constexpr int kPrKQ = 0;        // bf16 [K;Q] K-major, kblock b at b*16K (rows 0-63 K, 64-127 Q); K rows -> K' in place
+constexpr int kPrN = 32768;     // fp32 N [64][64], 16-byte chunks swizzled by (row & 15)  -> Ut staging
+constexpr int kPrPO = 49152;    // f16 P [64 i][64 j] K-major                              } -> Qt staging
+constexpr int kPrX = 57344;     // f16 A^-1 [64 i][64 m] K-major                           }
+constexpr int kPrRHS = 65536;   // f16 [bGK | bV] MN-major [64 j][256] (V by TMA) -> [W | U] -> M staging
+constexpr int kPrSmall = 98304;
+constexpr int kPrSmem = kPrSmall + 1024 + 1024;
+constexpr int kPrTmemCols = 256;
 
 struct PrepSmall {
-    float lg[2][kC];   // log2 g per token (0 for inactive rows)
-    float LG[2][kC];   // inclusive prefix of lg
-    float beta[2][kC];
+    float LG[kC];    // inclusive prefix of log2 g (0 past the chunk)
+    float beta[kC];  // 0 past the chunk
+    float wtot[4];
+    uint64_t bar_load;
     uint64_t bar_mma;
     uint32_t tmem_base;
 };
@@ -182,15 +184,7 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
     return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
-__device__ __forceinline__ void st_f32(uint8_t* img, uint32_t off, float v) {
-    *reinterpret_cast<float*>(img + off) = v;
-}
-
-__device__ __forceinline__ float4 tf32x4(float a, float b, float c, float d) {
-    return make_float4(to_tf32(a), to_tf32(b), to_tf32(c), to_tf32(d));
-}
-
-// 2^x on the SFU (ex2.approx: a couple of ulp); x <= 0 here, so no overflow.
+// 2^x on the SFU (ex2.approx: a couple of ulp); callers pass x <= 0 where the result is used.
 __device__ __forceinline__ float fast_exp2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -218,15 +212,6 @@ __device__ __forceinline__ uint4 f16x8(const float* f) {
     return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-__device__ __forceinline__ void st_shared_u4(uint32_t addr, uint4 v) {
-    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-                 : "memory");
-}
-__device__ __forceinline__ uint4 ld_shared_u4(uint32_t addr) {
-    uint4 v;
-    asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
-    return v;
-}
 __device__ __forceinline__ void h16x8_to_f32(uint4 u, float (&f)[8]) {
     const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
@@ -237,394 +222,343 @@ __device__ __forceinline__ void h16x8_to_f32(uint4 u, float (&f)[8]) {
     }
 }
 
+__device__ __forceinline__ void st_shared_u4(uint32_t addr, uint4 v) {
+    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+__device__ __forceinline__ uint4 ld_shared_u4(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ void st_f32(uint8_t* img, uint32_t off, float v) {
+    *reinterpret_cast<float*>(img + off) = v;
+}
+__device__ __forceinline__ void st_shared_u16(uint32_t addr, uint16_t v) {
+    asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"(v) : "memory");
+}
+
 // Offset of element (row, col) in a 16-bit SW128 image with `rows` rows per
 // 128-byte column block; the same formula serves K-major (row = M/N index)
-// and MN-major (row = K index) images.
+// and MN-major (row = K index) images, and the TMA SWIZZLE_128B box layout.
 __device__ __forceinline__ uint32_t h16(int row, int col, int rows) { return sw128_bf16(row, col, rows); }
 
-__global__ void __launch_bounds__(128, 2)
-    gdn_chunk_prepare_kernel(const PrefillParams p, uint8_t* __restrict__ ws, const WsLayout L) {
+// fp32 N image: row i is 256 bytes; its 16-byte chunk c sits at position c ^ (i & 15)
+__device__ __forceinline__ uint32_t n_off(int i, int m) { return i * 256 + ((((m >> 2) ^ (i & 15))) << 4); }
+
+__global__ void __launch_bounds__(kPrepThreads, 2)
+    gdn_chunk_prepare_kernel(const PrefillParams p, uint8_t* __restrict__ ws, const WsLayout L,
+                             const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
+                             const __grid_constant__ CUtensorMap tmV) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = align1024(smem_raw);
-    uint8_t* sKQ = sm + kPrepKQ;
-    PrepSmall& sml = *reinterpret_cast<PrepSmall*>(sm + kPrepSmall);
-    const uint32_t aKQ = smem_u32(sKQ), aX = smem_u32(sm + kPrepX), aPA = smem_u32(sm + kPrepPA),
-                   aPB = smem_u32(sm + kPrepPB), aPO = smem_u32(sm + kPrepPO), aRHS = smem_u32(sm + kPrepRHS),
-                   aKB = smem_u32(sm + kPrepKB);
+    PrepSmall& sml = *reinterpret_cast<PrepSmall*>(sm + kPrSmall);
+    const uint32_t aKQ = smem_u32(sm + kPrKQ), aN = smem_u32(sm + kPrN), aPO = smem_u32(sm + kPrPO),
+                   aX = smem_u32(sm + kPrX), aRHS = smem_u32(sm + kPrRHS);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t rec = blockIdx.x;
-    const int hq = blockIdx.y;
+    const int h = blockIdx.y, hq = h / kGva;
     const int nrec = reinterpret_cast<const int*>(ws + L.off_hdr)[0];
     if (rec >= nrec) return;
     const int4 te = reinterpret_cast<const int4*>(ws + L.off_table)[rec];
-    const int64_t t0 = te.y;
-    const int n = te.z;
+    const int t0 = te.y;  // first token (T < 2^31, checked on the host)
+    const int n = te.z;   // tokens in this chunk (1..64)
+    uint8_t* out_rec = ws + L.off_rec + (rec * kHV + h) * kHeadRecBytes;
 
-    const uint32_t bar = smem_u32(&sml.bar_mma);
+    const uint32_t barL = smem_u32(&sml.bar_load), barM = smem_u32(&sml.bar_mma);
     if (tid == 0) {
-        mbar_init(bar, 1);
+        mbar_init(barL, 1);
+        mbar_init(barM, 1);
         fence_mbar_init();
+        mbar_expect_tx(barL, 6 * 8192);
+        tma_load_3d(aKQ, &tmK, 0, hq, t0, barL);
+        tma_load_3d(aKQ + 16384, &tmK, 64, hq, t0, barL);
+        tma_load_3d(aKQ + 8192, &tmQ, 0, hq, t0, barL);
+        tma_load_3d(aKQ + 24576, &tmQ, 64, hq, t0, barL);
+        tma_load_3d(aRHS + 16384, &tmV, 0, h, t0, barL);
+        tma_load_3d(aRHS + 24576, &tmV, 64, h, t0, barL);
     }
-    if (warp == 0) {
-        tmem_alloc(smem_u32(&sml.tmem_base), kPrepTmemCols);
+    if (warp == 1) {
+        tmem_alloc(smem_u32(&sml.tmem_base), kPrTmemCols);
         tmem_relinquish();
     }
-
-    // 1. K and Q tiles -> [K;Q] bf16 image (rows >= n zero); gates of both v-heads
-#pragma unroll 4
-    for (int idx = tid; idx < 2 * kC * 16; idx += 128) {
-        const int m = idx >> 10;  // 0: K, 1: Q
-        const int row = (idx >> 4) & 63;
-        const int ch = idx & 15;  // 16-byte chunk of the 256-byte row
-        uint4 val = make_uint4(0, 0, 0, 0);
-        if (row < n) val = *reinterpret_cast<const uint4*>((m ? p.q : p.k) + ((t0 + row) * kHQK + hq) * kD + ch * 8);
-        const int r = 64 * m + row;
-        *reinterpret_cast<uint4*>(sKQ + (ch >> 3) * (128 * 128) + r * 128 + (((ch & 7) ^ (r & 7)) << 4)) = val;
-    }
-    {
-        const int hl = tid >> 6, i = tid & 63, h = 2 * hq + hl;
+    // gates and the inclusive prefix of log2 g (threads 0-63 = tokens; warp scans)
+    float lgs = 0.f;
+    if (tid < kC) {
         float lg = 0.f, bt = 0.f;
-        if (i < n) {
-            const int64_t t = t0 + i;
+        if (tid < n) {
+            const int64_t t = static_cast<int64_t>(t0) + tid;
             lg = gdn_log2_decay(p.A_log[h], p.dt_bias[h], bf16_bits_to_float(p.a[t * kHV + h]));
             bt = 1.0f / (1.0f + expf(-bf16_bits_to_float(p.b[t * kHV + h])));
         }
-        sml.lg[hl][i] = lg;
-        sml.beta[hl][i] = bt;
+        lgs = lg;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float y = __shfl_up_sync(0xffffffffu, lgs, o);
+            if (lane >= o) lgs += y;
+        }
+        if (lane == 31) sml.wtot[warp] = lgs;
+        sml.beta[tid] = bt;
     }
-    fence_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    if (tid >= 32 && tid < kC) lgs += sml.wtot[0];
+    if (tid < kC) sml.LG[tid] = lgs;
     const uint32_t tm = sml.tmem_base;
-    uint32_t phase = 0;
-    bool ok = true, aborted = false;
-    const int hl = lane >> 4;               // head of this thread in packed M=64 epilogues
-    const int row = 16 * warp + (lane & 15);  // its row there
-
-    // 2. Gram: rows 0-63 K K^T, rows 64-127 Q K^T (bf16, M=128, N=64, K=128)
-    if (tid == 0) {
-        mma_ct<kBF16, false, false, kD, 128, 128, 128, 64>(tm, aKQ, aKQ, false);
-        mma_commit(bar);
-    }
-    {  // inclusive prefix of log2 g (64 sequential adds; deterministic)
-        const int h2 = tid >> 6, i = tid & 63;
-        float acc = 0.f;
-        for (int m = 0; m <= i; ++m) acc += sml.lg[h2][m];
-        sml.LG[h2][i] = acc;
-    }
     __syncthreads();
-    ok = mbar_wait(bar, phase);
-    phase ^= 1;
+    bool ok = mbar_wait(barL, 0);
+
+    // 1. Gram [K;Q] K^T (bf16, M=128, N=64, K=128) -> TMEM columns 0-63
+    if (tid == 0 && ok) {
+        tc_fence_after();
+        mma_ct<kBF16, false, false, kD, 128, 128, 128, 64>(tm, aKQ, aKQ, false);
+        mma_commit(barM);
+    }
+    // meanwhile: [bGK | bV] in fp16 over the RHS (the scale depends on the row
+    // only, so 16-byte chunks convert in place of their swizzled position)
+#pragma unroll 4
+    for (int it = 0; it < 16; ++it) {
+        const int u = it * kPrepThreads + tid;
+        const int blk = u >> 9;  // 0, 1: K kblocks -> RHS columns 0-127; 2, 3: V blocks in place
+        const int row = (u >> 3) & 63;
+        const uint32_t in_row = row * 128 + (u & 7) * 16;
+        const uint32_t src = blk < 2 ? aKQ + blk * 16384 + in_row : aRHS + blk * 8192 + in_row;
+        const float sc = blk < 2 ? sml.beta[row] * fast_exp2(sml.LG[row]) : sml.beta[row];
+        const bool act = row < n;
+        float f[8];
+        bf16x8_to_f32(ld_shared_u4(src), f);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) f[q] = act ? sc * f[q] : 0.f;
+        st_shared_u4(aRHS + blk * 8192 + in_row, f16x8(f));
+    }
+    ok = mbar_wait(barM, 0) && ok;
     tc_fence_after();
-    __syncthreads();  // every thread is past the Gram MMA before X overwrites [K;Q]
     {
-        // 3. Gram epilogue (M=128 rows: thread = row).  Rows 0-63 build N, its
-        //    two operand copies and X = I - N of both heads; rows 64-127 the
-        //    output-side P = Gam (.) Q K^T (j <= i).
-        float gram[64];
+        // 2. Gram epilogue (thread = accumulator row): rows 0-63 give N (fp32),
+        //    rows 64-127 the output-side P = Gam (.) Q K^T, j <= i (f16 image)
+        float g[64];
         {
             float t32[32];
             tmem_ld32(taddr(tm, 32 * warp, 0), t32);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) gram[j] = t32[j];
+            for (int j = 0; j < 32; ++j) g[j] = t32[j];
             tmem_ld32(taddr(tm, 32 * warp, 32), t32);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) gram[32 + j] = t32[j];
             tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) g[32 + j] = t32[j];
         }
-        const int i = tid & 63;
+        if (warp < 2) {
+            const int i = tid;
+            const float LGi = sml.LG[i], bi = sml.beta[i];
+            const bool act = i < n;
+#pragma unroll
+            for (int j0 = 0; j0 < kC; j0 += 4) {
+                float nv[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int j = j0 + e;
+                    nv[e] = (j < i && act) ? bi * fast_exp2(LGi - sml.LG[j]) * g[j] : 0.f;
+                }
+                st_shared_v4(aN + n_off(i, j0), make_float4(nv[0], nv[1], nv[2], nv[3]));
+            }
+        } else {
+            const int i = tid - 64;
+            const float LGi = sml.LG[i];
+#pragma unroll
+            for (int j0 = 0; j0 < kC; j0 += 8) {
+                float pv[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const int j = j0 + e;
+                    pv[e] = (j <= i) ? fast_exp2(LGi - sml.LG[j]) * g[j] : 0.f;
+                }
+                st_shared_u4(aPO + h16(i, j0, 64), f16x8(pv));
+            }
+        }
+    }
+    tc_fence_before();
+    if (__syncthreads_or(!ok)) goto abort;
+    if (warp < 2) {
+        // 3a. A^-1 = (I + N)^-1 by forward substitution, column j = tid, fp32
+        //     (eight independent partial sums per row keep the FMA chains short)
+        const int j = tid;
+        float x[kC];
+#pragma unroll
+        for (int i = 0; i < kC; ++i) {
+            float a[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) a[e] = 0.f;
+            a[0] = (i == j) ? 1.f : 0.f;
+#pragma unroll
+            for (int m0 = 0; m0 < i; m0 += 4) {
+                const float4 nv = ld_shared_v4(aN + n_off(i, m0));
+                const int s = ((m0 >> 2) & 1) * 4;
+                a[s + 0] = fmaf(-nv.x, x[m0], a[s + 0]);
+                if (m0 + 1 < i) a[s + 1] = fmaf(-nv.y, x[m0 + 1], a[s + 1]);
+                if (m0 + 2 < i) a[s + 2] = fmaf(-nv.z, x[m0 + 2], a[s + 2]);
+                if (m0 + 3 < i) a[s + 3] = fmaf(-nv.w, x[m0 + 3], a[s + 3]);
+            }
+            x[i] = ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
+        }
+#pragma unroll
+        for (int i = 0; i < kC; ++i) st_shared_u16(aX + h16(i, j, 64), __half_as_ushort(__float2half_rn(x[i])));
+    } else {
+        // 3b. K' = tail (.) K in place over the K rows of [K;Q] (rows >= n zero)
+        const float LGc = sml.LG[kC - 1];
+#pragma unroll 4
+        for (int it = 0; it < 16; ++it) {
+            const int u = it * 64 + (tid - 64);
+            const int kb = u >> 9, row = (u >> 3) & 63;
+            const uint32_t addr = aKQ + kb * 16384 + row * 128 + (u & 7) * 16;
+            const float sc = fast_exp2(LGc - sml.LG[row]);
+            const bool act = row < n;
+            float f[8];
+            bf16x8_to_f32(ld_shared_u4(addr), f);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) f[q] = act ? sc * f[q] : 0.f;
+            st_shared_u4(addr, f16x8(f));
+        }
+    }
+    fence_async_smem();
+    __syncthreads();
+    if (tid == 0) {  // 4. W | U = A^-1 [bGK | bV]: W -> lanes 0-15, U -> lanes 16-31 (columns 0-127)
+        tc_fence_after();
+        mma_ct<kF16, false, true, 64, 64, 64, 64, 128>(taddr(tm, 0, 0), aX, aRHS, false);
+        mma_ct<kF16, false, true, 64, 64, 64, 64, 128>(taddr(tm, 16, 0), aX, aRHS + 16384, false);
+        mma_commit(barM);
+        bulk_s2g(out_rec + kRecKb, aKQ, 8192);  // K' (final): two 8 KiB kblocks
+        bulk_s2g(out_rec + kRecKb + 8192, aKQ + 16384, 8192);
+        bulk_commit();
+    }
+    ok = mbar_wait(barM, 1) && ok;
+    tc_fence_after();
+    {  // W | U rows -> fp16 MN-major B image over the RHS (W columns 0-127, U 128-255)
+        const int i = 16 * warp + (lane & 15);
+        const uint32_t dst = aRHS + (lane >= 16 ? 16384 : 0);
 #pragma unroll 1
-        for (int h2 = 0; h2 < 2; ++h2) {
-            const float LGi = sml.LG[h2][i];
-            if (tid < 64) {
-                const float bi = sml.beta[h2][i];
+        for (int c = 0; c < 4; ++c) {
+            float acc[32];
+            tmem_ld32(taddr(tm, 32 * warp, 32 * c), acc);
+            tmem_wait_ld();
 #pragma unroll
-                for (int j0 = 0; j0 < 64; j0 += 8) {
-                    float nv[8], xv[8];
+            for (int j0 = 0; j0 < 32; j0 += 8) st_shared_u4(dst + h16(i, 32 * c + j0, 64), f16x8(acc + j0));
+        }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    if (__syncthreads_or(!ok)) goto abort;
+    if (tid == 0) {  // 5. P W -> lanes 0-15, P U -> lanes 16-31 (columns 0-127); K'^T W (M=128) -> columns 128-255
+        tc_fence_after();
+        mma_ct<kF16, false, true, 64, 64, 64, 64, 128>(taddr(tm, 0, 0), aPO, aRHS, false);
+        mma_ct<kF16, false, true, 64, 64, 64, 64, 128>(taddr(tm, 16, 0), aPO, aRHS + 16384, false);
+        mma_ct<kF16, true, true, 64, 128, 64, 128, 128>(taddr(tm, 0, 128), aKQ, aRHS, false);
+        mma_commit(barM);
+        bulk_s2g(out_rec + kRecU, aRHS + 16384, 16384);  // U: two 64-column MN-major blocks
+        bulk_commit();
+    }
+    ok = mbar_wait(barM, 0) && ok;
+    if (tid == 0) bulk_wait_read_all();  // U and K' have left shared memory before it is reused
+    tc_fence_after();
+    if (__syncthreads_or(!ok)) goto abort;
+    {
+        // 6a. Qt = G (.) Q - P W (lanes 0-15) and Ut = P U (lanes 16-31), row i
+        const int i = 16 * warp + (lane & 15);
+        const bool act = i < n;
+        const float Gi = fast_exp2(sml.LG[i]);
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+            float acc[32];
+            tmem_ld32(taddr(tm, 32 * warp, 32 * c), acc);
+            tmem_wait_ld();
+            if (lane < 16) {
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const int j = j0 + e;
-                        nv[e] = (j < i) ? bi * fast_exp2(LGi - sml.LG[h2][j]) * gram[j] : 0.f;
-                        xv[e] = (j == i ? 1.f : 0.f) - nv[e];
-                    }
-                    const uint4 nh = f16x8(nv);
-                    st_shared_u4(aPA + h2 * 8192 + h16(i, j0, 64), nh);
-                    st_shared_u4(aPB + h2 * 8192 + h16(i, j0, 64), nh);
-                    st_shared_u4(aX + h2 * 8192 + h16(i, j0, 64), f16x8(xv));
+                for (int j0 = 0; j0 < 32; j0 += 8) {
+                    const int col = 32 * c + j0;
+                    float qf[8];
+                    bf16x8_to_f32(ld_shared_u4(aKQ + h16(64 + i, col, 128)), qf);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) qf[q] = act ? Gi * qf[q] - acc[j0 + q] : 0.f;
+                    st_shared_u4(aPO + h16(i, col, 64), f16x8(qf));  // Qt staging over P and A^-1
                 }
             } else {
 #pragma unroll
-                for (int j0 = 0; j0 < 64; j0 += 8) {
-                    float pv[8];
+                for (int j0 = 0; j0 < 32; j0 += 8) {
+                    const int col = 32 * c + j0;
+                    float uf[8];
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const int j = j0 + e;
-                        pv[e] = (j <= i) ? fast_exp2(LGi - sml.LG[h2][j]) * gram[j] : 0.f;
-                    }
-                    st_shared_u4(aPO + h2 * 8192 + h16(i, j0, 64), f16x8(pv));
+                    for (int q = 0; q < 8; ++q) uf[q] = act ? acc[j0 + q] : 0.f;
+                    st_shared_u4(aN + (col >> 6) * 8192 + h16(i, col & 63, 64), f16x8(uf));  // Ut staging over N
                 }
+            }
+        }
+        // 6b. M = G_C I - K'^T W, row k = tid (f16 K-major, staging over the RHS)
+        const float Gc = fast_exp2(sml.LG[kC - 1]);
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+            float acc[32];
+            tmem_ld32(taddr(tm, 32 * warp, 128 + 32 * c), acc);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j0 = 0; j0 < 32; j0 += 8) {
+                float f[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) f[q] = (32 * c + j0 + q == tid ? Gc : 0.f) - acc[j0 + q];
+                st_shared_u4(aRHS + h16(tid, 32 * c + j0, 128), f16x8(f));
             }
         }
     }
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
-    if (tid == 0) {  // Neumann round 0: N_h^2 for both heads (lanes 16 h, columns 64-127)
-        tc_fence_after();
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-            mma_ct<kF16, false, true, 64, 64, 64, 64, 64>(taddr(tm, 16 * h, 64), aPA + h * 8192, aPB + h * 8192,
-                                                         false);
-        mma_commit(bar);
+    if (tid == 0) {
+        bulk_s2g(out_rec + kRecQt, aPO, 16384);
+        bulk_s2g(out_rec + kRecUt, aN, 16384);
+        bulk_s2g(out_rec + kRecM, aRHS, 32768);
+        bulk_commit();
+        bulk_wait_all();
     }
-    // 4. Neumann doubling, both heads packed: epilogue e updates X (e >= 1) and P (e <= 4)
-    for (int e = 0; e <= 5; ++e) {
-        ok = mbar_wait(bar, phase);
-        phase ^= 1;
-        tc_fence_after();
-        if (e >= 1) {
-            const uint32_t xa = aX + hl * 8192;
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                float xp[32];
-                tmem_ld32(taddr(tm, 32 * warp, 32 * half), xp);
-                tmem_wait_ld();
-#pragma unroll
-                for (int j0 = 0; j0 < 32; j0 += 8) {
-                    const uint32_t off = xa + h16(row, 32 * half + j0, 64);
-                    float x[8];
-                    h16x8_to_f32(ld_shared_u4(off), x);
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) x[q] += xp[j0 + q];
-                    st_shared_u4(off, f16x8(x));
-                }
-            }
-        }
-        if (e <= 4) {
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                float pp[32];
-                tmem_ld32(taddr(tm, 32 * warp, 64 + 32 * half), pp);
-                tmem_wait_ld();
-#pragma unroll
-                for (int j0 = 0; j0 < 32; j0 += 8) {
-                    const uint4 t = f16x8(pp + j0);
-                    st_shared_u4(aPA + hl * 8192 + h16(row, 32 * half + j0, 64), t);
-                    st_shared_u4(aPB + hl * 8192 + h16(row, 32 * half + j0, 64), t);
-                }
-            }
-        }
-        fence_async_smem();
-        tc_fence_before();
-        if (__syncthreads_or(!ok)) {
-            aborted = true;
-            goto done;
-        }
-        if (tid == 0 && e <= 4) {
-            tc_fence_after();
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                mma_ct<kF16, false, true, 64, 64, 64, 64, 64>(taddr(tm, 16 * h, 0), aX + h * 8192, aPB + h * 8192,
-                                                             false);  // X P
-                if (e <= 3)
-                    mma_ct<kF16, false, true, 64, 64, 64, 64, 64>(taddr(tm, 16 * h, 64), aPA + h * 8192,
-                                                                 aPB + h * 8192, false);  // P P
-            }
-            mma_commit(bar);
-        }
-    }
-    // 5. per head: [beta G K | beta V] and tail K, then [W | U] = A^-1 [..], then
-    //    P [W | U] and (tail K)^T [W | U]; results straight to the workspace
-#pragma unroll 1
-    for (int h2 = 0; h2 < 2; ++h2) {
-        const int h = 2 * hq + h2;
-        const int64_t rh = rec * kHV + h;
-        {
-            const int j = tid & 63, part = tid >> 6;
-            const float LGj = sml.LG[h2][j], bj = sml.beta[h2][j];
-            const float Gj = exp2f(LGj), tail = exp2f(sml.LG[h2][63] - LGj);
-            const bool act = j < n;
-            if (part == 0) {  // K row j: beta G K -> RHS columns 0-127, tail K -> K-bar
-                const uint16_t* ksrc = p.k + ((t0 + j) * kHQK + hq) * kD;
-                const float s = bj * Gj;
-#pragma unroll 4
-                for (int d0 = 0; d0 < kD; d0 += 8) {
-                    float f[8], a[8], b[8];
-                    bf16x8_to_f32(act ? *reinterpret_cast<const uint4*>(ksrc + d0) : make_uint4(0, 0, 0, 0), f);
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) a[q] = s * f[q], b[q] = tail * f[q];
-                    st_shared_u4(aRHS + h16(j, d0, 64), f16x8(a));
-                    st_shared_u4(aKB + h16(j, d0, 64), f16x8(b));
-                }
-            } else {  // V row j: beta V -> RHS columns 128-255
-                const uint16_t* vsrc = p.v + ((t0 + j) * kHV + h) * kD;
-#pragma unroll 4
-                for (int d0 = 0; d0 < kD; d0 += 8) {
-                    float f[8], a[8];
-                    bf16x8_to_f32(act ? *reinterpret_cast<const uint4*>(vsrc + d0) : make_uint4(0, 0, 0, 0), f);
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) a[q] = bj * f[q];
-                    st_shared_u4(aRHS + h16(j, 128 + d0, 64), f16x8(a));
-                }
-            }
-        }
-        fence_async_smem();
-        tc_fence_before();
-        __syncthreads();
-        if (tid == 0) {
-            tc_fence_after();
-            mma_ct<kF16, false, true, 64, 64, 64, 64, 256>(tm, aX + h2 * 8192, aRHS, false);  // [W | U], lanes 0-15
-            mma_commit(bar);
-        }
-        ok = mbar_wait(bar, phase);
-        phase ^= 1;
-        tc_fence_after();
-        // [W | U] rows (lanes 0-15: this head) -> fp16 MN-major B image over the RHS;
-        // every lane takes part in the (warp-collective) TMEM loads
-#pragma unroll 1
-        for (int c = 0; c < 8; ++c) {
-            float acc[32];
-            tmem_ld32(taddr(tm, 32 * warp, 32 * c), acc);
-            tmem_wait_ld();
-            if ((lane & 16) == 0) {
-#pragma unroll
-                for (int j0 = 0; j0 < 32; j0 += 8) st_shared_u4(aRHS + h16(row, 32 * c + j0, 64), f16x8(acc + j0));
-            }
-        }
-        fence_async_smem();
-        tc_fence_before();
-        if (__syncthreads_or(!ok)) {
-            aborted = true;
-            goto done;
-        }
-        if (tid == 0) {  // P [W | U] (M=64, lanes 0-15, columns 0-255)
-            tc_fence_after();
-            mma_ct<kF16, false, true, 64, 64, 64, 64, 256>(tm, aPO + h2 * 8192, aRHS, false);
-            mma_commit(bar);
-        }
-        ok = mbar_wait(bar, phase);
-        phase ^= 1;
-        tc_fence_after();
-        {  // Qt = G (.) Q - P W and Ut = P U (rows i = row, lanes 0-15)
-            const float Gi = exp2f(sml.LG[h2][row & 63]);
-            const bool act = (row & 63) < n;
-            const uint16_t* qsrc = p.q + ((t0 + (row & 63)) * kHQK + hq) * kD;
-            uint8_t* gqt = ws + L.off_qt + rh * kQtImg;
-            uint16_t* gut = reinterpret_cast<uint16_t*>(ws + L.off_ut + rh * kUtBytes);
-#pragma unroll 1
-            for (int c = 0; c < 8; ++c) {
-                float acc[32];
-                tmem_ld32(taddr(tm, 32 * warp, 32 * c), acc);
-                tmem_wait_ld();
-                if ((lane & 16) == 0) {
-                    if (c < 4) {
-#pragma unroll
-                        for (int j0 = 0; j0 < 32; j0 += 8) {
-                            float f[8];
-                            bf16x8_to_f32(act ? *reinterpret_cast<const uint4*>(qsrc + 32 * c + j0)
-                                              : make_uint4(0, 0, 0, 0),
-                                          f);
-#pragma unroll
-                            for (int q = 0; q < 8; ++q) f[q] = Gi * f[q] - acc[j0 + q];
-                            *reinterpret_cast<uint4*>(gqt + h16(row, 32 * c + j0, 64)) = f16x8(f);
-                        }
-                    } else {  // Ut: [half][i][64] with half = value column / 64
-                        const int v = 32 * (c - 4);
-#pragma unroll
-                        for (int j0 = 0; j0 < 32; j0 += 8)
-                            *reinterpret_cast<uint4*>(gut + ((v + j0) >> 6) * (kC * 64) + row * 64 + ((v + j0) & 63)) =
-                                f16x8(acc + j0);
-                    }
-                }
-            }
-        }
-        tc_fence_before();
-        __syncthreads();
-        if (tid == 0) {  // (tail K)^T [W | U] (M=128: rows = state column k)
-            tc_fence_after();
-            mma_ct<kF16, true, true, 64, 64, 64, 128, 256>(tm, aKB, aRHS, false);
-            mma_commit(bar);
-        }
-        ok = mbar_wait(bar, phase);
-        phase ^= 1;
-        tc_fence_after();
-        {  // M = G_C I - (tail K)^T W (row k = tid, fp16 K-major) and D = (tail K)^T U (fp32 rows)
-            const float Gc = exp2f(sml.LG[h2][63]);
-            uint8_t* gm = ws + L.off_m + rh * kMImg;
-            float* gd = reinterpret_cast<float*>(ws + L.off_d + rh * kDBytes) + tid * kD;
-#pragma unroll 1
-            for (int c = 0; c < 8; ++c) {
-                float acc[32];
-                tmem_ld32(taddr(tm, 32 * warp, 32 * c), acc);
-                tmem_wait_ld();
-                if (c < 4) {
-#pragma unroll
-                    for (int j0 = 0; j0 < 32; j0 += 8) {
-                        float f[8];
-#pragma unroll
-                        for (int q = 0; q < 8; ++q) f[q] = (32 * c + j0 + q == tid ? Gc : 0.f) - acc[j0 + q];
-                        *reinterpret_cast<uint4*>(gm + h16(tid, 32 * c + j0, 128)) = f16x8(f);
-                    }
-                } else {
-#pragma unroll
-                    for (int j0 = 0; j0 < 32; j0 += 4)
-                        *reinterpret_cast<float4*>(gd + 32 * (c - 4) + j0) =
-                            make_float4(acc[j0], acc[j0 + 1], acc[j0 + 2], acc[j0 + 3]);
-                }
-            }
-        }
-        tc_fence_before();
-        if (__syncthreads_or(!ok)) {
-            aborted = true;
-            goto done;
-        }
+    goto done;
+abort:
+    if (tid == 0) {
+        record_status(32 /* GDN_ERR_DEVICE_TIMEOUT */);
+        mbar_wait(barL, 0);  // the input loads may still be in flight (bounded)
+        bulk_wait_all();
     }
 done:
-    if (tid == 0 && aborted) record_status(32 /* GDN_ERR_DEVICE_TIMEOUT */);
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) {
+    if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(sml.tmem_base, kPrepTmemCols);
+        tmem_dealloc(tm, kPrTmemCols);
     }
 }
 
 // ------------------------------------------------------------------ carry --
-// One CTA (256 threads) per sequence x v-head x 64 value rows.  The state
-// chain needs one tensor-core MMA per chunk:
-//   S_{c+1}^T = M_c S_c^T + D_c^T      (M fp16 K-major, S fp16 MN-major, fp32 accumulate)
-// Warps 0-3 own the state (thread k = column k of the 64 rows, fp32 registers):
-// they add D_c (prefetched one chunk ahead) to the accumulator and write the
-// next fp16 state image.  Warps 4-7 finish the outputs off the critical path:
-//   O_c = scale (Qt_c S_c^T + Ut_c)    (Qt fp16 K-major; the MMA reads the same state image)
-// Thread 0 issues every MMA and bulk copy.  M is double-buffered and
-// [Qt | Ut] triple-buffered, each refilled as soon as its readers are done,
-// so the copies run a chunk or more ahead of use.
+// One CTA per sequence x v-head x 64 value rows; the chunk-to-chunk chain
+//   S_{c+1}^T = K'_c^T U_c + M_c S_c^T
+// is one 12-instruction accumulation per chunk (the K'^T U part issued a chunk
+// early into the second accumulator).  Warp roles:
+//   warp 8 (one thread)  issues every MMA and bulk copy;
+//   warps 0-3 (state)    read the accumulator (thread k = state column k),
+//                        write the next fp16 state image, and at the end the
+//                        fp32 final state;
+//   warps 4-7 (output)   O_c = scale (Qt_c S_c^T + Ut_c) from a second MMA on
+//                        the same state image, overlapped with the next chunk.
+// M is double-buffered, [K' | U] and Qt triple-buffered, each refilled once
+// the MMA that read it is known complete, two chunks before use.
 constexpr int kCarryBV = 64;
-constexpr int kCarryThreads = 256;
-constexpr int kCarMI = 0;                         // f16 M K-major [128 k][128 k'], 2 x 32 KiB
-constexpr int kCarQU = 65536;                     // 3 x (Qt f16 K-major [64 i][128 k] 16 KiB + Ut [64 i][64 v] f16 8 KiB)
-constexpr int kCarQUBytes = 24576;
-constexpr int kCarSI = kCarQU + 3 * kCarQUBytes;  // f16 S MN-major [128 k][64 v], 2 x 16 KiB
-constexpr int kCarSmall = kCarSI + 2 * 16384;
-constexpr int kCarSmem = kCarSmall + 256 + 1024;
-constexpr int kCarTmemCols = 256;                 // accS [0,64), accO x 2 [64,192)
+constexpr int kCarryThreads = 288;
+constexpr int kCaM = 0;                          // f16 M K-major [128][128], 2 x 32 KiB
+constexpr int kCaKU = 65536;                     // K' [64 j][128 k] (16 KiB) + U tile [64 j][64 v] (8 KiB), 3 x
+constexpr int kCaKUBytes = 24576;
+constexpr int kCaQt = kCaKU + 3 * kCaKUBytes;    // f16 Qt K-major [64][128], 3 x 16 KiB
+constexpr int kCaSI = kCaQt + 3 * 16384;         // f16 S MN-major [128 k][64 v], 2 x 16 KiB
+constexpr int kCaSmall = kCaSI + 2 * 16384;
+constexpr int kCaSmem = kCaSmall + 256 + 1024;
+constexpr int kCaTmemCols = 256;                 // accS x 2 (columns 0-127), accO x 2 (128-255)
 
-// bar.red.or on named barrier `id` among `count` threads
-__device__ __forceinline__ bool named_sync_or(int id, int count, bool v) {
-    uint32_t r;
-    asm volatile(
-        "{\n\t.reg .pred p, q;\n\t"
-        "setp.ne.u32 p, %1, 0;\n\t"
-        "barrier.red.or.pred q, %2, %3, p;\n\t"
-        "selp.u32 %0, 1, 0, q;\n\t}"
-        : "=r"(r)
-        : "r"((uint32_t)v), "r"(id), "r"(count)
-        : "memory");
-    return r != 0;
-}
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
@@ -634,22 +568,22 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     constexpr int BV = kCarryBV;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = align1024(smem_raw);
-    const uint32_t aMI = smem_u32(sm + kCarMI), aQU = smem_u32(sm + kCarQU), aSI = smem_u32(sm + kCarSI);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kCarSmall);
-    // fullM[2], fullQ[3], mmaS, mmaO[2], oFree[2], quFree[3]
-    const uint32_t bar0 = smem_u32(bars);
-    auto fullM = [&](int b) { return bar0 + 8 * b; };
-    auto fullQ = [&](int b) { return bar0 + 16 + 8 * b; };
-    const uint32_t mmaS = bar0 + 40;
-    auto mmaO = [&](int b) { return bar0 + 48 + 8 * b; };
-    auto oFree = [&](int b) { return bar0 + 64 + 8 * b; };
-    auto quFree = [&](int b) { return bar0 + 80 + 8 * b; };
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kCarSmall + 128);
+    const uint32_t aM = smem_u32(sm + kCaM), aKU = smem_u32(sm + kCaKU), aQt = smem_u32(sm + kCaQt),
+                   aSI = smem_u32(sm + kCaSI);
+    const uint32_t bar0 = smem_u32(sm + kCaSmall);
+    auto fullM = [&](int b) { return bar0 + 8 * b; };         // 2
+    auto fullKU = [&](int b) { return bar0 + 16 + 8 * b; };   // 3
+    auto fullQt = [&](int b) { return bar0 + 40 + 8 * b; };   // 3
+    const uint32_t mmaS = bar0 + 64;
+    auto mmaO = [&](int b) { return bar0 + 72 + 8 * b; };     // 2
+    const uint32_t imgReady = bar0 + 88;
+    auto oFree = [&](int b) { return bar0 + 96 + 8 * b; };    // 2
+    const uint32_t drain = bar0 + 112;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kCaSmall + 128);
 
-    constexpr int kTiles = kD / BV;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int64_t unit = blockIdx.x / kTiles;
-    const int vt = static_cast<int>(blockIdx.x - unit * kTiles);
+    const int64_t unit = blockIdx.x >> 1;
+    const int vt = blockIdx.x & 1;
     const int64_t s = unit / kHV;
     const int h = static_cast<int>(unit - s * kHV);
     const int v0 = vt * BV;
@@ -659,189 +593,193 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     const int len = static_cast<int>(t1 - t0);
     const int nch = (len + kC - 1) / kC;
     const int rec0 = reinterpret_cast<const int*>(ws + L.off_base)[s];
-    const bool state_warp = warp < 4;
-    const int k = tid;  // state column owned by state threads
     if (nch == 0 || rec0 + nch > L.R) {
         if (nch != 0 && tid == 0) record_status(16);
-        if (state_warp) {  // empty sequence: zero state rows (oracle prefill :53-55)
-            float* ns_col = p.new_state + (unit * kD + v0) * kD + k;
+        if (tid < kD) {  // empty sequence: zero state rows (oracle prefill :53-55)
+            float* ns_col = p.new_state + (unit * kD + v0) * kD + tid;
 #pragma unroll 8
             for (int v = 0; v < BV; ++v) ns_col[v * kD] = 0.f;
         }
         return;
     }
-    auto rhead = [&](int c) { return (int64_t)(rec0 + c) * kHV + h; };
+    auto rec_ptr = [&](int c) { return ws + L.off_rec + (static_cast<int64_t>(rec0 + c) * kHV + h) * kHeadRecBytes; };
+    auto accS = [&](uint32_t tm, int b) { return tm + 64 * b; };
+    auto accO = [&](uint32_t tm, int b) { return tm + 128 + 64 * b; };
 
-    float S[BV];
-    float Dn[BV];  // D of the next chunk to apply
-    auto load_D = [&](int c) {
-        const float4* src = reinterpret_cast<const float4*>(
-            reinterpret_cast<const float*>(ws + L.off_d + rhead(c) * kDBytes) + k * kD + v0);
-#pragma unroll
-        for (int v = 0; v < BV; v += 4) {
-            const float4 x = src[v / 4];
-            Dn[v] = x.x, Dn[v + 1] = x.y, Dn[v + 2] = x.z, Dn[v + 3] = x.w;
-        }
-    };
-    auto write_state_image = [&](int b) {
-#pragma unroll
-        for (int v = 0; v < BV; v += 8) st_shared_u4(aSI + b * 16384 + h16(k, v, kD), f16x8(S + v));
-    };
-    if (state_warp) {
-        if (p.state != nullptr) {
-            const float* st = p.state + (unit * kD + v0) * kD + k;
-#pragma unroll
-            for (int v = 0; v < BV; ++v) S[v] = st[v * kD];
-        } else {
-#pragma unroll
-            for (int v = 0; v < BV; ++v) S[v] = 0.f;
-        }
-        write_state_image(0);
-        load_D(0);
-    }
+    const bool issuer = tid == 256;
+    int topM = -1, topKU = -1, topQt = -1;  // issuer: highest chunk whose copy was issued
     auto issue_M = [&](int c) {
-        mbar_expect_tx(fullM(c & 1), kMImg);
-        bulk_g2s(aMI + (c & 1) * kMImg, ws + L.off_m + rhead(c) * kMImg, kMImg, fullM(c & 1));
+        const int b = c & 1;
+        mbar_expect_tx(fullM(b), 32768);
+        bulk_g2s(aM + b * 32768, rec_ptr(c) + kRecM, 32768, fullM(b));
+        topM = c;
     };
-    auto issue_QU = [&](int c) {
+    auto issue_KU = [&](int c) {
         const int b = c % 3;
-        mbar_expect_tx(fullQ(b), kQtImg + kCarQUBytes - kQtImg);
-        bulk_g2s(aQU + b * kCarQUBytes, ws + L.off_qt + rhead(c) * kQtImg, kQtImg, fullQ(b));
-        bulk_g2s(aQU + b * kCarQUBytes + kQtImg, ws + L.off_ut + rhead(c) * kUtBytes + vt * (kC * 64 * 2),
-                 kC * 64 * 2, fullQ(b));
+        mbar_expect_tx(fullKU(b), kCaKUBytes);
+        bulk_g2s(aKU + b * kCaKUBytes, rec_ptr(c) + kRecKb, 16384, fullKU(b));
+        bulk_g2s(aKU + b * kCaKUBytes + 16384, rec_ptr(c) + kRecU + vt * 8192, 8192, fullKU(b));
+        topKU = c;
     };
-    int m_issued = -1, m_waited = -1, q_issued = -1, q_waited = -1;  // thread 0's copy bookkeeping
-    if (tid == 0) {
+    auto issue_Qt = [&](int c) {
+        const int b = c % 3;
+        mbar_expect_tx(fullQt(b), 16384);
+        bulk_g2s(aQt + b * 16384, rec_ptr(c) + kRecQt, 16384, fullQt(b));
+        topQt = c;
+    };
+    if (issuer) {
         for (int b = 0; b < 2; ++b) mbar_init(fullM(b), 1);
-        for (int b = 0; b < 3; ++b) mbar_init(fullQ(b), 1);
+        for (int b = 0; b < 3; ++b) mbar_init(fullKU(b), 1);
+        for (int b = 0; b < 3; ++b) mbar_init(fullQt(b), 1);
         mbar_init(mmaS, 1);
         for (int b = 0; b < 2; ++b) mbar_init(mmaO(b), 1);
+        mbar_init(imgReady, 4);
         for (int b = 0; b < 2; ++b) mbar_init(oFree(b), 4);
-        for (int b = 0; b < 3; ++b) mbar_init(quFree(b), 4);
+        mbar_init(drain, 1);
         fence_mbar_init();
-        for (int c = 0; c < 2 && c < nch; ++c) issue_M(c), m_issued = c;
-        for (int c = 0; c < 2 && c < nch; ++c) issue_QU(c), q_issued = c;  // chunk 2 is issued at c = 0
+        for (int c = 0; c < 2 && c < nch; ++c) issue_M(c);
+        for (int c = 0; c < 3 && c < nch; ++c) issue_KU(c);
+        for (int c = 0; c < 2 && c < nch; ++c) issue_Qt(c);
     }
     if (warp == 0) {
-        tmem_alloc(smem_u32(tmem_slot), kCarTmemCols);
+        tmem_alloc(smem_u32(tmem_slot), kCaTmemCols);
         tmem_relinquish();
+    }
+    if (warp < 4) {  // S_0 -> fp16 state image 0 (thread k = column k; coalesced over k)
+        float sv[8];
+#pragma unroll
+        for (int v = 0; v < BV; v += 8) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+                sv[e] = p.state != nullptr ? p.state[(unit * kD + v0 + v + e) * kD + tid] : 0.f;
+            st_shared_u4(aSI + h16(tid, v, kD), f16x8(sv));
+        }
     }
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tm = *tmem_slot;
-    const uint32_t t_accS = tm;
-    auto t_accO = [&](int b) { return tm + 64 + 64 * b; };
-    bool ok = true, aborted = false;
 
-    if (state_warp) {
-        for (int c = 0; c < nch; ++c) {
-            if (tid == 0) {
-                ok = ok && mbar_wait(fullM(c & 1), (c >> 1) & 1);  // ok is false after a failed refill wait
-                if (ok) m_waited = c;
-                ok = ok && mbar_wait(fullQ(c % 3), (c / 3) & 1);
-                if (ok) q_waited = c;
-                ok = ok && (c < 2 || mbar_wait(oFree(c & 1), ((c - 2) >> 1) & 1));
-                if (ok) {
-                    tc_fence_after();
-                    mma_ct<kF16, false, true, kD, 128, kD, 128, BV>(t_accS, aMI + (c & 1) * kMImg,
-                                                                   aSI + (c & 1) * 16384, false);
-                    mma_commit(mmaS);
-                    mma_ct<kF16, false, true, kD, 64, kD, 64, BV>(t_accO(c & 1), aQU + (c % 3) * kCarQUBytes,
-                                                                 aSI + (c & 1) * 16384, false);
-                    mma_commit(mmaO(c & 1));
-                }
-            }
-            if (named_sync_or(1, 128, !ok)) {
-                aborted = true;
-                break;
-            }
-            ok = mbar_wait(mmaS, c & 1);
+    if (issuer) {
+        bool ok = mbar_wait(fullKU(0), 0);
+        if (ok) {
             tc_fence_after();
-            {
-                float a[32];
-#pragma unroll
-                for (int c0 = 0; c0 < BV; c0 += 32) {
-                    tmem_ld32(taddr(t_accS, 32 * warp, c0), a);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int v = 0; v < 32; ++v) S[c0 + v] = a[v] + Dn[c0 + v];
-                }
+            mma_ct<kF16, true, true, 64, 64, 64, 128, BV>(accS(tm, 0), aKU, aKU + 16384, false);  // K'^T U of chunk 0
+        }
+        for (int c = 0; c < nch && ok; ++c) {
+            ok = (c == 0 || mbar_wait(imgReady, (c - 1) & 1)) && mbar_wait(fullM(c & 1), (c >> 1) & 1);
+            if (!ok) break;
+            tc_fence_after();
+            mma_ct<kF16, false, true, kD, 128, kD, 128, BV>(accS(tm, c & 1), aM + (c & 1) * 32768,
+                                                           aSI + (c & 1) * 16384, true);
+            mma_commit(mmaS);
+            if (c + 1 < nch) {  // next chunk's K'^T U into the other accumulator (its reader is done)
+                const int b = (c + 1) % 3;
+                ok = mbar_wait(fullKU(b), ((c + 1) / 3) & 1);
+                if (!ok) break;
+                mma_ct<kF16, true, true, 64, 64, 64, 128, BV>(accS(tm, (c + 1) & 1), aKU + b * kCaKUBytes,
+                                                             aKU + b * kCaKUBytes + 16384, false);
+            }
+            ok = mbar_wait(fullQt(c % 3), (c / 3) & 1) && (c < 2 || mbar_wait(oFree(c & 1), ((c - 2) >> 1) & 1));
+            if (!ok) break;
+            tc_fence_after();
+            mma_ct<kF16, false, true, kD, 64, kD, 64, BV>(accO(tm, c & 1), aQt + (c % 3) * 16384,
+                                                         aSI + (c & 1) * 16384, false);
+            mma_commit(mmaO(c & 1));
+            // MMA_S(c) complete => so is everything issued before it: refill
+            ok = mbar_wait(mmaS, c & 1);
+            if (!ok) break;
+            if (c + 2 < nch) {
+                issue_M(c + 2);
+                issue_Qt(c + 2);
+            }
+            if (c + 3 < nch) issue_KU(c + 3);
+        }
+        if (!ok) {
+            record_status(32 /* GDN_ERR_DEVICE_TIMEOUT */);
+            // wait (bounded) for the copies in flight: per buffer, its latest chunk
+            for (int c = topM > 1 ? topM - 1 : 0; c <= topM; ++c) mbar_wait(fullM(c & 1), (c >> 1) & 1);
+            for (int c = topKU > 2 ? topKU - 2 : 0; c <= topKU; ++c) mbar_wait(fullKU(c % 3), (c / 3) & 1);
+            for (int c = topQt > 2 ? topQt - 2 : 0; c <= topQt; ++c) mbar_wait(fullQt(c % 3), (c / 3) & 1);
+            mma_commit(drain);
+            mbar_wait(drain, 0);
+        }
+    } else if (warp < 4) {
+        const int k = tid;
+        for (int c = 0; c < nch; ++c) {
+            const bool okc = __all_sync(0xffffffffu, mbar_wait(mmaS, c & 1));  // warp-uniform exit
+            tc_fence_after();
+            float a0[32], a1[32];
+            tmem_ld32(taddr(accS(tm, c & 1), 32 * warp, 0), a0);
+            tmem_ld32(taddr(accS(tm, c & 1), 32 * warp, 32), a1);
+            tmem_wait_ld();
+            if (!okc) {
+                record_status(32);
+                break;
             }
             if (c + 1 < nch) {
-                write_state_image((c + 1) & 1);
-                load_D(c + 1);
-            }
-            fence_async_smem();
-            tc_fence_before();
-            if (named_sync_or(1, 128, !ok)) {
-                aborted = true;
-                break;
-            }
-            if (tid == 0) {  // refill: M of chunk c+2 (MMA_S(c) done), [Qt | Ut] of chunk c+2
-                tc_fence_after();
-                if (c + 2 < nch) {
-                    issue_M(c + 2);
-                    m_issued = c + 2;
-                    if (c >= 1 && !mbar_wait(quFree((c + 2) % 3), ((c - 1) / 3) & 1)) {
-                        ok = false;  // caught by the next chunk's barrier
-                    } else {
-                        issue_QU(c + 2);
-                        q_issued = c + 2;
-                    }
+                const uint32_t img = aSI + ((c + 1) & 1) * 16384;
+#pragma unroll
+                for (int v = 0; v < 32; v += 8) {
+                    st_shared_u4(img + h16(k, v, kD), f16x8(a0 + v));
+                    st_shared_u4(img + h16(k, 32 + v, kD), f16x8(a1 + v));
+                }
+                fence_async_smem();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(imgReady);
+            } else {
+                float* ns_col = p.new_state + (unit * kD + v0) * kD + k;
+#pragma unroll
+                for (int v = 0; v < 32; ++v) {
+                    ns_col[v * kD] = a0[v];
+                    ns_col[(32 + v) * kD] = a1[v];
                 }
             }
         }
-        if (tid == 0) {
-            if (aborted) {
-                record_status(32 /* GDN_ERR_DEVICE_TIMEOUT */);
-                for (int cc = m_waited + 1; cc <= m_issued; ++cc) mbar_wait(fullM(cc & 1), (cc >> 1) & 1);
-                for (int cc = q_waited + 1; cc <= q_issued; ++cc) mbar_wait(fullQ(cc % 3), (cc / 3) & 1);
-            }
-        }
-        float* ns_col = p.new_state + (unit * kD + v0) * kD + k;
-#pragma unroll
-        for (int v = 0; v < BV; ++v) ns_col[v * kD] = S[v];
-    } else {
-        // output warps: token i = 16 (warp - 4) + lane (lanes 0-15) of each chunk
+    } else if (warp < 8) {
+        // output rows: token i = 16 (warp - 4) + lane of each chunk (lanes 0-15)
         const int ow = warp - 4;
         const int i = 16 * ow + (lane & 15);
-        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
+        uint16_t* out = p.out;
         for (int c = 0; c < nch; ++c) {
-            bool okc = mbar_wait(mmaO(c & 1), (c >> 1) & 1) && mbar_wait(fullQ(c % 3), (c / 3) & 1);
-            tc_fence_after();
             const int tok = kC * c + i;
-            const uint32_t ut = aQU + (c % 3) * kCarQUBytes + kQtImg + (i & 63) * 128;
+            const bool act = lane < 16 && tok < len;
+            uint4 ut[8];  // Ut row i, logical 16-byte chunks (stored swizzled by i & 7)
+            const uint8_t* urow = rec_ptr(c) + kRecUt + vt * 8192 + i * 128;
 #pragma unroll
-            for (int c0 = 0; c0 < BV; c0 += 32) {
-                float o[32];
-                tmem_ld32(taddr(t_accO(c & 1), 32 * ow, c0), o);
-                tmem_wait_ld();
-                if (okc && lane < 16 && tok < len) {
-                    __nv_bfloat16* dst = out + ((t0 + tok) * kHV + h) * kD + v0 + c0;
-#pragma unroll
-                    for (int v = 0; v < 32; v += 8) {
-                        float u[8];
-                        h16x8_to_f32(ld_shared_u4(ut + (c0 + v) * 2), u);
-                        __nv_bfloat162 w[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e)
-                            w[e] = __floats2bfloat162_rn(p.scale * (o[v + 2 * e] + u[2 * e]),
-                                                         p.scale * (o[v + 2 * e + 1] + u[2 * e + 1]));
-                        *reinterpret_cast<uint4*>(dst + v) = *reinterpret_cast<uint4*>(w);
-                    }
-                }
-            }
+            for (int q = 0; q < 8; ++q)
+                ut[q] = act ? __ldg(reinterpret_cast<const uint4*>(urow + ((q ^ (i & 7)) << 4))) : make_uint4(0, 0, 0, 0);
+            const bool okc = __all_sync(0xffffffffu, mbar_wait(mmaO(c & 1), (c >> 1) & 1));
+            tc_fence_after();
+            float o0[32], o1[32];
+            tmem_ld32(taddr(accO(tm, c & 1), 32 * ow, 0), o0);
+            tmem_ld32(taddr(accO(tm, c & 1), 32 * ow, 32), o1);
+            tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(oFree(c & 1));
-                mbar_arrive(quFree(c % 3));
-            }
+            if (lane == 0) mbar_arrive(oFree(c & 1));
             if (!okc) {
                 if (lane == 0) record_status(32);
                 break;
+            }
+            if (act) {
+                uint16_t* dst = out + ((t0 + tok) * kHV + h) * kD + v0;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    float u[8];
+                    h16x8_to_f32(ut[q], u);
+                    const float* o = q < 4 ? o0 + 8 * q : o1 + 8 * (q - 4);
+                    uint32_t w[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const __nv_bfloat162 b2 = __floats2bfloat162_rn(p.scale * (o[2 * e] + u[2 * e]),
+                                                                        p.scale * (o[2 * e + 1] + u[2 * e + 1]));
+                        w[e] = *reinterpret_cast<const uint32_t*>(&b2);
+                    }
+                    *reinterpret_cast<uint4*>(dst + 8 * q) = make_uint4(w[0], w[1], w[2], w[3]);
+                }
             }
         }
     }
@@ -849,7 +787,7 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tm, kCarTmemCols);
+        tmem_dealloc(tm, kCaTmemCols);
     }
 }
 
@@ -863,20 +801,61 @@ static cudaError_t set_smem(K kernel, int bytes) {
 constexpr int kPathAuto = 0, kPathRecurrent = 1, kPathChunked = 2;
 constexpr int64_t kRecurrentMaxAvgLen = 48;
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against libcuda); looked up once per process.
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            f = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }();
+    return fn;
+}
+
+// Tensor map of a bf16 [T, heads, 128] token tensor: 3-D (dim, head, token),
+// box = 64 dims x 1 head x 64 tokens, SWIZZLE_128B -- one SW128 image of 64
+// rows per load; tokens >= T read as zeros.
+static cudaError_t token_tensor_map(CUtensorMap* m, const void* base, int heads, int64_t T) {
+    PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+    if (encode == nullptr) return cudaErrorNotSupported;
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(heads),
+                                static_cast<cuuint64_t>(T)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(kD) * 2, static_cast<cuuint64_t>(heads) * kD * 2};
+    const cuuint32_t box[3] = {64, 1, static_cast<cuuint32_t>(kC)};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 cudaError_t launch_prefill_chunked(const PrefillParams& p, void* workspace, cudaStream_t stream) {
     const WsLayout L = ws_layout(p.total_tokens, p.num_seqs);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
+    if (L.R > 0x7fffffffLL || p.total_tokens > 0x7fffffffLL) return cudaErrorInvalidValue;
+    CUtensorMap tmK, tmQ, tmV;
+    memset(&tmK, 0, sizeof(tmK));
+    memset(&tmQ, 0, sizeof(tmQ));
+    memset(&tmV, 0, sizeof(tmV));
     cudaError_t e;
+    if (p.total_tokens > 0) {  // with no tokens there are no records and no loads
+        if ((e = token_tensor_map(&tmK, p.k, kHQK, p.total_tokens)) != cudaSuccess) return e;
+        if ((e = token_tensor_map(&tmQ, p.q, kHQK, p.total_tokens)) != cudaSuccess) return e;
+        if ((e = token_tensor_map(&tmV, p.v, kHV, p.total_tokens)) != cudaSuccess) return e;
+    }
     gdn_chunk_table_kernel<<<1, 1024, 0, stream>>>(p, ws, L);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    if ((e = set_smem(gdn_chunk_prepare_kernel, kPrepSmem)) != cudaSuccess) return e;
-    if (L.R > 0x7fffffffLL) return cudaErrorInvalidValue;
-    gdn_chunk_prepare_kernel<<<dim3(static_cast<unsigned>(L.R), kHQK), 128, kPrepSmem, stream>>>(p, ws, L);
+    if ((e = set_smem(gdn_chunk_prepare_kernel, kPrSmem)) != cudaSuccess) return e;
+    gdn_chunk_prepare_kernel<<<dim3(static_cast<unsigned>(L.R), kHV), kPrepThreads, kPrSmem, stream>>>(
+        p, ws, L, tmK, tmQ, tmV);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    if ((e = set_smem(gdn_chunk_carry_kernel, kCarSmem)) != cudaSuccess) return e;
+    if ((e = set_smem(gdn_chunk_carry_kernel, kCaSmem)) != cudaSuccess) return e;
     const int64_t grid = p.num_seqs * kHV * (kD / kCarryBV);
     if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
-    gdn_chunk_carry_kernel<<<static_cast<unsigned>(grid), kCarryThreads, kCarSmem, stream>>>(p, ws, L);
+    gdn_chunk_carry_kernel<<<static_cast<unsigned>(grid), kCarryThreads, kCaSmem, stream>>>(p, ws, L);
     return cudaGetLastError();
 }
 

@@ -1,6 +1,6 @@
 // tc05.cuh -- thin inline-PTX layer over the sm_100a async units used here:
-// tcgen05 (tensor-core MMA with TMEM accumulators), TMA bulk copies
-// (cp.async.bulk, no tensor map, never multicast) and mbarriers.
+// tcgen05 (tensor-core MMA with TMEM accumulators), TMA copies (untiled
+// cp.async.bulk and tiled cp.async.bulk.tensor; never multicast) and mbarriers.
 //
 // Operand images.  Every MMA operand lives in shared memory as a K-major
 // "SW128" image: rows of 128 bytes grouped 8 per 1024-byte atom, the 16-byte
@@ -17,6 +17,7 @@
 // warp's 32-lane sub-partition.  Column n of the tile is TMEM column base + n.
 #pragma once
 
+#include <cuda.h>  // CUtensorMap
 #include <stdint.h>
 
 namespace gdn {
@@ -89,6 +90,17 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst_smem, const void* src, uin
 __device__ __forceinline__ void bulk_s2g(void* dst, uint32_t src_smem, uint32_t bytes) {
     asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src_smem), "r"(bytes)
                  : "memory");
+}
+// Tiled 3-D TMA load of one box into shared memory (box layout and swizzle
+// come from the tensor map); completes `bar`'s transaction count.  c0 is the
+// innermost coordinate: c0 * element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst_smem, const CUtensorMap* map, int c0, int c1, int c2,
+                                            uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(dst_smem),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
+        : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
