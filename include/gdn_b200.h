@@ -181,6 +181,7 @@ int gdn_abi_version(void);
 #define GDN_MMA_A_MN_MAJOR 1  /* A operand image stored MN-major */
 #define GDN_MMA_B_MN_MAJOR 2  /* B operand image stored MN-major */
 #define GDN_MMA_D_LANE16 4    /* accumulator at TMEM lane 16 (M = 64 only) */
+#define GDN_MMA_A_TMEM 8      /* A operand read from TMEM (16-bit kinds, M = 128, K-major) */
 
 /* D[M x N] = A[M x K] . B[N x K]^T on one CTA through the same shared-memory
  * operand images, tcgen05 descriptors and TMEM read-back the prefill kernels

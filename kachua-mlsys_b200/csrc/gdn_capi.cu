@@ -151,7 +151,8 @@ extern "C" int gdn_mma_selftest(int kind, int flags, int M, int N, int K, const 
     if (!A || !B || !D) return GDN_ERR_NULL_POINTER;
     if ((kind != GDN_MMA_KIND_BF16 && kind != GDN_MMA_KIND_TF32 && kind != GDN_MMA_KIND_F16) || (M != 64 && M != 128) ||
         N < 16 ||
-        N > 256 || N % 16 != 0 || (K != 64 && K != 128) || (flags & ~7) != 0 || ((flags & 4) && M != 64))
+        N > 256 || N % 16 != 0 || (K != 64 && K != 128) || (flags & ~15) != 0 || ((flags & 4) && M != 64) ||
+        ((flags & 8) && (M != 128 || kind == GDN_MMA_KIND_TF32 || (flags & 1))))
         return GDN_ERR_BAD_SIZE;
     // an MN-major image fills whole 128-byte rows: its M (or N) extent must be too
     const int row_elems = kind == GDN_MMA_KIND_TF32 ? 32 : 64;

@@ -243,6 +243,37 @@ __device__ __forceinline__ void st_shared_u16(uint32_t addr, uint16_t v) {
 // and MN-major (row = K index) images, and the TMA SWIZZLE_128B box layout.
 __device__ __forceinline__ uint32_t h16(int row, int col, int rows) { return sw128_bf16(row, col, rows); }
 
+// Plain (compiler-scheduled) shared-memory accesses addressed by the 32-bit
+// shared address used for descriptors: the generic pointer keeps the shared
+// address space visible, so loads batch and overlap instead of serialising
+// like volatile asm would.
+struct Smem {
+    uint8_t* p;  // generic pointer to the byte at shared address a
+    uint32_t a;
+    __device__ __forceinline__ uint4 ld16(uint32_t addr) const { return *reinterpret_cast<const uint4*>(p + (addr - a)); }
+    __device__ __forceinline__ float4 ldf4(uint32_t addr) const {
+        return *reinterpret_cast<const float4*>(p + (addr - a));
+    }
+    __device__ __forceinline__ void st16(uint32_t addr, uint4 v) const { *reinterpret_cast<uint4*>(p + (addr - a)) = v; }
+    __device__ __forceinline__ void stf4(uint32_t addr, float4 v) const {
+        *reinterpret_cast<float4*>(p + (addr - a)) = v;
+    }
+    __device__ __forceinline__ void st2(uint32_t addr, uint16_t v) const {
+        *reinterpret_cast<uint16_t*>(p + (addr - a)) = v;
+    }
+};
+
+// 1024-byte aligned base of the dynamic shared memory, derived from the
+// __shared__ array itself so the address space stays visible.
+__device__ __forceinline__ uint8_t* smem_align1024(uint8_t* raw) {
+    return raw + ((1024u - (smem_u32(raw) & 1023u)) & 1023u);
+}
+
+// bar.sync on named barrier `id` among `count` threads (a multiple of 32)
+__device__ __forceinline__ void named_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // fp32 N image: row i is 256 bytes; its 16-byte chunk c sits at position c ^ (i & 15)
 __device__ __forceinline__ uint32_t n_off(int i, int m) { return i * 256 + ((((m >> 2) ^ (i & 15))) << 4); }
 
@@ -251,7 +282,8 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
                              const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
                              const __grid_constant__ CUtensorMap tmV) {
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* sm = align1024(smem_raw);
+    uint8_t* sm = smem_align1024(smem_raw);
+    const Smem S{sm, smem_u32(sm)};
     PrepSmall& sml = *reinterpret_cast<PrepSmall*>(sm + kPrSmall);
     const uint32_t aKQ = smem_u32(sm + kPrKQ), aN = smem_u32(sm + kPrN), aPO = smem_u32(sm + kPrPO),
                    aX = smem_u32(sm + kPrX), aRHS = smem_u32(sm + kPrRHS);
@@ -328,10 +360,10 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
         const float sc = blk < 2 ? sml.beta[row] * fast_exp2(sml.LG[row]) : sml.beta[row];
         const bool act = row < n;
         float f[8];
-        bf16x8_to_f32(ld_shared_u4(src), f);
+        bf16x8_to_f32(S.ld16(src), f);
 #pragma unroll
         for (int q = 0; q < 8; ++q) f[q] = act ? sc * f[q] : 0.f;
-        st_shared_u4(aRHS + blk * 8192 + in_row, f16x8(f));
+        S.st16(aRHS + blk * 8192 + in_row, f16x8(f));
     }
     ok = mbar_wait(barM, 0) && ok;
     tc_fence_after();
@@ -361,7 +393,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
                     const int j = j0 + e;
                     nv[e] = (j < i && act) ? bi * fast_exp2(LGi - sml.LG[j]) * g[j] : 0.f;
                 }
-                st_shared_v4(aN + n_off(i, j0), make_float4(nv[0], nv[1], nv[2], nv[3]));
+                S.stf4(aN + n_off(i, j0), make_float4(nv[0], nv[1], nv[2], nv[3]));
             }
         } else {
             const int i = tid - 64;
@@ -374,36 +406,57 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
                     const int j = j0 + e;
                     pv[e] = (j <= i) ? fast_exp2(LGi - sml.LG[j]) * g[j] : 0.f;
                 }
-                st_shared_u4(aPO + h16(i, j0, 64), f16x8(pv));
+                S.st16(aPO + h16(i, j0, 64), f16x8(pv));
             }
         }
     }
     tc_fence_before();
     if (__syncthreads_or(!ok)) goto abort;
     if (warp < 2) {
-        // 3a. A^-1 = (I + N)^-1 by forward substitution, column j = tid, fp32
-        //     (eight independent partial sums per row keep the FMA chains short)
+        // 3a. A^-1 = (I + N)^-1 by blocked forward substitution in fp32, one
+        //     column j = tid per thread, 16-row blocks: earlier blocks enter as
+        //     a 16-accumulator update, then the block's own triangle.  Solved
+        //     rows of X are kept (fp32, row-major [m][j]) in the N rows they
+        //     replace -- a row of N is dead once its block is solved.
         const int j = tid;
-        float x[kC];
+#pragma unroll 1
+        for (int b = 0; b < 4; ++b) {
+            const int i0 = 16 * b;
+            float acc[16];
 #pragma unroll
-        for (int i = 0; i < kC; ++i) {
-            float a[8];
+            for (int r = 0; r < 16; ++r) acc[r] = (i0 + r == j) ? 1.f : 0.f;
+#pragma unroll 1
+            for (int m0 = 0; m0 < i0; m0 += 4) {
+                float xm[4];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) a[e] = 0.f;
-            a[0] = (i == j) ? 1.f : 0.f;
+                for (int e = 0; e < 4; ++e) xm[e] = *reinterpret_cast<const float*>(sm + kPrN + (m0 + e) * 256 + j * 4);
 #pragma unroll
-            for (int m0 = 0; m0 < i; m0 += 4) {
-                const float4 nv = ld_shared_v4(aN + n_off(i, m0));
-                const int s = ((m0 >> 2) & 1) * 4;
-                a[s + 0] = fmaf(-nv.x, x[m0], a[s + 0]);
-                if (m0 + 1 < i) a[s + 1] = fmaf(-nv.y, x[m0 + 1], a[s + 1]);
-                if (m0 + 2 < i) a[s + 2] = fmaf(-nv.z, x[m0 + 2], a[s + 2]);
-                if (m0 + 3 < i) a[s + 3] = fmaf(-nv.w, x[m0 + 3], a[s + 3]);
+                for (int r = 0; r < 16; ++r) {
+                    const float4 nv = S.ldf4(aN + n_off(i0 + r, m0));
+                    acc[r] = fmaf(-nv.x, xm[0], acc[r]);
+                    acc[r] = fmaf(-nv.y, xm[1], acc[r]);
+                    acc[r] = fmaf(-nv.z, xm[2], acc[r]);
+                    acc[r] = fmaf(-nv.w, xm[3], acc[r]);
+                }
             }
-            x[i] = ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
-        }
 #pragma unroll
-        for (int i = 0; i < kC; ++i) st_shared_u16(aX + h16(i, j, 64), __half_as_ushort(__float2half_rn(x[i])));
+            for (int r = 1; r < 16; ++r) {
+#pragma unroll
+                for (int m = 0; m < r; m += 4) {
+                    const float4 nv = S.ldf4(aN + n_off(i0 + r, i0 + m));
+                    acc[r] = fmaf(-nv.x, acc[m], acc[r]);
+                    if (m + 1 < r) acc[r] = fmaf(-nv.y, acc[m + 1], acc[r]);
+                    if (m + 2 < r) acc[r] = fmaf(-nv.z, acc[m + 2], acc[r]);
+                    if (m + 3 < r) acc[r] = fmaf(-nv.w, acc[m + 3], acc[r]);
+                }
+            }
+            named_sync(1, 64);  // both warps are done reading this block's N rows
+#pragma unroll
+            for (int r = 0; r < 16; ++r) {
+                *reinterpret_cast<float*>(sm + kPrN + (i0 + r) * 256 + j * 4) = acc[r];
+                S.st2(aX + h16(i0 + r, j, 64), __half_as_ushort(__float2half_rn(acc[r])));
+            }
+        }
     } else {
         // 3b. K' = tail (.) K in place over the K rows of [K;Q] (rows >= n zero)
         const float LGc = sml.LG[kC - 1];
@@ -415,10 +468,10 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
             const float sc = fast_exp2(LGc - sml.LG[row]);
             const bool act = row < n;
             float f[8];
-            bf16x8_to_f32(ld_shared_u4(addr), f);
+            bf16x8_to_f32(S.ld16(addr), f);
 #pragma unroll
             for (int q = 0; q < 8; ++q) f[q] = act ? sc * f[q] : 0.f;
-            st_shared_u4(addr, f16x8(f));
+            S.st16(addr, f16x8(f));
         }
     }
     fence_async_smem();
@@ -443,7 +496,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
             tmem_ld32(taddr(tm, 32 * warp, 32 * c), acc);
             tmem_wait_ld();
 #pragma unroll
-            for (int j0 = 0; j0 < 32; j0 += 8) st_shared_u4(dst + h16(i, 32 * c + j0, 64), f16x8(acc + j0));
+            for (int j0 = 0; j0 < 32; j0 += 8) S.st16(dst + h16(i, 32 * c + j0, 64), f16x8(acc + j0));
         }
     }
     fence_async_smem();
@@ -477,10 +530,10 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
                 for (int j0 = 0; j0 < 32; j0 += 8) {
                     const int col = 32 * c + j0;
                     float qf[8];
-                    bf16x8_to_f32(ld_shared_u4(aKQ + h16(64 + i, col, 128)), qf);
+                    bf16x8_to_f32(S.ld16(aKQ + h16(64 + i, col, 128)), qf);
 #pragma unroll
                     for (int q = 0; q < 8; ++q) qf[q] = act ? Gi * qf[q] - acc[j0 + q] : 0.f;
-                    st_shared_u4(aPO + h16(i, col, 64), f16x8(qf));  // Qt staging over P and A^-1
+                    S.st16(aPO + h16(i, col, 64), f16x8(qf));  // Qt staging over P and A^-1
                 }
             } else {
 #pragma unroll
@@ -489,7 +542,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
                     float uf[8];
 #pragma unroll
                     for (int q = 0; q < 8; ++q) uf[q] = act ? acc[j0 + q] : 0.f;
-                    st_shared_u4(aN + (col >> 6) * 8192 + h16(i, col & 63, 64), f16x8(uf));  // Ut staging over N
+                    S.st16(aN + (col >> 6) * 8192 + h16(i, col & 63, 64), f16x8(uf));  // Ut staging over N
                 }
             }
         }
@@ -505,7 +558,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
                 float f[8];
 #pragma unroll
                 for (int q = 0; q < 8; ++q) f[q] = (32 * c + j0 + q == tid ? Gc : 0.f) - acc[j0 + q];
-                st_shared_u4(aRHS + h16(tid, 32 * c + j0, 128), f16x8(f));
+                S.st16(aRHS + h16(tid, 32 * c + j0, 128), f16x8(f));
             }
         }
     }
@@ -536,40 +589,43 @@ done:
 }
 
 // ------------------------------------------------------------------ carry --
-// One CTA per sequence x v-head x 64 value rows; the chunk-to-chunk chain
-//   S_{c+1}^T = K'_c^T U_c + M_c S_c^T
-// is one 12-instruction accumulation per chunk (the K'^T U part issued a chunk
-// early into the second accumulator).  Warp roles:
-//   warp 8 (one thread)  issues every MMA and bulk copy;
-//   warps 0-3 (state)    read the accumulator (thread k = state column k),
-//                        write the next fp16 state image, and at the end the
-//                        fp32 final state;
-//   warps 4-7 (output)   O_c = scale (Qt_c S_c^T + Ut_c) from a second MMA on
-//                        the same state image, overlapped with the next chunk.
-// M is double-buffered, [K' | U] and Qt triple-buffered, each refilled once
+// One CTA per sequence x v-head.  The state lives in TMEM in transposed form
+// (lane = value row v, columns = k) and is its own MMA operand:
+//   chain   S_{c+1}^T <- U_c^T K'_c + S_c M_c^T     [v][k], fp32 accumulator
+//   output  O_c^T      = S_c Qt_c^T                  [v][i]
+// (U^T K' is issued one chunk early into the second accumulator; S M^T and
+// S Qt^T read S from TMEM as fp16 -- the A operand -- so no shared-memory
+// state image exists).  Warp roles:
+//   warps 0-7   state epilogue: warp w owns lanes 32 (w & 3).. and k columns
+//               64 (w >> 2)..: fp32 accumulator -> fp16 A operand of the next
+//               chunk, and the fp32 final state;
+//   warps 8-11  output epilogue: lane = v, 64 columns = tokens; adds Ut and
+//               writes bf16 rows (coalesced over v);
+//   warp 12     one thread issues every MMA and bulk copy.
+// M is double-buffered, [K' | U] and Qt triple-buffered, each refilled when
 // the MMA that read it is known complete, two chunks before use.
-constexpr int kCarryBV = 64;
-constexpr int kCarryThreads = 288;
-constexpr int kCaM = 0;                          // f16 M K-major [128][128], 2 x 32 KiB
-constexpr int kCaKU = 65536;                     // K' [64 j][128 k] (16 KiB) + U tile [64 j][64 v] (8 KiB), 3 x
-constexpr int kCaKUBytes = 24576;
-constexpr int kCaQt = kCaKU + 3 * kCaKUBytes;    // f16 Qt K-major [64][128], 3 x 16 KiB
-constexpr int kCaSI = kCaQt + 3 * 16384;         // f16 S MN-major [128 k][64 v], 2 x 16 KiB
-constexpr int kCaSmall = kCaSI + 2 * 16384;
+constexpr int kCarryThreads = 416;
+constexpr int kCaM = 0;                         // f16 M K-major [128 k][128 k'], 2 x 32 KiB
+constexpr int kCaKU = 65536;                    // K' [64 j][128 k] + U [64 j][128 v] (MN-major), 3 x 32 KiB
+constexpr int kCaQt = kCaKU + 3 * 32768;        // f16 Qt K-major [64 i][128 k], 3 x 16 KiB
+constexpr int kCaSmall = kCaQt + 3 * 16384;
 constexpr int kCaSmem = kCaSmall + 256 + 1024;
-constexpr int kCaTmemCols = 256;                 // accS x 2 (columns 0-127), accO x 2 (128-255)
+constexpr int kCaTmemCols = 512;  // accS x 2 [0, 256), fp16 S x 2 [256, 384), accO x 2 [384, 512)
 
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+    const __half2 h2 = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h2);
+}
+
 __global__ void __launch_bounds__(kCarryThreads, 1)
     gdn_chunk_carry_kernel(const PrefillParams p, const uint8_t* __restrict__ ws, const WsLayout L) {
-    constexpr int BV = kCarryBV;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* sm = align1024(smem_raw);
-    const uint32_t aM = smem_u32(sm + kCaM), aKU = smem_u32(sm + kCaKU), aQt = smem_u32(sm + kCaQt),
-                   aSI = smem_u32(sm + kCaSI);
+    uint8_t* sm = smem_align1024(smem_raw);
+    const uint32_t aM = smem_u32(sm + kCaM), aKU = smem_u32(sm + kCaKU), aQt = smem_u32(sm + kCaQt);
     const uint32_t bar0 = smem_u32(sm + kCaSmall);
     auto fullM = [&](int b) { return bar0 + 8 * b; };         // 2
     auto fullKU = [&](int b) { return bar0 + 16 + 8 * b; };   // 3
@@ -582,31 +638,26 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kCaSmall + 128);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int64_t unit = blockIdx.x >> 1;
-    const int vt = blockIdx.x & 1;
+    const int64_t unit = blockIdx.x;
     const int64_t s = unit / kHV;
     const int h = static_cast<int>(unit - s * kHV);
-    const int v0 = vt * BV;
 
     int64_t t0, t1;
     seq_bounds(p, s, t0, t1);
     const int len = static_cast<int>(t1 - t0);
     const int nch = (len + kC - 1) / kC;
     const int rec0 = reinterpret_cast<const int*>(ws + L.off_base)[s];
+    float* ns_head = p.new_state + unit * kD * kD;
     if (nch == 0 || rec0 + nch > L.R) {
         if (nch != 0 && tid == 0) record_status(16);
-        if (tid < kD) {  // empty sequence: zero state rows (oracle prefill :53-55)
-            float* ns_col = p.new_state + (unit * kD + v0) * kD + tid;
-#pragma unroll 8
-            for (int v = 0; v < BV; ++v) ns_col[v * kD] = 0.f;
-        }
+        // empty sequence: zero state (oracle prefill :53-55)
+        for (int i = tid; i < kD * kD / 4; i += kCarryThreads)
+            reinterpret_cast<float4*>(ns_head)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
         return;
     }
     auto rec_ptr = [&](int c) { return ws + L.off_rec + (static_cast<int64_t>(rec0 + c) * kHV + h) * kHeadRecBytes; };
-    auto accS = [&](uint32_t tm, int b) { return tm + 64 * b; };
-    auto accO = [&](uint32_t tm, int b) { return tm + 128 + 64 * b; };
 
-    const bool issuer = tid == 256;
+    const bool issuer = tid == 12 * 32;
     int topM = -1, topKU = -1, topQt = -1;  // issuer: highest chunk whose copy was issued
     auto issue_M = [&](int c) {
         const int b = c & 1;
@@ -614,11 +665,10 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
         bulk_g2s(aM + b * 32768, rec_ptr(c) + kRecM, 32768, fullM(b));
         topM = c;
     };
-    auto issue_KU = [&](int c) {
+    auto issue_KU = [&](int c) {  // K' and U are adjacent in the record
         const int b = c % 3;
-        mbar_expect_tx(fullKU(b), kCaKUBytes);
-        bulk_g2s(aKU + b * kCaKUBytes, rec_ptr(c) + kRecKb, 16384, fullKU(b));
-        bulk_g2s(aKU + b * kCaKUBytes + 16384, rec_ptr(c) + kRecU + vt * 8192, 8192, fullKU(b));
+        mbar_expect_tx(fullKU(b), 32768);
+        bulk_g2s(aKU + b * 32768, rec_ptr(c) + kRecKb, 32768, fullKU(b));
         topKU = c;
     };
     auto issue_Qt = [&](int c) {
@@ -633,7 +683,7 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
         for (int b = 0; b < 3; ++b) mbar_init(fullQt(b), 1);
         mbar_init(mmaS, 1);
         for (int b = 0; b < 2; ++b) mbar_init(mmaO(b), 1);
-        mbar_init(imgReady, 4);
+        mbar_init(imgReady, 8);
         for (int b = 0; b < 2; ++b) mbar_init(oFree(b), 4);
         mbar_init(drain, 1);
         fence_mbar_init();
@@ -645,49 +695,139 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
         tmem_alloc(smem_u32(tmem_slot), kCaTmemCols);
         tmem_relinquish();
     }
-    if (warp < 4) {  // S_0 -> fp16 state image 0 (thread k = column k; coalesced over k)
-        float sv[8];
-#pragma unroll
-        for (int v = 0; v < BV; v += 8) {
-#pragma unroll
-            for (int e = 0; e < 8; ++e)
-                sv[e] = p.state != nullptr ? p.state[(unit * kD + v0 + v + e) * kD + tid] : 0.f;
-            st_shared_u4(aSI + h16(tid, v, kD), f16x8(sv));
-        }
-    }
-    fence_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tm = *tmem_slot;
+    auto accS = [&](int b) { return tm + 128 * b; };
+    auto sA = [&](int b) { return tm + 256 + 64 * b; };
+    auto accO = [&](int b) { return tm + 384 + 64 * b; };
 
-    if (issuer) {
+    if (warp < 8) {
+        // state epilogue: lane v = 32 (w & 3) + lane, k columns [64 hk, 64 hk + 64)
+        const int q = warp & 3, hk = warp >> 2;
+        const int v = 32 * q + lane;
+        float* ns_row = ns_head + v * kD + 64 * hk;
+        {  // S_0 -> fp16 A operand 0
+            uint32_t w[32];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                const float4 x = p.state != nullptr ? reinterpret_cast<const float4*>(p.state + unit * kD * kD + v * kD + 64 * hk)[e]
+                                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+                w[2 * e] = pack_half2(x.x, x.y);
+                w[2 * e + 1] = pack_half2(x.z, x.w);
+            }
+            tmem_st32(taddr(sA(0), 32 * q, 32 * hk), w);
+            tmem_wait_st();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(imgReady);  // image 0 (phase 0)
+        for (int c = 0; c < nch; ++c) {
+            const bool okc = __all_sync(0xffffffffu, mbar_wait(mmaS, c & 1));  // warp-uniform exit
+            tc_fence_after();
+            float a0[32], a1[32];
+            tmem_ld32(taddr(accS(c & 1), 32 * q, 64 * hk), a0);
+            tmem_ld32(taddr(accS(c & 1), 32 * q, 64 * hk + 32), a1);
+            tmem_wait_ld();
+            if (!okc) {
+                if (lane == 0) record_status(32);
+                break;
+            }
+            if (c + 1 < nch) {
+                uint32_t w[32];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    w[e] = pack_half2(a0[2 * e], a0[2 * e + 1]);
+                    w[16 + e] = pack_half2(a1[2 * e], a1[2 * e + 1]);
+                }
+                tmem_st32(taddr(sA((c + 1) & 1), 32 * q, 32 * hk), w);
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(imgReady);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    reinterpret_cast<float4*>(ns_row)[e] = make_float4(a0[4 * e], a0[4 * e + 1], a0[4 * e + 2], a0[4 * e + 3]);
+                    reinterpret_cast<float4*>(ns_row + 32)[e] =
+                        make_float4(a1[4 * e], a1[4 * e + 1], a1[4 * e + 2], a1[4 * e + 3]);
+                }
+            }
+        }
+    } else if (warp < 12) {
+        // output epilogue: lane v, columns = the chunk's 64 tokens
+        const int q = warp - 8;
+        const int v = 32 * q + lane;
+        const uint32_t ut_off = (v >> 6) * 8192 + (v & 7) * 2;  // + i * 128 + swizzled chunk
+        uint16_t* out_col = p.out + h * kD + v;
+        for (int c = 0; c < nch; ++c) {
+            const int rows = len - kC * c < kC ? len - kC * c : kC;
+            const uint8_t* ut = rec_ptr(c) + kRecUt + ut_off;
+            uint32_t u[kC / 2];  // Ut[i][v] (fp16) for tokens i = 2e (low half) and 2e + 1
+#pragma unroll
+            for (int e = 0; e < kC / 2; ++e) {
+                uint32_t lo = 0, hi = 0;
+                if (2 * e < rows) lo = __ldg(reinterpret_cast<const unsigned short*>(ut + (2 * e) * 128 + ((((v & 63) >> 3) ^ ((2 * e) & 7)) << 4)));
+                if (2 * e + 1 < rows) hi = __ldg(reinterpret_cast<const unsigned short*>(ut + (2 * e + 1) * 128 + ((((v & 63) >> 3) ^ ((2 * e + 1) & 7)) << 4)));
+                u[e] = lo | (hi << 16);
+            }
+            const bool okc = __all_sync(0xffffffffu, mbar_wait(mmaO(c & 1), (c >> 1) & 1));
+            tc_fence_after();
+            if (!okc) {
+                if (lane == 0) record_status(32);
+                break;
+            }
+            uint16_t* dst = out_col + (t0 + static_cast<int64_t>(kC) * c) * (kHV * kD);
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {  // tokens 32 half + [0, 32)
+                float o[32];
+                tmem_ld32(taddr(accO(c & 1), 32 * q, 32 * half), o);
+                tmem_wait_ld();
+                if (half == 1) {  // the accumulator is read: release it
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(oFree(c & 1));
+                }
+#pragma unroll
+                for (int i0 = 0; i0 < 32; ++i0) {
+                    const int i = 32 * half + i0;
+                    if (i < rows) {
+                        const float uf = __half2float(__ushort_as_half(static_cast<unsigned short>(u[i >> 1] >> (16 * (i & 1)))));
+                        dst[static_cast<int64_t>(i) * (kHV * kD)] =
+                            __bfloat16_as_ushort(__float2bfloat16_rn(p.scale * (o[i0] + uf)));
+                    }
+                }
+            }
+        }
+    } else if (issuer) {
         bool ok = mbar_wait(fullKU(0), 0);
         if (ok) {
             tc_fence_after();
-            mma_ct<kF16, true, true, 64, 64, 64, 128, BV>(accS(tm, 0), aKU, aKU + 16384, false);  // K'^T U of chunk 0
+            // U_0^T K'_0 -> accS 0 (A = U MN-major [64 j][128 v], B = K' MN-major [64 j][128 k])
+            mma_ct<kF16, true, true, 64, 64, 64, 128, 128>(accS(0), aKU + 16384, aKU, false);
         }
         for (int c = 0; c < nch && ok; ++c) {
-            ok = (c == 0 || mbar_wait(imgReady, (c - 1) & 1)) && mbar_wait(fullM(c & 1), (c >> 1) & 1);
+            ok = mbar_wait(imgReady, c & 1) && mbar_wait(fullM(c & 1), (c >> 1) & 1);
             if (!ok) break;
             tc_fence_after();
-            mma_ct<kF16, false, true, kD, 128, kD, 128, BV>(accS(tm, c & 1), aM + (c & 1) * 32768,
-                                                           aSI + (c & 1) * 16384, true);
+            // S_c M_c^T accumulated onto U_c^T K'_c (B = M K-major [128 k][128 k'])
+            mma_ct_ta<kF16, false, kD, 128, 128>(accS(c & 1), sA(c & 1), aM + (c & 1) * 32768, true);
             mma_commit(mmaS);
-            if (c + 1 < nch) {  // next chunk's K'^T U into the other accumulator (its reader is done)
+            if (c + 1 < nch) {  // next chunk's U^T K' into the other accumulator (its reader is done)
                 const int b = (c + 1) % 3;
                 ok = mbar_wait(fullKU(b), ((c + 1) / 3) & 1);
                 if (!ok) break;
-                mma_ct<kF16, true, true, 64, 64, 64, 128, BV>(accS(tm, (c + 1) & 1), aKU + b * kCaKUBytes,
-                                                             aKU + b * kCaKUBytes + 16384, false);
+                mma_ct<kF16, true, true, 64, 64, 64, 128, 128>(accS((c + 1) & 1), aKU + b * 32768 + 16384,
+                                                              aKU + b * 32768, false);
             }
             ok = mbar_wait(fullQt(c % 3), (c / 3) & 1) && (c < 2 || mbar_wait(oFree(c & 1), ((c - 2) >> 1) & 1));
             if (!ok) break;
             tc_fence_after();
-            mma_ct<kF16, false, true, kD, 64, kD, 64, BV>(accO(tm, c & 1), aQt + (c % 3) * 16384,
-                                                         aSI + (c & 1) * 16384, false);
+            // O_c^T = S_c Qt_c^T (B = Qt K-major [64 i][128 k])
+            mma_ct_ta<kF16, false, kD, 64, 64>(accO(c & 1), sA(c & 1), aQt + (c % 3) * 16384, false);
             mma_commit(mmaO(c & 1));
-            // MMA_S(c) complete => so is everything issued before it: refill
+            // S_c M_c^T complete => so is everything issued before it: refill
             ok = mbar_wait(mmaS, c & 1);
             if (!ok) break;
             if (c + 2 < nch) {
@@ -704,83 +844,6 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
             for (int c = topQt > 2 ? topQt - 2 : 0; c <= topQt; ++c) mbar_wait(fullQt(c % 3), (c / 3) & 1);
             mma_commit(drain);
             mbar_wait(drain, 0);
-        }
-    } else if (warp < 4) {
-        const int k = tid;
-        for (int c = 0; c < nch; ++c) {
-            const bool okc = __all_sync(0xffffffffu, mbar_wait(mmaS, c & 1));  // warp-uniform exit
-            tc_fence_after();
-            float a0[32], a1[32];
-            tmem_ld32(taddr(accS(tm, c & 1), 32 * warp, 0), a0);
-            tmem_ld32(taddr(accS(tm, c & 1), 32 * warp, 32), a1);
-            tmem_wait_ld();
-            if (!okc) {
-                record_status(32);
-                break;
-            }
-            if (c + 1 < nch) {
-                const uint32_t img = aSI + ((c + 1) & 1) * 16384;
-#pragma unroll
-                for (int v = 0; v < 32; v += 8) {
-                    st_shared_u4(img + h16(k, v, kD), f16x8(a0 + v));
-                    st_shared_u4(img + h16(k, 32 + v, kD), f16x8(a1 + v));
-                }
-                fence_async_smem();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(imgReady);
-            } else {
-                float* ns_col = p.new_state + (unit * kD + v0) * kD + k;
-#pragma unroll
-                for (int v = 0; v < 32; ++v) {
-                    ns_col[v * kD] = a0[v];
-                    ns_col[(32 + v) * kD] = a1[v];
-                }
-            }
-        }
-    } else if (warp < 8) {
-        // output rows: token i = 16 (warp - 4) + lane of each chunk (lanes 0-15)
-        const int ow = warp - 4;
-        const int i = 16 * ow + (lane & 15);
-        uint16_t* out = p.out;
-        for (int c = 0; c < nch; ++c) {
-            const int tok = kC * c + i;
-            const bool act = lane < 16 && tok < len;
-            uint4 ut[8];  // Ut row i, logical 16-byte chunks (stored swizzled by i & 7)
-            const uint8_t* urow = rec_ptr(c) + kRecUt + vt * 8192 + i * 128;
-#pragma unroll
-            for (int q = 0; q < 8; ++q)
-                ut[q] = act ? __ldg(reinterpret_cast<const uint4*>(urow + ((q ^ (i & 7)) << 4))) : make_uint4(0, 0, 0, 0);
-            const bool okc = __all_sync(0xffffffffu, mbar_wait(mmaO(c & 1), (c >> 1) & 1));
-            tc_fence_after();
-            float o0[32], o1[32];
-            tmem_ld32(taddr(accO(tm, c & 1), 32 * ow, 0), o0);
-            tmem_ld32(taddr(accO(tm, c & 1), 32 * ow, 32), o1);
-            tmem_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(oFree(c & 1));
-            if (!okc) {
-                if (lane == 0) record_status(32);
-                break;
-            }
-            if (act) {
-                uint16_t* dst = out + ((t0 + tok) * kHV + h) * kD + v0;
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    float u[8];
-                    h16x8_to_f32(ut[q], u);
-                    const float* o = q < 4 ? o0 + 8 * q : o1 + 8 * (q - 4);
-                    uint32_t w[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const __nv_bfloat162 b2 = __floats2bfloat162_rn(p.scale * (o[2 * e] + u[2 * e]),
-                                                                        p.scale * (o[2 * e + 1] + u[2 * e + 1]));
-                        w[e] = *reinterpret_cast<const uint32_t*>(&b2);
-                    }
-                    *reinterpret_cast<uint4*>(dst + 8 * q) = make_uint4(w[0], w[1], w[2], w[3]);
-                }
-            }
         }
     }
     tc_fence_before();
@@ -853,7 +916,7 @@ cudaError_t launch_prefill_chunked(const PrefillParams& p, void* workspace, cuda
         p, ws, L, tmK, tmQ, tmV);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if ((e = set_smem(gdn_chunk_carry_kernel, kCaSmem)) != cudaSuccess) return e;
-    const int64_t grid = p.num_seqs * kHV * (kD / kCarryBV);
+    const int64_t grid = p.num_seqs * kHV;
     if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
     gdn_chunk_carry_kernel<<<static_cast<unsigned>(grid), kCarryThreads, kCaSmem, stream>>>(p, ws, L);
     return cudaGetLastError();
@@ -873,7 +936,8 @@ cudaError_t launch_prefill(const PrefillParams& p, int path, void* workspace, si
 // D[M x N] = A[M x K] . B[N x K]^T through the same image writers,
 // descriptors and TMEM read-back as the kernels above (one CTA).  flags:
 // bit 0 A MN-major, bit 1 B MN-major, bit 2 accumulator at TMEM lane 16
-// (the second M=64 tile of a lane-packed pair; M = 64 only).
+// (the second M=64 tile of a lane-packed pair; M = 64 only), bit 3 A read
+// from TMEM (16-bit kinds, M = 128, K-major).
 template <Kind KIND>
 __device__ __forceinline__ void selftest_issue(int flags, uint32_t d, uint32_t a, uint32_t b, int M, int N, int K) {
     const int ar = (flags & 1) ? K : M, br = (flags & 2) ? K : N;
@@ -892,7 +956,7 @@ __global__ void __launch_bounds__(128, 1)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int eb = kind == kTF32 ? 4 : 2;
     const int kblocks = K * eb / 128;
-    const bool a_mn = flags & 1, b_mn = flags & 2, lane16 = flags & 4;
+    const bool a_mn = flags & 1, b_mn = flags & 2, lane16 = flags & 4, a_tmem = flags & 8;
     uint8_t* sA = sm;
     uint8_t* sB = sm + M * K * eb;
     uint64_t* bar = reinterpret_cast<uint64_t*>(sB + N * K * eb);
@@ -918,6 +982,7 @@ __global__ void __launch_bounds__(128, 1)
     }
     int ncols = 32;
     while (ncols < N) ncols <<= 1;
+    if (a_tmem) ncols = 512;  // D at column 0, A from column 256
     if (tid == 0) {
         mbar_init(smem_u32(bar), 1);
         fence_mbar_init();
@@ -932,7 +997,31 @@ __global__ void __launch_bounds__(128, 1)
     tc_fence_after();
     const uint32_t tm = *tslot;
     const uint32_t d = lane16 ? taddr(tm, 16, 0) : tm;
-    if (tid == 0) {
+    if (a_tmem) {
+        // A (16-bit, M = 128) into TMEM: row m = lane m, k pairs packed low-first
+        const uint16_t* arow = static_cast<const uint16_t*>(A) + tid * K;
+        for (int c0 = 0; c0 < K / 2; c0 += 32) {
+            uint32_t w[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                w[i] = static_cast<uint32_t>(arow[2 * (c0 + i)]) | (static_cast<uint32_t>(arow[2 * (c0 + i) + 1]) << 16);
+            tmem_st32(taddr(tm, 32 * warp, 256 + c0), w);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+    }
+    if (tid == 0 && a_tmem) {
+        const uint32_t id = idesc(kind == kBF16 ? kBF16 : kF16, 128, N, false, b_mn);
+        const uint32_t b = smem_u32(sB);
+        for (int s = 0; s < K / 16; ++s) {
+            const uint64_t bd = b_mn ? sw128_desc_mn(b + s * 16 * 128, K * 128)
+                                     : sw128_desc(b + ((s * 32) >> 7) * N * 128 + ((s * 32) & 127));
+            mma_f16_ta(d, tm + 256 + 8 * s, bd, id, s > 0 ? 1u : 0u);
+        }
+        mma_commit(smem_u32(bar));
+    } else if (tid == 0) {
         if (kind == kBF16)
             selftest_issue<kBF16>(flags, d, smem_u32(sA), smem_u32(sB), M, N, K);
         else if (kind == kF16)

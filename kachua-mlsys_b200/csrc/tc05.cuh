@@ -158,6 +158,19 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&r)[16]) {
     for (int i = 0; i < 16; ++i) r[i] = __uint_as_float(u[i]);
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// 32 registers per thread -> 32 lanes x 32 consecutive columns.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&u)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(u[0]), "r"(u[1]), "r"(u[2]), "r"(u[3]), "r"(u[4]), "r"(u[5]), "r"(u[6]), "r"(u[7]), "r"(u[8]),
+        "r"(u[9]), "r"(u[10]), "r"(u[11]), "r"(u[12]), "r"(u[13]), "r"(u[14]), "r"(u[15]), "r"(u[16]), "r"(u[17]),
+        "r"(u[18]), "r"(u[19]), "r"(u[20]), "r"(u[21]), "r"(u[22]), "r"(u[23]), "r"(u[24]), "r"(u[25]), "r"(u[26]),
+        "r"(u[27]), "r"(u[28]), "r"(u[29]), "r"(u[30]), "r"(u[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // TMEM address of (lane, column) relative to an allocation base.
 __device__ __forceinline__ uint32_t taddr(uint32_t base, uint32_t lane, uint32_t col) {
@@ -216,6 +229,15 @@ __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(a), "l"(b), "r"(id), "r"(acc)
+        : "memory");
+}
+// kind::f16 with the A operand in TMEM (M = 128: row m in lane m, K packed two
+// 16-bit elements per 32-bit column, 8 columns per instruction's K = 16).
+__device__ __forceinline__ void mma_f16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t id, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b), "r"(id), "r"(acc)
         : "memory");
 }
 // Arrives once on `bar` when every tcgen05 op this thread issued so far is done.
@@ -286,6 +308,22 @@ __device__ __forceinline__ void mma_ct(uint32_t d_tmem, uint32_t a_smem, uint32_
             mma_bf16(d_tmem, ad, bd, id, acc);
         else
             mma_tf32(d_tmem, ad, bd, id, acc);
+    }
+}
+
+// D[128 x N] (+)= A[128 x KDIM] . B^T with A (16-bit) in TMEM from column
+// a_tmem (KDIM / 2 columns) and B a K-major SW128 image of BROWS rows per
+// K-block, or (B_MN) an MN-major image of KDIM rows.
+template <Kind KIND, bool B_MN, int KDIM, int BROWS, int N>
+__device__ __forceinline__ void mma_ct_ta(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_smem, bool accumulate) {
+    static_assert(KIND != kTF32, "A in TMEM: 16-bit kinds only");
+    constexpr uint32_t id = idesc(KIND, 128, N, false, B_MN);
+    constexpr int kSteps = KDIM / 16;
+    const uint64_t b0 = B_MN ? sw128_desc_mn(b_smem, BROWS * 128) : sw128_desc(b_smem);
+#pragma unroll
+    for (int s = 0; s < kSteps; ++s) {
+        const uint32_t b_off = B_MN ? s * 16 * 128 : ((s * 32) >> 7) * BROWS * 128 + ((s * 32) & 127);
+        mma_f16_ta(d_tmem, a_tmem + 8 * s, b0 + (b_off >> 4), id, (accumulate || s > 0) ? 1u : 0u);
     }
 }
 

@@ -1,6 +1,6 @@
 """The tcgen05 layer (SW128 operand images, smem/instruction descriptors,
-M=64 / M=128 TMEM layouts, bf16 and tf32 kinds) against torch matmul, for
-every shape the prefill kernels issue."""
+M=64 / M=128 TMEM layouts, A read from TMEM, bf16 / fp16 / tf32 kinds)
+against torch matmul, for every shape the prefill kernels issue."""
 import ctypes
 
 import pytest
@@ -43,6 +43,11 @@ SHAPES = [  # (kind, M, N, K): the prepare and carry kernels' MMAs, plus neighbo
     ("f16", 128, 128, 64, 3),
     ("f16", 64, 256, 64, 6),
     ("f16", 128, 64, 128, 2),
+    # A operand in TMEM (the carry's state and output MMAs)
+    ("f16", 128, 128, 128, 8),
+    ("f16", 128, 64, 128, 8),
+    ("f16", 128, 128, 64, 10),
+    ("bf16", 128, 64, 64, 8),
 ]
 
 
