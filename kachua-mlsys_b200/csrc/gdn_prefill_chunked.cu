@@ -52,9 +52,9 @@ constexpr int kC = 64;
 // images for the carry, at these offsets:
 constexpr int kRecM = 0;          // M = G_C I - K'^T W   [128 k][128 k']  K-major SW128        32 KiB
 constexpr int kRecKb = 32768;     // K' = tail (.) K      [64 j][128 k]    MN-major (2 kblocks) 16 KiB
-constexpr int kRecU = 49152;      // U                    [64 j][128 v]    MN-major (2 blocks)  16 KiB
-constexpr int kRecQt = 65536;     // Qt = G (.) Q - P W   [64 i][128 k]    K-major              16 KiB
-constexpr int kRecUt = 81920;     // Ut = P U             [64 i][128 v]    SW128 rows (2 blocks) 16 KiB
+constexpr int kRecUT = 49152;     // U^T                  [128 v][64 j]    K-major SW128        16 KiB
+constexpr int kRecQt = 65536;     // Qt^T = (G (.) Q - P W)^T [128 k][64 i] MN-major SW128      16 KiB
+constexpr int kRecUt = 81920;     // Ut^T = (P U)^T       [128 v][64 i]    SW128 rows           16 KiB
 constexpr int kHeadRecBytes = 98304;
 
 __host__ __device__ inline int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
@@ -151,22 +151,25 @@ __global__ void __launch_bounds__(1024) gdn_chunk_table_kernel(const PrefillPara
 // One CTA (128 threads) per chunk record and v-head: everything the carry's
 // chain does not need, finished per chunk in fp16 operand images (fp32
 // accumulation) and bulk-stored to the workspace:
-//   M   = G_C I - K'^T W    [k][k']   K-major        (A of the state MMA)
-//   K'  = tail (.) K        [j][k]    MN-major       (A of the carry's D = K'^T U)
-//   U                       [j][v]    MN-major, two 64-column blocks
-//   Qt  = G (.) Q - P W     [i][k]    K-major        (A of the output MMA)
-//   Ut  = P U               [i][v]    SW128 rows, two 64-column blocks
+//   M    = G_C I - K'^T W     [k][k']  K-major    (B of the state MMA S M^T)
+//   K'   = tail (.) K         [j][k]   MN-major   (B of the carry's U^T K')
+//   U^T                       [v][j]   K-major    (A of the carry's U^T K')
+//   Qt^T = (G (.) Q - P W)^T  [k][i]   MN-major   (B of the output MMA S Qt^T)
+//   Ut^T = (P U)^T            [v][i]   SW128 rows (added by the output epilogue)
 // K, Q and V arrive by tiled TMA loads straight into SW128 images (rows past
-// the chunk hold the next tokens or zeros; every use masks them).  A^-1 comes
-// from an fp32 forward substitution ((I + N) x = e_j, one column per thread);
-// W | U = A^-1 [bGK | bV] and the products with P and K' run on tcgen05 with
-// two M=64 results packed into TMEM lanes 0-15 / 16-31.
+// the chunk hold the next tokens or zeros; every use masks them).  A^-1 of
+// the unit-lower-triangular A = I + N is blocked 2 x 2: the two 32 x 32
+// diagonal inverses by fp32 forward substitution (a column per thread), the
+// off-diagonal block X21 = -X22 (N21 X11) by two tcgen05 products.  The
+// remaining products are computed transposed (M = 128 = k or v rows, all TMEM
+// lanes busy): [W | U]^T = [bGK | bV]^T A^-T, Qt^T = Q^T diag(G) + W^T (-P)^T,
+// Ut^T = -(U^T (-P)^T) and K'^T W.
 constexpr int kPrepThreads = 128;
 constexpr int kPrKQ = 0;        // bf16 [K;Q] K-major, kblock b at b*16K (rows 0-63 K, 64-127 Q); K rows -> K' in place
-constexpr int kPrN = 32768;     // fp32 N [64][64], 16-byte chunks swizzled by (row & 15)  -> Ut staging
-constexpr int kPrPO = 49152;    // f16 P [64 i][64 j] K-major                              } -> Qt staging
-constexpr int kPrX = 57344;     // f16 A^-1 [64 i][64 m] K-major                           }
-constexpr int kPrRHS = 65536;   // f16 [bGK | bV] MN-major [64 j][256] (V by TMA) -> [W | U] -> M staging
+constexpr int kPrN = 32768;     // fp32 diagonal blocks of N (8K) | f16 NL (8K); later TB | diag(G); then Qt^T staging
+constexpr int kPrPO = 49152;    // f16 -P [64 i][64 j] K-major                     } later Ut^T staging
+constexpr int kPrX = 57344;     // f16 A^-1 [64 i][64 m] K-major                  }
+constexpr int kPrRHS = 65536;   // f16 [bGK | bV] MN-major [64 j][256] (V by TMA) -> W^T | U^T K-major [128][64] -> M staging
 constexpr int kPrSmall = 98304;
 constexpr int kPrSmem = kPrSmall + 1024 + 1024;
 constexpr int kPrTmemCols = 256;
@@ -274,8 +277,11 @@ __device__ __forceinline__ void named_sync(int id, int count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
-// fp32 N image: row i is 256 bytes; its 16-byte chunk c sits at position c ^ (i & 15)
-__device__ __forceinline__ uint32_t n_off(int i, int m) { return i * 256 + ((((m >> 2) ^ (i & 15))) << 4); }
+// fp32 diagonal 32 x 32 block d of N: row r is 128 bytes, its 16-byte chunk c
+// at position c ^ (r & 7)
+__device__ __forceinline__ uint32_t nd_off(int d, int r, int m) {
+    return d * 4096 + r * 128 + ((((m >> 2) ^ (r & 7))) << 4) + (m & 3) * 4;
+}
 
 __global__ void __launch_bounds__(kPrepThreads, 2)
     gdn_chunk_prepare_kernel(const PrefillParams p, uint8_t* __restrict__ ws, const WsLayout L,
@@ -287,6 +293,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
     PrepSmall& sml = *reinterpret_cast<PrepSmall*>(sm + kPrSmall);
     const uint32_t aKQ = smem_u32(sm + kPrKQ), aN = smem_u32(sm + kPrN), aPO = smem_u32(sm + kPrPO),
                    aX = smem_u32(sm + kPrX), aRHS = smem_u32(sm + kPrRHS);
+    const uint32_t aNL = aN + 8192;  // f16 N21 image (later diag(G)); aN: fp32 diagonal blocks (later TB)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t rec = blockIdx.x;
@@ -315,6 +322,11 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
         tmem_alloc(smem_u32(&sml.tmem_base), kPrTmemCols);
         tmem_relinquish();
     }
+    // zero the A^-1 image (its off-diagonal blocks stay zero until X21 is known)
+    S.st16(aX + tid * 64, make_uint4(0, 0, 0, 0));
+    S.st16(aX + tid * 64 + 16, make_uint4(0, 0, 0, 0));
+    S.st16(aX + tid * 64 + 32, make_uint4(0, 0, 0, 0));
+    S.st16(aX + tid * 64 + 48, make_uint4(0, 0, 0, 0));
     // gates and the inclusive prefix of log2 g (threads 0-63 = tokens; warp scans)
     float lgs = 0.f;
     if (tid < kC) {
@@ -341,6 +353,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
     const uint32_t tm = sml.tmem_base;
     __syncthreads();
     bool ok = mbar_wait(barL, 0);
+    uint32_t phase = 0;
 
     // 1. Gram [K;Q] K^T (bf16, M=128, N=64, K=128) -> TMEM columns 0-63
     if (tid == 0 && ok) {
@@ -365,11 +378,14 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
         for (int q = 0; q < 8; ++q) f[q] = act ? sc * f[q] : 0.f;
         S.st16(aRHS + blk * 8192 + in_row, f16x8(f));
     }
-    ok = mbar_wait(barM, 0) && ok;
+    ok = mbar_wait(barM, phase) && ok;
+    phase ^= 1;
     tc_fence_after();
     {
-        // 2. Gram epilogue (thread = accumulator row): rows 0-63 give N (fp32),
-        //    rows 64-127 the output-side P = Gam (.) Q K^T, j <= i (f16 image)
+        // 2. Gram epilogue (thread = accumulator row).  Rows 0-63 give N: its
+        //    fp32 diagonal 32-blocks and the f16 image NL of its lower-left
+        //    block (zero elsewhere); rows 64-127 the f16 image of -P, with
+        //    P = Gam (.) Q K^T for j <= i.
         float g[64];
         {
             float t32[32];
@@ -382,18 +398,24 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
             for (int j = 0; j < 32; ++j) g[32 + j] = t32[j];
         }
         if (warp < 2) {
-            const int i = tid;
+            const int i = tid, d = warp, r = lane;
             const float LGi = sml.LG[i], bi = sml.beta[i];
             const bool act = i < n;
+            float nv[64];
 #pragma unroll
-            for (int j0 = 0; j0 < kC; j0 += 4) {
-                float nv[4];
+            for (int j = 0; j < kC; ++j) nv[j] = (j < i && act) ? bi * fast_exp2(LGi - sml.LG[j]) * g[j] : 0.f;
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int j = j0 + e;
-                    nv[e] = (j < i && act) ? bi * fast_exp2(LGi - sml.LG[j]) * g[j] : 0.f;
-                }
-                S.stf4(aN + n_off(i, j0), make_float4(nv[0], nv[1], nv[2], nv[3]));
+            for (int m0 = 0; m0 < 32; m0 += 4) {  // (compile-time indices: d selects, never indexes)
+                const float4 lo = make_float4(nv[m0], nv[m0 + 1], nv[m0 + 2], nv[m0 + 3]);
+                const float4 hi = make_float4(nv[32 + m0], nv[33 + m0], nv[34 + m0], nv[35 + m0]);
+                S.stf4(aN + nd_off(d, r, m0), d == 0 ? lo : hi);
+            }
+#pragma unroll
+            for (int j0 = 0; j0 < kC; j0 += 8) {
+                float f[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) f[e] = (d == 1 && j0 < 32) ? nv[j0 + e] : 0.f;
+                S.st16(aNL + h16(i, j0, 64), f16x8(f));
             }
         } else {
             const int i = tid - 64;
@@ -404,7 +426,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
                     const int j = j0 + e;
-                    pv[e] = (j <= i) ? fast_exp2(LGi - sml.LG[j]) * g[j] : 0.f;
+                    pv[e] = (j <= i) ? -fast_exp2(LGi - sml.LG[j]) * g[j] : 0.f;
                 }
                 S.st16(aPO + h16(i, j0, 64), f16x8(pv));
             }
@@ -413,59 +435,35 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
     tc_fence_before();
     if (__syncthreads_or(!ok)) goto abort;
     if (warp < 2) {
-        // 3a. A^-1 = (I + N)^-1 by blocked forward substitution in fp32, one
-        //     column j = tid per thread, 16-row blocks: earlier blocks enter as
-        //     a 16-accumulator update, then the block's own triangle.  Solved
-        //     rows of X are kept (fp32, row-major [m][j]) in the N rows they
-        //     replace -- a row of N is dead once its block is solved.
-        const int j = tid;
-#pragma unroll 1
-        for (int b = 0; b < 4; ++b) {
-            const int i0 = 16 * b;
-            float acc[16];
+        // 3a. diagonal blocks of A^-1: (I + N_dd) x = e_j, d = warp, column
+        //     j = lane, 32 rows in fp32 (four partial sums per row)
+        const int d = warp, j = lane;
+        float x[32];
 #pragma unroll
-            for (int r = 0; r < 16; ++r) acc[r] = (i0 + r == j) ? 1.f : 0.f;
-#pragma unroll 1
-            for (int m0 = 0; m0 < i0; m0 += 4) {
-                float xm[4];
+        for (int r = 0; r < 32; ++r) {
+            float a0 = (r == j) ? 1.f : 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll
-                for (int e = 0; e < 4; ++e) xm[e] = *reinterpret_cast<const float*>(sm + kPrN + (m0 + e) * 256 + j * 4);
-#pragma unroll
-                for (int r = 0; r < 16; ++r) {
-                    const float4 nv = S.ldf4(aN + n_off(i0 + r, m0));
-                    acc[r] = fmaf(-nv.x, xm[0], acc[r]);
-                    acc[r] = fmaf(-nv.y, xm[1], acc[r]);
-                    acc[r] = fmaf(-nv.z, xm[2], acc[r]);
-                    acc[r] = fmaf(-nv.w, xm[3], acc[r]);
-                }
+            for (int m = 0; m < r; m += 4) {
+                const float4 nv = S.ldf4(aN + nd_off(d, r, m));
+                a0 = fmaf(-nv.x, x[m], a0);
+                if (m + 1 < r) a1 = fmaf(-nv.y, x[m + 1], a1);
+                if (m + 2 < r) a2 = fmaf(-nv.z, x[m + 2], a2);
+                if (m + 3 < r) a3 = fmaf(-nv.w, x[m + 3], a3);
             }
-#pragma unroll
-            for (int r = 1; r < 16; ++r) {
-#pragma unroll
-                for (int m = 0; m < r; m += 4) {
-                    const float4 nv = S.ldf4(aN + n_off(i0 + r, i0 + m));
-                    acc[r] = fmaf(-nv.x, acc[m], acc[r]);
-                    if (m + 1 < r) acc[r] = fmaf(-nv.y, acc[m + 1], acc[r]);
-                    if (m + 2 < r) acc[r] = fmaf(-nv.z, acc[m + 2], acc[r]);
-                    if (m + 3 < r) acc[r] = fmaf(-nv.w, acc[m + 3], acc[r]);
-                }
-            }
-            named_sync(1, 64);  // both warps are done reading this block's N rows
-#pragma unroll
-            for (int r = 0; r < 16; ++r) {
-                *reinterpret_cast<float*>(sm + kPrN + (i0 + r) * 256 + j * 4) = acc[r];
-                S.st2(aX + h16(i0 + r, j, 64), __half_as_ushort(__float2half_rn(acc[r])));
-            }
+            x[r] = (a0 + a1) + (a2 + a3);
         }
+#pragma unroll
+        for (int r = 0; r < 32; ++r) S.st2(aX + h16(32 * d + r, 32 * d + j, 64), __half_as_ushort(__float2half_rn(x[r])));
     } else {
-        // 3b. K' = tail (.) K in place over the K rows of [K;Q] (rows >= n zero)
+        // 3b. in place over [K;Q] (bf16 -> f16, rows >= n zero): K' = tail (.) K
+        //     in the K rows, plain Q in the Q rows (the A operand of Qt^T)
         const float LGc = sml.LG[kC - 1];
 #pragma unroll 4
-        for (int it = 0; it < 16; ++it) {
+        for (int it = 0; it < 32; ++it) {
             const int u = it * 64 + (tid - 64);
-            const int kb = u >> 9, row = (u >> 3) & 63;
-            const uint32_t addr = aKQ + kb * 16384 + row * 128 + (u & 7) * 16;
-            const float sc = fast_exp2(LGc - sml.LG[row]);
+            const int kb = u >> 10, qrow = (u >> 9) & 1, row = (u >> 3) & 63;
+            const uint32_t addr = aKQ + kb * 16384 + qrow * 8192 + row * 128 + (u & 7) * 16;
+            const float sc = qrow ? 1.f : fast_exp2(LGc - sml.LG[row]);
             const bool act = row < n;
             float f[8];
             bf16x8_to_f32(S.ld16(addr), f);
@@ -475,78 +473,143 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
         }
     }
     fence_async_smem();
+    tc_fence_before();
     __syncthreads();
-    if (tid == 0) {  // 4. W | U = A^-1 [bGK | bV]: W -> lanes 0-15, U -> lanes 16-31 (columns 0-127)
+    if (tid == 0) {  // 4. T = N21 X11 (lower-left block of NL . diag(X11, X22)) -> columns 0-63, M=64
         tc_fence_after();
-        mma_ct<kF16, false, true, 64, 64, 64, 64, 128>(taddr(tm, 0, 0), aX, aRHS, false);
-        mma_ct<kF16, false, true, 64, 64, 64, 64, 128>(taddr(tm, 16, 0), aX, aRHS + 16384, false);
+        mma_ct<kF16, false, true, 64, 64, 64, 64, 64>(tm, aNL, aX, false);
         mma_commit(barM);
-        bulk_s2g(out_rec + kRecKb, aKQ, 8192);  // K' (final): two 8 KiB kblocks
-        bulk_s2g(out_rec + kRecKb + 8192, aKQ + 16384, 8192);
-        bulk_commit();
     }
-    ok = mbar_wait(barM, 1) && ok;
+    ok = mbar_wait(barM, phase) && ok;
+    phase ^= 1;
     tc_fence_after();
-    {  // W | U rows -> fp16 MN-major B image over the RHS (W columns 0-127, U 128-255)
-        const int i = 16 * warp + (lane & 15);
-        const uint32_t dst = aRHS + (lane >= 16 ? 16384 : 0);
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-            float acc[32];
-            tmem_ld32(taddr(tm, 32 * warp, 32 * c), acc);
-            tmem_wait_ld();
+    {
+        // rows i of T (lanes 0-15: i = 16 warp + lane) -> f16 MN-major B image TB
+        // (over the fp32 diagonal blocks); diag(G) (rows >= n zero) over NL
+        float t32[32], u32[32];
+        tmem_ld32(taddr(tm, 32 * warp, 0), t32);
+        tmem_ld32(taddr(tm, 32 * warp, 32), u32);
+        tmem_wait_ld();
+        if (lane < 16) {
+            const int i = 16 * warp + lane;
 #pragma unroll
-            for (int j0 = 0; j0 < 32; j0 += 8) S.st16(dst + h16(i, 32 * c + j0, 64), f16x8(acc + j0));
+            for (int j0 = 0; j0 < 32; j0 += 8) {
+                S.st16(aN + h16(i, j0, 64), f16x8(t32 + j0));
+                S.st16(aN + h16(i, 32 + j0, 64), f16x8(u32 + j0));
+            }
+        }
+        if (tid < kC) {
+            const int i = tid;
+            const float Gi = i < n ? fast_exp2(sml.LG[i]) : 0.f;
+#pragma unroll
+            for (int j0 = 0; j0 < kC; j0 += 8) {
+                float f[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) f[e] = (j0 + e == i) ? Gi : 0.f;
+                S.st16(aNL + h16(i, j0, 64), f16x8(f));
+            }
         }
     }
     fence_async_smem();
     tc_fence_before();
     if (__syncthreads_or(!ok)) goto abort;
-    if (tid == 0) {  // 5. P W -> lanes 0-15, P U -> lanes 16-31 (columns 0-127); K'^T W (M=128) -> columns 128-255
+    if (tid == 0) {  // 5. X22 T -> columns 64-127 (M=64); X21 = -(X22 T)
         tc_fence_after();
-        mma_ct<kF16, false, true, 64, 64, 64, 64, 128>(taddr(tm, 0, 0), aPO, aRHS, false);
-        mma_ct<kF16, false, true, 64, 64, 64, 64, 128>(taddr(tm, 16, 0), aPO, aRHS + 16384, false);
-        mma_ct<kF16, true, true, 64, 128, 64, 128, 128>(taddr(tm, 0, 128), aKQ, aRHS, false);
+        mma_ct<kF16, false, true, 64, 64, 64, 64, 64>(tm + 64, aX, aN, false);
         mma_commit(barM);
-        bulk_s2g(out_rec + kRecU, aRHS + 16384, 16384);  // U: two 64-column MN-major blocks
+    }
+    ok = mbar_wait(barM, phase) && ok;
+    phase ^= 1;
+    tc_fence_after();
+    {
+        float t32[32];
+        tmem_ld32(taddr(tm, 32 * warp, 64), t32);
+        tmem_wait_ld();
+        if (warp >= 2 && lane < 16) {  // rows 32-63: columns 0-31 of A^-1
+            const int i = 16 * warp + lane;
+#pragma unroll
+            for (int j0 = 0; j0 < 32; j0 += 8) {
+                float f[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) f[e] = -t32[j0 + e];
+                S.st16(aX + h16(i, j0, 64), f16x8(f));
+            }
+        }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    if (__syncthreads_or(!ok)) goto abort;
+    if (tid == 0) {  // 6. [W | U]^T = [bGK | bV]^T A^-T: W^T -> columns 0-63, U^T -> 64-127 (M=128)
+        tc_fence_after();
+        mma_ct<kF16, true, false, 64, 64, 64, 128, 64>(tm, aRHS, aX, false);
+        mma_ct<kF16, true, false, 64, 64, 64, 128, 64>(tm + 64, aRHS + 16384, aX, false);
+        mma_commit(barM);
+    }
+    ok = mbar_wait(barM, phase) && ok;
+    phase ^= 1;
+    tc_fence_after();
+    {  // row r of W^T and U^T -> f16 K-major images [128][64] over the RHS
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+            float acc[32], acc2[32];
+            tmem_ld32(taddr(tm, 32 * warp, 64 * half), acc);
+            tmem_ld32(taddr(tm, 32 * warp, 64 * half + 32), acc2);
+            tmem_wait_ld();
+            const uint32_t img = aRHS + half * 16384;
+#pragma unroll
+            for (int j0 = 0; j0 < 32; j0 += 8) {
+                S.st16(img + h16(tid, j0, 128), f16x8(acc + j0));
+                S.st16(img + h16(tid, 32 + j0, 128), f16x8(acc2 + j0));
+            }
+        }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    if (__syncthreads_or(!ok)) goto abort;
+    if (tid == 0) {
+        // 7. Qt^T = Q^T diag(G) + W^T (-P)^T -> columns 0-63; -(Ut^T) = U^T (-P)^T -> 64-127;
+        //    K'^T W -> 128-255 (all M=128)
+        tc_fence_after();
+        mma_ct<kF16, true, false, 64, 128, 64, 128, 64>(tm, aKQ + 8192, aNL, false);
+        mma_ct<kF16, false, false, 64, 128, 64, 128, 64>(tm, aRHS, aPO, true);
+        mma_ct<kF16, false, false, 64, 128, 64, 128, 64>(tm + 64, aRHS + 16384, aPO, false);
+        mma_ct<kF16, true, false, 64, 128, 128, 128, 128>(tm + 128, aKQ, aRHS, false);
+        mma_commit(barM);
+        bulk_s2g(out_rec + kRecUT, aRHS + 16384, 16384);  // U^T
+        bulk_s2g(out_rec + kRecKb, aKQ, 8192);             // K': two 8 KiB kblocks
+        bulk_s2g(out_rec + kRecKb + 8192, aKQ + 16384, 8192);
         bulk_commit();
     }
-    ok = mbar_wait(barM, 0) && ok;
-    if (tid == 0) bulk_wait_read_all();  // U and K' have left shared memory before it is reused
+    ok = mbar_wait(barM, phase) && ok;
+    phase ^= 1;
+    if (tid == 0) bulk_wait_read_all();  // U^T and K' have left shared memory before it is reused
     tc_fence_after();
     if (__syncthreads_or(!ok)) goto abort;
     {
-        // 6a. Qt = G (.) Q - P W (lanes 0-15) and Ut = P U (lanes 16-31), row i
-        const int i = 16 * warp + (lane & 15);
-        const bool act = i < n;
-        const float Gi = fast_exp2(sml.LG[i]);
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-            float acc[32];
-            tmem_ld32(taddr(tm, 32 * warp, 32 * c), acc);
+        // 8. row r = tid of Qt^T (staging over N), Ut^T (over -P and A^-1) and
+        //    M = G_C I - K'^T W (over [K;Q])
+        {
+            float acc[32], acc2[32];
+            tmem_ld32(taddr(tm, 32 * warp, 0), acc);
+            tmem_ld32(taddr(tm, 32 * warp, 32), acc2);
             tmem_wait_ld();
-            if (lane < 16) {
 #pragma unroll
-                for (int j0 = 0; j0 < 32; j0 += 8) {
-                    const int col = 32 * c + j0;
-                    float qf[8];
-                    bf16x8_to_f32(S.ld16(aKQ + h16(64 + i, col, 128)), qf);
+            for (int j0 = 0; j0 < 32; j0 += 8) {
+                S.st16(aN + h16(tid, j0, 128), f16x8(acc + j0));
+                S.st16(aN + h16(tid, 32 + j0, 128), f16x8(acc2 + j0));
+            }
+            tmem_ld32(taddr(tm, 32 * warp, 64), acc);
+            tmem_ld32(taddr(tm, 32 * warp, 96), acc2);
+            tmem_wait_ld();
 #pragma unroll
-                    for (int q = 0; q < 8; ++q) qf[q] = act ? Gi * qf[q] - acc[j0 + q] : 0.f;
-                    S.st16(aPO + h16(i, col, 64), f16x8(qf));  // Qt staging over P and A^-1
-                }
-            } else {
+            for (int j0 = 0; j0 < 32; j0 += 8) {
+                float f[8], f2[8];
 #pragma unroll
-                for (int j0 = 0; j0 < 32; j0 += 8) {
-                    const int col = 32 * c + j0;
-                    float uf[8];
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) uf[q] = act ? acc[j0 + q] : 0.f;
-                    S.st16(aN + (col >> 6) * 8192 + h16(i, col & 63, 64), f16x8(uf));  // Ut staging over N
-                }
+                for (int e = 0; e < 8; ++e) f[e] = -acc[j0 + e], f2[e] = -acc2[j0 + e];
+                S.st16(aPO + h16(tid, j0, 128), f16x8(f));
+                S.st16(aPO + h16(tid, 32 + j0, 128), f16x8(f2));
             }
         }
-        // 6b. M = G_C I - K'^T W, row k = tid (f16 K-major, staging over the RHS)
         const float Gc = fast_exp2(sml.LG[kC - 1]);
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
@@ -558,7 +621,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
                 float f[8];
 #pragma unroll
                 for (int q = 0; q < 8; ++q) f[q] = (32 * c + j0 + q == tid ? Gc : 0.f) - acc[j0 + q];
-                S.st16(aRHS + h16(tid, 32 * c + j0, 128), f16x8(f));
+                S.st16(aKQ + h16(tid, 32 * c + j0, 128), f16x8(f));
             }
         }
     }
@@ -566,11 +629,11 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
     tc_fence_before();
     __syncthreads();
     if (tid == 0) {
-        bulk_s2g(out_rec + kRecQt, aPO, 16384);
-        bulk_s2g(out_rec + kRecUt, aN, 16384);
-        bulk_s2g(out_rec + kRecM, aRHS, 32768);
+        bulk_s2g(out_rec + kRecQt, aN, 16384);
+        bulk_s2g(out_rec + kRecUt, aPO, 16384);
+        bulk_s2g(out_rec + kRecM, aKQ, 32768);
         bulk_commit();
-        bulk_wait_all();
+        bulk_wait_read_all();
     }
     goto done;
 abort:
@@ -601,14 +664,17 @@ done:
 //               chunk, and the fp32 final state;
 //   warps 8-11  output epilogue: lane = v, 64 columns = tokens; adds Ut and
 //               writes bf16 rows (coalesced over v);
-//   warp 12     one thread issues every MMA and bulk copy.
+//   warp 12     one thread issues every MMA;
+//   warp 13     one thread issues the bulk copies (refills follow the state
+//               MMA's completion, off the MMA issuer's path).
 // M is double-buffered, [K' | U] and Qt triple-buffered, each refilled when
 // the MMA that read it is known complete, two chunks before use.
-constexpr int kCarryThreads = 416;
+constexpr int kCarryThreads = 448;
 constexpr int kCaM = 0;                         // f16 M K-major [128 k][128 k'], 2 x 32 KiB
-constexpr int kCaKU = 65536;                    // K' [64 j][128 k] + U [64 j][128 v] (MN-major), 3 x 32 KiB
-constexpr int kCaQt = kCaKU + 3 * 32768;        // f16 Qt K-major [64 i][128 k], 3 x 16 KiB
-constexpr int kCaSmall = kCaQt + 3 * 16384;
+constexpr int kCaKU = 65536;                    // K' [64 j][128 k] (MN-major) + U^T [128 v][64 j] (K-major), 3 x 32 KiB
+constexpr int kCaQt = kCaKU + 3 * 32768;        // f16 Qt^T MN-major [128 k][64 i], 3 x 16 KiB
+constexpr int kCaO = kCaQt + 3 * 16384;         // bf16 output tile [64 i][128 v]
+constexpr int kCaSmall = kCaO + 16384;
 constexpr int kCaSmem = kCaSmall + 256 + 1024;
 constexpr int kCaTmemCols = 512;  // accS x 2 [0, 256), fp16 S x 2 [256, 384), accO x 2 [384, 512)
 
@@ -630,7 +696,9 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     auto fullM = [&](int b) { return bar0 + 8 * b; };         // 2
     auto fullKU = [&](int b) { return bar0 + 16 + 8 * b; };   // 3
     auto fullQt = [&](int b) { return bar0 + 40 + 8 * b; };   // 3
-    const uint32_t mmaS = bar0 + 64;
+    // state MMA done, alternating by chunk parity so that a late waiter never
+    // sees the same barrier complete twice
+    auto mmaS = [&](int c) { return (c & 1) ? bar0 + 120 : bar0 + 64; };
     auto mmaO = [&](int b) { return bar0 + 72 + 8 * b; };     // 2
     const uint32_t imgReady = bar0 + 88;
     auto oFree = [&](int b) { return bar0 + 96 + 8 * b; };    // 2
@@ -657,7 +725,7 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     }
     auto rec_ptr = [&](int c) { return ws + L.off_rec + (static_cast<int64_t>(rec0 + c) * kHV + h) * kHeadRecBytes; };
 
-    const bool issuer = tid == 12 * 32;
+    const bool issuer = tid == 12 * 32, loader = tid == 13 * 32;
     int topM = -1, topKU = -1, topQt = -1;  // issuer: highest chunk whose copy was issued
     auto issue_M = [&](int c) {
         const int b = c & 1;
@@ -665,7 +733,7 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
         bulk_g2s(aM + b * 32768, rec_ptr(c) + kRecM, 32768, fullM(b));
         topM = c;
     };
-    auto issue_KU = [&](int c) {  // K' and U are adjacent in the record
+    auto issue_KU = [&](int c) {  // K' and U^T are adjacent in the record
         const int b = c % 3;
         mbar_expect_tx(fullKU(b), 32768);
         bulk_g2s(aKU + b * 32768, rec_ptr(c) + kRecKb, 32768, fullKU(b));
@@ -681,15 +749,13 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
         for (int b = 0; b < 2; ++b) mbar_init(fullM(b), 1);
         for (int b = 0; b < 3; ++b) mbar_init(fullKU(b), 1);
         for (int b = 0; b < 3; ++b) mbar_init(fullQt(b), 1);
-        mbar_init(mmaS, 1);
+        mbar_init(mmaS(0), 1);
+        mbar_init(mmaS(1), 1);
         for (int b = 0; b < 2; ++b) mbar_init(mmaO(b), 1);
         mbar_init(imgReady, 8);
         for (int b = 0; b < 2; ++b) mbar_init(oFree(b), 4);
         mbar_init(drain, 1);
         fence_mbar_init();
-        for (int c = 0; c < 2 && c < nch; ++c) issue_M(c);
-        for (int c = 0; c < 3 && c < nch; ++c) issue_KU(c);
-        for (int c = 0; c < 2 && c < nch; ++c) issue_Qt(c);
     }
     if (warp == 0) {
         tmem_alloc(smem_u32(tmem_slot), kCaTmemCols);
@@ -698,6 +764,11 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    if (loader) {  // first copies (barrier init is visible after the barrier above)
+        for (int c = 0; c < 2 && c < nch; ++c) issue_M(c);
+        for (int c = 0; c < 3 && c < nch; ++c) issue_KU(c);
+        for (int c = 0; c < 2 && c < nch; ++c) issue_Qt(c);
+    }
     const uint32_t tm = *tmem_slot;
     auto accS = [&](int b) { return tm + 128 * b; };
     auto sA = [&](int b) { return tm + 256 + 64 * b; };
@@ -724,7 +795,7 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(imgReady);  // image 0 (phase 0)
         for (int c = 0; c < nch; ++c) {
-            const bool okc = __all_sync(0xffffffffu, mbar_wait(mmaS, c & 1));  // warp-uniform exit
+            const bool okc = __all_sync(0xffffffffu, mbar_wait(mmaS(c), (c >> 1) & 1));  // warp-uniform exit
             tc_fence_after();
             float a0[32], a1[32];
             tmem_ld32(taddr(accS(c & 1), 32 * q, 64 * hk), a0);
@@ -756,29 +827,24 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
             }
         }
     } else if (warp < 12) {
-        // output epilogue: lane v, columns = the chunk's 64 tokens
-        const int q = warp - 8;
+        // output epilogue: lane v, columns = the chunk's 64 tokens; the bf16
+        // tile goes through shared memory so rows leave as 16-byte stores
+        const int q = warp - 8, ot = tid - 256;
         const int v = 32 * q + lane;
-        const uint32_t ut_off = (v >> 6) * 8192 + (v & 7) * 2;  // + i * 128 + swizzled chunk
-        uint16_t* out_col = p.out + h * kD + v;
+        uint8_t* otile = sm + kCaO;
         for (int c = 0; c < nch; ++c) {
             const int rows = len - kC * c < kC ? len - kC * c : kC;
-            const uint8_t* ut = rec_ptr(c) + kRecUt + ut_off;
-            uint32_t u[kC / 2];  // Ut[i][v] (fp16) for tokens i = 2e (low half) and 2e + 1
+            uint4 ut[8];  // Ut^T row v: logical 16-byte chunk e (tokens 8e..8e+7) stored at e ^ (v & 7)
+            const uint8_t* urow = rec_ptr(c) + kRecUt + v * 128;
 #pragma unroll
-            for (int e = 0; e < kC / 2; ++e) {
-                uint32_t lo = 0, hi = 0;
-                if (2 * e < rows) lo = __ldg(reinterpret_cast<const unsigned short*>(ut + (2 * e) * 128 + ((((v & 63) >> 3) ^ ((2 * e) & 7)) << 4)));
-                if (2 * e + 1 < rows) hi = __ldg(reinterpret_cast<const unsigned short*>(ut + (2 * e + 1) * 128 + ((((v & 63) >> 3) ^ ((2 * e + 1) & 7)) << 4)));
-                u[e] = lo | (hi << 16);
-            }
+            for (int e = 0; e < 8; ++e) ut[e] = __ldg(reinterpret_cast<const uint4*>(urow + ((e ^ (v & 7)) << 4)));
             const bool okc = __all_sync(0xffffffffu, mbar_wait(mmaO(c & 1), (c >> 1) & 1));
             tc_fence_after();
             if (!okc) {
                 if (lane == 0) record_status(32);
                 break;
             }
-            uint16_t* dst = out_col + (t0 + static_cast<int64_t>(kC) * c) * (kHV * kD);
+            named_sync(2, 128);  // the previous tile has been copied out
 #pragma unroll
             for (int half = 0; half < 2; ++half) {  // tokens 32 half + [0, 32)
                 float o[32];
@@ -790,22 +856,31 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
                     if (lane == 0) mbar_arrive(oFree(c & 1));
                 }
 #pragma unroll
-                for (int i0 = 0; i0 < 32; ++i0) {
-                    const int i = 32 * half + i0;
-                    if (i < rows) {
-                        const float uf = __half2float(__ushort_as_half(static_cast<unsigned short>(u[i >> 1] >> (16 * (i & 1)))));
-                        dst[static_cast<int64_t>(i) * (kHV * kD)] =
-                            __bfloat16_as_ushort(__float2bfloat16_rn(p.scale * (o[i0] + uf)));
-                    }
+                for (int i0 = 0; i0 < 32; i0 += 8) {
+                    float u[8];
+                    h16x8_to_f32(ut[(32 * half + i0) >> 3], u);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        *reinterpret_cast<uint16_t*>(otile + (32 * half + i0 + e) * 256 + v * 2) =
+                            __bfloat16_as_ushort(__float2bfloat16_rn(p.scale * (o[i0 + e] + u[e])));
                 }
+            }
+            named_sync(2, 128);  // tile complete
+            uint16_t* out_chunk = p.out + ((t0 + static_cast<int64_t>(kC) * c) * kHV + h) * kD;
+#pragma unroll
+            for (int it = 0; it < 8; ++it) {
+                const int u = it * 128 + ot, i = u >> 4, ch = u & 15;
+                if (i < rows)
+                    *reinterpret_cast<uint4*>(out_chunk + static_cast<int64_t>(i) * (kHV * kD) + ch * 8) =
+                        *reinterpret_cast<const uint4*>(otile + i * 256 + ch * 16);
             }
         }
     } else if (issuer) {
         bool ok = mbar_wait(fullKU(0), 0);
         if (ok) {
             tc_fence_after();
-            // U_0^T K'_0 -> accS 0 (A = U MN-major [64 j][128 v], B = K' MN-major [64 j][128 k])
-            mma_ct<kF16, true, true, 64, 64, 64, 128, 128>(accS(0), aKU + 16384, aKU, false);
+            // U_0^T K'_0 -> accS 0 (A = U^T K-major [128 v][64 j], B = K' MN-major [64 j][128 k])
+            mma_ct<kF16, false, true, 64, 128, 64, 128, 128>(accS(0), aKU + 16384, aKU, false);
         }
         for (int c = 0; c < nch && ok; ++c) {
             ok = mbar_wait(imgReady, c & 1) && mbar_wait(fullM(c & 1), (c >> 1) & 1);
@@ -813,22 +888,32 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
             tc_fence_after();
             // S_c M_c^T accumulated onto U_c^T K'_c (B = M K-major [128 k][128 k'])
             mma_ct_ta<kF16, false, kD, 128, 128>(accS(c & 1), sA(c & 1), aM + (c & 1) * 32768, true);
-            mma_commit(mmaS);
+            mma_commit(mmaS(c));
             if (c + 1 < nch) {  // next chunk's U^T K' into the other accumulator (its reader is done)
                 const int b = (c + 1) % 3;
                 ok = mbar_wait(fullKU(b), ((c + 1) / 3) & 1);
                 if (!ok) break;
-                mma_ct<kF16, true, true, 64, 64, 64, 128, 128>(accS((c + 1) & 1), aKU + b * 32768 + 16384,
-                                                              aKU + b * 32768, false);
+                mma_ct<kF16, false, true, 64, 128, 64, 128, 128>(accS((c + 1) & 1), aKU + b * 32768 + 16384,
+                                                                aKU + b * 32768, false);
             }
             ok = mbar_wait(fullQt(c % 3), (c / 3) & 1) && (c < 2 || mbar_wait(oFree(c & 1), ((c - 2) >> 1) & 1));
             if (!ok) break;
             tc_fence_after();
-            // O_c^T = S_c Qt_c^T (B = Qt K-major [64 i][128 k])
-            mma_ct_ta<kF16, false, kD, 64, 64>(accO(c & 1), sA(c & 1), aQt + (c % 3) * 16384, false);
+            // O_c^T = S_c Qt_c^T (B = Qt^T MN-major [128 k][64 i])
+            mma_ct_ta<kF16, true, kD, kD, 64>(accO(c & 1), sA(c & 1), aQt + (c % 3) * 16384, false);
             mma_commit(mmaO(c & 1));
-            // S_c M_c^T complete => so is everything issued before it: refill
-            ok = mbar_wait(mmaS, c & 1);
+        }
+        if (!ok) {
+            record_status(32 /* GDN_ERR_DEVICE_TIMEOUT */);
+            mma_commit(drain);  // wait (bounded) for the MMAs in flight
+            mbar_wait(drain, 0);
+        }
+    } else if (loader) {
+        // S_c M_c^T complete => so is everything issued before it (U^T K' of c,
+        // S_{c-1} Qt_{c-1}^T): refill those buffers two chunks ahead
+        bool ok = true;
+        for (int c = 0; c < nch && ok; ++c) {
+            ok = mbar_wait(mmaS(c), (c >> 1) & 1);
             if (!ok) break;
             if (c + 2 < nch) {
                 issue_M(c + 2);
@@ -842,8 +927,6 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
             for (int c = topM > 1 ? topM - 1 : 0; c <= topM; ++c) mbar_wait(fullM(c & 1), (c >> 1) & 1);
             for (int c = topKU > 2 ? topKU - 2 : 0; c <= topKU; ++c) mbar_wait(fullKU(c % 3), (c / 3) & 1);
             for (int c = topQt > 2 ? topQt - 2 : 0; c <= topQt; ++c) mbar_wait(fullQt(c % 3), (c / 3) & 1);
-            mma_commit(drain);
-            mbar_wait(drain, 0);
         }
     }
     tc_fence_before();
