@@ -8,7 +8,7 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
-SHAPES = [  # (kind, M, N, K): the prepare and carry kernels' MMAs, plus neighbours
+SHAPES = [  # (kind, M, N, K[, flags]): shapes the prefill kernels issued in this and earlier designs
     ("bf16", 128, 64, 128),   # [K;Q] K^T
     ("tf32", 64, 64, 64),     # Neumann products
     ("tf32", 64, 256, 64),    # [W | U]

@@ -3,7 +3,8 @@
 Ranks are emulated one after another on cuda:0 (no cross-rank waits), which
 exercises the same plan / pack / merge code the multi-GPU bench uses.  The
 kernels are deterministic and per-sequence independent; shards keep the same
-kernel dispatch as the whole batch (chunked path, BV=32 value tiles).
+kernel dispatch as the whole batch (chunked path, one carry CTA per sequence
+and v-head).
 """
 import pytest
 import torch
