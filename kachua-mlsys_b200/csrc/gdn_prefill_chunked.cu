@@ -148,7 +148,7 @@ __global__ void __launch_bounds__(1024) gdn_chunk_table_kernel(const PrefillPara
 }
 
 // ---------------------------------------------------------------- prepare --
-// One CTA (128 threads) per chunk record and v-head: everything the carry's
+// One CTA (256 threads) per chunk record and v-head: everything the carry's
 // chain does not need, finished per chunk in fp16 operand images (fp32
 // accumulation) and bulk-stored to the workspace:
 //   M    = G_C I - K'^T W     [k][k']  K-major    (B of the state MMA S M^T)
@@ -164,19 +164,21 @@ __global__ void __launch_bounds__(1024) gdn_chunk_table_kernel(const PrefillPara
 // remaining products are computed transposed (M = 128 = k or v rows, all TMEM
 // lanes busy): [W | U]^T = [bGK | bV]^T A^-T, Qt^T = Q^T diag(G) + W^T (-P)^T,
 // Ut^T = -(U^T (-P)^T) and K'^T W.
-constexpr int kPrepThreads = 128;
+constexpr int kPrepThreads = 256;
 constexpr int kPrKQ = 0;        // bf16 [K;Q] K-major, kblock b at b*16K (rows 0-63 K, 64-127 Q); K rows -> K' in place
 constexpr int kPrN = 32768;     // fp32 diagonal blocks of N (8K) | f16 NL (8K); later TB | diag(G); then Qt^T staging
 constexpr int kPrPO = 49152;    // f16 -P [64 i][64 j] K-major                     } later Ut^T staging
 constexpr int kPrX = 57344;     // f16 A^-1 [64 i][64 m] K-major                  }
 constexpr int kPrRHS = 65536;   // f16 [bGK | bV] MN-major [64 j][256] (V by TMA) -> W^T | U^T K-major [128][64] -> M staging
 constexpr int kPrSmall = 98304;
-constexpr int kPrSmem = kPrSmall + 1024 + 1024;
+constexpr int kPrSmem = kPrSmall + 2048 + 1024;
 constexpr int kPrTmemCols = 256;
 
 struct PrepSmall {
-    float LG[kC];    // inclusive prefix of log2 g (0 past the chunk)
-    float beta[kC];  // 0 past the chunk
+    float LG[kC];     // inclusive prefix of log2 g (0 past the chunk)
+    float beta[kC];   // 0 past the chunk
+    float sBG[kC];    // beta G (0 past the chunk)
+    float sTail[kC];  // G_C / G (0 past the chunk)
     float wtot[4];
     uint64_t bar_load;
     uint64_t bar_mma;
@@ -295,7 +297,10 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
                    aX = smem_u32(sm + kPrX), aRHS = smem_u32(sm + kPrRHS);
     const uint32_t aNL = aN + 8192;  // f16 N21 image (later diag(G)); aN: fp32 diagonal blocks (later TB)
 
+    // Thread roles in the accumulator epilogues: warp w reads TMEM lanes
+    // 32 (w & 3).. (its sub-partition) and column half hc = w >> 2.
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int q = warp & 3, hc = warp >> 2;
     const int64_t rec = blockIdx.x;
     const int h = blockIdx.y, hq = h / kGva;
     const int nrec = reinterpret_cast<const int*>(ws + L.off_hdr)[0];
@@ -323,10 +328,8 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
         tmem_relinquish();
     }
     // zero the A^-1 image (its off-diagonal blocks stay zero until X21 is known)
-    S.st16(aX + tid * 64, make_uint4(0, 0, 0, 0));
-    S.st16(aX + tid * 64 + 16, make_uint4(0, 0, 0, 0));
-    S.st16(aX + tid * 64 + 32, make_uint4(0, 0, 0, 0));
-    S.st16(aX + tid * 64 + 48, make_uint4(0, 0, 0, 0));
+    S.st16(aX + tid * 32, make_uint4(0, 0, 0, 0));
+    S.st16(aX + tid * 32 + 16, make_uint4(0, 0, 0, 0));
     // gates and the inclusive prefix of log2 g (threads 0-63 = tokens; warp scans)
     float lgs = 0.f;
     if (tid < kC) {
@@ -352,83 +355,86 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
     if (tid < kC) sml.LG[tid] = lgs;
     const uint32_t tm = sml.tmem_base;
     __syncthreads();
+    if (tid < kC) {  // per-row scales (0 past the chunk)
+        const bool act = tid < n;
+        sml.sBG[tid] = act ? sml.beta[tid] * fast_exp2(lgs) : 0.f;
+        sml.sTail[tid] = act ? fast_exp2(sml.LG[kC - 1] - lgs) : 0.f;
+    }
     bool ok = mbar_wait(barL, 0);
     uint32_t phase = 0;
-
     // 1. Gram [K;Q] K^T (bf16, M=128, N=64, K=128) -> TMEM columns 0-63
     if (tid == 0 && ok) {
         tc_fence_after();
         mma_ct<kBF16, false, false, kD, 128, 128, 128, 64>(tm, aKQ, aKQ, false);
         mma_commit(barM);
     }
+    __syncthreads();  // the row scales are visible
     // meanwhile: [bGK | bV] in fp16 over the RHS (the scale depends on the row
     // only, so 16-byte chunks convert in place of their swizzled position)
-#pragma unroll 4
-    for (int it = 0; it < 16; ++it) {
+#pragma unroll 2
+    for (int it = 0; it < 8; ++it) {
         const int u = it * kPrepThreads + tid;
         const int blk = u >> 9;  // 0, 1: K kblocks -> RHS columns 0-127; 2, 3: V blocks in place
         const int row = (u >> 3) & 63;
         const uint32_t in_row = row * 128 + (u & 7) * 16;
         const uint32_t src = blk < 2 ? aKQ + blk * 16384 + in_row : aRHS + blk * 8192 + in_row;
-        const float sc = blk < 2 ? sml.beta[row] * fast_exp2(sml.LG[row]) : sml.beta[row];
-        const bool act = row < n;
-        float f[8];
-        bf16x8_to_f32(S.ld16(src), f);
+        uint4 res = make_uint4(0, 0, 0, 0);
+        if (row < n) {
+            const float sc = blk < 2 ? sml.sBG[row] : sml.beta[row];
+            float f[8];
+            bf16x8_to_f32(S.ld16(src), f);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) f[q] = act ? sc * f[q] : 0.f;
-        S.st16(aRHS + blk * 8192 + in_row, f16x8(f));
+            for (int e = 0; e < 8; ++e) f[e] *= sc;
+            res = f16x8(f);
+        }
+        S.st16(aRHS + blk * 8192 + in_row, res);
     }
     ok = mbar_wait(barM, phase) && ok;
     phase ^= 1;
     tc_fence_after();
     {
-        // 2. Gram epilogue (thread = accumulator row).  Rows 0-63 give N: its
-        //    fp32 diagonal 32-blocks and the f16 image NL of its lower-left
-        //    block (zero elsewhere); rows 64-127 the f16 image of -P, with
-        //    P = Gam (.) Q K^T for j <= i.
-        float g[64];
-        {
-            float t32[32];
-            tmem_ld32(taddr(tm, 32 * warp, 0), t32);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) g[j] = t32[j];
-            tmem_ld32(taddr(tm, 32 * warp, 32), t32);
-            tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 32; ++j) g[32 + j] = t32[j];
-        }
-        if (warp < 2) {
-            const int i = tid, d = warp, r = lane;
+        // 2. Gram epilogue, 32 columns j = 32 hc + e per thread.  Rows 0-63 give
+        //    N: its fp32 diagonal 32-blocks and the f16 image NL of its
+        //    lower-left block (zero elsewhere); rows 64-127 the f16 image of
+        //    -P, P = Gam (.) Q K^T for j <= i.
+        float g[32];
+        tmem_ld32(taddr(tm, 32 * q, 32 * hc), g);
+        tmem_wait_ld();
+        if (q < 2) {
+            const int i = 32 * q + lane;
             const float LGi = sml.LG[i], bi = sml.beta[i];
             const bool act = i < n;
-            float nv[64];
+            float nv[32];
 #pragma unroll
-            for (int j = 0; j < kC; ++j) nv[j] = (j < i && act) ? bi * fast_exp2(LGi - sml.LG[j]) * g[j] : 0.f;
-#pragma unroll
-            for (int m0 = 0; m0 < 32; m0 += 4) {  // (compile-time indices: d selects, never indexes)
-                const float4 lo = make_float4(nv[m0], nv[m0 + 1], nv[m0 + 2], nv[m0 + 3]);
-                const float4 hi = make_float4(nv[32 + m0], nv[33 + m0], nv[34 + m0], nv[35 + m0]);
-                S.stf4(aN + nd_off(d, r, m0), d == 0 ? lo : hi);
+            for (int e = 0; e < 32; ++e) {
+                const int j = 32 * hc + e;
+                nv[e] = (j < i && act) ? bi * fast_exp2(LGi - sml.LG[j]) * g[e] : 0.f;
             }
+            if (hc == q) {  // the diagonal block d = q: fp32 rows for the substitution
 #pragma unroll
-            for (int j0 = 0; j0 < kC; j0 += 8) {
+                for (int m0 = 0; m0 < 32; m0 += 4)
+                    S.stf4(aN + nd_off(q, lane, m0), make_float4(nv[m0], nv[m0 + 1], nv[m0 + 2], nv[m0 + 3]));
+            }
+            const bool lower_left = q == 1 && hc == 0;
+#pragma unroll
+            for (int e0 = 0; e0 < 32; e0 += 8) {
                 float f[8];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) f[e] = (d == 1 && j0 < 32) ? nv[j0 + e] : 0.f;
-                S.st16(aNL + h16(i, j0, 64), f16x8(f));
+                for (int e = 0; e < 8; ++e) f[e] = lower_left ? nv[e0 + e] : 0.f;
+                S.st16(aNL + h16(i, 32 * hc + e0, 64), f16x8(f));
             }
         } else {
-            const int i = tid - 64;
+            const int i = 32 * (q - 2) + lane;
             const float LGi = sml.LG[i];
 #pragma unroll
-            for (int j0 = 0; j0 < kC; j0 += 8) {
+            for (int e0 = 0; e0 < 32; e0 += 8) {
                 float pv[8];
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
-                    const int j = j0 + e;
-                    pv[e] = (j <= i) ? -fast_exp2(LGi - sml.LG[j]) * g[j] : 0.f;
+                    const int j = 32 * hc + e0 + e;
+                    pv[e] = (j <= i) ? -fast_exp2(LGi - sml.LG[j]) * g[e0 + e] : 0.f;
                 }
-                S.st16(aPO + h16(i, j0, 64), f16x8(pv));
+                S.st16(aPO + h16(i, 32 * hc + e0, 64), f16x8(pv));
             }
         }
     }
@@ -457,19 +463,23 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
     } else {
         // 3b. in place over [K;Q] (bf16 -> f16, rows >= n zero): K' = tail (.) K
         //     in the K rows, plain Q in the Q rows (the A operand of Qt^T)
-        const float LGc = sml.LG[kC - 1];
-#pragma unroll 4
-        for (int it = 0; it < 32; ++it) {
-            const int u = it * 64 + (tid - 64);
-            const int kb = u >> 10, qrow = (u >> 9) & 1, row = (u >> 3) & 63;
-            const uint32_t addr = aKQ + kb * 16384 + qrow * 8192 + row * 128 + (u & 7) * 16;
-            const float sc = qrow ? 1.f : fast_exp2(LGc - sml.LG[row]);
-            const bool act = row < n;
-            float f[8];
-            bf16x8_to_f32(S.ld16(addr), f);
+#pragma unroll 2
+        for (int it = 0; it < 11; ++it) {
+            const int u = it * (kPrepThreads - 64) + (tid - 64);
+            if (u < 2048) {
+                const int kb = u >> 10, qrow = (u >> 9) & 1, row = (u >> 3) & 63;
+                const uint32_t addr = aKQ + kb * 16384 + qrow * 8192 + row * 128 + (u & 7) * 16;
+                uint4 res = make_uint4(0, 0, 0, 0);
+                if (row < n) {
+                    const float sc = qrow ? 1.f : sml.sTail[row];
+                    float f[8];
+                    bf16x8_to_f32(S.ld16(addr), f);
 #pragma unroll
-            for (int q = 0; q < 8; ++q) f[q] = act ? sc * f[q] : 0.f;
-            S.st16(addr, f16x8(f));
+                    for (int e = 0; e < 8; ++e) f[e] *= sc;
+                    res = f16x8(f);
+                }
+                S.st16(addr, res);
+            }
         }
     }
     fence_async_smem();
@@ -484,29 +494,25 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
     phase ^= 1;
     tc_fence_after();
     {
-        // rows i of T (lanes 0-15: i = 16 warp + lane) -> f16 MN-major B image TB
+        // rows i of T (lanes 0-15: i = 16 q + lane) -> f16 MN-major B image TB
         // (over the fp32 diagonal blocks); diag(G) (rows >= n zero) over NL
-        float t32[32], u32[32];
-        tmem_ld32(taddr(tm, 32 * warp, 0), t32);
-        tmem_ld32(taddr(tm, 32 * warp, 32), u32);
+        float t32[32];
+        tmem_ld32(taddr(tm, 32 * q, 32 * hc), t32);
         tmem_wait_ld();
         if (lane < 16) {
-            const int i = 16 * warp + lane;
+            const int i = 16 * q + lane;
 #pragma unroll
-            for (int j0 = 0; j0 < 32; j0 += 8) {
-                S.st16(aN + h16(i, j0, 64), f16x8(t32 + j0));
-                S.st16(aN + h16(i, 32 + j0, 64), f16x8(u32 + j0));
-            }
+            for (int e0 = 0; e0 < 32; e0 += 8) S.st16(aN + h16(i, 32 * hc + e0, 64), f16x8(t32 + e0));
         }
-        if (tid < kC) {
-            const int i = tid;
+        if (tid < 2 * kC) {
+            const int i = tid >> 1, half = tid & 1;
             const float Gi = i < n ? fast_exp2(sml.LG[i]) : 0.f;
 #pragma unroll
-            for (int j0 = 0; j0 < kC; j0 += 8) {
+            for (int e0 = 0; e0 < 32; e0 += 8) {
                 float f[8];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) f[e] = (j0 + e == i) ? Gi : 0.f;
-                S.st16(aNL + h16(i, j0, 64), f16x8(f));
+                for (int e = 0; e < 8; ++e) f[e] = (32 * half + e0 + e == i) ? Gi : 0.f;
+                S.st16(aNL + h16(i, 32 * half + e0, 64), f16x8(f));
             }
         }
     }
@@ -521,18 +527,18 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
     ok = mbar_wait(barM, phase) && ok;
     phase ^= 1;
     tc_fence_after();
-    {
+    if (warp == 2 || warp == 3) {  // rows 32-63 (sub-partitions 2, 3): columns 0-31 of A^-1
         float t32[32];
-        tmem_ld32(taddr(tm, 32 * warp, 64), t32);
+        tmem_ld32(taddr(tm, 32 * q, 64), t32);
         tmem_wait_ld();
-        if (warp >= 2 && lane < 16) {  // rows 32-63: columns 0-31 of A^-1
-            const int i = 16 * warp + lane;
+        if (lane < 16) {
+            const int i = 16 * q + lane;
 #pragma unroll
-            for (int j0 = 0; j0 < 32; j0 += 8) {
+            for (int e0 = 0; e0 < 32; e0 += 8) {
                 float f[8];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) f[e] = -t32[j0 + e];
-                S.st16(aX + h16(i, j0, 64), f16x8(f));
+                for (int e = 0; e < 8; ++e) f[e] = -t32[e0 + e];
+                S.st16(aX + h16(i, e0, 64), f16x8(f));
             }
         }
     }
@@ -548,19 +554,17 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
     ok = mbar_wait(barM, phase) && ok;
     phase ^= 1;
     tc_fence_after();
-    {  // row r of W^T and U^T -> f16 K-major images [128][64] over the RHS
+    {  // row 32 q + lane of W^T (hc = 0) or U^T (hc = 1) -> f16 K-major images [128][64] over the RHS
+        float a0[32], a1[32];
+        tmem_ld32(taddr(tm, 32 * q, 64 * hc), a0);
+        tmem_ld32(taddr(tm, 32 * q, 64 * hc + 32), a1);
+        tmem_wait_ld();
+        const int r = 32 * q + lane;
+        const uint32_t img = aRHS + hc * 16384;
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-            float acc[32], acc2[32];
-            tmem_ld32(taddr(tm, 32 * warp, 64 * half), acc);
-            tmem_ld32(taddr(tm, 32 * warp, 64 * half + 32), acc2);
-            tmem_wait_ld();
-            const uint32_t img = aRHS + half * 16384;
-#pragma unroll
-            for (int j0 = 0; j0 < 32; j0 += 8) {
-                S.st16(img + h16(tid, j0, 128), f16x8(acc + j0));
-                S.st16(img + h16(tid, 32 + j0, 128), f16x8(acc2 + j0));
-            }
+        for (int e0 = 0; e0 < 32; e0 += 8) {
+            S.st16(img + h16(r, e0, 128), f16x8(a0 + e0));
+            S.st16(img + h16(r, 32 + e0, 128), f16x8(a1 + e0));
         }
     }
     fence_async_smem();
@@ -576,7 +580,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
         mma_ct<kF16, true, false, 64, 128, 128, 128, 128>(tm + 128, aKQ, aRHS, false);
         mma_commit(barM);
         bulk_s2g(out_rec + kRecUT, aRHS + 16384, 16384);  // U^T
-        bulk_s2g(out_rec + kRecKb, aKQ, 8192);             // K': two 8 KiB kblocks
+        bulk_s2g(out_rec + kRecKb, aKQ, 8192);            // K': two 8 KiB kblocks
         bulk_s2g(out_rec + kRecKb + 8192, aKQ + 16384, 8192);
         bulk_commit();
     }
@@ -586,42 +590,38 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
     tc_fence_after();
     if (__syncthreads_or(!ok)) goto abort;
     {
-        // 8. row r = tid of Qt^T (staging over N), Ut^T (over -P and A^-1) and
-        //    M = G_C I - K'^T W (over [K;Q])
+        // 8. row r = 32 q + lane: Qt^T (hc = 0, staging over N) or Ut^T (hc = 1,
+        //    over -P and A^-1), and half hc of M = G_C I - K'^T W (over [K;Q])
+        const int r = 32 * q + lane;
         {
-            float acc[32], acc2[32];
-            tmem_ld32(taddr(tm, 32 * warp, 0), acc);
-            tmem_ld32(taddr(tm, 32 * warp, 32), acc2);
+            float a0[32], a1[32];
+            tmem_ld32(taddr(tm, 32 * q, 64 * hc), a0);
+            tmem_ld32(taddr(tm, 32 * q, 64 * hc + 32), a1);
             tmem_wait_ld();
+            const float sg = hc ? -1.f : 1.f;
+            const uint32_t img = hc ? aPO : aN;
 #pragma unroll
-            for (int j0 = 0; j0 < 32; j0 += 8) {
-                S.st16(aN + h16(tid, j0, 128), f16x8(acc + j0));
-                S.st16(aN + h16(tid, 32 + j0, 128), f16x8(acc2 + j0));
-            }
-            tmem_ld32(taddr(tm, 32 * warp, 64), acc);
-            tmem_ld32(taddr(tm, 32 * warp, 96), acc2);
-            tmem_wait_ld();
-#pragma unroll
-            for (int j0 = 0; j0 < 32; j0 += 8) {
+            for (int e0 = 0; e0 < 32; e0 += 8) {
                 float f[8], f2[8];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) f[e] = -acc[j0 + e], f2[e] = -acc2[j0 + e];
-                S.st16(aPO + h16(tid, j0, 128), f16x8(f));
-                S.st16(aPO + h16(tid, 32 + j0, 128), f16x8(f2));
+                for (int e = 0; e < 8; ++e) f[e] = sg * a0[e0 + e], f2[e] = sg * a1[e0 + e];
+                S.st16(img + h16(r, e0, 128), f16x8(f));
+                S.st16(img + h16(r, 32 + e0, 128), f16x8(f2));
             }
         }
         const float Gc = fast_exp2(sml.LG[kC - 1]);
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
+            const int col0 = 64 * hc + 32 * c;  // M column k'
             float acc[32];
-            tmem_ld32(taddr(tm, 32 * warp, 128 + 32 * c), acc);
+            tmem_ld32(taddr(tm, 32 * q, 128 + col0), acc);
             tmem_wait_ld();
 #pragma unroll
-            for (int j0 = 0; j0 < 32; j0 += 8) {
+            for (int e0 = 0; e0 < 32; e0 += 8) {
                 float f[8];
 #pragma unroll
-                for (int q = 0; q < 8; ++q) f[q] = (32 * c + j0 + q == tid ? Gc : 0.f) - acc[j0 + q];
-                S.st16(aKQ + h16(tid, 32 * c + j0, 128), f16x8(f));
+                for (int e = 0; e < 8; ++e) f[e] = (col0 + e0 + e == r ? Gc : 0.f) - acc[e0 + e];
+                S.st16(aKQ + h16(r, col0 + e0, 128), f16x8(f));
             }
         }
     }
@@ -673,8 +673,7 @@ constexpr int kCarryThreads = 448;
 constexpr int kCaM = 0;                         // f16 M K-major [128 k][128 k'], 2 x 32 KiB
 constexpr int kCaKU = 65536;                    // K' [64 j][128 k] (MN-major) + U^T [128 v][64 j] (K-major), 3 x 32 KiB
 constexpr int kCaQt = kCaKU + 3 * 32768;        // f16 Qt^T MN-major [128 k][64 i], 3 x 16 KiB
-constexpr int kCaO = kCaQt + 3 * 16384;         // bf16 output tile [64 i][128 v]
-constexpr int kCaSmall = kCaO + 16384;
+constexpr int kCaSmall = kCaQt + 3 * 16384;
 constexpr int kCaSmem = kCaSmall + 256 + 1024;
 constexpr int kCaTmemCols = 512;  // accS x 2 [0, 256), fp16 S x 2 [256, 384), accO x 2 [384, 512)
 
@@ -827,11 +826,10 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
             }
         }
     } else if (warp < 12) {
-        // output epilogue: lane v, columns = the chunk's 64 tokens; the bf16
-        // tile goes through shared memory so rows leave as 16-byte stores
-        const int q = warp - 8, ot = tid - 256;
+        // output epilogue: lane v, columns = the chunk's 64 tokens; a warp
+        // stores 64 contiguous bytes (32 values of v) of a token row at a time
+        const int q = warp - 8;
         const int v = 32 * q + lane;
-        uint8_t* otile = sm + kCaO;
         for (int c = 0; c < nch; ++c) {
             const int rows = len - kC * c < kC ? len - kC * c : kC;
             uint4 ut[8];  // Ut^T row v: logical 16-byte chunk e (tokens 8e..8e+7) stored at e ^ (v & 7)
@@ -844,7 +842,6 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
                 if (lane == 0) record_status(32);
                 break;
             }
-            named_sync(2, 128);  // the previous tile has been copied out
 #pragma unroll
             for (int half = 0; half < 2; ++half) {  // tokens 32 half + [0, 32)
                 float o[32];
@@ -855,24 +852,17 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
                     __syncwarp();
                     if (lane == 0) mbar_arrive(oFree(c & 1));
                 }
+                uint16_t* dst = p.out + ((t0 + static_cast<int64_t>(kC) * c + 32 * half) * kHV + h) * kD + v;
 #pragma unroll
                 for (int i0 = 0; i0 < 32; i0 += 8) {
                     float u[8];
                     h16x8_to_f32(ut[(32 * half + i0) >> 3], u);
 #pragma unroll
                     for (int e = 0; e < 8; ++e)
-                        *reinterpret_cast<uint16_t*>(otile + (32 * half + i0 + e) * 256 + v * 2) =
-                            __bfloat16_as_ushort(__float2bfloat16_rn(p.scale * (o[i0 + e] + u[e])));
+                        if (32 * half + i0 + e < rows)
+                            dst[static_cast<int64_t>(i0 + e) * (kHV * kD)] =
+                                __bfloat16_as_ushort(__float2bfloat16_rn(p.scale * (o[i0 + e] + u[e])));
                 }
-            }
-            named_sync(2, 128);  // tile complete
-            uint16_t* out_chunk = p.out + ((t0 + static_cast<int64_t>(kC) * c) * kHV + h) * kD;
-#pragma unroll
-            for (int it = 0; it < 8; ++it) {
-                const int u = it * 128 + ot, i = u >> 4, ch = u & 15;
-                if (i < rows)
-                    *reinterpret_cast<uint4*>(out_chunk + static_cast<int64_t>(i) * (kHV * kD) + ch * 8) =
-                        *reinterpret_cast<const uint4*>(otile + i * 256 + ch * 16);
             }
         }
     } else if (issuer) {
