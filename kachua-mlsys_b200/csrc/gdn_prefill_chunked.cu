@@ -61,9 +61,18 @@ __host__ __device__ inline int64_t align_up(int64_t x, int64_t a) { return (x + 
 
 // Workspace: header, per-sequence record bases, the chunk table and the
 // per-record, per-head operand arrays (every array 1024-byte aligned).
+// Segmented carry summaries (few-sequence problems only): per sequence, v-head
+// and segment, T (f16 image, 32 KiB) and Z (fp32 rows, 64 KiB).
+constexpr int kSegMaxP = 8;
+constexpr int kSegMaxSeqs = 6;
+constexpr int kSegSlotBytes = 98304;
+
 struct WsLayout {
     int64_t R;  // record capacity: ceil(T / 64) + N bounds sum_s ceil(len_s / 64)
-    int64_t off_hdr, off_base, off_table, off_rec, total;
+    int64_t off_hdr, off_base, off_table, off_rec;
+    int64_t total;      // everything the single-pass carry needs
+    int64_t off_seg;    // segment summaries (0 when N > kSegMaxSeqs)
+    int64_t total_seg;  // total + the summaries
 };
 
 __host__ __device__ inline WsLayout ws_layout(int64_t T, int64_t N) {
@@ -79,10 +88,17 @@ __host__ __device__ inline WsLayout ws_layout(int64_t T, int64_t N) {
     L.off_rec = o;
     o += L.R * kHV * kHeadRecBytes;
     L.total = align_up(o, 1024);
+    L.off_seg = N <= kSegMaxSeqs ? L.total : 0;
+    L.total_seg = L.total + (N <= kSegMaxSeqs ? N * kHV * kSegMaxP * static_cast<int64_t>(kSegSlotBytes) : 0);
     return L;
 }
 
+// Workspace for the fastest dispatch (with room for the segmented carry when
+// it may apply) and the minimum every chunked launch needs.
 size_t chunked_workspace_bytes(int64_t total_tokens, int64_t num_seqs) {
+    return static_cast<size_t>(ws_layout(total_tokens, num_seqs).total_seg);
+}
+size_t chunked_workspace_min_bytes(int64_t total_tokens, int64_t num_seqs) {
     return static_cast<size_t>(ws_layout(total_tokens, num_seqs).total);
 }
 
@@ -182,6 +198,8 @@ struct PrepSmall {
     float wtot[4];
     uint64_t bar_load;
     uint64_t bar_mma;
+    uint64_t bar_w;
+    uint64_t bar_e;
     uint32_t tmem_base;
 };
 
@@ -288,7 +306,7 @@ __device__ __forceinline__ uint32_t nd_off(int d, int r, int m) {
 __global__ void __launch_bounds__(kPrepThreads, 2)
     gdn_chunk_prepare_kernel(const PrefillParams p, uint8_t* __restrict__ ws, const WsLayout L,
                              const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
-                             const __grid_constant__ CUtensorMap tmV) {
+                             const __grid_constant__ CUtensorMap tmV, const int prefetch_ahead) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = smem_align1024(smem_raw);
     const Smem S{sm, smem_u32(sm)};
@@ -301,19 +319,41 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
     // 32 (w & 3).. (its sub-partition) and column half hc = w >> 2.
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int q = warp & 3, hc = warp >> 2;
-    const int64_t rec = blockIdx.x;
-    const int h = blockIdx.y, hq = h / kGva;
+    // 1-D grid, record-major: the 8 v-heads of a chunk run back to back (their
+    // K and Q loads share L2 lines)
+    const int64_t rec = blockIdx.x / kHV;
+    const int h = static_cast<int>(blockIdx.x % kHV), hq = h / kGva;
     const int nrec = reinterpret_cast<const int*>(ws + L.off_hdr)[0];
     if (rec >= nrec) return;
     const int4 te = reinterpret_cast<const int4*>(ws + L.off_table)[rec];
+    if (tid == 32) {  // warm L2 for the CTA that takes this slot a wave later
+        const int64_t nidx = static_cast<int64_t>(blockIdx.x) + prefetch_ahead;
+        const int64_t nrecx = nidx / kHV;
+        if (nrecx < nrec) {
+            const int nh = static_cast<int>(nidx % kHV);
+            const int nt0 = reinterpret_cast<const int4*>(ws + L.off_table)[nrecx].y;
+            if ((nh & 1) == 0) {
+                tma_prefetch_3d(&tmK, 0, nh / kGva, nt0);
+                tma_prefetch_3d(&tmK, 64, nh / kGva, nt0);
+                tma_prefetch_3d(&tmQ, 0, nh / kGva, nt0);
+                tma_prefetch_3d(&tmQ, 64, nh / kGva, nt0);
+            }
+            tma_prefetch_3d(&tmV, 0, nh, nt0);
+            tma_prefetch_3d(&tmV, 64, nh, nt0);
+        }
+    }
     const int t0 = te.y;  // first token (T < 2^31, checked on the host)
     const int n = te.z;   // tokens in this chunk (1..64)
     uint8_t* out_rec = ws + L.off_rec + (rec * kHV + h) * kHeadRecBytes;
 
-    const uint32_t barL = smem_u32(&sml.bar_load), barM = smem_u32(&sml.bar_mma);
+    // barM: Gram, T, X22 T commits; barW: [W | U]^T and final commits; barE: TB and X21 written
+    const uint32_t barL = smem_u32(&sml.bar_load), barM = smem_u32(&sml.bar_mma), barW = smem_u32(&sml.bar_w),
+                   barE = smem_u32(&sml.bar_e);
     if (tid == 0) {
         mbar_init(barL, 1);
         mbar_init(barM, 1);
+        mbar_init(barW, 1);
+        mbar_init(barE, 2);
         fence_mbar_init();
         mbar_expect_tx(barL, 6 * 8192);
         tma_load_3d(aKQ, &tmK, 0, hq, t0, barL);
@@ -361,7 +401,6 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
         sml.sTail[tid] = act ? fast_exp2(sml.LG[kC - 1] - lgs) : 0.f;
     }
     bool ok = mbar_wait(barL, 0);
-    uint32_t phase = 0;
     // 1. Gram [K;Q] K^T (bf16, M=128, N=64, K=128) -> TMEM columns 0-63
     if (tid == 0 && ok) {
         tc_fence_after();
@@ -389,8 +428,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
         }
         S.st16(aRHS + blk * 8192 + in_row, res);
     }
-    ok = mbar_wait(barM, phase) && ok;
-    phase ^= 1;
+    ok = mbar_wait(barM, 0) && ok;
     tc_fence_after();
     {
         // 2. Gram epilogue, 32 columns j = 32 hc + e per thread.  Rows 0-63 give
@@ -460,27 +498,6 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
         }
 #pragma unroll
         for (int r = 0; r < 32; ++r) S.st2(aX + h16(32 * d + r, 32 * d + j, 64), __half_as_ushort(__float2half_rn(x[r])));
-    } else {
-        // 3b. in place over [K;Q] (bf16 -> f16, rows >= n zero): K' = tail (.) K
-        //     in the K rows, plain Q in the Q rows (the A operand of Qt^T)
-#pragma unroll 2
-        for (int it = 0; it < 11; ++it) {
-            const int u = it * (kPrepThreads - 64) + (tid - 64);
-            if (u < 2048) {
-                const int kb = u >> 10, qrow = (u >> 9) & 1, row = (u >> 3) & 63;
-                const uint32_t addr = aKQ + kb * 16384 + qrow * 8192 + row * 128 + (u & 7) * 16;
-                uint4 res = make_uint4(0, 0, 0, 0);
-                if (row < n) {
-                    const float sc = qrow ? 1.f : sml.sTail[row];
-                    float f[8];
-                    bf16x8_to_f32(S.ld16(addr), f);
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) f[e] *= sc;
-                    res = f16x8(f);
-                }
-                S.st16(addr, res);
-            }
-        }
     }
     fence_async_smem();
     tc_fence_before();
@@ -490,45 +507,36 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
         mma_ct<kF16, false, true, 64, 64, 64, 64, 64>(tm, aNL, aX, false);
         mma_commit(barM);
     }
-    ok = mbar_wait(barM, phase) && ok;
-    phase ^= 1;
-    tc_fence_after();
-    {
-        // rows i of T (lanes 0-15: i = 16 q + lane) -> f16 MN-major B image TB
-        // (over the fp32 diagonal blocks); diag(G) (rows >= n zero) over NL
+    if (warp == 2 || warp == 3) {
+        // The completion of A^-1 runs on sub-partitions 2, 3 (rows 32-63)
+        // while the other warps convert K and Q:
+        //   TB = [0 0; T 0] as the f16 MN-major B image (over the fp32
+        //   diagonal blocks; lanes 16-31 write its zero rows 0-31), then
+        //   X21 = -(X22 T) into A^-1 -- each step handed to the MMA issuer
+        //   through barE.
+        bool okw = mbar_wait(barM, 1);
+        tc_fence_after();
         float t32[32];
-        tmem_ld32(taddr(tm, 32 * q, 32 * hc), t32);
+        tmem_ld32(taddr(tm, 32 * q, 0), t32);
         tmem_wait_ld();
-        if (lane < 16) {
-            const int i = 16 * q + lane;
-#pragma unroll
-            for (int e0 = 0; e0 < 32; e0 += 8) S.st16(aN + h16(i, 32 * hc + e0, 64), f16x8(t32 + e0));
-        }
-        if (tid < 2 * kC) {
-            const int i = tid >> 1, half = tid & 1;
-            const float Gi = i < n ? fast_exp2(sml.LG[i]) : 0.f;
+        {
+            const int i = lane < 16 ? 16 * q + lane : 16 * (q - 2) + (lane - 16);
+            const bool tri = lane < 16;
 #pragma unroll
             for (int e0 = 0; e0 < 32; e0 += 8) {
                 float f[8];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) f[e] = (32 * half + e0 + e == i) ? Gi : 0.f;
-                S.st16(aNL + h16(i, 32 * half + e0, 64), f16x8(f));
+                for (int e = 0; e < 8; ++e) f[e] = tri ? t32[e0 + e] : 0.f;
+                S.st16(aN + h16(i, e0, 64), f16x8(f));
+                S.st16(aN + h16(i, 32 + e0, 64), make_uint4(0, 0, 0, 0));
             }
         }
-    }
-    fence_async_smem();
-    tc_fence_before();
-    if (__syncthreads_or(!ok)) goto abort;
-    if (tid == 0) {  // 5. X22 T -> columns 64-127 (M=64); X21 = -(X22 T)
+        fence_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(barE);
+        okw = mbar_wait(barM, 0) && okw;
         tc_fence_after();
-        mma_ct<kF16, false, true, 64, 64, 64, 64, 64>(tm + 64, aX, aN, false);
-        mma_commit(barM);
-    }
-    ok = mbar_wait(barM, phase) && ok;
-    phase ^= 1;
-    tc_fence_after();
-    if (warp == 2 || warp == 3) {  // rows 32-63 (sub-partitions 2, 3): columns 0-31 of A^-1
-        float t32[32];
         tmem_ld32(taddr(tm, 32 * q, 64), t32);
         tmem_wait_ld();
         if (lane < 16) {
@@ -541,19 +549,59 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
                 S.st16(aX + h16(i, e0, 64), f16x8(f));
             }
         }
+        fence_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(barE);
+        ok = ok && okw;
+    } else if (warp >= 4) {
+        // 3b. in place over [K;Q] (bf16 -> f16, rows >= n zero): K' = tail (.) K
+        //     in the K rows, plain Q in the Q rows (the A operand of Qt^T)
+#pragma unroll 2
+        for (int it = 0; it < 16; ++it) {
+            const int u = it * 128 + (tid - 128);
+            const int kb = u >> 10, qrow = (u >> 9) & 1, row = (u >> 3) & 63;
+            const uint32_t addr = aKQ + kb * 16384 + qrow * 8192 + row * 128 + (u & 7) * 16;
+            uint4 res = make_uint4(0, 0, 0, 0);
+            if (row < n) {
+                const float sc = qrow ? 1.f : sml.sTail[row];
+                float f[8];
+                bf16x8_to_f32(S.ld16(addr), f);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) f[e] *= sc;
+                res = f16x8(f);
+            }
+            S.st16(addr, res);
+        }
+        fence_async_smem();
     }
-    fence_async_smem();
-    tc_fence_before();
-    if (__syncthreads_or(!ok)) goto abort;
-    if (tid == 0) {  // 6. [W | U]^T = [bGK | bV]^T A^-T: W^T -> columns 0-63, U^T -> 64-127 (M=128)
+    if (tid == 0) {
+        // 5. X22 T -> columns 64-127 (M=64), once TB is written
+        ok = mbar_wait(barE, 0) && ok;
+        tc_fence_after();
+        mma_ct<kF16, false, true, 64, 64, 64, 64, 64>(tm + 64, aX, aN, false);
+        mma_commit(barM);
+        // 6. [W | U]^T = [bGK | bV]^T A^-T, once X21 is written: W^T -> columns 0-63,
+        //    U^T -> 64-127 (M=128)
+        ok = mbar_wait(barE, 1) && ok;
         tc_fence_after();
         mma_ct<kF16, true, false, 64, 64, 64, 128, 64>(tm, aRHS, aX, false);
         mma_ct<kF16, true, false, 64, 64, 64, 128, 64>(tm + 64, aRHS + 16384, aX, false);
-        mma_commit(barM);
+        mma_commit(barW);
     }
-    ok = mbar_wait(barM, phase) && ok;
-    phase ^= 1;
+    ok = mbar_wait(barW, 0) && ok;
     tc_fence_after();
+    if (tid < 2 * kC) {  // diag(G) (rows >= n zero) over NL, dead since T = N21 X11
+        const int i = tid >> 1, half = tid & 1;
+        const float Gi = i < n ? fast_exp2(sml.LG[i]) : 0.f;
+#pragma unroll
+        for (int e0 = 0; e0 < 32; e0 += 8) {
+            float f[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] = (32 * half + e0 + e == i) ? Gi : 0.f;
+            S.st16(aNL + h16(i, 32 * half + e0, 64), f16x8(f));
+        }
+    }
     {  // row 32 q + lane of W^T (hc = 0) or U^T (hc = 1) -> f16 K-major images [128][64] over the RHS
         float a0[32], a1[32];
         tmem_ld32(taddr(tm, 32 * q, 64 * hc), a0);
@@ -578,14 +626,13 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
         mma_ct<kF16, false, false, 64, 128, 64, 128, 64>(tm, aRHS, aPO, true);
         mma_ct<kF16, false, false, 64, 128, 64, 128, 64>(tm + 64, aRHS + 16384, aPO, false);
         mma_ct<kF16, true, false, 64, 128, 128, 128, 128>(tm + 128, aKQ, aRHS, false);
-        mma_commit(barM);
+        mma_commit(barW);
         bulk_s2g(out_rec + kRecUT, aRHS + 16384, 16384);  // U^T
         bulk_s2g(out_rec + kRecKb, aKQ, 8192);            // K': two 8 KiB kblocks
         bulk_s2g(out_rec + kRecKb + 8192, aKQ + 16384, 8192);
         bulk_commit();
     }
-    ok = mbar_wait(barM, phase) && ok;
-    phase ^= 1;
+    ok = mbar_wait(barW, 1) && ok;
     if (tid == 0) bulk_wait_read_all();  // U^T and K' have left shared memory before it is reused
     tc_fence_after();
     if (__syncthreads_or(!ok)) goto abort;
@@ -652,8 +699,9 @@ done:
 }
 
 // ------------------------------------------------------------------ carry --
-// One CTA per sequence x v-head.  The state lives in TMEM in transposed form
-// (lane = value row v, columns = k) and is its own MMA operand:
+// One CTA per sequence x v-head (or per segment of one, below).  The state
+// lives in TMEM in transposed form (lane = value row v, columns = k) and is
+// its own MMA operand:
 //   chain   S_{c+1}^T <- U_c^T K'_c + S_c M_c^T     [v][k], fp32 accumulator
 //   output  O_c^T      = S_c Qt_c^T                  [v][i]
 // (U^T K' is issued one chunk early into the second accumulator; S M^T and
@@ -667,8 +715,17 @@ done:
 //   warp 12     one thread issues every MMA;
 //   warp 13     one thread issues the bulk copies (refills follow the state
 //               MMA's completion, off the MMA issuer's path).
-// M is double-buffered, [K' | U] and Qt triple-buffered, each refilled when
-// the MMA that read it is known complete, two chunks before use.
+// M is double-buffered, [K' | U^T] and Qt^T triple-buffered, each refilled
+// when the MMA that read it is known complete, two chunks before use.
+//
+// Segmented carry (few, long sequences): the chunks of a sequence are split
+// into P segments and the affine chunk maps composed, S_b = S_a T + Z over a
+// segment [a, b), with T = M_a^T ... M_{b-1}^T and Z the chain from S_a = 0.
+// Pass A (mode 1) runs, per segment s < P-1, the chain from the true initial
+// state (s = 0, giving S at the start of segment 1), or from I without the
+// U^T K' terms (T_s) and from 0 (Z_s); pass C (mode 2) rebuilds each
+// segment's initial state, S_{s+1} = S_s T_s + Z_s, and runs the segment with
+// outputs.  Mode 0 is the single pass over whole sequences.
 constexpr int kCarryThreads = 448;
 constexpr int kCaM = 0;                         // f16 M K-major [128 k][128 k'], 2 x 32 KiB
 constexpr int kCaKU = 65536;                    // K' [64 j][128 k] (MN-major) + U^T [128 v][64 j] (K-major), 3 x 32 KiB
@@ -677,19 +734,23 @@ constexpr int kCaSmall = kCaQt + 3 * 16384;
 constexpr int kCaSmem = kCaSmall + 256 + 1024;
 constexpr int kCaTmemCols = 512;  // accS x 2 [0, 256), fp16 S x 2 [256, 384), accO x 2 [384, 512)
 
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
+enum CarryRole { kRoleMain = 0, kRoleSum0 = 1, kRoleSumT = 2, kRoleSumZ = 3 };
 
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     const __half2 h2 = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<const uint32_t*>(&h2);
 }
 
+// fp32 [128 v][128 k] matrices of the segment summaries: row v is 512 bytes,
+// its 16-byte chunk c (k = 4c .. 4c+3) stored at position c ^ (v & 31)
+__device__ __forceinline__ uint32_t zrow_off(int v, int c) { return v * 512 + ((c ^ (v & 31)) << 4); }
+
 __global__ void __launch_bounds__(kCarryThreads, 1)
-    gdn_chunk_carry_kernel(const PrefillParams p, const uint8_t* __restrict__ ws, const WsLayout L) {
+    gdn_chunk_carry_kernel(const PrefillParams p, uint8_t* __restrict__ ws, const WsLayout L, const int mode,
+                           const int P) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = smem_align1024(smem_raw);
+    const Smem Sm{sm, smem_u32(sm)};
     const uint32_t aM = smem_u32(sm + kCaM), aKU = smem_u32(sm + kCaKU), aQt = smem_u32(sm + kCaQt);
     const uint32_t bar0 = smem_u32(sm + kCaSmall);
     auto fullM = [&](int b) { return bar0 + 8 * b; };         // 2
@@ -702,30 +763,66 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     const uint32_t imgReady = bar0 + 88;
     auto oFree = [&](int b) { return bar0 + 96 + 8 * b; };    // 2
     const uint32_t drain = bar0 + 112;
+    const uint32_t proLoad = bar0 + 136, proMma = bar0 + 144;  // pass C's composition steps
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kCaSmall + 128);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int64_t unit = blockIdx.x;
+    // this CTA's task
+    int64_t unit;
+    int seg = 0, role = kRoleMain, nP = 1;
+    if (mode == 0) {
+        unit = blockIdx.x;
+    } else if (mode == 2) {
+        nP = P;
+        unit = blockIdx.x / P;
+        seg = static_cast<int>(blockIdx.x % P);
+    } else {
+        nP = P;
+        const int per = 2 * P - 3;
+        unit = blockIdx.x / per;
+        const int r = static_cast<int>(blockIdx.x % per);
+        if (r == 0) {
+            role = kRoleSum0;
+        } else if (r <= P - 2) {
+            seg = r;
+            role = kRoleSumT;
+        } else {
+            seg = r - (P - 2);
+            role = kRoleSumZ;
+        }
+    }
     const int64_t s = unit / kHV;
     const int h = static_cast<int>(unit - s * kHV);
 
     int64_t t0, t1;
     seq_bounds(p, s, t0, t1);
-    const int len = static_cast<int>(t1 - t0);
-    const int nch = (len + kC - 1) / kC;
-    const int rec0 = reinterpret_cast<const int*>(ws + L.off_base)[s];
+    const int len_all = static_cast<int>(t1 - t0);
+    const int nch_all = (len_all + kC - 1) / kC;
+    const int rec0_all = reinterpret_cast<const int*>(ws + L.off_base)[s];
     float* ns_head = p.new_state + unit * kD * kD;
-    if (nch == 0 || rec0 + nch > L.R) {
-        if (nch != 0 && tid == 0) record_status(16);
-        // empty sequence: zero state (oracle prefill :53-55)
-        for (int i = tid; i < kD * kD / 4; i += kCarryThreads)
-            reinterpret_cast<float4*>(ns_head)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (nch_all == 0 || rec0_all + nch_all > L.R) {
+        if (role == kRoleMain && seg == 0) {
+            if (nch_all != 0 && tid == 0) record_status(16);
+            // empty sequence: zero state (oracle prefill :53-55)
+            for (int i = tid; i < kD * kD / 4; i += kCarryThreads)
+                reinterpret_cast<float4*>(ns_head)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
         return;
     }
+    const int Lseg = (nch_all + nP - 1) / nP;
+    const int cb = seg * Lseg < nch_all ? seg * Lseg : nch_all;
+    const int ce = cb + Lseg < nch_all ? cb + Lseg : nch_all;
+    if (cb >= ce) return;                             // empty segment of a short sequence
+    if (role != kRoleMain && ce >= nch_all) return;   // a summary nobody composes
+    const bool last = ce == nch_all, outputs = role == kRoleMain, dpart = role != kRoleSumT;
+    const int nch = ce - cb, rec0 = rec0_all + cb;
+    t0 += static_cast<int64_t>(kC) * cb;
+    const int len = len_all - kC * cb < kC * nch ? len_all - kC * cb : kC * nch;
     auto rec_ptr = [&](int c) { return ws + L.off_rec + (static_cast<int64_t>(rec0 + c) * kHV + h) * kHeadRecBytes; };
+    auto slot = [&](int sg) { return ws + L.off_seg + (unit * kSegMaxP + sg) * static_cast<int64_t>(kSegSlotBytes); };
 
     const bool issuer = tid == 12 * 32, loader = tid == 13 * 32;
-    int topM = -1, topKU = -1, topQt = -1;  // issuer: highest chunk whose copy was issued
+    int topM = -1, topKU = -1, topQt = -1;  // loader: highest chunk whose copy was issued
     auto issue_M = [&](int c) {
         const int b = c & 1;
         mbar_expect_tx(fullM(b), 32768);
@@ -754,6 +851,8 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
         mbar_init(imgReady, 8);
         for (int b = 0; b < 2; ++b) mbar_init(oFree(b), 4);
         mbar_init(drain, 1);
+        mbar_init(proLoad, 1);
+        mbar_init(proMma, 1);
         fence_mbar_init();
     }
     if (warp == 0) {
@@ -763,42 +862,100 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (loader) {  // first copies (barrier init is visible after the barrier above)
-        for (int c = 0; c < 2 && c < nch; ++c) issue_M(c);
-        for (int c = 0; c < 3 && c < nch; ++c) issue_KU(c);
-        for (int c = 0; c < 2 && c < nch; ++c) issue_Qt(c);
-    }
     const uint32_t tm = *tmem_slot;
     auto accS = [&](int b) { return tm + 128 * b; };
     auto sA = [&](int b) { return tm + 256 + 64 * b; };
     auto accO = [&](int b) { return tm + 384 + 64 * b; };
+    const int qw = warp & 3, hk = warp >> 2;  // state warps: sub-partition, k half
+    const int vrow = 32 * qw + lane;
 
+    // initial state -> fp16 A operand 0 (state warps)
     if (warp < 8) {
-        // state epilogue: lane v = 32 (w & 3) + lane, k columns [64 hk, 64 hk + 64)
-        const int q = warp & 3, hk = warp >> 2;
-        const int v = 32 * q + lane;
-        float* ns_row = ns_head + v * kD + 64 * hk;
-        {  // S_0 -> fp16 A operand 0
-            uint32_t w[32];
+        uint32_t w[32];
+        if (role == kRoleMain && seg > 0) {  // S at the start of segment 1 (pass A, segment 0)
+            const uint8_t* x1 = slot(0) + 32768;
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
-                const float4 x = p.state != nullptr ? reinterpret_cast<const float4*>(p.state + unit * kD * kD + v * kD + 64 * hk)[e]
-                                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+                const float4 x = *reinterpret_cast<const float4*>(x1 + zrow_off(vrow, 16 * hk + e));
                 w[2 * e] = pack_half2(x.x, x.y);
                 w[2 * e + 1] = pack_half2(x.z, x.w);
             }
-            tmem_st32(taddr(sA(0), 32 * q, 32 * hk), w);
-            tmem_wait_st();
+        } else if (role == kRoleSumT || role == kRoleSumZ) {  // I (T) or 0 (Z)
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+                const int k = 64 * hk + 2 * e;
+                const float one = role == kRoleSumT ? 1.f : 0.f;
+                w[e] = pack_half2(k == vrow ? one : 0.f, k + 1 == vrow ? one : 0.f);
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                const float4 x = p.state != nullptr
+                                     ? reinterpret_cast<const float4*>(p.state + unit * kD * kD + vrow * kD + 64 * hk)[e]
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+                w[2 * e] = pack_half2(x.x, x.y);
+                w[2 * e + 1] = pack_half2(x.z, x.w);
+            }
         }
+        tmem_st32(taddr(sA(0), 32 * qw, 32 * hk), w);
+        tmem_wait_st();
         tc_fence_before();
-        __syncwarp();
+    }
+    __syncthreads();
+    // pass C: S_{j+1} = S_j T_j + Z_j for j = 1 .. seg-1 (in place in A operand 0)
+    bool ok = true;
+    for (int j = 1; role == kRoleMain && j < seg; ++j) {
+        if (loader) {  // T_j (f16 MN-major [128 j][128 k]) -> M buffer 0; Z_j (fp32 rows) -> [K' | U^T] buffers 0-1
+            mbar_expect_tx(proLoad, 32768 + 65536);
+            bulk_g2s(aM, slot(j), 32768, proLoad);
+            bulk_g2s(aKU, slot(j) + 32768, 65536, proLoad);
+        }
+        if (issuer) {
+            ok = mbar_wait(proLoad, (j - 1) & 1) && ok;
+            tc_fence_after();
+            mma_ct_ta<kF16, true, kD, kD, kD>(accS(0), sA(0), aM, false);
+            mma_commit(proMma);
+        }
+        if (warp < 8) {
+            // Z_j arrived by TMA (observe its barrier) and S_j T_j is complete
+            const bool okj = __all_sync(0xffffffffu, mbar_wait(proLoad, (j - 1) & 1) && mbar_wait(proMma, (j - 1) & 1));
+            tc_fence_after();
+            float a0[32], a1[32];
+            tmem_ld32(taddr(accS(0), 32 * qw, 64 * hk), a0);
+            tmem_ld32(taddr(accS(0), 32 * qw, 64 * hk + 32), a1);
+            tmem_wait_ld();
+            uint32_t w[32];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                const float4 z = Sm.ldf4(aKU + zrow_off(vrow, 16 * hk + e));
+                const float* a = e < 8 ? a0 + 4 * e : a1 + 4 * (e - 8);
+                w[2 * e] = pack_half2(a[0] + z.x, a[1] + z.y);
+                w[2 * e + 1] = pack_half2(a[2] + z.z, a[3] + z.w);
+            }
+            tmem_st32(taddr(sA(0), 32 * qw, 32 * hk), w);
+            tmem_wait_st();
+            tc_fence_before();
+            ok = ok && okj;
+        }
+        __syncthreads();
+        tc_fence_after();
+    }
+    if (loader) {  // first copies of the segment's chunks
+        for (int c = 0; c < 2 && c < nch; ++c) issue_M(c);
+        if (dpart)
+            for (int c = 0; c < 3 && c < nch; ++c) issue_KU(c);
+        if (outputs)
+            for (int c = 0; c < 2 && c < nch; ++c) issue_Qt(c);
+    }
+
+    if (warp < 8) {
         if (lane == 0) mbar_arrive(imgReady);  // image 0 (phase 0)
         for (int c = 0; c < nch; ++c) {
             const bool okc = __all_sync(0xffffffffu, mbar_wait(mmaS(c), (c >> 1) & 1));  // warp-uniform exit
             tc_fence_after();
             float a0[32], a1[32];
-            tmem_ld32(taddr(accS(c & 1), 32 * q, 64 * hk), a0);
-            tmem_ld32(taddr(accS(c & 1), 32 * q, 64 * hk + 32), a1);
+            tmem_ld32(taddr(accS(c & 1), 32 * qw, 64 * hk), a0);
+            tmem_ld32(taddr(accS(c & 1), 32 * qw, 64 * hk + 32), a1);
             tmem_wait_ld();
             if (!okc) {
                 if (lane == 0) record_status(32);
@@ -811,17 +968,35 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
                     w[e] = pack_half2(a0[2 * e], a0[2 * e + 1]);
                     w[16 + e] = pack_half2(a1[2 * e], a1[2 * e + 1]);
                 }
-                tmem_st32(taddr(sA((c + 1) & 1), 32 * q, 32 * hk), w);
+                tmem_st32(taddr(sA((c + 1) & 1), 32 * qw, 32 * hk), w);
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(imgReady);
-            } else {
+            } else if (role == kRoleMain) {
+                if (last) {
+                    float* ns_row = ns_head + vrow * kD + 64 * hk;
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    reinterpret_cast<float4*>(ns_row)[e] = make_float4(a0[4 * e], a0[4 * e + 1], a0[4 * e + 2], a0[4 * e + 3]);
-                    reinterpret_cast<float4*>(ns_row + 32)[e] =
-                        make_float4(a1[4 * e], a1[4 * e + 1], a1[4 * e + 2], a1[4 * e + 3]);
+                    for (int e = 0; e < 8; ++e) {
+                        reinterpret_cast<float4*>(ns_row)[e] =
+                            make_float4(a0[4 * e], a0[4 * e + 1], a0[4 * e + 2], a0[4 * e + 3]);
+                        reinterpret_cast<float4*>(ns_row + 32)[e] =
+                            make_float4(a1[4 * e], a1[4 * e + 1], a1[4 * e + 2], a1[4 * e + 3]);
+                    }
+                }
+            } else if (role == kRoleSumT) {  // T_seg as the f16 MN-major image [128 j][128 k]
+                uint8_t* img = slot(seg);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    *reinterpret_cast<uint4*>(img + h16(vrow, 64 * hk + 8 * e, kD)) = f16x8(a0 + 8 * e);
+                    *reinterpret_cast<uint4*>(img + h16(vrow, 64 * hk + 32 + 8 * e, kD)) = f16x8(a1 + 8 * e);
+                }
+            } else {  // Z_seg (or S at the start of segment 1): fp32 rows
+                uint8_t* z = slot(role == kRoleSum0 ? 0 : seg) + 32768;
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const float* a = e < 8 ? a0 + 4 * e : a1 + 4 * (e - 8);
+                    *reinterpret_cast<float4*>(z + zrow_off(vrow, 16 * hk + e)) = make_float4(a[0], a[1], a[2], a[3]);
                 }
             }
         }
@@ -830,7 +1005,7 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
         // stores 64 contiguous bytes (32 values of v) of a token row at a time
         const int q = warp - 8;
         const int v = 32 * q + lane;
-        for (int c = 0; c < nch; ++c) {
+        for (int c = 0; outputs && c < nch; ++c) {
             const int rows = len - kC * c < kC ? len - kC * c : kC;
             uint4 ut[8];  // Ut^T row v: logical 16-byte chunk e (tokens 8e..8e+7) stored at e ^ (v & 7)
             const uint8_t* urow = rec_ptr(c) + kRecUt + v * 128;
@@ -866,8 +1041,8 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
             }
         }
     } else if (issuer) {
-        bool ok = mbar_wait(fullKU(0), 0);
-        if (ok) {
+        if (dpart) {
+            ok = mbar_wait(fullKU(0), 0) && ok;
             tc_fence_after();
             // U_0^T K'_0 -> accS 0 (A = U^T K-major [128 v][64 j], B = K' MN-major [64 j][128 k])
             mma_ct<kF16, false, true, 64, 128, 64, 128, 128>(accS(0), aKU + 16384, aKU, false);
@@ -876,22 +1051,24 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
             ok = mbar_wait(imgReady, c & 1) && mbar_wait(fullM(c & 1), (c >> 1) & 1);
             if (!ok) break;
             tc_fence_after();
-            // S_c M_c^T accumulated onto U_c^T K'_c (B = M K-major [128 k][128 k'])
-            mma_ct_ta<kF16, false, kD, 128, 128>(accS(c & 1), sA(c & 1), aM + (c & 1) * 32768, true);
+            // S_c M_c^T, accumulated onto U_c^T K'_c (B = M K-major [128 k][128 k'])
+            mma_ct_ta<kF16, false, kD, 128, 128>(accS(c & 1), sA(c & 1), aM + (c & 1) * 32768, dpart);
             mma_commit(mmaS(c));
-            if (c + 1 < nch) {  // next chunk's U^T K' into the other accumulator (its reader is done)
+            if (dpart && c + 1 < nch) {  // next chunk's U^T K' into the other accumulator (its reader is done)
                 const int b = (c + 1) % 3;
                 ok = mbar_wait(fullKU(b), ((c + 1) / 3) & 1);
                 if (!ok) break;
                 mma_ct<kF16, false, true, 64, 128, 64, 128, 128>(accS((c + 1) & 1), aKU + b * 32768 + 16384,
                                                                 aKU + b * 32768, false);
             }
-            ok = mbar_wait(fullQt(c % 3), (c / 3) & 1) && (c < 2 || mbar_wait(oFree(c & 1), ((c - 2) >> 1) & 1));
-            if (!ok) break;
-            tc_fence_after();
-            // O_c^T = S_c Qt_c^T (B = Qt^T MN-major [128 k][64 i])
-            mma_ct_ta<kF16, true, kD, kD, 64>(accO(c & 1), sA(c & 1), aQt + (c % 3) * 16384, false);
-            mma_commit(mmaO(c & 1));
+            if (outputs) {
+                ok = mbar_wait(fullQt(c % 3), (c / 3) & 1) && (c < 2 || mbar_wait(oFree(c & 1), ((c - 2) >> 1) & 1));
+                if (!ok) break;
+                tc_fence_after();
+                // O_c^T = S_c Qt_c^T (B = Qt^T MN-major [128 k][64 i])
+                mma_ct_ta<kF16, true, kD, kD, 64>(accO(c & 1), sA(c & 1), aQt + (c % 3) * 16384, false);
+                mma_commit(mmaO(c & 1));
+            }
         }
         if (!ok) {
             record_status(32 /* GDN_ERR_DEVICE_TIMEOUT */);
@@ -901,15 +1078,14 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     } else if (loader) {
         // S_c M_c^T complete => so is everything issued before it (U^T K' of c,
         // S_{c-1} Qt_{c-1}^T): refill those buffers two chunks ahead
-        bool ok = true;
         for (int c = 0; c < nch && ok; ++c) {
             ok = mbar_wait(mmaS(c), (c >> 1) & 1);
             if (!ok) break;
             if (c + 2 < nch) {
                 issue_M(c + 2);
-                issue_Qt(c + 2);
+                if (outputs) issue_Qt(c + 2);
             }
-            if (c + 3 < nch) issue_KU(c + 3);
+            if (dpart && c + 3 < nch) issue_KU(c + 3);
         }
         if (!ok) {
             record_status(32 /* GDN_ERR_DEVICE_TIMEOUT */);
@@ -933,8 +1109,9 @@ static cudaError_t set_smem(K kernel, int bytes) {
     return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
-// Path selection: 0 = auto, 1 = token-recurrent, 2 = chunked tensor-core.
-constexpr int kPathAuto = 0, kPathRecurrent = 1, kPathChunked = 2;
+// Path selection: 0 = auto, 1 = token-recurrent, 2 = chunked tensor-core, 3 = chunked
+// with the segmented carry forced (P = 4; needs the summary space, N <= 6).
+constexpr int kPathAuto = 0, kPathRecurrent = 1, kPathChunked = 2, kPathSegmented = 3;
 constexpr int64_t kRecurrentMaxAvgLen = 48;
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link
@@ -968,10 +1145,11 @@ static cudaError_t token_tensor_map(CUtensorMap* m, const void* base, int heads,
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-cudaError_t launch_prefill_chunked(const PrefillParams& p, void* workspace, cudaStream_t stream) {
+cudaError_t launch_prefill_chunked(const PrefillParams& p, void* workspace, size_t workspace_bytes, int path,
+                                   cudaStream_t stream) {
     const WsLayout L = ws_layout(p.total_tokens, p.num_seqs);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
-    if (L.R > 0x7fffffffLL || p.total_tokens > 0x7fffffffLL) return cudaErrorInvalidValue;
+    if (L.R * kHV > 0x7fffffffLL || p.total_tokens > 0x7fffffffLL) return cudaErrorInvalidValue;
     CUtensorMap tmK, tmQ, tmV;
     memset(&tmK, 0, sizeof(tmK));
     memset(&tmQ, 0, sizeof(tmQ));
@@ -985,13 +1163,32 @@ cudaError_t launch_prefill_chunked(const PrefillParams& p, void* workspace, cuda
     gdn_chunk_table_kernel<<<1, 1024, 0, stream>>>(p, ws, L);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if ((e = set_smem(gdn_chunk_prepare_kernel, kPrSmem)) != cudaSuccess) return e;
-    gdn_chunk_prepare_kernel<<<dim3(static_cast<unsigned>(L.R), kHV), kPrepThreads, kPrSmem, stream>>>(
-        p, ws, L, tmK, tmQ, tmV);
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    gdn_chunk_prepare_kernel<<<static_cast<unsigned>(L.R * kHV), kPrepThreads, kPrSmem, stream>>>(
+        p, ws, L, tmK, tmQ, tmV, 2 * sms);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if ((e = set_smem(gdn_chunk_carry_kernel, kCaSmem)) != cudaSuccess) return e;
-    const int64_t grid = p.num_seqs * kHV;
-    if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
-    gdn_chunk_carry_kernel<<<static_cast<unsigned>(grid), kCarryThreads, kCaSmem, stream>>>(p, ws, L);
+    const int64_t units = p.num_seqs * kHV;
+    if (units > 0x7fffffffLL / (2 * kSegMaxP)) return cudaErrorInvalidValue;
+    // Segmented carry: when the chains (sequence x v-head) fill under a third
+    // of the SMs and sequences average 16 chunks or more (or when asked for),
+    // split each sequence into P segments (pass A, then pass C).
+    int P = 1;
+    if (L.off_seg > 0 && workspace_bytes >= static_cast<size_t>(L.total_seg)) {
+        if (path == kPathSegmented)
+            P = 4;
+        else if (units * 3 <= sms && p.total_tokens >= p.num_seqs * 16 * kC)
+            P = static_cast<int>(sms / (units * 2)) < kSegMaxP ? static_cast<int>(sms / (units * 2)) : kSegMaxP;
+    }
+    if (P >= 2) {
+        gdn_chunk_carry_kernel<<<static_cast<unsigned>(units * (2 * P - 3)), kCarryThreads, kCaSmem, stream>>>(
+            p, ws, L, 1, P);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        gdn_chunk_carry_kernel<<<static_cast<unsigned>(units * P), kCarryThreads, kCaSmem, stream>>>(p, ws, L, 2, P);
+    } else {
+        gdn_chunk_carry_kernel<<<static_cast<unsigned>(units), kCarryThreads, kCaSmem, stream>>>(p, ws, L, 0, 1);
+    }
     return cudaGetLastError();
 }
 
@@ -1000,9 +1197,9 @@ cudaError_t launch_prefill(const PrefillParams& p, int path, void* workspace, si
     const int64_t avg = p.total_tokens / (p.num_seqs > 0 ? p.num_seqs : 1);
     const bool recurrent = path == kPathRecurrent || (path == kPathAuto && avg <= kRecurrentMaxAvgLen);
     if (recurrent) return launch_prefill_recurrent(p, stream);
-    if (workspace == nullptr || workspace_bytes < chunked_workspace_bytes(p.total_tokens, p.num_seqs))
+    if (workspace == nullptr || workspace_bytes < chunked_workspace_min_bytes(p.total_tokens, p.num_seqs))
         return cudaErrorInvalidValue;
-    return launch_prefill_chunked(p, workspace, stream);
+    return launch_prefill_chunked(p, workspace, workspace_bytes, path, stream);
 }
 
 // ------------------------------------------------------------- self-test --

@@ -53,7 +53,7 @@ extern "C" int gdn_prefill_launch_noalloc(const GdnPrefillArgs* args, void* stre
     if (args->total_tokens < 0 || args->num_seqs < 0) return GDN_ERR_BAD_SIZE;
     // the token-recurrent path needs no scratch; every other path must fit the array
     if (args->path != GDN_PREFILL_PATH_RECURRENT &&
-        gdn_prefill_workspace_size(args->total_tokens, args->num_seqs) > gdn::kNoAllocScratchBytes)
+        gdn::chunked_workspace_min_bytes(args->total_tokens, args->num_seqs) > gdn::kNoAllocScratchBytes)
         return GDN_ERR_WORKSPACE;
     void* scratch = nullptr;
     if (int rc = gdn::noalloc_scratch(&scratch)) return rc;

@@ -87,7 +87,7 @@ def _ptr(t):
     return ctypes.c_void_p(None if t is None else t.data_ptr())
 
 
-PATHS = {"auto": 0, "recurrent": 1, "chunked": 2}
+PATHS = {"auto": 0, "recurrent": 1, "chunked": 2, "segmented": 3}
 
 
 def launch_gdn(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None, output=None,

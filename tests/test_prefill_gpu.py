@@ -19,8 +19,10 @@ pytestmark = pytest.mark.gpu
 OUT_TOL = dict(atol=1e-2, rtol=1e-2)
 
 
-@pytest.fixture(params=["recurrent", "chunked"])
+@pytest.fixture(params=["recurrent", "chunked", "segmented"])
 def path(request):
+    """recurrent: token recurrence; chunked: chunked path with its own carry
+    choice; segmented: chunked with the segmented (composed) carry forced."""
     return request.param
 
 
@@ -124,6 +126,23 @@ def test_prefill_deterministic(pkg, cuda_dev, path):
     o1, s1 = _run(pkg, inp, cuda_dev, path=path)
     o2, s2 = _run(pkg, inp, cuda_dev, path=path)
     assert torch.equal(o1, o2) and torch.equal(s1, s2)
+
+
+@pytest.mark.parametrize("lengths", [[1000], [2048, 700], [5, 3000, 0], [640, 64, 65, 1]])
+def test_prefill_segmented_long(pkg, orc, cuda_dev, lengths):
+    """The segmented carry (sequences split into composed segments) on long
+    sequences, uneven segment splits and empty / one-chunk neighbours."""
+    _check(pkg, orc, pkg.inputs.make_prefill_inputs(lengths, seed=sum(lengths) + 7, with_state=True),
+           cuda_dev, path="segmented")
+
+
+def test_segmented_matches_single_pass(pkg, cuda_dev):
+    """Segmented and single-pass carries agree closely on the same batch."""
+    inp = pkg.inputs.make_prefill_inputs([1500, 900], seed=48, with_state=True)
+    o_s, s_s = _run(pkg, inp, cuda_dev, path="segmented")
+    o_c, s_c = _run(pkg, inp, cuda_dev, path="recurrent")
+    torch.testing.assert_close(o_s.float(), o_c.float(), **OUT_TOL)
+    assert state_rel_err(s_s, s_c) < 1e-3
 
 
 def test_chunked_matches_recurrent(pkg, cuda_dev):
