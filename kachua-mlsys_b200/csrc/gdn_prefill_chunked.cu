@@ -323,6 +323,8 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
     // K and Q loads share L2 lines)
     const int64_t rec = blockIdx.x / kHV;
     const int h = static_cast<int>(blockIdx.x % kHV), hq = h / kGva;
+    griddep_launch_dependents();  // the carry may start its prologue on freed SMs
+    griddep_wait();               // the chunk table is complete
     const int nrec = reinterpret_cast<const int*>(ws + L.off_hdr)[0];
     if (rec >= nrec) return;
     const int4 te = reinterpret_cast<const int4*>(ws + L.off_table)[rec];
@@ -763,10 +765,11 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     const uint32_t imgReady = bar0 + 88;
     auto oFree = [&](int b) { return bar0 + 96 + 8 * b; };    // 2
     const uint32_t drain = bar0 + 112;
-    const uint32_t proLoad = bar0 + 136, proMma = bar0 + 144;  // pass C's composition steps
+    const uint32_t proLoad = bar0 + 136, proMma = bar0 + 152;  // pass C's composition steps (proLoad x 2)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kCaSmall + 128);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    griddep_launch_dependents();
     // this CTA's task
     int64_t unit;
     int seg = 0, role = kRoleMain, nP = 1;
@@ -852,6 +855,7 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
         for (int b = 0; b < 2; ++b) mbar_init(oFree(b), 4);
         mbar_init(drain, 1);
         mbar_init(proLoad, 1);
+        mbar_init(proLoad + 8, 1);
         mbar_init(proMma, 1);
         fence_mbar_init();
     }
@@ -862,6 +866,7 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    griddep_wait();  // the operand images / segment summaries of the preceding kernel are complete
     const uint32_t tm = *tmem_slot;
     auto accS = [&](int b) { return tm + 128 * b; };
     auto sA = [&](int b) { return tm + 256 + 64 * b; };
@@ -902,35 +907,46 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
         tc_fence_before();
     }
     __syncthreads();
-    // pass C: S_{j+1} = S_j T_j + Z_j for j = 1 .. seg-1 (in place in A operand 0)
+    // pass C: S_{j+1} = S_j T_j + Z_j for j = 1 .. seg-1 (in place in A operand 0).
+    // T_j (f16 MN-major [128 j][128 k]) goes to M buffer j & 1 and Z_j (fp32
+    // rows) to a 64 KiB Z buffer over the [K' | U^T] and Qt^T space, both
+    // double-buffered and loaded one step ahead.
     bool ok = true;
+    const uint32_t aZ = aKU;  // 2 x 64 KiB (the [K' | U^T] and Qt^T buffers, 144 KiB)
+    auto issue_TZ = [&](int j) {
+        const int b = j & 1;
+        mbar_expect_tx(proLoad + 8 * b, 32768 + 65536);
+        bulk_g2s(aM + b * 32768, slot(j), 32768, proLoad + 8 * b);
+        bulk_g2s(aZ + b * 65536, slot(j) + 32768, 65536, proLoad + 8 * b);
+    };
+    if (loader && role == kRoleMain)
+        for (int j = 1; j < seg && j <= 2; ++j) issue_TZ(j);
     for (int j = 1; role == kRoleMain && j < seg; ++j) {
-        if (loader) {  // T_j (f16 MN-major [128 j][128 k]) -> M buffer 0; Z_j (fp32 rows) -> [K' | U^T] buffers 0-1
-            mbar_expect_tx(proLoad, 32768 + 65536);
-            bulk_g2s(aM, slot(j), 32768, proLoad);
-            bulk_g2s(aKU, slot(j) + 32768, 65536, proLoad);
-        }
+        const int b = j & 1;
+        const uint32_t ldbar = proLoad + 8 * b, ldpar = ((j - 1) >> 1) & 1;
         if (issuer) {
-            ok = mbar_wait(proLoad, (j - 1) & 1) && ok;
+            ok = mbar_wait(ldbar, ldpar) && ok;
             tc_fence_after();
-            mma_ct_ta<kF16, true, kD, kD, kD>(accS(0), sA(0), aM, false);
+            mma_ct_ta<kF16, true, kD, kD, kD>(accS(0), sA(0), aM + b * 32768, false);
             mma_commit(proMma);
         }
         if (warp < 8) {
             // Z_j arrived by TMA (observe its barrier) and S_j T_j is complete
-            const bool okj = __all_sync(0xffffffffu, mbar_wait(proLoad, (j - 1) & 1) && mbar_wait(proMma, (j - 1) & 1));
+            const bool okj =
+                __all_sync(0xffffffffu, mbar_wait(ldbar, ldpar) && mbar_wait(proMma, (j - 1) & 1));
             tc_fence_after();
-            float a0[32], a1[32];
-            tmem_ld32(taddr(accS(0), 32 * qw, 64 * hk), a0);
-            tmem_ld32(taddr(accS(0), 32 * qw, 64 * hk + 32), a1);
-            tmem_wait_ld();
             uint32_t w[32];
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-                const float4 z = Sm.ldf4(aKU + zrow_off(vrow, 16 * hk + e));
-                const float* a = e < 8 ? a0 + 4 * e : a1 + 4 * (e - 8);
-                w[2 * e] = pack_half2(a[0] + z.x, a[1] + z.y);
-                w[2 * e + 1] = pack_half2(a[2] + z.z, a[3] + z.w);
+            for (int half = 0; half < 2; ++half) {
+                float a[32];
+                tmem_ld32(taddr(accS(0), 32 * qw, 64 * hk + 32 * half), a);
+                tmem_wait_ld();
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const float4 z = Sm.ldf4(aZ + b * 65536 + zrow_off(vrow, 16 * hk + 8 * half + e));
+                    w[16 * half + 2 * e] = pack_half2(a[4 * e] + z.x, a[4 * e + 1] + z.y);
+                    w[16 * half + 2 * e + 1] = pack_half2(a[4 * e + 2] + z.z, a[4 * e + 3] + z.w);
+                }
             }
             tmem_st32(taddr(sA(0), 32 * qw, 32 * hk), w);
             tmem_wait_st();
@@ -939,6 +955,7 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
         }
         __syncthreads();
         tc_fence_after();
+        if (loader && j + 2 < seg) issue_TZ(j + 2);  // into the buffers step j just released
     }
     if (loader) {  // first copies of the segment's chunks
         for (int c = 0; c < 2 && c < nch; ++c) issue_M(c);
@@ -1114,6 +1131,24 @@ static cudaError_t set_smem(K kernel, int bytes) {
 constexpr int kPathAuto = 0, kPathRecurrent = 1, kPathChunked = 2, kPathSegmented = 3;
 constexpr int64_t kRecurrentMaxAvgLen = 48;
 
+// Launch `kernel` so that it may begin (prologue up to griddep_wait) while the
+// previous kernel in the stream finishes (programmatic dependent launch).
+template <typename... Params, typename... Args>
+static cudaError_t launch_dependent(void (*kernel)(Params...), unsigned grid, unsigned block, size_t smem,
+                                    cudaStream_t stream, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);
+}
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link
 // against libcuda); looked up once per process.
 static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
@@ -1165,8 +1200,9 @@ cudaError_t launch_prefill_chunked(const PrefillParams& p, void* workspace, size
     if ((e = set_smem(gdn_chunk_prepare_kernel, kPrSmem)) != cudaSuccess) return e;
     int dev = 0, sms = 148;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    gdn_chunk_prepare_kernel<<<static_cast<unsigned>(L.R * kHV), kPrepThreads, kPrSmem, stream>>>(
-        p, ws, L, tmK, tmQ, tmV, 2 * sms);
+    if ((e = launch_dependent(gdn_chunk_prepare_kernel, static_cast<unsigned>(L.R * kHV), kPrepThreads, kPrSmem,
+                              stream, p, ws, L, tmK, tmQ, tmV, 2 * sms)) != cudaSuccess)
+        return e;
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if ((e = set_smem(gdn_chunk_carry_kernel, kCaSmem)) != cudaSuccess) return e;
     const int64_t units = p.num_seqs * kHV;
@@ -1182,14 +1218,14 @@ cudaError_t launch_prefill_chunked(const PrefillParams& p, void* workspace, size
             P = static_cast<int>(sms / (units * 2)) < kSegMaxP ? static_cast<int>(sms / (units * 2)) : kSegMaxP;
     }
     if (P >= 2) {
-        gdn_chunk_carry_kernel<<<static_cast<unsigned>(units * (2 * P - 3)), kCarryThreads, kCaSmem, stream>>>(
-            p, ws, L, 1, P);
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
-        gdn_chunk_carry_kernel<<<static_cast<unsigned>(units * P), kCarryThreads, kCaSmem, stream>>>(p, ws, L, 2, P);
-    } else {
-        gdn_chunk_carry_kernel<<<static_cast<unsigned>(units), kCarryThreads, kCaSmem, stream>>>(p, ws, L, 0, 1);
+        if ((e = launch_dependent(gdn_chunk_carry_kernel, static_cast<unsigned>(units * (2 * P - 3)), kCarryThreads,
+                                  kCaSmem, stream, p, ws, L, 1, P)) != cudaSuccess)
+            return e;
+        return launch_dependent(gdn_chunk_carry_kernel, static_cast<unsigned>(units * P), kCarryThreads, kCaSmem,
+                                stream, p, ws, L, 2, P);
     }
-    return cudaGetLastError();
+    return launch_dependent(gdn_chunk_carry_kernel, static_cast<unsigned>(units), kCarryThreads, kCaSmem, stream, p,
+                            ws, L, 0, 1);
 }
 
 cudaError_t launch_prefill(const PrefillParams& p, int path, void* workspace, size_t workspace_bytes,
