@@ -342,6 +342,12 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
             }
             tma_prefetch_3d(&tmV, 0, nh, nt0);
             tma_prefetch_3d(&tmV, 64, nh, nt0);
+            if (nh == 0 && ((reinterpret_cast<uintptr_t>(p.a) | reinterpret_cast<uintptr_t>(p.b)) & 15) == 0) {
+                // gate rows a, b of the record: [tokens][8] bf16, 16 bytes per token (16-byte aligned bases only)
+                const int64_t ntok = p.total_tokens - nt0 < kC ? p.total_tokens - nt0 : kC;
+                bulk_prefetch_l2(p.a + static_cast<int64_t>(nt0) * kHV, static_cast<uint32_t>(ntok * 16));
+                bulk_prefetch_l2(p.b + static_cast<int64_t>(nt0) * kHV, static_cast<uint32_t>(ntok * 16));
+            }
         }
     }
     const int t0 = te.y;  // first token (T < 2^31, checked on the host)
@@ -635,12 +641,12 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
         bulk_commit();
     }
     ok = mbar_wait(barW, 1) && ok;
-    if (tid == 0) bulk_wait_read_all();  // U^T and K' have left shared memory before it is reused
     tc_fence_after();
-    if (__syncthreads_or(!ok)) goto abort;
     {
         // 8. row r = 32 q + lane: Qt^T (hc = 0, staging over N) or Ut^T (hc = 1,
-        //    over -P and A^-1), and half hc of M = G_C I - K'^T W (over [K;Q])
+        //    over -P and A^-1) -- regions no bulk store is reading -- then,
+        //    once U^T and K' have left shared memory, half hc of
+        //    M = G_C I - K'^T W (over [K;Q])
         const int r = 32 * q + lane;
         {
             float a0[32], a1[32];
@@ -658,18 +664,28 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
                 S.st16(img + h16(r, 32 + e0, 128), f16x8(f2));
             }
         }
+        fence_async_smem();
+        if (__syncthreads_or(!ok)) goto abort;
+        if (tid == 0) {
+            bulk_s2g(out_rec + kRecQt, aN, 16384);
+            bulk_s2g(out_rec + kRecUt, aPO, 16384);
+            bulk_commit();
+            bulk_wait_read<1>();  // U^T and K' (the older group) have left shared memory
+        }
         const float Gc = fast_exp2(sml.LG[kC - 1]);
-#pragma unroll 1
+        float acc[2][32];
+#pragma unroll
+        for (int c = 0; c < 2; ++c) tmem_ld32(taddr(tm, 32 * q, 128 + 64 * hc + 32 * c), acc[c]);
+        tmem_wait_ld();
+        __syncthreads();  // [K;Q] is free
+#pragma unroll
         for (int c = 0; c < 2; ++c) {
             const int col0 = 64 * hc + 32 * c;  // M column k'
-            float acc[32];
-            tmem_ld32(taddr(tm, 32 * q, 128 + col0), acc);
-            tmem_wait_ld();
 #pragma unroll
             for (int e0 = 0; e0 < 32; e0 += 8) {
                 float f[8];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) f[e] = (col0 + e0 + e == r ? Gc : 0.f) - acc[e0 + e];
+                for (int e = 0; e < 8; ++e) f[e] = (col0 + e0 + e == r ? Gc : 0.f) - acc[c][e0 + e];
                 S.st16(aKQ + h16(r, col0 + e0, 128), f16x8(f));
             }
         }
@@ -678,11 +694,9 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
     tc_fence_before();
     __syncthreads();
     if (tid == 0) {
-        bulk_s2g(out_rec + kRecQt, aN, 16384);
-        bulk_s2g(out_rec + kRecUt, aPO, 16384);
         bulk_s2g(out_rec + kRecM, aKQ, 32768);
         bulk_commit();
-        bulk_wait_read_all();
+        bulk_wait_read<0>();
     }
     goto done;
 abort:
