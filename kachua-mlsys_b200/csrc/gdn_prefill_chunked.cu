@@ -416,26 +416,6 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
         mma_commit(barM);
     }
     __syncthreads();  // the row scales are visible
-    // meanwhile: [bGK | bV] in fp16 over the RHS (the scale depends on the row
-    // only, so 16-byte chunks convert in place of their swizzled position)
-#pragma unroll 2
-    for (int it = 0; it < 8; ++it) {
-        const int u = it * kPrepThreads + tid;
-        const int blk = u >> 9;  // 0, 1: K kblocks -> RHS columns 0-127; 2, 3: V blocks in place
-        const int row = (u >> 3) & 63;
-        const uint32_t in_row = row * 128 + (u & 7) * 16;
-        const uint32_t src = blk < 2 ? aKQ + blk * 16384 + in_row : aRHS + blk * 8192 + in_row;
-        uint4 res = make_uint4(0, 0, 0, 0);
-        if (row < n) {
-            const float sc = blk < 2 ? sml.sBG[row] : sml.beta[row];
-            float f[8];
-            bf16x8_to_f32(S.ld16(src), f);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) f[e] *= sc;
-            res = f16x8(f);
-        }
-        S.st16(aRHS + blk * 8192 + in_row, res);
-    }
     ok = mbar_wait(barM, 0) && ok;
     tc_fence_after();
     {
@@ -506,6 +486,30 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
         }
 #pragma unroll
         for (int r = 0; r < 32; ++r) S.st2(aX + h16(32 * d + r, 32 * d + j, 64), __half_as_ushort(__float2half_rn(x[r])));
+    } else {
+        // 3b. [bGK | bV] in fp16 over the RHS (the scale depends on the row only,
+        //     so 16-byte chunks convert in place of their swizzled position),
+        //     while warps 0-1 solve; K stays bf16 here (read by the Gram MMA)
+#pragma unroll 2
+        for (int it = 0; it < 11; ++it) {
+            const int u = it * (kPrepThreads - 64) + (tid - 64);
+            if (u < 2048) {
+                const int blk = u >> 9;  // 0, 1: K kblocks -> RHS columns 0-127; 2, 3: V blocks in place
+                const int row = (u >> 3) & 63;
+                const uint32_t in_row = row * 128 + (u & 7) * 16;
+                const uint32_t src = blk < 2 ? aKQ + blk * 16384 + in_row : aRHS + blk * 8192 + in_row;
+                uint4 res = make_uint4(0, 0, 0, 0);
+                if (row < n) {
+                    const float sc = blk < 2 ? sml.sBG[row] : sml.beta[row];
+                    float f[8];
+                    bf16x8_to_f32(S.ld16(src), f);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) f[e] *= sc;
+                    res = f16x8(f);
+                }
+                S.st16(aRHS + blk * 8192 + in_row, res);
+            }
+        }
     }
     fence_async_smem();
     tc_fence_before();
@@ -563,7 +567,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
         if (lane == 0) mbar_arrive(barE);
         ok = ok && okw;
     } else if (warp >= 4) {
-        // 3b. in place over [K;Q] (bf16 -> f16, rows >= n zero): K' = tail (.) K
+        // 4b. in place over [K;Q] (bf16 -> f16, rows >= n zero): K' = tail (.) K
         //     in the K rows, plain Q in the Q rows (the A operand of Qt^T)
 #pragma unroll 2
         for (int it = 0; it < 16; ++it) {
