@@ -127,8 +127,8 @@ extern "C" int gdn_prefill_launch(const GdnPrefillArgs* a, void* workspace, size
     p.out = static_cast<uint16_t*>(a->output);
     p.new_state = a->new_state;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (a->total_tokens > 0 && launch_prefill_zero_uncovered(p, s) != cudaSuccess) return GDN_ERR_CUDA;
-    if (a->num_seqs == 0) return GDN_OK;
+    if (a->num_seqs == 0)  // every token is uncovered: zero output
+        return a->total_tokens > 0 && launch_prefill_zero_uncovered(p, s) != cudaSuccess ? GDN_ERR_CUDA : GDN_OK;
     const cudaError_t e = launch_prefill(p, a->path, workspace, workspace_bytes, s);
     return e == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
 }

@@ -107,60 +107,66 @@ size_t chunked_workspace_min_bytes(int64_t total_tokens, int64_t num_seqs) {
 // table[rec] = (seq, first token, length <= 64).  Records past the capacity
 // (only reachable with overlapping, invalid cu_seqlens) are dropped and
 // reported.
+// Block 0 builds the table; every block also zeroes the output rows of
+// tokens outside [cu_seqlens[0], cu_seqlens[N]) (the oracle's torch.zeros),
+// which saves the chunked path a separate launch.
 __global__ void __launch_bounds__(1024) gdn_chunk_table_kernel(const PrefillParams p, uint8_t* ws, WsLayout L) {
-    int* base = reinterpret_cast<int*>(ws + L.off_base);
-    int4* table = reinterpret_cast<int4*>(ws + L.off_table);
-    __shared__ int warp_tot[32];
-    __shared__ long long carry_s;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    if (tid == 0) carry_s = 0;
-    __syncthreads();
-    for (int64_t s0 = 0; s0 < p.num_seqs; s0 += 1024) {
-        const int64_t s = s0 + tid;
-        int64_t t0 = 0, t1 = 0;
-        if (s < p.num_seqs) seq_bounds(p, s, t0, t1);
-        const int nch = static_cast<int>((t1 - t0 + kC - 1) / kC);
-        int x = nch;  // inclusive warp scan
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, x, o);
-            if (lane >= o) x += y;
-        }
-        if (lane == 31) warp_tot[warp] = x;
+    if (blockIdx.x == 0) {
+        int* base = reinterpret_cast<int*>(ws + L.off_base);
+        int4* table = reinterpret_cast<int4*>(ws + L.off_table);
+        __shared__ int warp_tot[32];
+        __shared__ long long carry_s;
+        const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+        if (tid == 0) carry_s = 0;
         __syncthreads();
-        if (warp == 0) {
-            int w = warp_tot[lane];
-#pragma unroll
+        for (int64_t s0 = 0; s0 < p.num_seqs; s0 += 1024) {
+            const int64_t s = s0 + tid;
+            int64_t t0 = 0, t1 = 0;
+            if (s < p.num_seqs) seq_bounds(p, s, t0, t1);
+            const int nch = static_cast<int>((t1 - t0 + kC - 1) / kC);
+            int x = nch;  // inclusive warp scan
+    #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
-                const int y = __shfl_up_sync(0xffffffffu, w, o);
-                if (lane >= o) w += y;
+                const int y = __shfl_up_sync(0xffffffffu, x, o);
+                if (lane >= o) x += y;
             }
-            warp_tot[lane] = w;  // inclusive over warps
-        }
-        __syncthreads();
-        const long long excl = carry_s + (warp > 0 ? warp_tot[warp - 1] : 0) + (x - nch);
-        if (s < p.num_seqs) {
-            base[s] = static_cast<int>(excl < L.R ? excl : L.R);
-            for (int j = 0; j < nch; ++j) {
-                const long long rec = excl + j;
-                if (rec >= L.R) {
-                    record_status(16 /* GDN_ERR_DEVICE_BAD_SEQLENS */);
-                    break;
+            if (lane == 31) warp_tot[warp] = x;
+            __syncthreads();
+            if (warp == 0) {
+                int w = warp_tot[lane];
+    #pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int y = __shfl_up_sync(0xffffffffu, w, o);
+                    if (lane >= o) w += y;
                 }
-                const int64_t ts = t0 + static_cast<int64_t>(j) * kC;
-                const int64_t len = t1 - ts < kC ? t1 - ts : kC;
-                table[rec] = make_int4(static_cast<int>(s), static_cast<int>(ts), static_cast<int>(len), 0);
+                warp_tot[lane] = w;  // inclusive over warps
             }
+            __syncthreads();
+            const long long excl = carry_s + (warp > 0 ? warp_tot[warp - 1] : 0) + (x - nch);
+            if (s < p.num_seqs) {
+                base[s] = static_cast<int>(excl < L.R ? excl : L.R);
+                for (int j = 0; j < nch; ++j) {
+                    const long long rec = excl + j;
+                    if (rec >= L.R) {
+                        record_status(16 /* GDN_ERR_DEVICE_BAD_SEQLENS */);
+                        break;
+                    }
+                    const int64_t ts = t0 + static_cast<int64_t>(j) * kC;
+                    const int64_t len = t1 - ts < kC ? t1 - ts : kC;
+                    table[rec] = make_int4(static_cast<int>(s), static_cast<int>(ts), static_cast<int>(len), 0);
+                }
+            }
+            __syncthreads();
+            if (tid == 0) carry_s += warp_tot[31];
+            __syncthreads();
         }
-        __syncthreads();
-        if (tid == 0) carry_s += warp_tot[31];
-        __syncthreads();
+        if (tid == 0) {
+            const long long tot = carry_s;
+            base[p.num_seqs] = static_cast<int>(tot < L.R ? tot : L.R);
+            reinterpret_cast<int*>(ws + L.off_hdr)[0] = static_cast<int>(tot < L.R ? tot : L.R);
+        }
     }
-    if (tid == 0) {
-        const long long tot = carry_s;
-        base[p.num_seqs] = static_cast<int>(tot < L.R ? tot : L.R);
-        reinterpret_cast<int*>(ws + L.off_hdr)[0] = static_cast<int>(tot < L.R ? tot : L.R);
-    }
+    zero_uncovered_rows(p);
 }
 
 // ---------------------------------------------------------------- prepare --
@@ -1213,7 +1219,7 @@ cudaError_t launch_prefill_chunked(const PrefillParams& p, void* workspace, size
         if ((e = token_tensor_map(&tmQ, p.q, kHQK, p.total_tokens)) != cudaSuccess) return e;
         if ((e = token_tensor_map(&tmV, p.v, kHV, p.total_tokens)) != cudaSuccess) return e;
     }
-    gdn_chunk_table_kernel<<<1, 1024, 0, stream>>>(p, ws, L);
+    gdn_chunk_table_kernel<<<kSmCount, 1024, 0, stream>>>(p, ws, L);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if ((e = set_smem(gdn_chunk_prepare_kernel, kPrSmem)) != cudaSuccess) return e;
     int dev = 0, sms = 148;
@@ -1250,7 +1256,10 @@ cudaError_t launch_prefill(const PrefillParams& p, int path, void* workspace, si
                            cudaStream_t stream) {
     const int64_t avg = p.total_tokens / (p.num_seqs > 0 ? p.num_seqs : 1);
     const bool recurrent = path == kPathRecurrent || (path == kPathAuto && avg <= kRecurrentMaxAvgLen);
-    if (recurrent) return launch_prefill_recurrent(p, stream);
+    if (recurrent) {
+        cudaError_t e = launch_prefill_zero_uncovered(p, stream);
+        return e != cudaSuccess ? e : launch_prefill_recurrent(p, stream);
+    }
     if (workspace == nullptr || workspace_bytes < chunked_workspace_min_bytes(p.total_tokens, p.num_seqs))
         return cudaErrorInvalidValue;
     return launch_prefill_chunked(p, workspace, workspace_bytes, path, stream);

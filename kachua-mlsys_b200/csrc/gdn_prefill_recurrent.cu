@@ -147,7 +147,9 @@ __global__ void __launch_bounds__(128) gdn_prefill_recurrent_kernel(const Prefil
 
 // Zeroes output rows of tokens outside [cu[0], cu[N]) (the reference
 // allocates its output with torch.zeros, prefill reference_torch_impl.py:41-45).
-__global__ void gdn_prefill_zero_uncovered_kernel(const PrefillParams p) {
+// Zero the output rows of tokens outside [cu_seqlens[0], cu_seqlens[N]) over
+// the whole grid (the oracle's torch.zeros output).
+__device__ __forceinline__ void zero_uncovered_rows(const PrefillParams& p) {
     int64_t lo = load_cu(p, 0), hi = load_cu(p, p.num_seqs);
     lo = lo < 0 ? 0 : (lo > p.total_tokens ? p.total_tokens : lo);
     hi = hi < lo ? lo : (hi > p.total_tokens ? p.total_tokens : hi);
@@ -160,6 +162,8 @@ __global__ void gdn_prefill_zero_uncovered_kernel(const PrefillParams p) {
         o[i < n_head ? i : hi * per_tok + (i - n_head)] = z;
     }
 }
+
+__global__ void gdn_prefill_zero_uncovered_kernel(const PrefillParams p) { zero_uncovered_rows(p); }
 
 cudaError_t launch_prefill_recurrent(const PrefillParams& p, cudaStream_t stream) {
     const int64_t grid = p.num_seqs * kHV * kRecTiles;
