@@ -74,7 +74,7 @@ constexpr int kPhases = 4;
 
 struct WsLayout {
     int64_t R;  // record capacity: ceil(T / 64) + N bounds sum_s ceil(len_s / 64)
-    int64_t off_hdr, off_base, off_table, off_perm, off_rec;
+    int64_t off_hdr, off_base, off_order, off_table, off_perm, off_rec;
     int64_t total;      // everything the single-pass carry needs
     int64_t off_seg;    // segment summaries (0 when N > kSegMaxSeqs)
     int64_t off_chain;  // phase hand-off states (0 when N > kPhaseMaxSeqs)
@@ -89,6 +89,8 @@ __host__ __device__ inline WsLayout ws_layout(int64_t T, int64_t N) {
     o += 1024;
     L.off_base = o;
     o = align_up(o + 4 * (N + 1), 1024);
+    L.off_order = o;  // sequences by chunk count, longest first
+    o = align_up(o + 4 * N, 1024);
     L.off_table = o;
     o = align_up(o + 16 * L.R, 1024);
     L.off_perm = o;  // phase-major record order (phased mode)
@@ -177,6 +179,44 @@ __global__ void __launch_bounds__(1024) gdn_chunk_table_kernel(const PrefillPara
             const long long tot = carry_s;
             base[p.num_seqs] = static_cast<int>(tot < L.R ? tot : L.R);
             reinterpret_cast<int*>(ws + L.off_hdr)[0] = static_cast<int>(tot < L.R ? tot : L.R);
+        }
+        {
+            // Sequences in order of decreasing chunk count (counting sort, counts
+            // above 1023 share the first bin): the single-pass carry starts the
+            // longest chains first, so that short ones fill in behind them.
+            __shared__ int hist[1024];
+            hist[tid] = 0;
+            __syncthreads();
+            const int N = static_cast<int>(p.num_seqs);
+            auto bin_of = [&](int s2) {
+                const int n = base[s2 + 1] - base[s2];
+                return 1023 - (n < 1023 ? n : 1023);
+            };
+            for (int s2 = tid; s2 < N; s2 += 1024) atomicAdd(&hist[bin_of(s2)], 1);
+            __syncthreads();
+            const int hv = hist[tid];
+            int x = hv;  // exclusive scan of the 1024 bins
+    #pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, x, o);
+                if (lane >= o) x += y;
+            }
+            if (lane == 31) warp_tot[warp] = x;
+            __syncthreads();
+            if (warp == 0) {
+                int w = warp_tot[lane];
+    #pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int y = __shfl_up_sync(0xffffffffu, w, o);
+                    if (lane >= o) w += y;
+                }
+                warp_tot[lane] = w;
+            }
+            __syncthreads();
+            hist[tid] = (warp > 0 ? warp_tot[warp - 1] : 0) + x - hv;
+            __syncthreads();
+            int* order = reinterpret_cast<int*>(ws + L.off_order);
+            for (int s2 = tid; s2 < N; s2 += 1024) order[atomicAdd(&hist[bin_of(s2)], 1)] = s2;
         }
         if (phases > 0) {
             // Phase-major record order for the phased prefill (N <= 18): phase
@@ -863,7 +903,10 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     // this CTA's task
     int64_t unit;
     int seg = 0, role = kRoleMain, nP = 1;
-    if (mode == 0 || mode == 3) {
+    if (mode == 0) {  // longest sequences first
+        unit = static_cast<int64_t>(reinterpret_cast<const int*>(ws + L.off_order)[blockIdx.x / kHV]) * kHV +
+               blockIdx.x % kHV;
+    } else if (mode == 3) {
         unit = blockIdx.x;
     } else if (mode == 2) {
         nP = P;
