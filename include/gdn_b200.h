@@ -100,11 +100,6 @@ int gdn_decode_launch(const GdnDecodeArgs* args, void* stream);
                                          sequence (used automatically when few long sequences leave
                                          most SMs idle; needs the full workspace and num_seqs <= 6,
                                          else falls back to CHUNKED) */
-#define GDN_PREFILL_PATH_PHASED 4     /* chunked, each sequence's chunks in 4 consecutive phases: the
-                                         carry of phase p overlaps the prepare of phase p + 1 (used
-                                         automatically when the sequence x v-head chains fill at most
-                                         half the SMs; needs the full workspace and num_seqs <= 18,
-                                         else falls back to CHUNKED) */
 
 /* Variable-length prefill over packed sequences.  Shapes:
  *   q, k       bf16 [T, 4, 128]        16-byte aligned
@@ -139,8 +134,7 @@ typedef struct GdnPrefillArgs {
 } GdnPrefillArgs;
 
 /* Bytes of device workspace for gdn_prefill_launch at these sizes (256-byte
- * aligned base).  Includes, for num_seqs <= 6, room for the segmented carry
- * and, for num_seqs <= 18, the phased prefill's hand-off states;
+ * aligned base).  Includes, for num_seqs <= 6, room for the segmented carry;
  * a smaller workspace that still holds the per-chunk operand images (about
  * 768 KiB per 64 tokens) is accepted and runs the single-pass carry.
  * Replaces the torch.empty scratch tensors the reference allocates per call

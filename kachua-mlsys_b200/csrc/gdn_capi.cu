@@ -94,7 +94,7 @@ extern "C" int gdn_prefill_launch(const GdnPrefillArgs* a, void* workspace, size
     if (a->total_tokens < 0 || a->num_seqs < 0) return GDN_ERR_BAD_SIZE;
     if (a->cu_seqlens_dtype != GDN_SEQLENS_INT32 && a->cu_seqlens_dtype != GDN_SEQLENS_INT64)
         return GDN_ERR_BAD_DTYPE;
-    if (a->path < GDN_PREFILL_PATH_AUTO || a->path > GDN_PREFILL_PATH_PHASED) return GDN_ERR_BAD_SIZE;
+    if (a->path < GDN_PREFILL_PATH_AUTO || a->path > GDN_PREFILL_PATH_SEGMENTED) return GDN_ERR_BAD_SIZE;
     if (!a->cu_seqlens || !a->A_log || !a->dt_bias) return GDN_ERR_NULL_POINTER;
     if (a->total_tokens > 0 &&
         (!a->q || !a->k || !a->v || !a->a || !a->b || !a->output))

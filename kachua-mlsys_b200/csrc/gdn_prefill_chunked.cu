@@ -67,18 +67,12 @@ constexpr int kSegMaxP = 8;
 constexpr int kSegMaxSeqs = 6;
 constexpr int kSegSlotBytes = 98304;
 
-// Phased prefill (few long sequences, chains < SMs): per sequence x v-head the
-// fp32 state between phases (64 KiB).
-constexpr int kPhaseMaxSeqs = 18;
-constexpr int kPhases = 4;
-
 struct WsLayout {
     int64_t R;  // record capacity: ceil(T / 64) + N bounds sum_s ceil(len_s / 64)
-    int64_t off_hdr, off_base, off_order, off_table, off_perm, off_rec;
+    int64_t off_hdr, off_base, off_order, off_table, off_rec;
     int64_t total;      // everything the single-pass carry needs
     int64_t off_seg;    // segment summaries (0 when N > kSegMaxSeqs)
-    int64_t off_chain;  // phase hand-off states (0 when N > kPhaseMaxSeqs)
-    int64_t total_seg;  // total + the optional regions
+    int64_t total_seg;  // total + the summaries
 };
 
 __host__ __device__ inline WsLayout ws_layout(int64_t T, int64_t N) {
@@ -93,17 +87,11 @@ __host__ __device__ inline WsLayout ws_layout(int64_t T, int64_t N) {
     o = align_up(o + 4 * N, 1024);
     L.off_table = o;
     o = align_up(o + 16 * L.R, 1024);
-    L.off_perm = o;  // phase-major record order (phased mode)
-    o = align_up(o + 4 * L.R, 1024);
     L.off_rec = o;
     o += L.R * kHV * kHeadRecBytes;
     L.total = align_up(o, 1024);
-    o = L.total;
-    L.off_seg = N <= kSegMaxSeqs ? o : 0;
-    if (N <= kSegMaxSeqs) o += N * kHV * kSegMaxP * static_cast<int64_t>(kSegSlotBytes);
-    L.off_chain = N <= kPhaseMaxSeqs ? o : 0;
-    if (N <= kPhaseMaxSeqs) o += N * kHV * static_cast<int64_t>(kD * kD * 4);
-    L.total_seg = o;
+    L.off_seg = N <= kSegMaxSeqs ? L.total : 0;
+    L.total_seg = L.total + (N <= kSegMaxSeqs ? N * kHV * kSegMaxP * static_cast<int64_t>(kSegSlotBytes) : 0);
     return L;
 }
 
@@ -124,8 +112,7 @@ size_t chunked_workspace_min_bytes(int64_t total_tokens, int64_t num_seqs) {
 // Block 0 builds the table; every block also zeroes the output rows of
 // tokens outside [cu_seqlens[0], cu_seqlens[N]) (the oracle's torch.zeros),
 // which saves the chunked path a separate launch.
-__global__ void __launch_bounds__(1024) gdn_chunk_table_kernel(const PrefillParams p, uint8_t* ws, WsLayout L,
-                                                               const int phases) {
+__global__ void __launch_bounds__(1024) gdn_chunk_table_kernel(const PrefillParams p, uint8_t* ws, WsLayout L) {
     if (blockIdx.x == 0) {
         int* base = reinterpret_cast<int*>(ws + L.off_base);
         int4* table = reinterpret_cast<int4*>(ws + L.off_table);
@@ -217,35 +204,6 @@ __global__ void __launch_bounds__(1024) gdn_chunk_table_kernel(const PrefillPara
             __syncthreads();
             int* order = reinterpret_cast<int*>(ws + L.off_order);
             for (int s2 = tid; s2 < N; s2 += 1024) order[atomicAdd(&hist[bin_of(s2)], 1)] = s2;
-        }
-        if (phases > 0) {
-            // Phase-major record order for the phased prefill (N <= 18): phase
-            // ph holds, per sequence s, chunks [n_s ph / P, n_s (ph + 1) / P).
-            // Offsets in the header (ints 16 .. 16 + P); thread s writes its own.
-            __syncthreads();
-            int* perm = reinterpret_cast<int*>(ws + L.off_perm);
-            int* poff = reinterpret_cast<int*>(ws + L.off_hdr) + 16;
-            const int N = static_cast<int>(p.num_seqs);
-            auto cnt = [&](int n, int ph) { return n * (ph + 1) / phases - n * ph / phases; };
-            if (tid < N) {
-                const int b0 = base[tid], n = base[tid + 1] - b0;
-                for (int ph = 0; ph < phases; ++ph) {
-                    int off = 0;
-                    for (int s2 = 0; s2 < N; ++s2) {
-                        const int n2 = base[s2 + 1] - base[s2];
-                        for (int ph2 = 0; ph2 < ph; ++ph2) off += cnt(n2, ph2);
-                        if (s2 < tid) off += cnt(n2, ph);
-                    }
-                    const int cb = n * ph / phases, ce = n * (ph + 1) / phases;
-                    for (int c = cb; c < ce; ++c) perm[off + c - cb] = b0 + c;
-                }
-            }
-            if (tid <= phases) {
-                int off = 0;
-                for (int s2 = 0; s2 < N; ++s2)
-                    for (int ph2 = 0; ph2 < tid; ++ph2) off += cnt(base[s2 + 1] - base[s2], ph2);
-                poff[tid] = off;
-            }
         }
     }
     zero_uncovered_rows(p);
@@ -394,8 +352,7 @@ __device__ __forceinline__ uint32_t nd_off(int d, int r, int m) {
 __global__ void __launch_bounds__(kPrepThreads, 2)
     gdn_chunk_prepare_kernel(const PrefillParams p, uint8_t* __restrict__ ws, const WsLayout L,
                              const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
-                             const __grid_constant__ CUtensorMap tmV, const int prefetch_ahead,
-                             const int phase) {
+                             const __grid_constant__ CUtensorMap tmV, const int prefetch_ahead) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = smem_align1024(smem_raw);
     const Smem S{sm, smem_u32(sm)};
@@ -409,33 +366,18 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int q = warp & 3, hc = warp >> 2;
     // 1-D grid, record-major: the 8 v-heads of a chunk run back to back (their
-    // K and Q loads share L2 lines).  In the phased prefill (phase >= 0) the
-    // grid walks that phase's slice of the phase-major record list.
+    // K and Q loads share L2 lines)
+    const int64_t rec = blockIdx.x / kHV;
     const int h = static_cast<int>(blockIdx.x % kHV), hq = h / kGva;
     griddep_launch_dependents();  // the carry may start its prologue on freed SMs
-    if (phase <= 0) {
-        griddep_wait();  // the chunk table is complete
-    } else if (blockIdx.x == gridDim.x - 1) {
-        // Phased prefill, phase >= 1: this grid runs beside the previous
-        // phase's carry (its predecessor in the stream) and does not wait for
-        // it, except in this one extra CTA, so that the grid completes only
-        // after that carry has; the next carry waits for this grid and so
-        // finds the previous phase's hand-off state.  The chunk table was
-        // complete before the previous carry let this grid start.
-        griddep_wait();
-        return;
-    }
-    const int* hdr = reinterpret_cast<const int*>(ws + L.off_hdr);
-    const int* perm = reinterpret_cast<const int*>(ws + L.off_perm);
-    const int nrec = phase < 0 ? hdr[0] : hdr[16 + phase + 1] - hdr[16 + phase];
-    auto record_of = [&](int64_t li) -> int64_t { return phase < 0 ? li : perm[hdr[16 + phase] + li]; };
-    if (static_cast<int64_t>(blockIdx.x / kHV) >= nrec) return;
-    const int64_t rec = record_of(blockIdx.x / kHV);
+    griddep_wait();               // the chunk table is complete
+    const int nrec = reinterpret_cast<const int*>(ws + L.off_hdr)[0];
+    if (rec >= nrec) return;
     const int4 te = reinterpret_cast<const int4*>(ws + L.off_table)[rec];
     if (tid == 32) {  // warm L2 for the CTA that takes this slot a wave later
         const int64_t nidx = static_cast<int64_t>(blockIdx.x) + prefetch_ahead;
-        if (nidx / kHV < nrec) {
-            const int64_t nrecx = record_of(nidx / kHV);
+        const int64_t nrecx = nidx / kHV;
+        if (nrecx < nrec) {
             const int nh = static_cast<int>(nidx % kHV);
             const int nt0 = reinterpret_cast<const int4*>(ws + L.off_table)[nrecx].y;
             if ((nh & 1) == 0) {
@@ -849,11 +791,7 @@ done:
 // state (s = 0, giving S at the start of segment 1), or from I without the
 // U^T K' terms (T_s) and from 0 (Z_s); pass C (mode 2) rebuilds each
 // segment's initial state, S_{s+1} = S_s T_s + Z_s, and runs the segment with
-// outputs.  Mode 0 is the single pass over whole sequences.  Mode 3 is one
-// phase (P = phase index) of the phased prefill: chunks
-// [n ph / kPhases, n (ph + 1) / kPhases) of each sequence, starting from the
-// initial state or the previous phase's hand-off state and ending in the
-// final state or the next hand-off.
+// outputs.  Mode 0 is the single pass over whole sequences.
 constexpr int kCarryThreads = 448;
 constexpr int kCaM = 0;                         // f16 M K-major [128 k][128 k'], 2 x 32 KiB
 constexpr int kCaKU = 65536;                    // K' [64 j][128 k] (MN-major) + U^T [128 v][64 j] (K-major), 3 x 32 KiB
@@ -895,19 +833,13 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kCaSmall + 128);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    // The next kernel may start on the SMs left free.  In the phased prefill
-    // that is the next phase's prepare, which reads the chunk table without
-    // waiting for this grid: it starts only once the current phase's prepare
-    // (hence the table kernel) is complete, i.e. after this grid's wait.
-    if (mode != 3) griddep_launch_dependents();
+    griddep_launch_dependents();
     // this CTA's task
     int64_t unit;
     int seg = 0, role = kRoleMain, nP = 1;
     if (mode == 0) {  // longest sequences first
         unit = static_cast<int64_t>(reinterpret_cast<const int*>(ws + L.off_order)[blockIdx.x / kHV]) * kHV +
                blockIdx.x % kHV;
-    } else if (mode == 3) {
-        unit = blockIdx.x;
     } else if (mode == 2) {
         nP = P;
         unit = blockIdx.x / P;
@@ -937,8 +869,7 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     const int rec0_all = reinterpret_cast<const int*>(ws + L.off_base)[s];
     float* ns_head = p.new_state + unit * kD * kD;
     if (nch_all == 0 || rec0_all + nch_all > L.R) {
-        if (mode == 3) griddep_wait();
-        if (role == kRoleMain && seg == 0 && (mode != 3 || P == 0)) {
+        if (role == kRoleMain && seg == 0) {
             if (nch_all != 0 && tid == 0) record_status(16);
             // empty sequence: zero state (oracle prefill :53-55)
             for (int i = tid; i < kD * kD / 4; i += kCarryThreads)
@@ -947,12 +878,9 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
         return;
     }
     const int Lseg = (nch_all + nP - 1) / nP;
-    const int cb = mode == 3 ? nch_all * P / kPhases : seg * Lseg < nch_all ? seg * Lseg : nch_all;
-    const int ce = mode == 3 ? nch_all * (P + 1) / kPhases : cb + Lseg < nch_all ? cb + Lseg : nch_all;
-    if (cb >= ce) {  // empty segment (phase) of a short sequence
-        if (mode == 3) griddep_wait();
-        return;
-    }
+    const int cb = seg * Lseg < nch_all ? seg * Lseg : nch_all;
+    const int ce = cb + Lseg < nch_all ? cb + Lseg : nch_all;
+    if (cb >= ce) return;                             // empty segment of a short sequence
     if (role != kRoleMain && ce >= nch_all) return;   // a summary nobody composes
     const bool last = ce == nch_all, outputs = role == kRoleMain, dpart = role != kRoleSumT;
     const int nch = ce - cb, rec0 = rec0_all + cb;
@@ -960,7 +888,6 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     const int len = len_all - kC * cb < kC * nch ? len_all - kC * cb : kC * nch;
     auto rec_ptr = [&](int c) { return ws + L.off_rec + (static_cast<int64_t>(rec0 + c) * kHV + h) * kHeadRecBytes; };
     auto slot = [&](int sg) { return ws + L.off_seg + (unit * kSegMaxP + sg) * static_cast<int64_t>(kSegSlotBytes); };
-    uint8_t* chain = ws + L.off_chain + unit * static_cast<int64_t>(kD * kD * 4);  // phase hand-off, fp32 rows
 
     const bool issuer = tid == 12 * 32, loader = tid == 13 * 32;
     int topM = -1, topKU = -1, topQt = -1;  // loader: highest chunk whose copy was issued
@@ -1005,7 +932,6 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     __syncthreads();
     tc_fence_after();
     griddep_wait();  // the operand images / segment summaries of the preceding kernel are complete
-    if (mode == 3) griddep_launch_dependents();
     const uint32_t tm = *tmem_slot;
     auto accS = [&](int b) { return tm + 128 * b; };
     auto sA = [&](int b) { return tm + 256 + 64 * b; };
@@ -1016,9 +942,8 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     // initial state -> fp16 A operand 0 (state warps)
     if (warp < 8) {
         uint32_t w[32];
-        if ((role == kRoleMain && seg > 0) || (mode == 3 && cb > 0)) {
-            // S at the start of segment 1 (pass A, segment 0) or of this phase
-            const uint8_t* x1 = mode == 3 ? chain : slot(0) + 32768;
+        if (role == kRoleMain && seg > 0) {  // S at the start of segment 1 (pass A, segment 0)
+            const uint8_t* x1 = slot(0) + 32768;
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
                 const float4 x = *reinterpret_cast<const float4*>(x1 + zrow_off(vrow, 16 * hk + e));
@@ -1131,14 +1056,6 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(imgReady);
             } else if (role == kRoleMain) {
-                if (!last && mode == 3) {  // hand-off to the next phase
-#pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        const float* a = e < 8 ? a0 + 4 * e : a1 + 4 * (e - 8);
-                        *reinterpret_cast<float4*>(chain + zrow_off(vrow, 16 * hk + e)) =
-                            make_float4(a[0], a[1], a[2], a[3]);
-                    }
-                }
                 if (last) {
                     float* ns_row = ns_head + vrow * kD + 64 * hk;
 #pragma unroll
@@ -1275,9 +1192,8 @@ static cudaError_t set_smem(K kernel, int bytes) {
 }
 
 // Path selection: 0 = auto, 1 = token-recurrent, 2 = chunked tensor-core, 3 = chunked
-// with the segmented carry forced (P = 4; needs the summary space, N <= 6),
-// 4 = chunked, phased (needs the hand-off space, N <= 18; else as 2).
-constexpr int kPathAuto = 0, kPathRecurrent = 1, kPathChunked = 2, kPathSegmented = 3, kPathPhased = 4;
+// with the segmented carry forced (P = 4; needs the summary space, N <= 6).
+constexpr int kPathAuto = 0, kPathRecurrent = 1, kPathChunked = 2, kPathSegmented = 3;
 constexpr int64_t kRecurrentMaxAvgLen = 48;
 
 // Launch `kernel` so that it may begin (prologue up to griddep_wait) while the
@@ -1344,50 +1260,28 @@ cudaError_t launch_prefill_chunked(const PrefillParams& p, void* workspace, size
         if ((e = token_tensor_map(&tmQ, p.q, kHQK, p.total_tokens)) != cudaSuccess) return e;
         if ((e = token_tensor_map(&tmV, p.v, kHV, p.total_tokens)) != cudaSuccess) return e;
     }
+    gdn_chunk_table_kernel<<<kSmCount, 1024, 0, stream>>>(p, ws, L);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    if ((e = set_smem(gdn_chunk_prepare_kernel, kPrSmem)) != cudaSuccess) return e;
     int dev = 0, sms = 148;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if ((e = launch_dependent(gdn_chunk_prepare_kernel, static_cast<unsigned>(L.R * kHV), kPrepThreads, kPrSmem,
+                              stream, p, ws, L, tmK, tmQ, tmV, 2 * sms)) != cudaSuccess)
+        return e;
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    if ((e = set_smem(gdn_chunk_carry_kernel, kCaSmem)) != cudaSuccess) return e;
     const int64_t units = p.num_seqs * kHV;
     if (units > 0x7fffffffLL / (2 * kSegMaxP)) return cudaErrorInvalidValue;
-    const bool room = workspace_bytes >= static_cast<size_t>(L.total_seg);
     // Segmented carry: when the chains (sequence x v-head) fill under a third
     // of the SMs and sequences average 16 chunks or more (or when asked for),
     // split each sequence into P segments (pass A, then pass C).
     int P = 1;
-    if (L.off_seg > 0 && room && path != kPathPhased) {
+    if (L.off_seg > 0 && workspace_bytes >= static_cast<size_t>(L.total_seg)) {
         if (path == kPathSegmented)
             P = 4;
         else if (units * 3 <= sms && p.total_tokens >= p.num_seqs * 16 * kC)
             P = static_cast<int>(sms / (units * 2)) < kSegMaxP ? static_cast<int>(sms / (units * 2)) : kSegMaxP;
     }
-    // Phased prefill: when the chains fill at most half the SMs (and are long),
-    // split every sequence into kPhases consecutive chunk ranges; the carry of
-    // range ph runs on its SMs while the prepare of range ph + 1 runs on the rest.
-    const bool phased = P == 1 && L.off_chain > 0 && room &&
-                        (path == kPathPhased || (units * 2 <= sms && p.total_tokens >= p.num_seqs * 32 * kC));
-    gdn_chunk_table_kernel<<<kSmCount, 1024, 0, stream>>>(p, ws, L, phased ? kPhases : 0);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    if ((e = set_smem(gdn_chunk_prepare_kernel, kPrSmem)) != cudaSuccess) return e;
-    if ((e = set_smem(gdn_chunk_carry_kernel, kCaSmem)) != cudaSuccess) return e;
-    if (phased) {
-        // table -> prepare(0) -> carry(0) -> prepare(1) -> carry(1) -> ..., each a
-        // dependent launch: a carry's CTAs take their SMs before the next
-        // prepare's CTAs fill the rest.  Per phase at most R / kPhases + N records.
-        const int64_t per = (L.R + kPhases - 1) / kPhases + p.num_seqs;
-        for (int ph = 0; ph < kPhases; ++ph) {
-            const unsigned grid = static_cast<unsigned>(per * kHV + (ph > 0 ? 1 : 0));
-            if ((e = launch_dependent(gdn_chunk_prepare_kernel, grid, kPrepThreads, kPrSmem, stream, p, ws, L, tmK,
-                                      tmQ, tmV, 2 * sms, ph)) != cudaSuccess)
-                return e;
-            if ((e = launch_dependent(gdn_chunk_carry_kernel, static_cast<unsigned>(units), kCarryThreads, kCaSmem,
-                                      stream, p, ws, L, 3, ph)) != cudaSuccess)
-                return e;
-        }
-        return cudaSuccess;
-    }
-    if ((e = launch_dependent(gdn_chunk_prepare_kernel, static_cast<unsigned>(L.R * kHV), kPrepThreads, kPrSmem,
-                              stream, p, ws, L, tmK, tmQ, tmV, 2 * sms, -1)) != cudaSuccess)
-        return e;
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if (P >= 2) {
         if ((e = launch_dependent(gdn_chunk_carry_kernel, static_cast<unsigned>(units * (2 * P - 3)), kCarryThreads,
                                   kCaSmem, stream, p, ws, L, 1, P)) != cudaSuccess)

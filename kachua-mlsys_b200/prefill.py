@@ -87,7 +87,7 @@ def _ptr(t):
     return ctypes.c_void_p(None if t is None else t.data_ptr())
 
 
-PATHS = {"auto": 0, "recurrent": 1, "chunked": 2, "segmented": 3, "phased": 4}
+PATHS = {"auto": 0, "recurrent": 1, "chunked": 2, "segmented": 3}
 
 
 def launch_gdn(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None, output=None,
@@ -97,10 +97,7 @@ def launch_gdn(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None, out
 
     ``path`` selects the algorithm: ``"auto"`` (token-recurrent kernel for
     batches of short sequences, chunked tensor-core kernels otherwise),
-    ``"recurrent"``, ``"chunked"``, or the chunked path with one carry layout
-    forced, ``"segmented"`` (up to 6 sequences) or ``"phased"`` (up to 18
-    sequences; both fall back to ``"chunked"`` beyond that or with a workspace
-    of less than ``workspace_bytes(T, N)``).  ``workspace`` may be passed to reuse a
+    ``"recurrent"`` or ``"chunked"``.  ``workspace`` may be passed to reuse a
     device buffer of at least ``workspace_bytes(T, N)`` bytes.
     """
     _need(path in PATHS, f"path must be one of {sorted(PATHS)}")

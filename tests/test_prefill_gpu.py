@@ -19,11 +19,10 @@ pytestmark = pytest.mark.gpu
 OUT_TOL = dict(atol=1e-2, rtol=1e-2)
 
 
-@pytest.fixture(params=["recurrent", "chunked", "segmented", "phased"])
+@pytest.fixture(params=["recurrent", "chunked", "segmented"])
 def path(request):
     """recurrent: token recurrence; chunked: chunked path with its own carry
-    choice; segmented: chunked with the segmented (composed) carry forced;
-    phased: chunked with the phased prepare/carry overlap forced."""
+    choice; segmented: chunked with the segmented (composed) carry forced."""
     return request.param
 
 
@@ -135,26 +134,6 @@ def test_prefill_segmented_long(pkg, orc, cuda_dev, lengths):
     sequences, uneven segment splits and empty / one-chunk neighbours."""
     _check(pkg, orc, pkg.inputs.make_prefill_inputs(lengths, seed=sum(lengths) + 7, with_state=True),
            cuda_dev, path="segmented")
-
-
-@pytest.mark.parametrize("lengths", [[1000], [2048, 700], [5, 3000, 0], [640, 64, 65, 1], [130, 3, 4100, 192, 64]])
-def test_prefill_phased_long(pkg, orc, cuda_dev, lengths):
-    """The phased prefill on long sequences, sequences shorter than the number
-    of phases (empty phases) and empty / one-chunk neighbours."""
-    _check(pkg, orc, pkg.inputs.make_prefill_inputs(lengths, seed=sum(lengths) + 9, with_state=True),
-           cuda_dev, path="phased")
-
-
-def test_phased_matches_single_pass(pkg, cuda_dev):
-    """The phased and single-pass carries give the same bits: the chunk work
-    and the state rounding are identical, only the launch order differs.  Ten
-    sequences: 80 chains, too many for the automatic phased or segmented
-    choice, so "chunked" runs the single pass."""
-    inp = pkg.inputs.make_prefill_inputs([700, 1, 1300, 256, 64, 0, 900, 129, 2000, 65], seed=49,
-                                         with_state=True)
-    o_p, s_p = _run(pkg, inp, cuda_dev, path="phased")
-    o_c, s_c = _run(pkg, inp, cuda_dev, path="chunked")
-    assert torch.equal(o_p, o_c) and torch.equal(s_p, s_c)
 
 
 def test_segmented_matches_single_pass(pkg, cuda_dev):
