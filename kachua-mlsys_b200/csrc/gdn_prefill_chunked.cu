@@ -342,6 +342,17 @@ __device__ __forceinline__ uint8_t* smem_align1024(uint8_t* raw) {
 __device__ __forceinline__ void named_sync(int id, int count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
+// named barrier that also returns the AND of `pred` over the `count` threads
+__device__ __forceinline__ bool named_sync_and(int id, int count, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, %2, %3, p;\n"
+        " selp.u32 %0, 1, 0, q;\n}"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(count)
+        : "memory");
+    return r != 0;
+}
 
 // fp32 diagonal 32 x 32 block d of N: row r is 128 bytes, its 16-byte chunk c
 // at position c ^ (r & 7)
@@ -797,7 +808,8 @@ constexpr int kCaM = 0;                         // f16 M K-major [128 k][128 k']
 constexpr int kCaKU = 65536;                    // K' [64 j][128 k] (MN-major) + U^T [128 v][64 j] (K-major), 3 x 32 KiB
 constexpr int kCaQt = kCaKU + 3 * 32768;        // f16 Qt^T MN-major [128 k][64 i], 3 x 16 KiB
 constexpr int kCaSmall = kCaQt + 3 * 16384;
-constexpr int kCaSmem = kCaSmall + 256 + 1024;
+constexpr int kCaOut = kCaSmall + 1024;         // bf16 output tile [64 i][128 v]: two SW128 images (v 0-63, 64-127)
+constexpr int kCaSmem = kCaOut + 16384 + 1024;
 constexpr int kCaTmemCols = 512;  // accS x 2 [0, 256), fp16 S x 2 [256, 384), accO x 2 [384, 512)
 
 enum CarryRole { kRoleMain = 0, kRoleSum0 = 1, kRoleSumT = 2, kRoleSumZ = 3 };
@@ -813,7 +825,7 @@ __device__ __forceinline__ uint32_t zrow_off(int v, int c) { return v * 512 + ((
 
 __global__ void __launch_bounds__(kCarryThreads, 1)
     gdn_chunk_carry_kernel(const PrefillParams p, uint8_t* __restrict__ ws, const WsLayout L, const int mode,
-                           const int P) {
+                           const int P, const __grid_constant__ CUtensorMap tmO) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = smem_align1024(smem_raw);
     const Smem Sm{sm, smem_u32(sm)};
@@ -1028,6 +1040,8 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
             for (int c = 0; c < 3 && c < nch; ++c) issue_KU(c);
         if (outputs)
             for (int c = 0; c < 2 && c < nch; ++c) issue_Qt(c);
+        if (outputs)  // Ut^T is read by the output warps straight from global memory
+            for (int c = 0; c < 2 && c < nch; ++c) bulk_prefetch_l2(rec_ptr(c) + kRecUt, 16384);
     }
 
     if (warp < 8) {
@@ -1083,45 +1097,83 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
             }
         }
     } else if (warp < 12) {
-        // output epilogue: lane v, columns = the chunk's 64 tokens; a warp
-        // stores 64 contiguous bytes (32 values of v) of a token row at a time
+        // output epilogue: lane v, columns = the chunk's 64 tokens.  A full
+        // chunk is staged as the bf16 tile [64 i][128 v] (two SW128 images)
+        // and written by two tiled TMA stores; the last, partial chunk of a
+        // sequence is stored element by element (a tile would spill into the
+        // next sequence's rows).
         const int q = warp - 8;
         const int v = 32 * q + lane;
-        for (int c = 0; outputs && c < nch; ++c) {
-            const int rows = len - kC * c < kC ? len - kC * c : kC;
-            uint4 ut[8];  // Ut^T row v: logical 16-byte chunk e (tokens 8e..8e+7) stored at e ^ (v & 7)
+        const bool lead = tid == 8 * 32;  // issues the tile stores
+        const uint32_t aOut = smem_u32(sm + kCaOut);
+        const uint32_t ov = aOut + (v >> 6) * 8192 + (v & 7) * 2;
+        const int och = (v & 63) >> 3;
+        uint4 ut[8];  // Ut^T row v of the chunk: logical 16-byte chunk e (tokens 8e..8e+7) stored at e ^ (v & 7)
+        auto load_ut = [&](int c) {
             const uint8_t* urow = rec_ptr(c) + kRecUt + v * 128;
 #pragma unroll
             for (int e = 0; e < 8; ++e) ut[e] = __ldg(reinterpret_cast<const uint4*>(urow + ((e ^ (v & 7)) << 4)));
-            const bool okc = __all_sync(0xffffffffu, mbar_wait(mmaO(c & 1), (c >> 1) & 1));
+        };
+        if (outputs && nch > 0) load_ut(0);
+        for (int c = 0; outputs && c < nch; ++c) {
+            const int rows = len - kC * c < kC ? len - kC * c : kC;
+            // one verdict for the four warps (they meet at named barriers below)
+            const bool okc = named_sync_and(1, 128, mbar_wait(mmaO(c & 1), (c >> 1) & 1));
             tc_fence_after();
             if (!okc) {
                 if (lane == 0) record_status(32);
                 break;
             }
+            // scale (O + Ut) as bf16 pairs pk[j] = tokens (2j, 2j + 1), one TMEM half at a time
+            uint32_t pk[32];
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {  // tokens 32 half + [0, 32)
+            for (int half = 0; half < 2; ++half) {
                 float o[32];
                 tmem_ld32(taddr(accO(c & 1), 32 * q, 32 * half), o);
                 tmem_wait_ld();
-                if (half == 1) {  // the accumulator is read: release it
+                if (half == 1) {  // the accumulator is read: release it before the stores
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(oFree(c & 1));
                 }
-                uint16_t* dst = p.out + ((t0 + static_cast<int64_t>(kC) * c + 32 * half) * kHV + h) * kD + v;
 #pragma unroll
                 for (int i0 = 0; i0 < 32; i0 += 8) {
                     float u[8];
                     h16x8_to_f32(ut[(32 * half + i0) >> 3], u);
 #pragma unroll
-                    for (int e = 0; e < 8; ++e)
-                        if (32 * half + i0 + e < rows)
-                            dst[static_cast<int64_t>(i0 + e) * (kHV * kD)] =
-                                __bfloat16_as_ushort(__float2bfloat16_rn(p.scale * (o[i0 + e] + u[e])));
+                    for (int e = 0; e < 8; e += 2) {
+                        const __nv_bfloat162 b2 = __floats2bfloat162_rn(p.scale * (o[i0 + e] + u[e]),
+                                                                        p.scale * (o[i0 + e + 1] + u[e + 1]));
+                        pk[(32 * half + i0 + e) >> 1] = *reinterpret_cast<const uint32_t*>(&b2);
+                    }
                 }
             }
+            if (c + 1 < nch) load_ut(c + 1);  // in flight during this chunk's stores
+            if (rows == kC) {
+                if (lead) bulk_wait_read<0>();  // the previous tile has left the staging buffer
+                named_sync(1, 128);
+#pragma unroll
+                for (int i = 0; i < kC; ++i)
+                    st_shared_u16(ov + i * 128 + ((och ^ (i & 7)) << 4),
+                                  static_cast<uint16_t>((i & 1) ? pk[i >> 1] >> 16 : pk[i >> 1] & 0xffffu));
+                fence_async_smem();
+                named_sync(1, 128);
+                if (lead) {
+                    const int tok = static_cast<int>(t0) + kC * c;
+                    tma_store_3d(&tmO, aOut, 0, h, tok);
+                    tma_store_3d(&tmO, aOut + 8192, 64, h, tok);
+                    bulk_commit();
+                }
+            } else {
+                uint16_t* dst = p.out + ((t0 + static_cast<int64_t>(kC) * c) * kHV + h) * kD + v;
+#pragma unroll
+                for (int i = 0; i < kC; ++i)
+                    if (i < rows)
+                        dst[static_cast<int64_t>(i) * (kHV * kD)] =
+                            static_cast<uint16_t>((i & 1) ? pk[i >> 1] >> 16 : pk[i >> 1] & 0xffffu);
+            }
         }
+        if (lead) bulk_wait_read<0>();  // the last tile has left shared memory (its writes complete with the grid)
     } else if (issuer) {
         if (dpart) {
             ok = mbar_wait(fullKU(0), 0) && ok;
@@ -1165,7 +1217,10 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
             if (!ok) break;
             if (c + 2 < nch) {
                 issue_M(c + 2);
-                if (outputs) issue_Qt(c + 2);
+                if (outputs) {
+                    issue_Qt(c + 2);
+                    bulk_prefetch_l2(rec_ptr(c + 2) + kRecUt, 16384);
+                }
             }
             if (dpart && c + 3 < nch) issue_KU(c + 3);
         }
@@ -1250,15 +1305,17 @@ cudaError_t launch_prefill_chunked(const PrefillParams& p, void* workspace, size
     const WsLayout L = ws_layout(p.total_tokens, p.num_seqs);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     if (L.R * kHV > 0x7fffffffLL || p.total_tokens > 0x7fffffffLL) return cudaErrorInvalidValue;
-    CUtensorMap tmK, tmQ, tmV;
+    CUtensorMap tmK, tmQ, tmV, tmO;
     memset(&tmK, 0, sizeof(tmK));
     memset(&tmQ, 0, sizeof(tmQ));
     memset(&tmV, 0, sizeof(tmV));
+    memset(&tmO, 0, sizeof(tmO));
     cudaError_t e;
     if (p.total_tokens > 0) {  // with no tokens there are no records and no loads
         if ((e = token_tensor_map(&tmK, p.k, kHQK, p.total_tokens)) != cudaSuccess) return e;
         if ((e = token_tensor_map(&tmQ, p.q, kHQK, p.total_tokens)) != cudaSuccess) return e;
         if ((e = token_tensor_map(&tmV, p.v, kHV, p.total_tokens)) != cudaSuccess) return e;
+        if ((e = token_tensor_map(&tmO, p.out, kHV, p.total_tokens)) != cudaSuccess) return e;
     }
     gdn_chunk_table_kernel<<<kSmCount, 1024, 0, stream>>>(p, ws, L);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
@@ -1284,13 +1341,13 @@ cudaError_t launch_prefill_chunked(const PrefillParams& p, void* workspace, size
     }
     if (P >= 2) {
         if ((e = launch_dependent(gdn_chunk_carry_kernel, static_cast<unsigned>(units * (2 * P - 3)), kCarryThreads,
-                                  kCaSmem, stream, p, ws, L, 1, P)) != cudaSuccess)
+                                  kCaSmem, stream, p, ws, L, 1, P, tmO)) != cudaSuccess)
             return e;
         return launch_dependent(gdn_chunk_carry_kernel, static_cast<unsigned>(units * P), kCarryThreads, kCaSmem,
-                                stream, p, ws, L, 2, P);
+                                stream, p, ws, L, 2, P, tmO);
     }
     return launch_dependent(gdn_chunk_carry_kernel, static_cast<unsigned>(units), kCarryThreads, kCaSmem, stream, p,
-                            ws, L, 0, 1);
+                            ws, L, 0, 1, tmO);
 }
 
 cudaError_t launch_prefill(const PrefillParams& p, int path, void* workspace, size_t workspace_bytes,
