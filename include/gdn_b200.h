@@ -97,9 +97,10 @@ int gdn_decode_launch(const GdnDecodeArgs* args, void* stream);
 #define GDN_PREFILL_PATH_RECURRENT 1
 #define GDN_PREFILL_PATH_CHUNKED 2
 #define GDN_PREFILL_PATH_SEGMENTED 3  /* chunked, inter-chunk carry split into 4 composed segments per
-                                         sequence (used automatically when few long sequences leave
-                                         most SMs idle; needs the full workspace and num_seqs <= 6,
-                                         else falls back to CHUNKED) */
+                                         sequence (fewer for num_seqs > 3; used automatically, with as
+                                         many segments as fit the SMs, when few long sequences leave
+                                         SMs idle; needs the full workspace and num_seqs <= 4, else
+                                         falls back to CHUNKED) */
 
 /* Variable-length prefill over packed sequences.  Shapes:
  *   q, k       bf16 [T, 4, 128]        16-byte aligned
@@ -134,7 +135,7 @@ typedef struct GdnPrefillArgs {
 } GdnPrefillArgs;
 
 /* Bytes of device workspace for gdn_prefill_launch at these sizes (256-byte
- * aligned base).  Includes, for num_seqs <= 6, room for the segmented carry;
+ * aligned base).  Includes, for num_seqs <= 4, room for the segmented carry;
  * a smaller workspace that still holds the per-chunk operand images (about
  * 768 KiB per 64 tokens) is accepted and runs the single-pass carry.
  * Replaces the torch.empty scratch tensors the reference allocates per call

@@ -64,14 +64,27 @@ __host__ __device__ inline int64_t align_up(int64_t x, int64_t a) { return (x + 
 // Segmented carry summaries (few-sequence problems only): per sequence, v-head
 // and segment, T (f16 image, 32 KiB) and Z (fp32 rows, 64 KiB).
 constexpr int kSegMaxP = 8;
-constexpr int kSegMaxSeqs = 6;
 constexpr int kSegSlotBytes = 98304;
+
+// Segments per chain for N sequences: the most (up to 8) for which both
+// passes of the segmented carry fit one wave of CTAs, N x 8 x max(P, 2P - 3)
+// <= sms, and pass C (which streams every chunk's operands) keeps to two
+// thirds of the SMs, N x 8 x P <= 2 sms / 3: more concurrent chains than that
+// saturate HBM (about 70 GB/s each) and the split costs more than it saves.
+// Two segments were measured to gain nothing; 1 = no segmented carry.
+__host__ __device__ inline int seg_segments(int64_t N, int sms) {
+    int best = 1;
+    for (int P = 3; P <= kSegMaxP; ++P)
+        if (N > 0 && N * kHV * (P > 2 * P - 3 ? P : 2 * P - 3) <= sms && 3 * N * kHV * P <= 2 * sms) best = P;
+    return best;
+}
 
 struct WsLayout {
     int64_t R;  // record capacity: ceil(T / 64) + N bounds sum_s ceil(len_s / 64)
     int64_t off_hdr, off_base, off_order, off_table, off_rec;
     int64_t total;      // everything the single-pass carry needs
-    int64_t off_seg;    // segment summaries (0 when N > kSegMaxSeqs)
+    int64_t seg_slots;  // summary slots per chain (segments on a 148-SM part; 1: none)
+    int64_t off_seg;    // segment summaries (0 without slots)
     int64_t total_seg;  // total + the summaries
 };
 
@@ -90,8 +103,9 @@ __host__ __device__ inline WsLayout ws_layout(int64_t T, int64_t N) {
     L.off_rec = o;
     o += L.R * kHV * kHeadRecBytes;
     L.total = align_up(o, 1024);
-    L.off_seg = N <= kSegMaxSeqs ? L.total : 0;
-    L.total_seg = L.total + (N <= kSegMaxSeqs ? N * kHV * kSegMaxP * static_cast<int64_t>(kSegSlotBytes) : 0);
+    L.seg_slots = seg_segments(N, kSmCount);
+    L.off_seg = L.seg_slots >= 2 ? L.total : 0;
+    L.total_seg = L.total + (L.seg_slots >= 2 ? N * kHV * L.seg_slots * static_cast<int64_t>(kSegSlotBytes) : 0);
     return L;
 }
 
@@ -899,7 +913,7 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     t0 += static_cast<int64_t>(kC) * cb;
     const int len = len_all - kC * cb < kC * nch ? len_all - kC * cb : kC * nch;
     auto rec_ptr = [&](int c) { return ws + L.off_rec + (static_cast<int64_t>(rec0 + c) * kHV + h) * kHeadRecBytes; };
-    auto slot = [&](int sg) { return ws + L.off_seg + (unit * kSegMaxP + sg) * static_cast<int64_t>(kSegSlotBytes); };
+    auto slot = [&](int sg) { return ws + L.off_seg + (unit * L.seg_slots + sg) * static_cast<int64_t>(kSegSlotBytes); };
 
     const bool issuer = tid == 12 * 32, loader = tid == 13 * 32;
     int topM = -1, topKU = -1, topQt = -1;  // loader: highest chunk whose copy was issued
@@ -1247,7 +1261,8 @@ static cudaError_t set_smem(K kernel, int bytes) {
 }
 
 // Path selection: 0 = auto, 1 = token-recurrent, 2 = chunked tensor-core, 3 = chunked
-// with the segmented carry forced (P = 4; needs the summary space, N <= 6).
+// with the segmented carry forced (P = 4, or the workspace's slots if fewer; needs
+// the summary space, N <= 4).
 constexpr int kPathAuto = 0, kPathRecurrent = 1, kPathChunked = 2, kPathSegmented = 3;
 constexpr int64_t kRecurrentMaxAvgLen = 48;
 
@@ -1329,15 +1344,17 @@ cudaError_t launch_prefill_chunked(const PrefillParams& p, void* workspace, size
     if ((e = set_smem(gdn_chunk_carry_kernel, kCaSmem)) != cudaSuccess) return e;
     const int64_t units = p.num_seqs * kHV;
     if (units > 0x7fffffffLL / (2 * kSegMaxP)) return cudaErrorInvalidValue;
-    // Segmented carry: when the chains (sequence x v-head) fill under a third
-    // of the SMs and sequences average 16 chunks or more (or when asked for),
-    // split each sequence into P segments (pass A, then pass C).
+    // Segmented carry: when sequences average 16 chunks or more and both
+    // passes fit one wave with P >= 2 segments per chain (or when asked for:
+    // P = 4 where the workspace has the slots), split each sequence into P
+    // segments (pass A, then pass C).
     int P = 1;
     if (L.off_seg > 0 && workspace_bytes >= static_cast<size_t>(L.total_seg)) {
+        const int fit = seg_segments(p.num_seqs, sms);
         if (path == kPathSegmented)
-            P = 4;
-        else if (units * 3 <= sms && p.total_tokens >= p.num_seqs * 16 * kC)
-            P = static_cast<int>(sms / (units * 2)) < kSegMaxP ? static_cast<int>(sms / (units * 2)) : kSegMaxP;
+            P = L.seg_slots < 4 ? static_cast<int>(L.seg_slots) : 4;
+        else if (p.total_tokens >= p.num_seqs * 16 * kC)
+            P = fit < L.seg_slots ? fit : static_cast<int>(L.seg_slots);
     }
     if (P >= 2) {
         if ((e = launch_dependent(gdn_chunk_carry_kernel, static_cast<unsigned>(units * (2 * P - 3)), kCarryThreads,

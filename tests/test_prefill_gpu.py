@@ -128,12 +128,23 @@ def test_prefill_deterministic(pkg, cuda_dev, path):
     assert torch.equal(o1, o2) and torch.equal(s1, s2)
 
 
-@pytest.mark.parametrize("lengths", [[1000], [2048, 700], [5, 3000, 0], [640, 64, 65, 1]])
+@pytest.mark.parametrize("lengths", [[1000], [2048, 700], [5, 3000, 0], [640, 64, 65, 1],
+                                     [1100, 700, 1500, 2048, 1]])
 def test_prefill_segmented_long(pkg, orc, cuda_dev, lengths):
     """The segmented carry (sequences split into composed segments) on long
-    sequences, uneven segment splits and empty / one-chunk neighbours."""
+    sequences, uneven segment splits and empty / one-chunk neighbours; with
+    1-3 and 4 sequences it runs 4 and 3 segments per chain, with 5 none."""
     _check(pkg, orc, pkg.inputs.make_prefill_inputs(lengths, seed=sum(lengths) + 7, with_state=True),
            cuda_dev, path="segmented")
+
+
+@pytest.mark.parametrize("lengths", [[4096], [2048] * 2, [2048] * 3, [1536] * 4, [1100] * 6])
+def test_prefill_segmented_auto(pkg, orc, cuda_dev, lengths):
+    """The automatic choice on long sequences: 1, 2, 3 and 4 of them take the
+    segmented carry with 8, 6, 4 and 3 segments per chain on a 148-SM part,
+    6 the single pass."""
+    _check(pkg, orc, pkg.inputs.make_prefill_inputs(lengths, seed=len(lengths) + 50, with_state=True),
+           cuda_dev, path="auto")
 
 
 def test_segmented_matches_single_pass(pkg, cuda_dev):
