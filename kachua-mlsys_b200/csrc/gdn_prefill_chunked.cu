@@ -224,8 +224,9 @@ __global__ void __launch_bounds__(1024) gdn_chunk_table_kernel(const PrefillPara
 }
 
 // ---------------------------------------------------------------- prepare --
-// One CTA (256 threads) per chunk record and v-head: everything the carry's
-// chain does not need, finished per chunk in fp16 operand images (fp32
+// Per chunk record and v-head (an item; persistent CTAs of 256 threads, two per
+// SM, take items blockIdx.x, + gridDim.x, ...): everything the carry's chain
+// does not need, finished per chunk in fp16 operand images (fp32
 // accumulation) and bulk-stored to the workspace:
 //   M    = G_C I - K'^T W     [k][k']  K-major    (B of the state MMA S M^T)
 //   K'   = tail (.) K         [j][k]   MN-major   (B of the carry's U^T K')
@@ -377,7 +378,7 @@ __device__ __forceinline__ uint32_t nd_off(int d, int r, int m) {
 __global__ void __launch_bounds__(kPrepThreads, 2)
     gdn_chunk_prepare_kernel(const PrefillParams p, uint8_t* __restrict__ ws, const WsLayout L,
                              const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
-                             const __grid_constant__ CUtensorMap tmV, const int prefetch_ahead) {
+                             const __grid_constant__ CUtensorMap tmV) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = smem_align1024(smem_raw);
     const Smem S{sm, smem_u32(sm)};
@@ -390,42 +391,16 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
     // 32 (w & 3).. (its sub-partition) and column half hc = w >> 2.
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int q = warp & 3, hc = warp >> 2;
-    // 1-D grid, record-major: the 8 v-heads of a chunk run back to back (their
-    // K and Q loads share L2 lines)
-    const int64_t rec = blockIdx.x / kHV;
-    const int h = static_cast<int>(blockIdx.x % kHV), hq = h / kGva;
     griddep_launch_dependents();  // the carry may start its prologue on freed SMs
     griddep_wait();               // the chunk table is complete
     const int nrec = reinterpret_cast<const int*>(ws + L.off_hdr)[0];
-    if (rec >= nrec) return;
-    const int4 te = reinterpret_cast<const int4*>(ws + L.off_table)[rec];
-    if (tid == 32) {  // warm L2 for the CTA that takes this slot a wave later
-        const int64_t nidx = static_cast<int64_t>(blockIdx.x) + prefetch_ahead;
-        const int64_t nrecx = nidx / kHV;
-        if (nrecx < nrec) {
-            const int nh = static_cast<int>(nidx % kHV);
-            const int nt0 = reinterpret_cast<const int4*>(ws + L.off_table)[nrecx].y;
-            if ((nh & 1) == 0) {
-                tma_prefetch_3d(&tmK, 0, nh / kGva, nt0);
-                tma_prefetch_3d(&tmK, 64, nh / kGva, nt0);
-                tma_prefetch_3d(&tmQ, 0, nh / kGva, nt0);
-                tma_prefetch_3d(&tmQ, 64, nh / kGva, nt0);
-            }
-            tma_prefetch_3d(&tmV, 0, nh, nt0);
-            tma_prefetch_3d(&tmV, 64, nh, nt0);
-            if (nh == 0 && ((reinterpret_cast<uintptr_t>(p.a) | reinterpret_cast<uintptr_t>(p.b)) & 15) == 0) {
-                // gate rows a, b of the record: [tokens][8] bf16, 16 bytes per token (16-byte aligned bases only)
-                const int64_t ntok = p.total_tokens - nt0 < kC ? p.total_tokens - nt0 : kC;
-                bulk_prefetch_l2(p.a + static_cast<int64_t>(nt0) * kHV, static_cast<uint32_t>(ntok * 16));
-                bulk_prefetch_l2(p.b + static_cast<int64_t>(nt0) * kHV, static_cast<uint32_t>(ntok * 16));
-            }
-        }
-    }
-    const int t0 = te.y;  // first token (T < 2^31, checked on the host)
-    const int n = te.z;   // tokens in this chunk (1..64)
-    uint8_t* out_rec = ws + L.off_rec + (rec * kHV + h) * kHeadRecBytes;
+    const int64_t nitems = static_cast<int64_t>(nrec) * kHV;
+    if (static_cast<int64_t>(blockIdx.x) >= nitems) return;
+    const int4* table = reinterpret_cast<const int4*>(ws + L.off_table);
 
-    // barM: Gram, T, X22 T commits; barW: [W | U]^T and final commits; barE: TB and X21 written
+    // barL: the item's input loads (one phase per item); barM: Gram, T, X22 T
+    // commits (three per item); barW: [W | U]^T and final commits; barE: TB and
+    // X21 written (two phases per item each)
     const uint32_t barL = smem_u32(&sml.bar_load), barM = smem_u32(&sml.bar_mma), barW = smem_u32(&sml.bar_w),
                    barE = smem_u32(&sml.bar_e);
     if (tid == 0) {
@@ -434,355 +409,409 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
         mbar_init(barW, 1);
         mbar_init(barE, 2);
         fence_mbar_init();
-        mbar_expect_tx(barL, 6 * 8192);
-        tma_load_3d(aKQ, &tmK, 0, hq, t0, barL);
-        tma_load_3d(aKQ + 16384, &tmK, 64, hq, t0, barL);
-        tma_load_3d(aKQ + 8192, &tmQ, 0, hq, t0, barL);
-        tma_load_3d(aKQ + 24576, &tmQ, 64, hq, t0, barL);
-        tma_load_3d(aRHS + 16384, &tmV, 0, h, t0, barL);
-        tma_load_3d(aRHS + 24576, &tmV, 64, h, t0, barL);
     }
     if (warp == 1) {
         tmem_alloc(smem_u32(&sml.tmem_base), kPrTmemCols);
         tmem_relinquish();
     }
-    // zero the A^-1 image (its off-diagonal blocks stay zero until X21 is known)
-    S.st16(aX + tid * 32, make_uint4(0, 0, 0, 0));
-    S.st16(aX + tid * 32 + 16, make_uint4(0, 0, 0, 0));
-    // gates and the inclusive prefix of log2 g (threads 0-63 = tokens; warp scans)
-    float lgs = 0.f;
-    if (tid < kC) {
-        float lg = 0.f, bt = 0.f;
-        if (tid < n) {
-            const int64_t t = static_cast<int64_t>(t0) + tid;
-            lg = gdn_log2_decay(p.A_log[h], p.dt_bias[h], bf16_bits_to_float(p.a[t * kHV + h]));
-            bt = 1.0f / (1.0f + expf(-bf16_bits_to_float(p.b[t * kHV + h])));
-        }
-        lgs = lg;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const float y = __shfl_up_sync(0xffffffffu, lgs, o);
-            if (lane >= o) lgs += y;
-        }
-        if (lane == 31) sml.wtot[warp] = lgs;
-        sml.beta[tid] = bt;
-    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (tid >= 32 && tid < kC) lgs += sml.wtot[0];
-    if (tid < kC) sml.LG[tid] = lgs;
     const uint32_t tm = sml.tmem_base;
-    __syncthreads();
-    if (tid < kC) {  // per-row scales (0 past the chunk)
-        const bool act = tid < n;
-        sml.sBG[tid] = act ? sml.beta[tid] * fast_exp2(lgs) : 0.f;
-        sml.sTail[tid] = act ? fast_exp2(sml.LG[kC - 1] - lgs) : 0.f;
+
+    // Persistent CTAs (two per SM) walk the items (chunk record, v-head)
+    // blockIdx.x, + gridDim.x, ...; items are record-major, so the 8 v-heads of
+    // a chunk run side by side (their K and Q loads share L2 lines).  The next
+    // item's table entry and gate inputs are read, and its K, Q and V prefetched
+    // into L2, while the current one is processed.
+    int4 te = table[blockIdx.x / kHV];
+    uint16_t ga = 0, gb = 0;  // raw bf16 gate inputs a, b of token tid of the item (tid < 64)
+    if (tid < te.z) {
+        const int64_t t = static_cast<int64_t>(te.y) + tid;
+        ga = p.a[t * kHV + blockIdx.x % kHV];
+        gb = p.b[t * kHV + blockIdx.x % kHV];
     }
-    bool ok = mbar_wait(barL, 0);
-    // 1. Gram [K;Q] K^T (bf16, M=128, N=64, K=128) -> TMEM columns 0-63
-    if (tid == 0 && ok) {
+    bool stop = false;
+    int it = 0;
+    for (int64_t item = blockIdx.x; item < nitems && !stop; item += gridDim.x, ++it) {
+        const int64_t rec = item / kHV;
+        const int h = static_cast<int>(item % kHV), hq = h / kGva;
+        const uint32_t pl = static_cast<uint32_t>(it) & 1u;  // parity of the item's barL and first barM phase
+        const int t0 = te.y;  // first token (T < 2^31, checked on the host)
+        const int n = te.z;   // tokens in this chunk (1..64)
+        uint8_t* out_rec = ws + L.off_rec + (rec * kHV + h) * kHeadRecBytes;
+        const int64_t nitem = item + gridDim.x;
+        const int4 te_next = nitem < nitems ? table[nitem / kHV] : te;  // used after the Gram issue
+        uint16_t ga_next = 0, gb_next = 0;
+        if (tid == 0) {
+            mbar_expect_tx(barL, 6 * 8192);
+            tma_load_3d(aKQ, &tmK, 0, hq, t0, barL);
+            tma_load_3d(aKQ + 16384, &tmK, 64, hq, t0, barL);
+            tma_load_3d(aKQ + 8192, &tmQ, 0, hq, t0, barL);
+            tma_load_3d(aKQ + 24576, &tmQ, 64, hq, t0, barL);
+            tma_load_3d(aRHS + 16384, &tmV, 0, h, t0, barL);
+            tma_load_3d(aRHS + 24576, &tmV, 64, h, t0, barL);
+        }
+        // zero the A^-1 image (its off-diagonal blocks stay zero until X21 is known)
+        S.st16(aX + tid * 32, make_uint4(0, 0, 0, 0));
+        S.st16(aX + tid * 32 + 16, make_uint4(0, 0, 0, 0));
+        // gates and the inclusive prefix of log2 g (threads 0-63 = tokens; warp scans)
+        float lgs = 0.f;
+        if (tid < kC) {
+            float lg = 0.f, bt = 0.f;
+            if (tid < n) {
+                lg = gdn_log2_decay(p.A_log[h], p.dt_bias[h], bf16_bits_to_float(ga));
+                bt = 1.0f / (1.0f + expf(-bf16_bits_to_float(gb)));
+            }
+            lgs = lg;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const float y = __shfl_up_sync(0xffffffffu, lgs, o);
+                if (lane >= o) lgs += y;
+            }
+            if (lane == 31) sml.wtot[warp] = lgs;
+            sml.beta[tid] = bt;
+        }
+        tc_fence_before();
+        __syncthreads();
         tc_fence_after();
-        mma_ct<kBF16, false, false, kD, 128, 128, 128, 64>(tm, aKQ, aKQ, false);
-        mma_commit(barM);
-    }
-    __syncthreads();  // the row scales are visible
-    ok = mbar_wait(barM, 0) && ok;
-    tc_fence_after();
-    {
-        // 2. Gram epilogue, 32 columns j = 32 hc + e per thread.  Rows 0-63 give
-        //    N: its fp32 diagonal 32-blocks and the f16 image NL of its
-        //    lower-left block (zero elsewhere); rows 64-127 the f16 image of
-        //    -P, P = Gam (.) Q K^T for j <= i.
-        float g[32];
-        tmem_ld32(taddr(tm, 32 * q, 32 * hc), g);
-        tmem_wait_ld();
-        if (q < 2) {
-            const int i = 32 * q + lane;
-            const float LGi = sml.LG[i], bi = sml.beta[i];
-            const bool act = i < n;
-            float nv[32];
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-                const int j = 32 * hc + e;
-                nv[e] = (j < i && act) ? bi * fast_exp2(LGi - sml.LG[j]) * g[e] : 0.f;
+        if (tid >= 32 && tid < kC) lgs += sml.wtot[0];
+        if (tid < kC) sml.LG[tid] = lgs;
+        __syncthreads();
+        if (tid < kC) {  // per-row scales (0 past the chunk)
+            const bool act = tid < n;
+            sml.sBG[tid] = act ? sml.beta[tid] * fast_exp2(lgs) : 0.f;
+            sml.sTail[tid] = act ? fast_exp2(sml.LG[kC - 1] - lgs) : 0.f;
+        }
+        bool ok = mbar_wait(barL, pl);
+        // 1. Gram [K;Q] K^T (bf16, M=128, N=64, K=128) -> TMEM columns 0-63
+        if (tid == 0 && ok) {
+            tc_fence_after();
+            mma_ct<kBF16, false, false, kD, 128, 128, 128, 64>(tm, aKQ, aKQ, false);
+            mma_commit(barM);
+        }
+        __syncthreads();  // the row scales are visible
+        if (nitem < nitems && tid < kC) {  // the next item: gate inputs, and its K, Q and V into L2
+            const int nh = static_cast<int>(nitem % kHV);
+            if (tid < te_next.z) {
+                const int64_t t = static_cast<int64_t>(te_next.y) + tid;
+                ga_next = p.a[t * kHV + nh];
+                gb_next = p.b[t * kHV + nh];
             }
-            if (hc == q) {  // the diagonal block d = q: fp32 rows for the substitution
-#pragma unroll
-                for (int m0 = 0; m0 < 32; m0 += 4)
-                    S.stf4(aN + nd_off(q, lane, m0), make_float4(nv[m0], nv[m0 + 1], nv[m0 + 2], nv[m0 + 3]));
-            }
-            const bool lower_left = q == 1 && hc == 0;
-#pragma unroll
-            for (int e0 = 0; e0 < 32; e0 += 8) {
-                float f[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) f[e] = lower_left ? nv[e0 + e] : 0.f;
-                S.st16(aNL + h16(i, 32 * hc + e0, 64), f16x8(f));
-            }
-        } else {
-            const int i = 32 * (q - 2) + lane;
-            const float LGi = sml.LG[i];
-#pragma unroll
-            for (int e0 = 0; e0 < 32; e0 += 8) {
-                float pv[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const int j = 32 * hc + e0 + e;
-                    pv[e] = (j <= i) ? -fast_exp2(LGi - sml.LG[j]) * g[e0 + e] : 0.f;
+            if (tid == 32) {
+                const int nt0 = te_next.y;
+                if ((nh & 1) == 0) {
+                    tma_prefetch_3d(&tmK, 0, nh / kGva, nt0);
+                    tma_prefetch_3d(&tmK, 64, nh / kGva, nt0);
+                    tma_prefetch_3d(&tmQ, 0, nh / kGva, nt0);
+                    tma_prefetch_3d(&tmQ, 64, nh / kGva, nt0);
                 }
-                S.st16(aPO + h16(i, 32 * hc + e0, 64), f16x8(pv));
+                tma_prefetch_3d(&tmV, 0, nh, nt0);
+                tma_prefetch_3d(&tmV, 64, nh, nt0);
             }
         }
-    }
-    tc_fence_before();
-    if (__syncthreads_or(!ok)) goto abort;
-    if (warp < 2) {
-        // 3a. diagonal blocks of A^-1: (I + N_dd) x = e_j, d = warp, column
-        //     j = lane, 32 rows in fp32 (four partial sums per row)
-        const int d = warp, j = lane;
-        float x[32];
+        ok = mbar_wait(barM, pl) && ok;
+        tc_fence_after();
+        {
+            // 2. Gram epilogue, 32 columns j = 32 hc + e per thread.  Rows 0-63 give
+            //    N: its fp32 diagonal 32-blocks and the f16 image NL of its
+            //    lower-left block (zero elsewhere); rows 64-127 the f16 image of
+            //    -P, P = Gam (.) Q K^T for j <= i.
+            float g[32];
+            tmem_ld32(taddr(tm, 32 * q, 32 * hc), g);
+            tmem_wait_ld();
+            if (q < 2) {
+                const int i = 32 * q + lane;
+                const float LGi = sml.LG[i], bi = sml.beta[i];
+                const bool act = i < n;
+                float nv[32];
 #pragma unroll
-        for (int r = 0; r < 32; ++r) {
-            float a0 = (r == j) ? 1.f : 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+                for (int e = 0; e < 32; ++e) {
+                    const int j = 32 * hc + e;
+                    nv[e] = (j < i && act) ? bi * fast_exp2(LGi - sml.LG[j]) * g[e] : 0.f;
+                }
+                if (hc == q) {  // the diagonal block d = q: fp32 rows for the substitution
 #pragma unroll
-            for (int m = 0; m < r; m += 4) {
-                const float4 nv = S.ldf4(aN + nd_off(d, r, m));
-                a0 = fmaf(-nv.x, x[m], a0);
-                if (m + 1 < r) a1 = fmaf(-nv.y, x[m + 1], a1);
-                if (m + 2 < r) a2 = fmaf(-nv.z, x[m + 2], a2);
-                if (m + 3 < r) a3 = fmaf(-nv.w, x[m + 3], a3);
+                    for (int m0 = 0; m0 < 32; m0 += 4)
+                        S.stf4(aN + nd_off(q, lane, m0), make_float4(nv[m0], nv[m0 + 1], nv[m0 + 2], nv[m0 + 3]));
+                }
+                const bool lower_left = q == 1 && hc == 0;
+#pragma unroll
+                for (int e0 = 0; e0 < 32; e0 += 8) {
+                    float f[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) f[e] = lower_left ? nv[e0 + e] : 0.f;
+                    S.st16(aNL + h16(i, 32 * hc + e0, 64), f16x8(f));
+                }
+            } else {
+                const int i = 32 * (q - 2) + lane;
+                const float LGi = sml.LG[i];
+#pragma unroll
+                for (int e0 = 0; e0 < 32; e0 += 8) {
+                    float pv[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const int j = 32 * hc + e0 + e;
+                        pv[e] = (j <= i) ? -fast_exp2(LGi - sml.LG[j]) * g[e0 + e] : 0.f;
+                    }
+                    S.st16(aPO + h16(i, 32 * hc + e0, 64), f16x8(pv));
+                }
             }
-            x[r] = (a0 + a1) + (a2 + a3);
         }
+        tc_fence_before();
+        if (__syncthreads_or(!ok)) goto abort;
+        if (warp < 2) {
+            // 3a. diagonal blocks of A^-1: (I + N_dd) x = e_j, d = warp, column
+            //     j = lane, 32 rows in fp32 (four partial sums per row)
+            const int d = warp, j = lane;
+            float x[32];
 #pragma unroll
-        for (int r = 0; r < 32; ++r) S.st2(aX + h16(32 * d + r, 32 * d + j, 64), __half_as_ushort(__float2half_rn(x[r])));
-    } else {
-        // 3b. [bGK | bV] in fp16 over the RHS (the scale depends on the row only,
-        //     so 16-byte chunks convert in place of their swizzled position),
-        //     while warps 0-1 solve; K stays bf16 here (read by the Gram MMA)
+            for (int r = 0; r < 32; ++r) {
+                float a0 = (r == j) ? 1.f : 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+                for (int m = 0; m < r; m += 4) {
+                    const float4 nv = S.ldf4(aN + nd_off(d, r, m));
+                    a0 = fmaf(-nv.x, x[m], a0);
+                    if (m + 1 < r) a1 = fmaf(-nv.y, x[m + 1], a1);
+                    if (m + 2 < r) a2 = fmaf(-nv.z, x[m + 2], a2);
+                    if (m + 3 < r) a3 = fmaf(-nv.w, x[m + 3], a3);
+                }
+                x[r] = (a0 + a1) + (a2 + a3);
+            }
+#pragma unroll
+            for (int r = 0; r < 32; ++r) S.st2(aX + h16(32 * d + r, 32 * d + j, 64), __half_as_ushort(__float2half_rn(x[r])));
+        } else {
+            // 3b. [bGK | bV] in fp16 over the RHS (the scale depends on the row only,
+            //     so 16-byte chunks convert in place of their swizzled position),
+            //     while warps 0-1 solve; K stays bf16 here (read by the Gram MMA)
 #pragma unroll 2
-        for (int it = 0; it < 11; ++it) {
-            const int u = it * (kPrepThreads - 64) + (tid - 64);
-            if (u < 2048) {
-                const int blk = u >> 9;  // 0, 1: K kblocks -> RHS columns 0-127; 2, 3: V blocks in place
-                const int row = (u >> 3) & 63;
-                const uint32_t in_row = row * 128 + (u & 7) * 16;
-                const uint32_t src = blk < 2 ? aKQ + blk * 16384 + in_row : aRHS + blk * 8192 + in_row;
+            for (int it = 0; it < 11; ++it) {
+                const int u = it * (kPrepThreads - 64) + (tid - 64);
+                if (u < 2048) {
+                    const int blk = u >> 9;  // 0, 1: K kblocks -> RHS columns 0-127; 2, 3: V blocks in place
+                    const int row = (u >> 3) & 63;
+                    const uint32_t in_row = row * 128 + (u & 7) * 16;
+                    const uint32_t src = blk < 2 ? aKQ + blk * 16384 + in_row : aRHS + blk * 8192 + in_row;
+                    uint4 res = make_uint4(0, 0, 0, 0);
+                    if (row < n) {
+                        const float sc = blk < 2 ? sml.sBG[row] : sml.beta[row];
+                        float f[8];
+                        bf16x8_to_f32(S.ld16(src), f);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) f[e] *= sc;
+                        res = f16x8(f);
+                    }
+                    S.st16(aRHS + blk * 8192 + in_row, res);
+                }
+            }
+        }
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        if (tid == 0) {  // 4. T = N21 X11 (lower-left block of NL . diag(X11, X22)) -> columns 0-63, M=64
+            tc_fence_after();
+            mma_ct<kF16, false, true, 64, 64, 64, 64, 64>(tm, aNL, aX, false);
+            mma_commit(barM);
+        }
+        if (warp == 2 || warp == 3) {
+            // The completion of A^-1 runs on sub-partitions 2, 3 (rows 32-63)
+            // while the other warps convert K and Q:
+            //   TB = [0 0; T 0] as the f16 MN-major B image (over the fp32
+            //   diagonal blocks; lanes 16-31 write its zero rows 0-31), then
+            //   X21 = -(X22 T) into A^-1 -- each step handed to the MMA issuer
+            //   through barE.
+            bool okw = mbar_wait(barM, pl ^ 1u);
+            tc_fence_after();
+            float t32[32];
+            tmem_ld32(taddr(tm, 32 * q, 0), t32);
+            tmem_wait_ld();
+            {
+                const int i = lane < 16 ? 16 * q + lane : 16 * (q - 2) + (lane - 16);
+                const bool tri = lane < 16;
+#pragma unroll
+                for (int e0 = 0; e0 < 32; e0 += 8) {
+                    float f[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) f[e] = tri ? t32[e0 + e] : 0.f;
+                    S.st16(aN + h16(i, e0, 64), f16x8(f));
+                    S.st16(aN + h16(i, 32 + e0, 64), make_uint4(0, 0, 0, 0));
+                }
+            }
+            fence_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(barE);
+            okw = mbar_wait(barM, pl) && okw;
+            tc_fence_after();
+            tmem_ld32(taddr(tm, 32 * q, 64), t32);
+            tmem_wait_ld();
+            if (lane < 16) {
+                const int i = 16 * q + lane;
+#pragma unroll
+                for (int e0 = 0; e0 < 32; e0 += 8) {
+                    float f[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) f[e] = -t32[e0 + e];
+                    S.st16(aX + h16(i, e0, 64), f16x8(f));
+                }
+            }
+            fence_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(barE);
+            ok = ok && okw;
+        } else if (warp >= 4) {
+            // 4b. in place over [K;Q] (bf16 -> f16, rows >= n zero): K' = tail (.) K
+            //     in the K rows, plain Q in the Q rows (the A operand of Qt^T)
+#pragma unroll 2
+            for (int it = 0; it < 16; ++it) {
+                const int u = it * 128 + (tid - 128);
+                const int kb = u >> 10, qrow = (u >> 9) & 1, row = (u >> 3) & 63;
+                const uint32_t addr = aKQ + kb * 16384 + qrow * 8192 + row * 128 + (u & 7) * 16;
                 uint4 res = make_uint4(0, 0, 0, 0);
                 if (row < n) {
-                    const float sc = blk < 2 ? sml.sBG[row] : sml.beta[row];
+                    const float sc = qrow ? 1.f : sml.sTail[row];
                     float f[8];
-                    bf16x8_to_f32(S.ld16(src), f);
+                    bf16x8_to_f32(S.ld16(addr), f);
 #pragma unroll
                     for (int e = 0; e < 8; ++e) f[e] *= sc;
                     res = f16x8(f);
                 }
-                S.st16(aRHS + blk * 8192 + in_row, res);
+                S.st16(addr, res);
             }
+            fence_async_smem();
         }
-    }
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {  // 4. T = N21 X11 (lower-left block of NL . diag(X11, X22)) -> columns 0-63, M=64
+        if (tid == 0) {
+            // 5. X22 T -> columns 64-127 (M=64), once TB is written
+            ok = mbar_wait(barE, 0) && ok;
+            tc_fence_after();
+            mma_ct<kF16, false, true, 64, 64, 64, 64, 64>(tm + 64, aX, aN, false);
+            mma_commit(barM);
+            // 6. [W | U]^T = [bGK | bV]^T A^-T, once X21 is written: W^T -> columns 0-63,
+            //    U^T -> 64-127 (M=128)
+            ok = mbar_wait(barE, 1) && ok;
+            tc_fence_after();
+            mma_ct<kF16, true, false, 64, 64, 64, 128, 64>(tm, aRHS, aX, false);
+            mma_ct<kF16, true, false, 64, 64, 64, 128, 64>(tm + 64, aRHS + 16384, aX, false);
+            mma_commit(barW);
+        }
+        ok = mbar_wait(barW, 0) && ok;
         tc_fence_after();
-        mma_ct<kF16, false, true, 64, 64, 64, 64, 64>(tm, aNL, aX, false);
-        mma_commit(barM);
-    }
-    if (warp == 2 || warp == 3) {
-        // The completion of A^-1 runs on sub-partitions 2, 3 (rows 32-63)
-        // while the other warps convert K and Q:
-        //   TB = [0 0; T 0] as the f16 MN-major B image (over the fp32
-        //   diagonal blocks; lanes 16-31 write its zero rows 0-31), then
-        //   X21 = -(X22 T) into A^-1 -- each step handed to the MMA issuer
-        //   through barE.
-        bool okw = mbar_wait(barM, 1);
-        tc_fence_after();
-        float t32[32];
-        tmem_ld32(taddr(tm, 32 * q, 0), t32);
-        tmem_wait_ld();
-        {
-            const int i = lane < 16 ? 16 * q + lane : 16 * (q - 2) + (lane - 16);
-            const bool tri = lane < 16;
+        if (tid < 2 * kC) {  // diag(G) (rows >= n zero) over NL, dead since T = N21 X11
+            const int i = tid >> 1, half = tid & 1;
+            const float Gi = i < n ? fast_exp2(sml.LG[i]) : 0.f;
 #pragma unroll
             for (int e0 = 0; e0 < 32; e0 += 8) {
                 float f[8];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) f[e] = tri ? t32[e0 + e] : 0.f;
-                S.st16(aN + h16(i, e0, 64), f16x8(f));
-                S.st16(aN + h16(i, 32 + e0, 64), make_uint4(0, 0, 0, 0));
+                for (int e = 0; e < 8; ++e) f[e] = (32 * half + e0 + e == i) ? Gi : 0.f;
+                S.st16(aNL + h16(i, 32 * half + e0, 64), f16x8(f));
             }
         }
-        fence_async_smem();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(barE);
-        okw = mbar_wait(barM, 0) && okw;
-        tc_fence_after();
-        tmem_ld32(taddr(tm, 32 * q, 64), t32);
-        tmem_wait_ld();
-        if (lane < 16) {
-            const int i = 16 * q + lane;
-#pragma unroll
-            for (int e0 = 0; e0 < 32; e0 += 8) {
-                float f[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) f[e] = -t32[e0 + e];
-                S.st16(aX + h16(i, e0, 64), f16x8(f));
-            }
-        }
-        fence_async_smem();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(barE);
-        ok = ok && okw;
-    } else if (warp >= 4) {
-        // 4b. in place over [K;Q] (bf16 -> f16, rows >= n zero): K' = tail (.) K
-        //     in the K rows, plain Q in the Q rows (the A operand of Qt^T)
-#pragma unroll 2
-        for (int it = 0; it < 16; ++it) {
-            const int u = it * 128 + (tid - 128);
-            const int kb = u >> 10, qrow = (u >> 9) & 1, row = (u >> 3) & 63;
-            const uint32_t addr = aKQ + kb * 16384 + qrow * 8192 + row * 128 + (u & 7) * 16;
-            uint4 res = make_uint4(0, 0, 0, 0);
-            if (row < n) {
-                const float sc = qrow ? 1.f : sml.sTail[row];
-                float f[8];
-                bf16x8_to_f32(S.ld16(addr), f);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) f[e] *= sc;
-                res = f16x8(f);
-            }
-            S.st16(addr, res);
-        }
-        fence_async_smem();
-    }
-    if (tid == 0) {
-        // 5. X22 T -> columns 64-127 (M=64), once TB is written
-        ok = mbar_wait(barE, 0) && ok;
-        tc_fence_after();
-        mma_ct<kF16, false, true, 64, 64, 64, 64, 64>(tm + 64, aX, aN, false);
-        mma_commit(barM);
-        // 6. [W | U]^T = [bGK | bV]^T A^-T, once X21 is written: W^T -> columns 0-63,
-        //    U^T -> 64-127 (M=128)
-        ok = mbar_wait(barE, 1) && ok;
-        tc_fence_after();
-        mma_ct<kF16, true, false, 64, 64, 64, 128, 64>(tm, aRHS, aX, false);
-        mma_ct<kF16, true, false, 64, 64, 64, 128, 64>(tm + 64, aRHS + 16384, aX, false);
-        mma_commit(barW);
-    }
-    ok = mbar_wait(barW, 0) && ok;
-    tc_fence_after();
-    if (tid < 2 * kC) {  // diag(G) (rows >= n zero) over NL, dead since T = N21 X11
-        const int i = tid >> 1, half = tid & 1;
-        const float Gi = i < n ? fast_exp2(sml.LG[i]) : 0.f;
-#pragma unroll
-        for (int e0 = 0; e0 < 32; e0 += 8) {
-            float f[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) f[e] = (32 * half + e0 + e == i) ? Gi : 0.f;
-            S.st16(aNL + h16(i, 32 * half + e0, 64), f16x8(f));
-        }
-    }
-    {  // row 32 q + lane of W^T (hc = 0) or U^T (hc = 1) -> f16 K-major images [128][64] over the RHS
-        float a0[32], a1[32];
-        tmem_ld32(taddr(tm, 32 * q, 64 * hc), a0);
-        tmem_ld32(taddr(tm, 32 * q, 64 * hc + 32), a1);
-        tmem_wait_ld();
-        const int r = 32 * q + lane;
-        const uint32_t img = aRHS + hc * 16384;
-#pragma unroll
-        for (int e0 = 0; e0 < 32; e0 += 8) {
-            S.st16(img + h16(r, e0, 128), f16x8(a0 + e0));
-            S.st16(img + h16(r, 32 + e0, 128), f16x8(a1 + e0));
-        }
-    }
-    fence_async_smem();
-    tc_fence_before();
-    if (__syncthreads_or(!ok)) goto abort;
-    if (tid == 0) {
-        // 7. Qt^T = Q^T diag(G) + W^T (-P)^T -> columns 0-63; -(Ut^T) = U^T (-P)^T -> 64-127;
-        //    K'^T W -> 128-255 (all M=128)
-        tc_fence_after();
-        mma_ct<kF16, true, false, 64, 128, 64, 128, 64>(tm, aKQ + 8192, aNL, false);
-        mma_ct<kF16, false, false, 64, 128, 64, 128, 64>(tm, aRHS, aPO, true);
-        mma_ct<kF16, false, false, 64, 128, 64, 128, 64>(tm + 64, aRHS + 16384, aPO, false);
-        mma_ct<kF16, true, false, 64, 128, 128, 128, 128>(tm + 128, aKQ, aRHS, false);
-        mma_commit(barW);
-        bulk_s2g(out_rec + kRecUT, aRHS + 16384, 16384);  // U^T
-        bulk_s2g(out_rec + kRecKb, aKQ, 8192);            // K': two 8 KiB kblocks
-        bulk_s2g(out_rec + kRecKb + 8192, aKQ + 16384, 8192);
-        bulk_commit();
-    }
-    ok = mbar_wait(barW, 1) && ok;
-    tc_fence_after();
-    {
-        // 8. row r = 32 q + lane: Qt^T (hc = 0, staging over N) or Ut^T (hc = 1,
-        //    over -P and A^-1) -- regions no bulk store is reading -- then,
-        //    once U^T and K' have left shared memory, half hc of
-        //    M = G_C I - K'^T W (over [K;Q])
-        const int r = 32 * q + lane;
-        {
+        {  // row 32 q + lane of W^T (hc = 0) or U^T (hc = 1) -> f16 K-major images [128][64] over the RHS
             float a0[32], a1[32];
             tmem_ld32(taddr(tm, 32 * q, 64 * hc), a0);
             tmem_ld32(taddr(tm, 32 * q, 64 * hc + 32), a1);
             tmem_wait_ld();
-            const float sg = hc ? -1.f : 1.f;
-            const uint32_t img = hc ? aPO : aN;
+            const int r = 32 * q + lane;
+            const uint32_t img = aRHS + hc * 16384;
 #pragma unroll
             for (int e0 = 0; e0 < 32; e0 += 8) {
-                float f[8], f2[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) f[e] = sg * a0[e0 + e], f2[e] = sg * a1[e0 + e];
-                S.st16(img + h16(r, e0, 128), f16x8(f));
-                S.st16(img + h16(r, 32 + e0, 128), f16x8(f2));
+                S.st16(img + h16(r, e0, 128), f16x8(a0 + e0));
+                S.st16(img + h16(r, 32 + e0, 128), f16x8(a1 + e0));
             }
         }
         fence_async_smem();
+        tc_fence_before();
         if (__syncthreads_or(!ok)) goto abort;
         if (tid == 0) {
-            bulk_s2g(out_rec + kRecQt, aN, 16384);
-            bulk_s2g(out_rec + kRecUt, aPO, 16384);
+            // 7. Qt^T = Q^T diag(G) + W^T (-P)^T -> columns 0-63; -(Ut^T) = U^T (-P)^T -> 64-127;
+            //    K'^T W -> 128-255 (all M=128)
+            tc_fence_after();
+            mma_ct<kF16, true, false, 64, 128, 64, 128, 64>(tm, aKQ + 8192, aNL, false);
+            mma_ct<kF16, false, false, 64, 128, 64, 128, 64>(tm, aRHS, aPO, true);
+            mma_ct<kF16, false, false, 64, 128, 64, 128, 64>(tm + 64, aRHS + 16384, aPO, false);
+            mma_ct<kF16, true, false, 64, 128, 128, 128, 128>(tm + 128, aKQ, aRHS, false);
+            mma_commit(barW);
+            bulk_s2g(out_rec + kRecUT, aRHS + 16384, 16384);  // U^T
+            bulk_s2g(out_rec + kRecKb, aKQ, 8192);            // K': two 8 KiB kblocks
+            bulk_s2g(out_rec + kRecKb + 8192, aKQ + 16384, 8192);
             bulk_commit();
-            bulk_wait_read<1>();  // U^T and K' (the older group) have left shared memory
         }
-        const float Gc = fast_exp2(sml.LG[kC - 1]);
-        float acc[2][32];
+        ok = mbar_wait(barW, 1) && ok;
+        tc_fence_after();
+        {
+            // 8. row r = 32 q + lane: Qt^T (hc = 0, staging over N) or Ut^T (hc = 1,
+            //    over -P and A^-1) -- regions no bulk store is reading -- then,
+            //    once U^T and K' have left shared memory, half hc of
+            //    M = G_C I - K'^T W (over [K;Q])
+            const int r = 32 * q + lane;
+            {
+                float a0[32], a1[32];
+                tmem_ld32(taddr(tm, 32 * q, 64 * hc), a0);
+                tmem_ld32(taddr(tm, 32 * q, 64 * hc + 32), a1);
+                tmem_wait_ld();
+                const float sg = hc ? -1.f : 1.f;
+                const uint32_t img = hc ? aPO : aN;
 #pragma unroll
-        for (int c = 0; c < 2; ++c) tmem_ld32(taddr(tm, 32 * q, 128 + 64 * hc + 32 * c), acc[c]);
-        tmem_wait_ld();
-        __syncthreads();  // [K;Q] is free
+                for (int e0 = 0; e0 < 32; e0 += 8) {
+                    float f[8], f2[8];
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-            const int col0 = 64 * hc + 32 * c;  // M column k'
+                    for (int e = 0; e < 8; ++e) f[e] = sg * a0[e0 + e], f2[e] = sg * a1[e0 + e];
+                    S.st16(img + h16(r, e0, 128), f16x8(f));
+                    S.st16(img + h16(r, 32 + e0, 128), f16x8(f2));
+                }
+            }
+            fence_async_smem();
+            if (__syncthreads_or(!ok)) goto abort;
+            if (tid == 0) {
+                bulk_s2g(out_rec + kRecQt, aN, 16384);
+                bulk_s2g(out_rec + kRecUt, aPO, 16384);
+                bulk_commit();
+                bulk_wait_read<1>();  // U^T and K' (the older group) have left shared memory
+            }
+            const float Gc = fast_exp2(sml.LG[kC - 1]);
+            float acc[2][32];
 #pragma unroll
-            for (int e0 = 0; e0 < 32; e0 += 8) {
-                float f[8];
+            for (int c = 0; c < 2; ++c) tmem_ld32(taddr(tm, 32 * q, 128 + 64 * hc + 32 * c), acc[c]);
+            tmem_wait_ld();
+            __syncthreads();  // [K;Q] is free
 #pragma unroll
-                for (int e = 0; e < 8; ++e) f[e] = (col0 + e0 + e == r ? Gc : 0.f) - acc[c][e0 + e];
-                S.st16(aKQ + h16(r, col0 + e0, 128), f16x8(f));
+            for (int c = 0; c < 2; ++c) {
+                const int col0 = 64 * hc + 32 * c;  // M column k'
+#pragma unroll
+                for (int e0 = 0; e0 < 32; e0 += 8) {
+                    float f[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) f[e] = (col0 + e0 + e == r ? Gc : 0.f) - acc[c][e0 + e];
+                    S.st16(aKQ + h16(r, col0 + e0, 128), f16x8(f));
+                }
             }
         }
-    }
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-        bulk_s2g(out_rec + kRecM, aKQ, 32768);
-        bulk_commit();
-        bulk_wait_read<0>();
-    }
-    goto done;
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        if (tid == 0) {
+            bulk_s2g(out_rec + kRecM, aKQ, 32768);
+            bulk_commit();
+            bulk_wait_read<0>();
+        }
+        goto done;
 abort:
-    if (tid == 0) {
-        record_status(32 /* GDN_ERR_DEVICE_TIMEOUT */);
-        mbar_wait(barL, 0);  // the input loads may still be in flight (bounded)
-        bulk_wait_all();
-    }
+        if (tid == 0) {
+            record_status(32 /* GDN_ERR_DEVICE_TIMEOUT */);
+            mbar_wait(barL, pl);  // the input loads may still be in flight (bounded)
+            bulk_wait_all();
+        }
+        stop = true;
 done:
-    tc_fence_before();
-    __syncthreads();
+        tc_fence_before();
+        __syncthreads();  // shared memory and TMEM are free for the next item
+        tc_fence_after();
+        te = te_next;
+        ga = ga_next;
+        gb = gb_next;
+    }
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tm, kPrTmemCols);
@@ -1337,8 +1366,10 @@ cudaError_t launch_prefill_chunked(const PrefillParams& p, void* workspace, size
     if ((e = set_smem(gdn_chunk_prepare_kernel, kPrSmem)) != cudaSuccess) return e;
     int dev = 0, sms = 148;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if ((e = launch_dependent(gdn_chunk_prepare_kernel, static_cast<unsigned>(L.R * kHV), kPrepThreads, kPrSmem,
-                              stream, p, ws, L, tmK, tmQ, tmV, 2 * sms)) != cudaSuccess)
+    // persistent prepare: two CTAs per SM (or one per item when there are fewer)
+    const int64_t items = L.R * kHV;
+    if ((e = launch_dependent(gdn_chunk_prepare_kernel, static_cast<unsigned>(items < 2 * sms ? items : 2 * sms),
+                              kPrepThreads, kPrSmem, stream, p, ws, L, tmK, tmQ, tmV)) != cudaSuccess)
         return e;
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if ((e = set_smem(gdn_chunk_carry_kernel, kCaSmem)) != cudaSuccess) return e;
