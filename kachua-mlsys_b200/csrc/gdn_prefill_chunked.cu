@@ -445,12 +445,13 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
         uint16_t ga_next = 0, gb_next = 0;
         if (tid == 0) {
             mbar_expect_tx(barL, 6 * 8192);
+            tma_load_3d(aRHS + 16384, &tmV, 0, h, t0, barL);
+            tma_load_3d(aRHS + 24576, &tmV, 64, h, t0, barL);
+            bulk_wait_read<0>();  // the previous item's M has left [K;Q]
             tma_load_3d(aKQ, &tmK, 0, hq, t0, barL);
             tma_load_3d(aKQ + 16384, &tmK, 64, hq, t0, barL);
             tma_load_3d(aKQ + 8192, &tmQ, 0, hq, t0, barL);
             tma_load_3d(aKQ + 24576, &tmQ, 64, hq, t0, barL);
-            tma_load_3d(aRHS + 16384, &tmV, 0, h, t0, barL);
-            tma_load_3d(aRHS + 24576, &tmV, 64, h, t0, barL);
         }
         // zero the A^-1 image (its off-diagonal blocks stay zero until X21 is known)
         S.st16(aX + tid * 32, make_uint4(0, 0, 0, 0));
@@ -794,7 +795,10 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
         if (tid == 0) {
             bulk_s2g(out_rec + kRecM, aKQ, 32768);
             bulk_commit();
-            bulk_wait_read<0>();
+            // Qt and Ut have left N, -P and A^-1 (rewritten from the next item's
+            // start on); M's read of [K;Q] overlaps the next item's start and is
+            // awaited before its K and Q loads
+            bulk_wait_read<1>();
         }
         goto done;
 abort:
@@ -812,6 +816,7 @@ done:
         ga = ga_next;
         gb = gb_next;
     }
+    if (tid == 0) bulk_wait_read<0>();  // the last M has left shared memory
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tm, kPrTmemCols);
