@@ -345,7 +345,7 @@ def bench_decode(pkg, args, device, ws, rank, flush, peaks, peaks_kind):
         res["e2e"] = {"value": round(ws * state_bytes / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
                       "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d,
                       "d2h_bytes_per_step": d2h,
-                      "api": "decode.HostStager -> launch_gdn (pinned host buffers, PCIe copies timed)"}
+                      "api": "decode.HostStager -> gdn_decode_launch_host_staged (pinned host buffers; state sliced, H2D / kernel / D2H overlapped on three streams; PCIe copies timed)"}
     return res
 
 

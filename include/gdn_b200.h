@@ -83,6 +83,20 @@ typedef struct GdnDecodeArgs {
 
 int gdn_decode_launch(const GdnDecodeArgs* args, void* stream);
 
+/* One decode step for a caller that keeps the state in HOST memory (state
+ * offloaded between steps).  `host` holds host pointers to every input and
+ * to output / new_state (pinned memory, or the copies do not overlap); `dev`
+ * holds device buffers of the same batch that receive the inputs (q, k, v,
+ * A_log, a, dt_bias, b), the output, and the state in place (dev->new_state;
+ * dev->state must be NULL or equal to it).  The state is cut into `slices`
+ * (1..64) whose host->device copy, kernel and device->host copy overlap on
+ * three streams this library creates once per device; the call orders
+ * itself after the work already on `stream`, and `stream` waits for all of
+ * it.  Calls on one device are enqueued one at a time (they share those
+ * streams).  No reference counterpart: the reference plugin took device
+ * tensors only (kernel.cu:982-994). */
+int gdn_decode_launch_host_staged(const GdnDecodeArgs* host, const GdnDecodeArgs* dev, int slices, void* stream);
+
 /* --------------------------------------------------------------- prefill -- */
 
 #define GDN_SEQLENS_INT32 0
@@ -177,7 +191,7 @@ const char* gdn_status_string(int status);
  * the reference performs no error checking (kernel.cu:982-1064). */
 int gdn_read_device_status(int* out, int clear, void* stream);
 
-/* ABI version of this header (bumped on any struct or signature change). */
+/* ABI version of this header (bumped on any struct or signature change, or a new entry point). */
 int gdn_abi_version(void);
 
 /* ------------------------------------------------------------ diagnostics -- */

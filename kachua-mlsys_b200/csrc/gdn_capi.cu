@@ -37,7 +37,7 @@ static float resolve_scale(float s) { return s == 0.0f ? 1.0f / sqrtf((float)kD)
 
 using namespace gdn;
 
-extern "C" int gdn_abi_version(void) { return 3; }
+extern "C" int gdn_abi_version(void) { return 4; }
 
 extern "C" const char* gdn_status_string(int status) {
     switch (status) {
@@ -166,3 +166,6 @@ extern "C" int gdn_mma_selftest(int kind, int flags, int M, int N, int K, const 
 
 // Allocation-free prefill entry point (fixed scratch array in this library).
 #include "gdn_prefill_noalloc.cu"
+
+// Decode with the state in host memory, transfers pipelined with the kernel.
+#include "gdn_decode_staged.cu"

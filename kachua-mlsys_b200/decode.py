@@ -124,17 +124,20 @@ def kernel(q, k, v, state, A_log, a, dt_bias, b, scale=None):
 
 
 class HostStager:
-    """``launch_gdn`` over HOST (pinned) tensors, copies pipelined with compute.
+    """``launch_gdn`` for a state kept in HOST memory (offloaded between steps).
 
-    The batch is cut into slices; slice i's host->device copy, slice i-1's
-    kernel and slice i-2's device->host copy run on three streams at once, so
-    a step costs about max(H2D, D2H) of PCIe time rather than their sum.
-    Device buffers are allocated once per (batch, device) and reused.
+    Inputs and outputs are host tensors (pinned, or the copies do not
+    overlap).  Each call is one ``gdn_decode_launch_host_staged``: the state
+    is cut into ``slices`` whose host->device copy, decode kernel and
+    device->host copy overlap on three streams, so a step costs about the
+    bidirectional PCIe time of the state rather than the sum of both
+    directions.  Device buffers for one batch size are allocated here once and
+    reused by every call.
     """
 
     def __init__(self, batch: int, device, slices: int = 8):
         self.batch, self.device = batch, torch.device(device)
-        self.slices = max(1, min(slices, batch))
+        self.slices = max(1, min(slices, 64, max(batch, 1)))
         dev = self.device
         self.q = torch.empty((batch, 1, HQK, D), dtype=torch.bfloat16, device=dev)
         self.k = torch.empty_like(self.q)
@@ -145,7 +148,10 @@ class HostStager:
         self.out = torch.empty((batch, HV, D), dtype=torch.bfloat16, device=dev)
         self.A_log = torch.empty(HV, dtype=torch.float32, device=dev)
         self.dt_bias = torch.empty(HV, dtype=torch.float32, device=dev)
-        self.streams = [torch.cuda.Stream(dev) for _ in range(3)]
+        self.lib = _capi.load()
+        self.dev_args = _capi.GdnDecodeArgs(
+            _ptr(self.q), _ptr(self.k), _ptr(self.v), None, _ptr(self.A_log), _ptr(self.a), _ptr(self.dt_bias),
+            _ptr(self.b), _ptr(self.out), _ptr(self.state), batch, 0.0)
 
     def bytes_per_step(self) -> tuple[int, int]:
         h2d = sum(t.numel() * t.element_size() for t in (self.q, self.k, self.v, self.a, self.b, self.state,
@@ -154,38 +160,17 @@ class HostStager:
         return h2d, d2h
 
     def __call__(self, q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state):
-        """All tensors on the host (pinned for overlap); writes output/new_state."""
-        B = self.batch
-        h2d, comp, d2h = self.streams
-        cur = torch.cuda.current_stream(self.device)
-        for s in self.streams:
-            s.wait_stream(cur)
-        with torch.cuda.stream(h2d):
-            self.A_log.copy_(A_log, non_blocking=True)
-            self.dt_bias.copy_(dt_bias, non_blocking=True)
-        bounds = [B * i // self.slices for i in range(self.slices + 1)]
-        ev_in, ev_done = [], []
-        for i in range(self.slices):
-            lo, hi = bounds[i], bounds[i + 1]
-            with torch.cuda.stream(h2d):
-                for dst, src in ((self.q, q), (self.k, k), (self.v, v), (self.a, a), (self.b, b),
-                                 (self.state, state)):
-                    dst[lo:hi].copy_(src[lo:hi], non_blocking=True)
-                e = torch.cuda.Event()
-                e.record(h2d)
-                ev_in.append(e)
-            with torch.cuda.stream(comp):
-                comp.wait_event(ev_in[i])
-                launch_gdn(self.q[lo:hi], self.k[lo:hi], self.v[lo:hi], self.state[lo:hi], self.A_log,
-                           self.a[lo:hi], self.dt_bias, self.b[lo:hi], scale, self.out[lo:hi],
-                           self.state[lo:hi])
-                e = torch.cuda.Event()
-                e.record(comp)
-                ev_done.append(e)
-            with torch.cuda.stream(d2h):
-                d2h.wait_event(ev_done[i])
-                output.view(B, HV, D)[lo:hi].copy_(self.out[lo:hi], non_blocking=True)
-                new_state[lo:hi].copy_(self.state[lo:hi], non_blocking=True)
-        for s in self.streams:
-            cur.wait_stream(s)
+        """All tensors on the host; writes output / new_state (may be ``state``)."""
+        B = validate(q, k, v, state, A_log, a, dt_bias, b, output, new_state, require_cuda=False)
+        _need(B == self.batch, f"stager built for batch {self.batch}, got {B}")
+        _need(q.device.type == "cpu", "HostStager takes host tensors")
+        host = _capi.GdnDecodeArgs(
+            _ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a), _ptr(dt_bias), _ptr(b),
+            _ptr(output), _ptr(new_state), B, 0.0 if scale is None else float(scale))
+        self.dev_args.batch = B
+        with torch.cuda.device(self.device):
+            stream = torch.cuda.current_stream(self.device).cuda_stream
+            _capi.check(self.lib.gdn_decode_launch_host_staged(ctypes.byref(host), ctypes.byref(self.dev_args),
+                                                               self.slices, ctypes.c_void_p(stream)),
+                        "gdn_decode_launch_host_staged")
         return output, new_state

@@ -52,6 +52,29 @@ def test_decode_host_validation(pkg):
     assert lib.gdn_decode_launch(ctypes.byref(args), None) == 3
 
 
+def test_decode_host_staged_validation(pkg):
+    lib = pkg._capi.load()
+    C = pkg._capi
+    host, dev = C.GdnDecodeArgs(), C.GdnDecodeArgs()
+    assert lib.gdn_decode_launch_host_staged(None, ctypes.byref(dev), 8, None) == 1
+    host.batch, dev.batch = 4, 3  # batch mismatch
+    assert lib.gdn_decode_launch_host_staged(ctypes.byref(host), ctypes.byref(dev), 8, None) == 2
+    dev.batch = 4
+    for slices in (0, 65):
+        assert lib.gdn_decode_launch_host_staged(ctypes.byref(host), ctypes.byref(dev), slices, None) == 2
+    assert lib.gdn_decode_launch_host_staged(ctypes.byref(host), ctypes.byref(dev), 8, None) == 1  # NULLs
+    for f in ("q", "k", "v", "state", "A_log", "a", "dt_bias", "b", "output", "new_state"):
+        setattr(host, f, 0x1000)
+        setattr(dev, f, 0x3000)
+    dev.state = 0x4000  # the device state buffer is dev->new_state, updated in place
+    assert lib.gdn_decode_launch_host_staged(ctypes.byref(host), ctypes.byref(dev), 8, None) == 2
+    dev.state = None
+    dev.new_state = 0x3008  # not 16-byte aligned
+    assert lib.gdn_decode_launch_host_staged(ctypes.byref(host), ctypes.byref(dev), 8, None) == 3
+    host.batch = dev.batch = 0
+    assert lib.gdn_decode_launch_host_staged(ctypes.byref(host), ctypes.byref(dev), 8, None) == 0
+
+
 def test_prefill_host_validation(pkg):
     lib = pkg._capi.load()
     C = pkg._capi

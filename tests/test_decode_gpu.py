@@ -89,3 +89,39 @@ def test_decode_large_values_finite(pkg, orc, cuda_dev):
     assert torch.isfinite(out.float()).all() and torch.isfinite(ns).all()
     torch.testing.assert_close(out.float(), ro, atol=1e-2, rtol=1e-2)
     assert state_rel_err(ns, rs) < 1e-3
+
+
+@pytest.mark.parametrize("batch,slices", [(256, 16), (37, 8), (3, 16)])
+def test_host_stager_matches_device_call(pkg, cuda_dev, batch, slices):
+    """HostStager (pinned host tensors in and out, state sliced over three
+    streams) gives the same bits as one device-side launch_gdn; the same
+    stager called twice (the second time with the result as the new input)
+    stays equal."""
+    inp = pkg.inputs.make_decode_inputs(batch, seed=batch + 5)
+    st = pkg.decode.HostStager(batch, cuda_dev, slices=slices)
+    h = [t.pin_memory() for t in (inp.q, inp.k, inp.v, inp.state, inp.A_log, inp.a, inp.dt_bias, inp.b)]
+    state = h[3]
+    for _ in range(2):
+        out = torch.empty((batch, 8, 128), dtype=torch.bfloat16).pin_memory()
+        ns = torch.empty_like(state).pin_memory()
+        st(h[0], h[1], h[2], state, h[4], h[5], h[6], h[7], inp.scale, out, ns)
+        torch.cuda.synchronize()
+        g = [t.to(cuda_dev) for t in (h[0], h[1], h[2], state, h[4], h[5], h[6], h[7])]
+        ref_out, ref_ns = pkg.decode.launch_gdn(*g[:8], scale=inp.scale)
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref_out.cpu()) and torch.equal(ns, ref_ns.cpu())
+        state = ns
+
+
+def test_host_stager_in_place(pkg, cuda_dev):
+    """The host state may be updated in place (new_state is state)."""
+    batch = 20
+    inp = pkg.inputs.make_decode_inputs(batch, seed=77)
+    st = pkg.decode.HostStager(batch, cuda_dev, slices=6)
+    h = [t.pin_memory() for t in (inp.q, inp.k, inp.v, inp.state, inp.A_log, inp.a, inp.dt_bias, inp.b)]
+    g = [t.to(cuda_dev) for t in h]
+    ref_out, ref_ns = pkg.decode.launch_gdn(*g, scale=inp.scale)
+    out = torch.empty((batch, 8, 128), dtype=torch.bfloat16).pin_memory()
+    st(h[0], h[1], h[2], h[3], h[4], h[5], h[6], h[7], inp.scale, out, h[3])
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref_out.cpu()) and torch.equal(h[3], ref_ns.cpu())
