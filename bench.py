@@ -241,6 +241,22 @@ def bench_prefill(pkg, device, lengths, seed, steps, warmup, ws, flush, with_sta
     return res
 
 
+def bench_decode_small(pkg, device, flush, batches=(1, 8, 16, 32, 64), steps=20):
+    """Per-call device time (median, L2 flushed, us) of one decode step at the
+    small batch sizes the reference's published decode numbers cover (B <= 64),
+    where the step is latency- rather than bandwidth-bound."""
+    res = {}
+    for B in batches:
+        inp = pkg.inputs.make_decode_inputs(B, seed=B).to(device)
+        out = torch.empty((B, 8, 128), dtype=torch.bfloat16, device=device)
+        ns = torch.empty_like(inp.state)
+        launch = pkg.decode.PreparedLaunch(inp.q, inp.k, inp.v, inp.state, inp.A_log, inp.a, inp.dt_bias, inp.b,
+                                           inp.scale, out, ns)
+        times, _ = time_steps(launch, steps, 3, 1, device, flush)
+        res[str(B)] = round(sorted(times)[len(times) // 2] * 1e3, 2)
+    return res
+
+
 def time_gather(pkg, out, ns, ws, device):
     """The final gather of every rank's outputs and states to rank 0 (NCCL
     point-to-point over NVLink), timed on the device, max over ranks."""
@@ -392,6 +408,8 @@ def run_ours(args):
         }
         if "e2e" in d:
             line["e2e"] = d["e2e"]
+        if ws == 1:
+            line["decode_small_batch_us"] = bench_decode_small(pkg, device, flush)
     pf = {}
     psteps = max(3, args.steps // 2)
     if ws == 1:
