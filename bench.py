@@ -257,6 +257,26 @@ def bench_decode_small(pkg, device, flush, batches=(1, 8, 16, 32, 64), steps=20)
     return res
 
 
+def bench_decode_tokens(pkg, device, flush, batch=256, tokens=(2, 4, 8), steps=20):
+    """Multi-token (speculative) decode at config 1's batch: T tokens per
+    sequence in one call; the state is read and written once per call, so the
+    state-stream GB/s stays near the single-token step's."""
+    res = {}
+    for T in tokens:
+        inp = pkg.inputs.make_decode_inputs(batch, seed=T, tokens=T).to(device)
+        out = torch.empty((batch, T, 8, 128), dtype=torch.bfloat16, device=device)
+        ns = torch.empty_like(inp.state)
+
+        def step():
+            pkg.decode.launch_gdn(*inp.args(), output=out, new_state=ns)
+
+        times, _ = time_steps(step, steps, 3, 1, device, flush)
+        ms = sorted(times)[len(times) // 2]
+        res[str(T)] = {"us_per_call": round(ms * 1e3, 2), "us_per_token": round(ms * 1e3 / T, 2),
+                       "state_gbs": round(batch * STATE_BYTES_PER_SEQ * 2 / (ms * 1e-3) / 1e9, 1)}
+    return res
+
+
 def time_gather(pkg, out, ns, ws, device):
     """The final gather of every rank's outputs and states to rank 0 (NCCL
     point-to-point over NVLink), timed on the device, max over ranks."""
@@ -410,6 +430,7 @@ def run_ours(args):
             line["e2e"] = d["e2e"]
         if ws == 1:
             line["decode_small_batch_us"] = bench_decode_small(pkg, device, flush)
+            line["decode_multi_token"] = bench_decode_tokens(pkg, device, flush)
     pf = {}
     psteps = max(3, args.steps // 2)
     if ws == 1:

@@ -83,6 +83,15 @@ typedef struct GdnDecodeArgs {
 
 int gdn_decode_launch(const GdnDecodeArgs* args, void* stream);
 
+/* Decode of `tokens` >= 1 tokens per sequence in one call (speculative or
+ * multi-token decode; the decode definition's seq_len axis,
+ * flashinfer/trace/templates/gdn.py:104-110): q, k bf16 [B, T, 4, 128],
+ * v bf16 [B, T, 8, 128], a, b bf16 [B, T, 8], output bf16 [B, T, 8, 128];
+ * state / new_state as for gdn_decode_launch (may be the same buffer), the
+ * state after all T tokens.  Alignment rules as gdn_decode_launch.  The
+ * state is read and written once per call.  T = 1 is gdn_decode_launch. */
+int gdn_decode_launch_tokens(const GdnDecodeArgs* args, int64_t tokens, void* stream);
+
 /* One decode step for a caller that keeps the state in HOST memory (state
  * offloaded between steps).  `host` holds host pointers to every input and
  * to output / new_state (pinned memory, or the copies do not overlap); `dev`

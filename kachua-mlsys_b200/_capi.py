@@ -30,6 +30,7 @@ EXPORTED_SYMBOLS = (
     "gdn_mma_selftest",
     "gdn_prefill_launch_noalloc",
     "gdn_decode_launch_host_staged",
+    "gdn_decode_launch_tokens",
 )
 ABI_VERSION = 4
 PATH_AUTO, PATH_RECURRENT, PATH_CHUNKED, PATH_SEGMENTED = 0, 1, 2, 3
@@ -104,6 +105,8 @@ def load(build_if_needed: bool = True) -> ctypes.CDLL:
         lib.gdn_decode_launch_host_staged.argtypes = [ctypes.POINTER(GdnDecodeArgs), ctypes.POINTER(GdnDecodeArgs),
                                                       ctypes.c_int, P]
         lib.gdn_decode_launch_host_staged.restype = ctypes.c_int
+        lib.gdn_decode_launch_tokens.argtypes = [ctypes.POINTER(GdnDecodeArgs), ctypes.c_int64, P]
+        lib.gdn_decode_launch_tokens.restype = ctypes.c_int
         lib.gdn_prefill_workspace_size.argtypes = [ctypes.c_int64, ctypes.c_int64]
         lib.gdn_prefill_workspace_size.restype = ctypes.c_size_t
         lib.gdn_prefill_launch.argtypes = [ctypes.POINTER(GdnPrefillArgs), P, ctypes.c_size_t, P]

@@ -83,6 +83,44 @@ extern "C" int gdn_decode_launch(const GdnDecodeArgs* a, void* stream) {
     return launch_decode(p, static_cast<cudaStream_t>(stream)) == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
 }
 
+// T tokens per sequence (speculative or multi-token decode): the recurrence
+// runs token by token on the state rows held in registers, so the state is
+// read and written once per call, as in a single-token step.  This is the
+// token-recurrent prefill kernel with every sequence T tokens long.
+extern "C" int gdn_decode_launch_tokens(const GdnDecodeArgs* a, int64_t tokens, void* stream) {
+    if (a == nullptr) return GDN_ERR_NULL_POINTER;
+    if (tokens < 1 || a->batch < 0) return GDN_ERR_BAD_SIZE;
+    if (tokens == 1) return gdn_decode_launch(a, stream);
+    if (a->batch == 0) return GDN_OK;
+    if (a->batch > (int64_t(1) << 40) / tokens || a->batch * kHV * (kD / 16) > 0x7fffffffLL) return GDN_ERR_BAD_SIZE;
+    if (!a->q || !a->k || !a->v || !a->state || !a->A_log || !a->a || !a->dt_bias || !a->b || !a->output ||
+        !a->new_state)
+        return GDN_ERR_NULL_POINTER;
+    if (!aligned(a->q, 8) || !aligned(a->k, 8) || !aligned(a->state, 16) || !aligned(a->new_state, 16) ||
+        !aligned(a->v, 2) || !aligned(a->a, 2) || !aligned(a->b, 2) || !aligned(a->output, 2) ||
+        !aligned(a->A_log, 4) || !aligned(a->dt_bias, 4))
+        return GDN_ERR_MISALIGNED;
+    if (int rc = check_device()) return rc;
+    PrefillParams p;
+    p.q = static_cast<const uint16_t*>(a->q);
+    p.k = static_cast<const uint16_t*>(a->k);
+    p.v = static_cast<const uint16_t*>(a->v);
+    p.state = a->state;  // may equal new_state: each CTA reads its rows before writing them
+    p.A_log = a->A_log;
+    p.a = static_cast<const uint16_t*>(a->a);
+    p.dt_bias = a->dt_bias;
+    p.b = static_cast<const uint16_t*>(a->b);
+    p.cu_seqlens = nullptr;
+    p.cu_is_int64 = 0;
+    p.total_tokens = a->batch * tokens;
+    p.num_seqs = a->batch;
+    p.scale = resolve_scale(a->scale);
+    p.out = static_cast<uint16_t*>(a->output);
+    p.new_state = a->new_state;
+    p.uniform_len = tokens;
+    return launch_prefill_recurrent(p, static_cast<cudaStream_t>(stream)) == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
+}
+
 extern "C" size_t gdn_prefill_workspace_size(int64_t total_tokens, int64_t num_seqs) {
     if (total_tokens < 0 || num_seqs < 0) return 0;
     return chunked_workspace_bytes(total_tokens, num_seqs);
@@ -126,6 +164,7 @@ extern "C" int gdn_prefill_launch(const GdnPrefillArgs* a, void* workspace, size
     p.scale = resolve_scale(a->scale);
     p.out = static_cast<uint16_t*>(a->output);
     p.new_state = a->new_state;
+    p.uniform_len = 0;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (a->num_seqs == 0)  // every token is uncovered: zero output
         return a->total_tokens > 0 && launch_prefill_zero_uncovered(p, s) != cudaSuccess ? GDN_ERR_CUDA : GDN_OK;

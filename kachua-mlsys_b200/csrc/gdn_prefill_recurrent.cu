@@ -4,13 +4,15 @@
 // oracle (prefill reference_torch_impl.py:66-91), with the state rows held in
 // registers.  Rows of S (the v index) never interact, so a CTA owns
 // (sequence, v-head, 16 state rows) and walks the sequence; the lane layout is
-// the decode kernel's (8 lanes per row, float4 x 4 per lane).  The next
-// token's q/k/v/gate inputs are fetched one step ahead of use.
+// the decode kernel's (8 lanes per row, float4 x 4 per lane).  Token inputs
+// (q, k, the CTA's v rows, the gates) are staged in shared memory 32 tokens
+// at a time.
 //
 // Cost is O(T d^2) on CUDA cores with a T-long dependency chain, so the host
 // dispatcher only sends it short sequences; long ones go to the chunked
-// tensor-core path.  It also gives the GPU tests an fp32 cross-check of the
-// chunked path.
+// tensor-core path.  It is also the multi-token decode (T tokens per sequence,
+// state read and written once) and gives the GPU tests an fp32 cross-check
+// of the chunked path.
 #include "gdn_common.cuh"
 
 namespace gdn {
@@ -31,9 +33,11 @@ struct PrefillParams {
     float scale;
     uint16_t* out;
     float* new_state;
+    int64_t uniform_len;  // > 0: every sequence has this many tokens and cu_seqlens is unused
 };
 
 __device__ __forceinline__ int64_t load_cu(const PrefillParams& p, int64_t i) {
+    if (p.uniform_len > 0) return i * p.uniform_len;
     return p.cu_is_int64 ? reinterpret_cast<const int64_t*>(p.cu_seqlens)[i]
                          : static_cast<int64_t>(reinterpret_cast<const int32_t*>(p.cu_seqlens)[i]);
 }
@@ -54,25 +58,7 @@ __device__ __forceinline__ bool seq_bounds(const PrefillParams& p, int64_t s, in
 
 constexpr int kRecRowsPerCta = 16;  // 4 warps x 4 rows
 constexpr int kRecTiles = kD / kRecRowsPerCta;
-
-struct TokenIn {
-    float4 q[4], k[4];
-    float v, a, b;
-};
-
-__device__ __forceinline__ void load_token(const PrefillParams& p, int64_t t, int hq, int h, int row,
-                                           int sub, TokenIn& x) {
-    const uint16_t* qp = p.q + (t * kHQK + hq) * kD + 4 * sub;
-    const uint16_t* kp = p.k + (t * kHQK + hq) * kD + 4 * sub;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        x.q[j] = bf16x4_to_float4(ld_u2(qp + 32 * j));
-        x.k[j] = bf16x4_to_float4(ld_u2(kp + 32 * j));
-    }
-    x.v = bf16_bits_to_float(p.v[(t * kHV + h) * kD + row]);
-    x.a = bf16_bits_to_float(p.a[t * kHV + h]);
-    x.b = bf16_bits_to_float(p.b[t * kHV + h]);
-}
+constexpr int kRecBlk = 32;  // tokens staged in shared memory at a time
 
 __global__ void __launch_bounds__(128) gdn_prefill_recurrent_kernel(const PrefillParams p) {
     const int warp = threadIdx.x >> 5;
@@ -108,38 +94,75 @@ __global__ void __launch_bounds__(128) gdn_prefill_recurrent_kernel(const Prefil
     const float dt_bias = p.dt_bias[h];
     __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
 
-    TokenIn cur, nxt;
-    load_token(p, t0, hq, h, row, sub, nxt);
-    for (int64_t t = t0; t < t1; ++t) {
-        cur = nxt;
-        if (t + 1 < t1) load_token(p, t + 1, hq, h, row, sub, nxt);
-        float g, beta;
-        gdn_gates(A_log, dt_bias, cur.a, cur.b, g, beta);
-        float ks = 0.f, qs = 0.f, qk = 0.f;
+    // Tokens in blocks of 32: the CTA stages the block's q and k (its qk head),
+    // v (its 16 rows) and gates (one token per lane of warp 0) in shared memory
+    // with loads that are all in flight at once, then walks the block from
+    // there, so a token costs shared-memory latency, not an L2 round trip.
+    __shared__ uint2 s_q[kRecBlk][kD / 4], s_k[kRecBlk][kD / 4];  // 4 bf16 per uint2
+    __shared__ uint16_t s_v[kRecBlk][kRecRowsPerCta];
+    __shared__ float s_g[kRecBlk], s_b[kRecBlk], s_qk[kRecBlk];
+    const int tid = threadIdx.x;
+    const int vrow0 = tile * kRecRowsPerCta;
+    for (int64_t tb = t0; tb < t1; tb += kRecBlk) {
+        const int nb = t1 - tb < kRecBlk ? static_cast<int>(t1 - tb) : kRecBlk;
+        __syncthreads();  // the previous block is consumed
+        // a warp stages one token's q and k per pass (32 x 4 dims) and reduces q.k
+        for (int e = tid; e < nb * (kD / 4); e += 128) {
+            const int i = e / (kD / 4), c = e % (kD / 4);
+            const int64_t base = ((tb + i) * kHQK + hq) * (kD / 4) + c;
+            const uint2 qu = reinterpret_cast<const uint2*>(p.q)[base], ku = reinterpret_cast<const uint2*>(p.k)[base];
+            s_q[i][c] = qu;
+            s_k[i][c] = ku;
+            const float4 qf = bf16x4_to_float4(qu), kf = bf16x4_to_float4(ku);
+            float d = qf.x * kf.x + qf.y * kf.y + qf.z * kf.z + qf.w * kf.w;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            ks += st[j].x * cur.k[j].x + st[j].y * cur.k[j].y + st[j].z * cur.k[j].z +
-                  st[j].w * cur.k[j].w;
-            qs += st[j].x * cur.q[j].x + st[j].y * cur.q[j].y + st[j].z * cur.q[j].z +
-                  st[j].w * cur.q[j].w;
-            qk += cur.q[j].x * cur.k[j].x + cur.q[j].y * cur.k[j].y + cur.q[j].z * cur.k[j].z +
-                  cur.q[j].w * cur.k[j].w;
+            for (int off = 1; off < 32; off <<= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+            if (c == 0) s_qk[i] = d;
         }
+        for (int e = tid; e < nb * kRecRowsPerCta; e += 128) {
+            const int i = e / kRecRowsPerCta, r = e % kRecRowsPerCta;
+            s_v[i][r] = p.v[((tb + i) * kHV + h) * kD + vrow0 + r];
+        }
+        if (tid < nb) {
+            const int64_t t = tb + tid;
+            float g, beta;
+            gdn_gates(A_log, dt_bias, bf16_bits_to_float(p.a[t * kHV + h]), bf16_bits_to_float(p.b[t * kHV + h]), g,
+                      beta);
+            s_g[tid] = g;
+            s_b[tid] = beta;
+        }
+        __syncthreads();
+        for (int i = 0; i < nb; ++i) {
+            const int64_t t = tb + i;
+            float4 q4[4], k4[4];
 #pragma unroll
-        for (int off = 1; off < 8; off <<= 1) {
-            ks += __shfl_xor_sync(0xffffffffu, ks, off);
-            qs += __shfl_xor_sync(0xffffffffu, qs, off);
-            qk += __shfl_xor_sync(0xffffffffu, qk, off);
-        }
-        const float delta = beta * (cur.v - g * ks);
+            for (int j = 0; j < 4; ++j) {
+                q4[j] = bf16x4_to_float4(s_q[i][sub + 8 * j]);
+                k4[j] = bf16x4_to_float4(s_k[i][sub + 8 * j]);
+            }
+            const float v = bf16_bits_to_float(s_v[i][warp * 4 + grp]);
+            const float g = s_g[i], beta = s_b[i], qk = s_qk[i];
+            float ks = 0.f, qs = 0.f;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            st[j].x = fmaf(g, st[j].x, delta * cur.k[j].x);
-            st[j].y = fmaf(g, st[j].y, delta * cur.k[j].y);
-            st[j].z = fmaf(g, st[j].z, delta * cur.k[j].z);
-            st[j].w = fmaf(g, st[j].w, delta * cur.k[j].w);
+            for (int j = 0; j < 4; ++j) {
+                ks += st[j].x * k4[j].x + st[j].y * k4[j].y + st[j].z * k4[j].z + st[j].w * k4[j].w;
+                qs += st[j].x * q4[j].x + st[j].y * q4[j].y + st[j].z * q4[j].z + st[j].w * q4[j].w;
+            }
+#pragma unroll
+            for (int off = 1; off < 8; off <<= 1) {
+                ks += __shfl_xor_sync(0xffffffffu, ks, off);
+                qs += __shfl_xor_sync(0xffffffffu, qs, off);
+            }
+            const float delta = beta * (v - g * ks);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                st[j].x = fmaf(g, st[j].x, delta * k4[j].x);
+                st[j].y = fmaf(g, st[j].y, delta * k4[j].y);
+                st[j].z = fmaf(g, st[j].z, delta * k4[j].z);
+                st[j].w = fmaf(g, st[j].w, delta * k4[j].w);
+            }
+            if (sub == 0) out[(t * kHV + h) * kD + row] = __float2bfloat16_rn(p.scale * fmaf(g, qs, delta * qk));
         }
-        if (sub == 0) out[(t * kHV + h) * kD + row] = __float2bfloat16_rn(p.scale * fmaf(g, qs, delta * qk));
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j) st_stream_f4(dst + 32 * j, st[j]);

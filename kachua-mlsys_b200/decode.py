@@ -41,22 +41,24 @@ def _check(t: torch.Tensor, name: str, dtype: torch.dtype, numel: int, device) -
 def validate(q, k, v, state, A_log, a, dt_bias, b, output, new_state, require_cuda: bool = True) -> int:
     """Checks every argument; returns the batch size B.
 
+    q is ``[B, T, 4, 128]`` with T tokens per sequence (T = 1 for a plain
+    decode step); k, v, a, b and output carry the same T.
     ``require_cuda=False`` checks only shapes/dtypes/layout (host-side tests).
     """
-    _need(isinstance(q, torch.Tensor) and q.dim() == 4, "q must be a [B, 1, 4, 128] tensor")
-    B = q.shape[0]
-    _need(tuple(q.shape) == (B, 1, HQK, D), f"q must be [B, 1, 4, 128], got {tuple(q.shape)}")
+    _need(isinstance(q, torch.Tensor) and q.dim() == 4, "q must be a [B, T, 4, 128] tensor")
+    B, T = q.shape[0], q.shape[1]
+    _need(T >= 1 and tuple(q.shape) == (B, T, HQK, D), f"q must be [B, T, 4, 128], got {tuple(q.shape)}")
     dev = q.device
     _need(dev.type == "cuda" or not require_cuda, "q must be a CUDA tensor (there is no CPU path)")
-    _check(q, "q", torch.bfloat16, B * HQK * D, dev)
-    _check(k, "k", torch.bfloat16, B * HQK * D, dev)
-    _check(v, "v", torch.bfloat16, B * HV * D, dev)
+    _check(q, "q", torch.bfloat16, B * T * HQK * D, dev)
+    _check(k, "k", torch.bfloat16, B * T * HQK * D, dev)
+    _check(v, "v", torch.bfloat16, B * T * HV * D, dev)
     _check(state, "state", torch.float32, B * HV * D * D, dev)
     _check(A_log, "A_log", torch.float32, HV, dev)
-    _check(a, "a", torch.bfloat16, B * HV, dev)
+    _check(a, "a", torch.bfloat16, B * T * HV, dev)
     _check(dt_bias, "dt_bias", torch.float32, HV, dev)
-    _check(b, "b", torch.bfloat16, B * HV, dev)
-    _check(output, "output", torch.bfloat16, B * HV * D, dev)
+    _check(b, "b", torch.bfloat16, B * T * HV, dev)
+    _check(output, "output", torch.bfloat16, B * T * HV * D, dev)
     _check(new_state, "new_state", torch.float32, B * HV * D * D, dev)
     _need(tuple(state.shape) == (B, HV, D, D), f"state must be [B, 8, 128, 128], got {tuple(state.shape)}")
     _need(tuple(new_state.shape) == (B, HV, D, D), "new_state must be [B, 8, 128, 128]")
@@ -71,11 +73,16 @@ def launch_gdn(q, k, v, state, A_log, a, dt_bias, b, scale=None, output=None, ne
     """One GDN decode step (destination-passing); returns ``(output, new_state)``.
 
     ``output`` is bf16 ``[B, 8, 128]`` (``[B, 1, 8, 128]`` is accepted too);
-    ``new_state`` is the fp32 k-last state after the step.
+    ``new_state`` is the fp32 k-last state after the step.  With T > 1 tokens
+    per sequence (q ``[B, T, 4, 128]``: speculative or multi-token decode)
+    the tokens are applied in order in one call, ``output`` is
+    ``[B, T, 8, 128]`` and ``new_state`` the state after the last token.
     """
-    _need(isinstance(q, torch.Tensor), "q must be a torch.Tensor")
+    _need(isinstance(q, torch.Tensor) and q.dim() == 4, "q must be a [B, T, 4, 128] tensor")
+    T = q.shape[1]
     if output is None:
-        output = torch.empty((q.shape[0], HV, D), dtype=torch.bfloat16, device=q.device)
+        shape = (q.shape[0], HV, D) if T == 1 else (q.shape[0], T, HV, D)
+        output = torch.empty(shape, dtype=torch.bfloat16, device=q.device)
     if new_state is None:
         new_state = torch.empty_like(state)
     B = validate(q, k, v, state, A_log, a, dt_bias, b, output, new_state)
@@ -85,8 +92,12 @@ def launch_gdn(q, k, v, state, A_log, a, dt_bias, b, scale=None, output=None, ne
         _ptr(output), _ptr(new_state), B, 0.0 if scale is None else float(scale))
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream
-        _capi.check(lib.gdn_decode_launch(ctypes.byref(args), ctypes.c_void_p(stream)),
-                    "gdn_decode_launch")
+        if T == 1:
+            _capi.check(lib.gdn_decode_launch(ctypes.byref(args), ctypes.c_void_p(stream)),
+                        "gdn_decode_launch")
+        else:
+            _capi.check(lib.gdn_decode_launch_tokens(ctypes.byref(args), T, ctypes.c_void_p(stream)),
+                        "gdn_decode_launch_tokens")
     return output, new_state
 
 
@@ -100,6 +111,7 @@ class PreparedLaunch:
 
     def __init__(self, q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state):
         B = validate(q, k, v, state, A_log, a, dt_bias, b, output, new_state)
+        _need(q.shape[1] == 1, "PreparedLaunch is for one token per sequence")
         self._keep = (q, k, v, state, A_log, a, dt_bias, b, output, new_state)
         self.device = q.device
         self.lib = _capi.load()
@@ -163,6 +175,7 @@ class HostStager:
         """All tensors on the host; writes output / new_state (may be ``state``)."""
         B = validate(q, k, v, state, A_log, a, dt_bias, b, output, new_state, require_cuda=False)
         _need(B == self.batch, f"stager built for batch {self.batch}, got {B}")
+        _need(q.shape[1] == 1, "HostStager is for one token per sequence")
         _need(q.device.type == "cpu", "HostStager takes host tensors")
         host = _capi.GdnDecodeArgs(
             _ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a), _ptr(dt_bias), _ptr(b),

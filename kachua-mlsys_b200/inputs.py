@@ -89,14 +89,15 @@ class PrefillInputs:
         return self.q.shape[0]
 
 
-def make_decode_inputs(batch: int, seed: int = 0) -> DecodeInputs:
-    """Decode config 0/1/4a inputs: ``batch`` sequences, one token each."""
+def make_decode_inputs(batch: int, seed: int = 0, tokens: int = 1) -> DecodeInputs:
+    """Decode config 0/1/4a inputs: ``batch`` sequences, ``tokens`` tokens each
+    (1 for a plain decode step; more for speculative / multi-token decode)."""
     gen = torch.Generator().manual_seed(seed)
-    q = _qk(gen, (batch, 1, NUM_QK_HEADS, HEAD_DIM))
-    k = _qk(gen, (batch, 1, NUM_QK_HEADS, HEAD_DIM))
-    v = torch.randn((batch, 1, NUM_V_HEADS, HEAD_DIM), generator=gen).to(torch.bfloat16)
-    a = torch.randn((batch, 1, NUM_V_HEADS), generator=gen).to(torch.bfloat16)
-    b = torch.randn((batch, 1, NUM_V_HEADS), generator=gen).to(torch.bfloat16)
+    q = _qk(gen, (batch, tokens, NUM_QK_HEADS, HEAD_DIM))
+    k = _qk(gen, (batch, tokens, NUM_QK_HEADS, HEAD_DIM))
+    v = torch.randn((batch, tokens, NUM_V_HEADS, HEAD_DIM), generator=gen).to(torch.bfloat16)
+    a = torch.randn((batch, tokens, NUM_V_HEADS), generator=gen).to(torch.bfloat16)
+    b = torch.randn((batch, tokens, NUM_V_HEADS), generator=gen).to(torch.bfloat16)
     A_log, dt_bias = _gate_params(gen)
     state = torch.randn((batch, NUM_V_HEADS, HEAD_DIM, HEAD_DIM), generator=gen) * 0.02
     return DecodeInputs(q, k, v, state, A_log, a, dt_bias, b)

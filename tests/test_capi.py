@@ -52,6 +52,22 @@ def test_decode_host_validation(pkg):
     assert lib.gdn_decode_launch(ctypes.byref(args), None) == 3
 
 
+def test_decode_tokens_validation(pkg):
+    lib = pkg._capi.load()
+    C = pkg._capi
+    args = C.GdnDecodeArgs()
+    assert lib.gdn_decode_launch_tokens(None, 2, None) == 1
+    args.batch = 4
+    assert lib.gdn_decode_launch_tokens(ctypes.byref(args), 0, None) == 2
+    assert lib.gdn_decode_launch_tokens(ctypes.byref(args), 3, None) == 1  # NULL pointers
+    for f in ("q", "k", "v", "state", "A_log", "a", "dt_bias", "b", "output", "new_state"):
+        setattr(args, f, 0x1000)
+    args.q = 0x1002  # q, k need 8-byte alignment
+    assert lib.gdn_decode_launch_tokens(ctypes.byref(args), 3, None) == 3
+    args.batch = 0
+    assert lib.gdn_decode_launch_tokens(ctypes.byref(args), 3, None) == 0
+
+
 def test_decode_host_staged_validation(pkg):
     lib = pkg._capi.load()
     C = pkg._capi

@@ -91,6 +91,43 @@ def test_decode_large_values_finite(pkg, orc, cuda_dev):
     assert state_rel_err(ns, rs) < 1e-3
 
 
+@pytest.mark.parametrize("batch,tokens", [(3, 2), (5, 4), (16, 8), (1, 17), (64, 3)])
+def test_decode_multi_token_matches_oracle(pkg, orc, cuda_dev, batch, tokens):
+    """T tokens per sequence in one call equal the oracle's token recurrence
+    over T-token sequences (the prefill oracle with uniform lengths)."""
+    inp = pkg.inputs.make_decode_inputs(batch, seed=batch * 31 + tokens, tokens=tokens)
+    cu = torch.arange(0, (batch + 1) * tokens, tokens, dtype=torch.int64)
+    flat = lambda t: t.reshape(batch * tokens, *t.shape[2:])  # noqa: E731
+    ro, rs = orc.prefill(flat(inp.q), flat(inp.k), flat(inp.v), inp.state, inp.A_log, flat(inp.a),
+                         inp.dt_bias, flat(inp.b), cu, inp.scale)
+    g = inp.to(cuda_dev)
+    out, ns = pkg.decode.launch_gdn(*g.args())
+    torch.cuda.synchronize()
+    assert tuple(out.shape) == (batch, tokens, 8, 128)
+    torch.testing.assert_close(out.cpu().float().reshape(batch * tokens, 8, 128), ro.float(), atol=1e-2, rtol=1e-2)
+    assert state_rel_err(ns.cpu(), rs) < 1e-3
+
+
+def test_decode_multi_token_matches_steps_and_in_place(pkg, cuda_dev):
+    """One T-token call agrees with T single-token calls, also with the state
+    updated in place."""
+    batch, tokens = 9, 5
+    g = pkg.inputs.make_decode_inputs(batch, seed=3, tokens=tokens).to(cuda_dev)
+    out, ns = pkg.decode.launch_gdn(*g.args())
+    s = g.state.clone()
+    for t in range(tokens):
+        sl = lambda x: x[:, t:t + 1].contiguous()  # noqa: E731
+        o_t, s = pkg.decode.launch_gdn(sl(g.q), sl(g.k), sl(g.v), s, g.A_log, sl(g.a), g.dt_bias, sl(g.b),
+                                       g.scale)
+        torch.testing.assert_close(out[:, t].float(), o_t.float(), atol=1e-2, rtol=1e-2)
+    assert state_rel_err(ns.cpu(), s.cpu()) < 1e-5
+    inplace = g.state.clone()
+    out2, ns2 = pkg.decode.launch_gdn(g.q, g.k, g.v, inplace, g.A_log, g.a, g.dt_bias, g.b, g.scale,
+                                      new_state=inplace)
+    torch.cuda.synchronize()
+    assert torch.equal(out2, out) and torch.equal(inplace, ns)
+
+
 @pytest.mark.parametrize("batch,slices", [(256, 16), (37, 8), (3, 16)])
 def test_host_stager_matches_device_call(pkg, cuda_dev, batch, slices):
     """HostStager (pinned host tensors in and out, state sliced over three

@@ -36,6 +36,22 @@ def test_decode_validate_shapes_and_dtypes(pkg):
         pkg.decode.validate(*bad, require_cuda=False)
 
 
+def test_decode_validate_multi_token(pkg):
+    d = pkg.inputs.make_decode_inputs(2, seed=0, tokens=3)
+    out = torch.empty(2, 3, 8, 128, dtype=torch.bfloat16)
+    ns = torch.empty_like(d.state)
+    args = [d.q, d.k, d.v, d.state, d.A_log, d.a, d.dt_bias, d.b, out, ns]
+    assert pkg.decode.validate(*args, require_cuda=False) == 2
+    bad = list(args)
+    bad[8] = torch.empty(2, 8, 128, dtype=torch.bfloat16)  # one token's output for three tokens
+    with pytest.raises(ValueError, match="output"):
+        pkg.decode.validate(*bad, require_cuda=False)
+    bad = list(args)
+    bad[2] = d.v[:, :2].contiguous()
+    with pytest.raises(ValueError, match="v has"):
+        pkg.decode.validate(*bad, require_cuda=False)
+
+
 def test_prefill_validate_seqlens(pkg):
     p = pkg.inputs.make_prefill_inputs([3, 4], seed=0)
     out = torch.empty(7, 8, 128, dtype=torch.bfloat16)
