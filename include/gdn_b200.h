@@ -112,7 +112,7 @@ int gdn_decode_launch_host_staged(const GdnDecodeArgs* host, const GdnDecodeArgs
 #define GDN_SEQLENS_INT64 1
 
 /* Prefill algorithm selector (GdnPrefillArgs.path).  AUTO sends batches of
- * short sequences (mean length <= 48) to the token-recurrent kernel and the
+ * short sequences (mean length <= 24) to the token-recurrent kernel and the
  * rest to the chunked tensor-core kernels.  No reference counterpart: the
  * reference's host dispatch chose among its Triton paths internally
  * (triton/kernel.py:93-129). */
