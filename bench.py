@@ -277,6 +277,24 @@ def bench_decode_tokens(pkg, device, flush, batch=256, tokens=(2, 4, 8), steps=2
     return res
 
 
+def bench_decode_bf16(pkg, device, flush, batch=256, steps=20):
+    """Config 1's step with the state stored in bf16 (half the state stream)."""
+    inp = pkg.inputs.make_decode_inputs(batch, seed=7).to(device)
+    s16 = inp.state.to(torch.bfloat16)
+    out = torch.empty((batch, 8, 128), dtype=torch.bfloat16, device=device)
+    ns = torch.empty_like(s16)
+
+    def step():
+        pkg.decode.launch_gdn(inp.q, inp.k, inp.v, s16, inp.A_log, inp.a, inp.dt_bias, inp.b, inp.scale,
+                              output=out, new_state=ns)
+
+    times, _ = time_steps(step, steps, 3, 1, device, flush)
+    ms = sorted(times)[len(times) // 2]
+    return {"batch": batch, "us_per_step": round(ms * 1e3, 2),
+            "state_gbs": round(batch * STATE_BYTES_PER_SEQ / (ms * 1e-3) / 1e9, 1),
+            "note": "state bytes = 2 x B x 256 KiB (bf16), read and written once; device time, L2 flushed"}
+
+
 def time_gather(pkg, out, ns, ws, device):
     """The final gather of every rank's outputs and states to rank 0 (NCCL
     point-to-point over NVLink), timed on the device, max over ranks."""
@@ -431,6 +449,7 @@ def run_ours(args):
         if ws == 1:
             line["decode_small_batch_us"] = bench_decode_small(pkg, device, flush)
             line["decode_multi_token"] = bench_decode_tokens(pkg, device, flush)
+            line["decode_bf16_state"] = bench_decode_bf16(pkg, device, flush)
     pf = {}
     psteps = max(3, args.steps // 2)
     if ws == 1:

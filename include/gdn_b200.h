@@ -92,6 +92,15 @@ int gdn_decode_launch(const GdnDecodeArgs* args, void* stream);
  * state is read and written once per call.  T = 1 is gdn_decode_launch. */
 int gdn_decode_launch_tokens(const GdnDecodeArgs* args, int64_t tokens, void* stream);
 
+/* gdn_decode_launch with the state stored in bf16: args->state and
+ * args->new_state point to bf16 [B, 8, 128, 128] arrays (8-byte aligned; they
+ * may be the same array).  The update is computed in fp32 and the new state
+ * rounded to bf16 once per step, so the state stream (the whole cost of a
+ * large-batch step) is half that of the fp32 state.  The reference keeps
+ * the state in fp32 (kernel.cu:982-994); this variant trades its precision
+ * (about 3 significant digits per element) for bandwidth. */
+int gdn_decode_launch_bf16_state(const GdnDecodeArgs* args, void* stream);
+
 /* One decode step for a caller that keeps the state in HOST memory (state
  * offloaded between steps).  `host` holds host pointers to every input and
  * to output / new_state (pinned memory, or the copies do not overlap); `dev`

@@ -31,8 +31,9 @@ EXPORTED_SYMBOLS = (
     "gdn_prefill_launch_noalloc",
     "gdn_decode_launch_host_staged",
     "gdn_decode_launch_tokens",
+    "gdn_decode_launch_bf16_state",
 )
-ABI_VERSION = 4
+ABI_VERSION = 5
 PATH_AUTO, PATH_RECURRENT, PATH_CHUNKED, PATH_SEGMENTED = 0, 1, 2, 3
 MMA_KIND_BF16, MMA_KIND_TF32, MMA_KIND_F16 = 1, 2, 3
 MMA_A_MN, MMA_B_MN, MMA_D_LANE16, MMA_A_TMEM = 1, 2, 4, 8
@@ -107,6 +108,8 @@ def load(build_if_needed: bool = True) -> ctypes.CDLL:
         lib.gdn_decode_launch_host_staged.restype = ctypes.c_int
         lib.gdn_decode_launch_tokens.argtypes = [ctypes.POINTER(GdnDecodeArgs), ctypes.c_int64, P]
         lib.gdn_decode_launch_tokens.restype = ctypes.c_int
+        lib.gdn_decode_launch_bf16_state.argtypes = [ctypes.POINTER(GdnDecodeArgs), P]
+        lib.gdn_decode_launch_bf16_state.restype = ctypes.c_int
         lib.gdn_prefill_workspace_size.argtypes = [ctypes.c_int64, ctypes.c_int64]
         lib.gdn_prefill_workspace_size.restype = ctypes.c_size_t
         lib.gdn_prefill_launch.argtypes = [ctypes.POINTER(GdnPrefillArgs), P, ctypes.c_size_t, P]

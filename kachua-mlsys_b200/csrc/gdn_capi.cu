@@ -37,7 +37,7 @@ static float resolve_scale(float s) { return s == 0.0f ? 1.0f / sqrtf((float)kD)
 
 using namespace gdn;
 
-extern "C" int gdn_abi_version(void) { return 4; }
+extern "C" int gdn_abi_version(void) { return 5; }
 
 extern "C" const char* gdn_status_string(int status) {
     switch (status) {
@@ -55,14 +55,15 @@ extern "C" const char* gdn_status_string(int status) {
     }
 }
 
-extern "C" int gdn_decode_launch(const GdnDecodeArgs* a, void* stream) {
+static int decode_launch(const GdnDecodeArgs* a, void* stream, bool bf16_state) {
     if (a == nullptr) return GDN_ERR_NULL_POINTER;
     if (a->batch < 0) return GDN_ERR_BAD_SIZE;
     if (a->batch == 0) return GDN_OK;
     if (!a->q || !a->k || !a->v || !a->state || !a->A_log || !a->a || !a->dt_bias || !a->b ||
         !a->output || !a->new_state)
         return GDN_ERR_NULL_POINTER;
-    if (!aligned(a->q, 8) || !aligned(a->k, 8) || !aligned(a->state, 16) || !aligned(a->new_state, 16) ||
+    const uintptr_t sa = bf16_state ? 8 : 16;  // state rows are read 4 elements at a time
+    if (!aligned(a->q, 8) || !aligned(a->k, 8) || !aligned(a->state, sa) || !aligned(a->new_state, sa) ||
         !aligned(a->v, 2) || !aligned(a->a, 2) || !aligned(a->b, 2) || !aligned(a->output, 2) ||
         !aligned(a->A_log, 4) || !aligned(a->dt_bias, 4))
         return GDN_ERR_MISALIGNED;
@@ -80,7 +81,15 @@ extern "C" int gdn_decode_launch(const GdnDecodeArgs* a, void* stream) {
     p.new_state = a->new_state;
     p.batch = a->batch;
     p.scale = resolve_scale(a->scale);
-    return launch_decode(p, static_cast<cudaStream_t>(stream)) == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
+    return launch_decode(p, static_cast<cudaStream_t>(stream), bf16_state) == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
+}
+
+extern "C" int gdn_decode_launch(const GdnDecodeArgs* a, void* stream) { return decode_launch(a, stream, false); }
+
+// The state kept in bf16 (half the HBM stream of the fp32 state); args->state
+// and args->new_state point to bf16 arrays.
+extern "C" int gdn_decode_launch_bf16_state(const GdnDecodeArgs* a, void* stream) {
+    return decode_launch(a, stream, true);
 }
 
 // T tokens per sequence (speculative or multi-token decode): the recurrence

@@ -71,4 +71,19 @@ __device__ __forceinline__ uint2 ld_u2(const void* p) {
     return *reinterpret_cast<const uint2*>(p);
 }
 
+// 8-byte forms of the streaming state accesses (4 bf16 values)
+__device__ __forceinline__ uint2 ld_stream_u2(const void* p) {
+    uint2 r;
+    asm volatile("ld.global.L1::no_allocate.L2::256B.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+    return r;
+}
+__device__ __forceinline__ void st_stream_u2(void* p, uint2 v) {
+    asm volatile("st.global.cs.v2.u32 [%0], {%1,%2};" ::"l"(p), "r"(v.x), "r"(v.y) : "memory");
+}
+// 4 floats -> 4 packed bf16, round to nearest even
+__device__ __forceinline__ uint2 float4_to_bf16x4(float4 f) {
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(f.x, f.y), hi = __floats2bfloat162_rn(f.z, f.w);
+    return make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+}
+
 }  // namespace gdn

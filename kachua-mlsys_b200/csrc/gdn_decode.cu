@@ -41,7 +41,9 @@ struct DecodeParams {
     float scale;
 };
 
-template <int RPW>
+// BF16S: the state (in and out) is stored as bf16 instead of fp32; the
+// arithmetic is the same fp32, the new state rounded to bf16 once.
+template <int RPW, bool BF16S>
 __global__ void __launch_bounds__(128) gdn_decode_kernel(const DecodeParams p) {
     static_assert(RPW % 4 == 0, "rows per warp must be a multiple of 4");
     constexpr int kPasses = RPW / 4;
@@ -63,14 +65,17 @@ __global__ void __launch_bounds__(128) gdn_decode_kernel(const DecodeParams p) {
 
     const float* src = p.state + bh * (kD * kD) + 4 * sub;
     float* dst = p.new_state + bh * (kD * kD) + 4 * sub;
+    const uint16_t* src16 = reinterpret_cast<const uint16_t*>(p.state) + bh * (kD * kD) + 4 * sub;
+    uint16_t* dst16 = reinterpret_cast<uint16_t*>(p.new_state) + bh * (kD * kD) + 4 * sub;
 
-    // 1. issue every state load first (kPasses x 4 x 16 B per thread)
+    // 1. issue every state load first (kPasses x 4 x 16 B per thread; 8 B with a bf16 state)
     float4 s[kPasses][4];
 #pragma unroll
     for (int ps = 0; ps < kPasses; ++ps) {
-        const float* r = src + (row0 + 4 * ps) * kD;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) s[ps][j] = ld_stream_f4(r + 32 * j);
+        for (int j = 0; j < 4; ++j)
+            s[ps][j] = BF16S ? bf16x4_to_float4(ld_stream_u2(src16 + (row0 + 4 * ps) * kD + 32 * j))
+                             : ld_stream_f4(src + (row0 + 4 * ps) * kD + 32 * j);
     }
 
     // 2. per-head vectors and gates (small, L2/L1 resident)
@@ -115,7 +120,6 @@ __global__ void __launch_bounds__(128) gdn_decode_kernel(const DecodeParams p) {
             qs += __shfl_xor_sync(0xffffffffu, qs, off);
         }
         const float delta = beta * (vrow[ps] - g * ks);
-        float* r = dst + (row0 + 4 * ps) * kD;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             float4 o;
@@ -123,7 +127,10 @@ __global__ void __launch_bounds__(128) gdn_decode_kernel(const DecodeParams p) {
             o.y = fmaf(g, s[ps][j].y, delta * k4[j].y);
             o.z = fmaf(g, s[ps][j].z, delta * k4[j].z);
             o.w = fmaf(g, s[ps][j].w, delta * k4[j].w);
-            st_stream_f4(r + 32 * j, o);
+            if (BF16S)
+                st_stream_u2(dst16 + (row0 + 4 * ps) * kD + 32 * j, float4_to_bf16x4(o));
+            else
+                st_stream_f4(dst + (row0 + 4 * ps) * kD + 32 * j, o);
         }
         if (sub == 0) {
             const float o = p.scale * fmaf(g, qs, delta * qk);
@@ -140,17 +147,26 @@ static int pick_rows_per_warp(int64_t batch) {
     return 4;
 }
 
-cudaError_t launch_decode(const DecodeParams& p, cudaStream_t stream) {
+template <bool BF16S>
+static void launch_decode_rpw(int rpw, unsigned grid, const DecodeParams& p, cudaStream_t stream) {
+    switch (rpw) {
+        case 16: gdn_decode_kernel<16, BF16S><<<grid, 128, 0, stream>>>(p); break;
+        case 8: gdn_decode_kernel<8, BF16S><<<grid, 128, 0, stream>>>(p); break;
+        default: gdn_decode_kernel<4, BF16S><<<grid, 128, 0, stream>>>(p); break;
+    }
+}
+
+// bf16_state: p.state / p.new_state point to bf16 [B, 8, 128, 128] arrays.
+cudaError_t launch_decode(const DecodeParams& p, cudaStream_t stream, bool bf16_state = false) {
     if (p.batch == 0) return cudaSuccess;
     const int rpw = pick_rows_per_warp(p.batch);
     const int64_t heads = p.batch * kHV;
     const int64_t grid = heads * (kD / (4 * rpw));
     if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
-    switch (rpw) {
-        case 16: gdn_decode_kernel<16><<<(unsigned)grid, 128, 0, stream>>>(p); break;
-        case 8: gdn_decode_kernel<8><<<(unsigned)grid, 128, 0, stream>>>(p); break;
-        default: gdn_decode_kernel<4><<<(unsigned)grid, 128, 0, stream>>>(p); break;
-    }
+    if (bf16_state)
+        launch_decode_rpw<true>(rpw, static_cast<unsigned>(grid), p, stream);
+    else
+        launch_decode_rpw<false>(rpw, static_cast<unsigned>(grid), p, stream);
     return cudaGetLastError();
 }
 

@@ -53,13 +53,16 @@ def validate(q, k, v, state, A_log, a, dt_bias, b, output, new_state, require_cu
     _check(q, "q", torch.bfloat16, B * T * HQK * D, dev)
     _check(k, "k", torch.bfloat16, B * T * HQK * D, dev)
     _check(v, "v", torch.bfloat16, B * T * HV * D, dev)
-    _check(state, "state", torch.float32, B * HV * D * D, dev)
+    sdt = state.dtype if isinstance(state, torch.Tensor) else None
+    _need(sdt in (torch.float32, torch.bfloat16), "state must be float32 (or bfloat16: the bf16-state variant)")
+    _need(sdt == torch.float32 or T == 1, "a bf16 state takes one token per step")
+    _check(state, "state", sdt, B * HV * D * D, dev)
     _check(A_log, "A_log", torch.float32, HV, dev)
     _check(a, "a", torch.bfloat16, B * T * HV, dev)
     _check(dt_bias, "dt_bias", torch.float32, HV, dev)
     _check(b, "b", torch.bfloat16, B * T * HV, dev)
     _check(output, "output", torch.bfloat16, B * T * HV * D, dev)
-    _check(new_state, "new_state", torch.float32, B * HV * D * D, dev)
+    _check(new_state, "new_state", sdt, B * HV * D * D, dev)
     _need(tuple(state.shape) == (B, HV, D, D), f"state must be [B, 8, 128, 128], got {tuple(state.shape)}")
     _need(tuple(new_state.shape) == (B, HV, D, D), "new_state must be [B, 8, 128, 128]")
     return B
@@ -73,7 +76,9 @@ def launch_gdn(q, k, v, state, A_log, a, dt_bias, b, scale=None, output=None, ne
     """One GDN decode step (destination-passing); returns ``(output, new_state)``.
 
     ``output`` is bf16 ``[B, 8, 128]`` (``[B, 1, 8, 128]`` is accepted too);
-    ``new_state`` is the fp32 k-last state after the step.  With T > 1 tokens
+    ``new_state`` is the fp32 k-last state after the step.  A bf16 ``state``
+    (and ``new_state``) selects the bf16-state variant: the same step with
+    the state stored in bf16, half the bytes to stream.  With T > 1 tokens
     per sequence (q ``[B, T, 4, 128]``: speculative or multi-token decode)
     the tokens are applied in order in one call, ``output`` is
     ``[B, T, 8, 128]`` and ``new_state`` the state after the last token.
@@ -92,7 +97,10 @@ def launch_gdn(q, k, v, state, A_log, a, dt_bias, b, scale=None, output=None, ne
         _ptr(output), _ptr(new_state), B, 0.0 if scale is None else float(scale))
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream
-        if T == 1:
+        if state.dtype == torch.bfloat16:
+            _capi.check(lib.gdn_decode_launch_bf16_state(ctypes.byref(args), ctypes.c_void_p(stream)),
+                        "gdn_decode_launch_bf16_state")
+        elif T == 1:
             _capi.check(lib.gdn_decode_launch(ctypes.byref(args), ctypes.c_void_p(stream)),
                         "gdn_decode_launch")
         else:
@@ -112,6 +120,7 @@ class PreparedLaunch:
     def __init__(self, q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state):
         B = validate(q, k, v, state, A_log, a, dt_bias, b, output, new_state)
         _need(q.shape[1] == 1, "PreparedLaunch is for one token per sequence")
+        _need(state.dtype == torch.float32, "PreparedLaunch takes the fp32 state")
         self._keep = (q, k, v, state, A_log, a, dt_bias, b, output, new_state)
         self.device = q.device
         self.lib = _capi.load()
@@ -176,6 +185,7 @@ class HostStager:
         B = validate(q, k, v, state, A_log, a, dt_bias, b, output, new_state, require_cuda=False)
         _need(B == self.batch, f"stager built for batch {self.batch}, got {B}")
         _need(q.shape[1] == 1, "HostStager is for one token per sequence")
+        _need(state.dtype == torch.float32, "HostStager takes the fp32 state")
         _need(q.device.type == "cpu", "HostStager takes host tensors")
         host = _capi.GdnDecodeArgs(
             _ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a), _ptr(dt_bias), _ptr(b),

@@ -128,6 +128,26 @@ def test_decode_multi_token_matches_steps_and_in_place(pkg, cuda_dev):
     assert torch.equal(out2, out) and torch.equal(inplace, ns)
 
 
+@pytest.mark.parametrize("batch", [1, 8, 64, 300])
+def test_decode_bf16_state(pkg, orc, cuda_dev, batch):
+    """The bf16-state variant equals the oracle run on the bf16 state (read
+    as fp32), its new state within bf16 rounding (norm-wise 2^-8), also in
+    place."""
+    inp = pkg.inputs.make_decode_inputs(batch, seed=batch + 11)
+    s16 = inp.state.to(torch.bfloat16)
+    ro, rs = orc.decode(inp.q, inp.k, inp.v, s16.float(), inp.A_log, inp.a, inp.dt_bias, inp.b, inp.scale)
+    g = inp.to(cuda_dev)
+    out, ns = pkg.decode.launch_gdn(g.q, g.k, g.v, s16.to(cuda_dev), g.A_log, g.a, g.dt_bias, g.b, g.scale)
+    torch.cuda.synchronize()
+    assert ns.dtype == torch.bfloat16
+    torch.testing.assert_close(out.cpu().float(), ro.float(), atol=1e-2, rtol=1e-2)
+    assert state_rel_err(ns.cpu().float(), rs) < 2 ** -8
+    st = s16.to(cuda_dev)
+    out2, _ = pkg.decode.launch_gdn(g.q, g.k, g.v, st, g.A_log, g.a, g.dt_bias, g.b, g.scale, new_state=st)
+    torch.cuda.synchronize()
+    assert torch.equal(out2, out) and torch.equal(st, ns)
+
+
 @pytest.mark.parametrize("batch,slices", [(256, 16), (37, 8), (3, 16)])
 def test_host_stager_matches_device_call(pkg, cuda_dev, batch, slices):
     """HostStager (pinned host tensors in and out, state sliced over three

@@ -52,6 +52,23 @@ def test_decode_validate_multi_token(pkg):
         pkg.decode.validate(*bad, require_cuda=False)
 
 
+def test_decode_validate_bf16_state(pkg):
+    d = pkg.inputs.make_decode_inputs(2, seed=0)
+    out = torch.empty(2, 8, 128, dtype=torch.bfloat16)
+    s16 = d.state.to(torch.bfloat16)
+    args = [d.q, d.k, d.v, s16, d.A_log, d.a, d.dt_bias, d.b, out, torch.empty_like(s16)]
+    assert pkg.decode.validate(*args, require_cuda=False) == 2
+    bad = list(args)
+    bad[9] = torch.empty_like(d.state)  # fp32 new_state for a bf16 state
+    with pytest.raises(ValueError, match="new_state"):
+        pkg.decode.validate(*bad, require_cuda=False)
+    m = pkg.inputs.make_decode_inputs(2, seed=0, tokens=2)
+    with pytest.raises(ValueError, match="one token"):
+        pkg.decode.validate(m.q, m.k, m.v, s16, m.A_log, m.a, m.dt_bias, m.b,
+                            torch.empty(2, 2, 8, 128, dtype=torch.bfloat16), torch.empty_like(s16),
+                            require_cuda=False)
+
+
 def test_prefill_validate_seqlens(pkg):
     p = pkg.inputs.make_prefill_inputs([3, 4], seed=0)
     out = torch.empty(7, 8, 128, dtype=torch.bfloat16)
