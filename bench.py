@@ -295,6 +295,23 @@ def bench_decode_bf16(pkg, device, flush, batch=256, steps=20):
             "note": "state bytes = 2 x B x 256 KiB (bf16), read and written once; device time, L2 flushed"}
 
 
+def bench_decode_heads(pkg, device, flush, batch=64, hqk=16, hv=32, steps=20):
+    """The contest's other head layout (16 q/k, 32 v heads): one step of
+    ``batch`` sequences (2 MiB of fp32 state each)."""
+    inp = pkg.inputs.make_decode_inputs(batch, seed=3, hqk=hqk, hv=hv).to(device)
+    out = torch.empty((batch, hv, 128), dtype=torch.bfloat16, device=device)
+    ns = torch.empty_like(inp.state)
+
+    def step():
+        pkg.decode.launch_gdn(*inp.args(), output=out, new_state=ns)
+
+    times, _ = time_steps(step, steps, 3, 1, device, flush)
+    ms = sorted(times)[len(times) // 2]
+    state_bytes = 2 * inp.state.numel() * 4
+    return {"batch": batch, "heads": [hqk, hv], "us_per_step": round(ms * 1e3, 2),
+            "state_gbs": round(state_bytes / (ms * 1e-3) / 1e9, 1)}
+
+
 def time_gather(pkg, out, ns, ws, device):
     """The final gather of every rank's outputs and states to rank 0 (NCCL
     point-to-point over NVLink), timed on the device, max over ranks."""
@@ -479,6 +496,7 @@ def run_ours(args):
             line["decode_small_batch_us"] = bench_decode_small(pkg, device, flush)
             line["decode_multi_token"] = bench_decode_tokens(pkg, device, flush)
             line["decode_bf16_state"] = bench_decode_bf16(pkg, device, flush)
+            line["decode_qk16_v32"] = bench_decode_heads(pkg, device, flush)
     pf = {}
     psteps = max(3, args.steps // 2)
     if ws == 1:

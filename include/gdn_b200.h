@@ -101,6 +101,16 @@ int gdn_decode_launch_tokens(const GdnDecodeArgs* args, int64_t tokens, void* st
  * (about 3 significant digits per element) for bandwidth. */
 int gdn_decode_launch_bf16_state(const GdnDecodeArgs* args, void* stream);
 
+/* Head counts other than 4 q/k and 8 v heads (head dim 128; num_v_heads a
+ * multiple of num_qk_heads, v head h reading q/k head h / (num_v_heads /
+ * num_qk_heads), the reference's repeat_interleave grouping,
+ * reference_torch_impl.py:46-47; e.g. 16 / 32, the contest's other shape).
+ * Every tensor's head axis has the given count; otherwise as
+ * gdn_decode_launch_tokens (tokens >= 1, fp32 state) or, with bf16_state != 0,
+ * gdn_decode_launch_bf16_state (tokens = 1). */
+int gdn_decode_launch_heads(const GdnDecodeArgs* args, int32_t num_qk_heads, int32_t num_v_heads, int64_t tokens,
+                            int32_t bf16_state, void* stream);
+
 /* One decode step for a caller that keeps the state in HOST memory (state
  * offloaded between steps).  `host` holds host pointers to every input and
  * to output / new_state (pinned memory, or the copies do not overlap); `dev`
@@ -176,6 +186,12 @@ size_t gdn_prefill_workspace_size(int64_t total_tokens, int64_t num_seqs);
 
 int gdn_prefill_launch(const GdnPrefillArgs* args, void* workspace, size_t workspace_bytes,
                        void* stream);
+
+/* gdn_prefill_launch for head counts other than 4 / 8 (rules as
+ * gdn_decode_launch_heads): runs the token-recurrent kernel whatever
+ * args->path says and needs no workspace.  The chunked tensor-core kernels
+ * exist for 4 q/k and 8 v heads only. */
+int gdn_prefill_launch_heads(const GdnPrefillArgs* args, int32_t num_qk_heads, int32_t num_v_heads, void* stream);
 
 /* Size of the fixed scratch array behind gdn_prefill_launch_noalloc. */
 #define GDN_NOALLOC_SCRATCH_BYTES (32u << 20)

@@ -37,7 +37,7 @@ static float resolve_scale(float s) { return s == 0.0f ? 1.0f / sqrtf((float)kD)
 
 using namespace gdn;
 
-extern "C" int gdn_abi_version(void) { return 5; }
+extern "C" int gdn_abi_version(void) { return 6; }
 
 extern "C" const char* gdn_status_string(int status) {
     switch (status) {
@@ -55,7 +55,9 @@ extern "C" const char* gdn_status_string(int status) {
     }
 }
 
-static int decode_launch(const GdnDecodeArgs* a, void* stream, bool bf16_state) {
+static bool heads_ok(int hqk, int hv) { return hqk >= 1 && hv >= hqk && hv % hqk == 0 && hv <= 4096; }
+
+static int decode_launch(const GdnDecodeArgs* a, void* stream, bool bf16_state, int hqk = kHQK, int hv = kHV) {
     if (a == nullptr) return GDN_ERR_NULL_POINTER;
     if (a->batch < 0) return GDN_ERR_BAD_SIZE;
     if (a->batch == 0) return GDN_OK;
@@ -81,6 +83,9 @@ static int decode_launch(const GdnDecodeArgs* a, void* stream, bool bf16_state) 
     p.new_state = a->new_state;
     p.batch = a->batch;
     p.scale = resolve_scale(a->scale);
+    p.hqk = hqk;
+    p.hv = hv;
+    if (p.batch * hv * (kD / 16) > 0x7fffffffLL) return GDN_ERR_BAD_SIZE;
     return launch_decode(p, static_cast<cudaStream_t>(stream), bf16_state) == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
 }
 
@@ -96,12 +101,12 @@ extern "C" int gdn_decode_launch_bf16_state(const GdnDecodeArgs* a, void* stream
 // runs token by token on the state rows held in registers, so the state is
 // read and written once per call, as in a single-token step.  This is the
 // token-recurrent prefill kernel with every sequence T tokens long.
-extern "C" int gdn_decode_launch_tokens(const GdnDecodeArgs* a, int64_t tokens, void* stream) {
+static int decode_tokens(const GdnDecodeArgs* a, int64_t tokens, void* stream, int hqk, int hv) {
     if (a == nullptr) return GDN_ERR_NULL_POINTER;
     if (tokens < 1 || a->batch < 0) return GDN_ERR_BAD_SIZE;
-    if (tokens == 1) return gdn_decode_launch(a, stream);
+    if (tokens == 1) return decode_launch(a, stream, false, hqk, hv);
     if (a->batch == 0) return GDN_OK;
-    if (a->batch > (int64_t(1) << 40) / tokens || a->batch * kHV * (kD / 16) > 0x7fffffffLL) return GDN_ERR_BAD_SIZE;
+    if (a->batch > (int64_t(1) << 40) / tokens || a->batch * hv * (kD / 16) > 0x7fffffffLL) return GDN_ERR_BAD_SIZE;
     if (!a->q || !a->k || !a->v || !a->state || !a->A_log || !a->a || !a->dt_bias || !a->b || !a->output ||
         !a->new_state)
         return GDN_ERR_NULL_POINTER;
@@ -127,7 +132,23 @@ extern "C" int gdn_decode_launch_tokens(const GdnDecodeArgs* a, int64_t tokens, 
     p.out = static_cast<uint16_t*>(a->output);
     p.new_state = a->new_state;
     p.uniform_len = tokens;
+    p.hqk = hqk;
+    p.hv = hv;
     return launch_prefill_recurrent(p, static_cast<cudaStream_t>(stream)) == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
+}
+
+extern "C" int gdn_decode_launch_tokens(const GdnDecodeArgs* a, int64_t tokens, void* stream) {
+    return decode_tokens(a, tokens, stream, kHQK, kHV);
+}
+
+// Other head counts: every decode form (tokens >= 1, fp32 state; or one token
+// with a bf16 state) with num_qk_heads / num_v_heads given.
+extern "C" int gdn_decode_launch_heads(const GdnDecodeArgs* a, int32_t num_qk_heads, int32_t num_v_heads,
+                                       int64_t tokens, int32_t bf16_state, void* stream) {
+    if (a == nullptr) return GDN_ERR_NULL_POINTER;
+    if (!heads_ok(num_qk_heads, num_v_heads) || tokens < 1 || (bf16_state && tokens != 1)) return GDN_ERR_BAD_SIZE;
+    if (bf16_state) return decode_launch(a, stream, true, num_qk_heads, num_v_heads);
+    return decode_tokens(a, tokens, stream, num_qk_heads, num_v_heads);
 }
 
 extern "C" size_t gdn_prefill_workspace_size(int64_t total_tokens, int64_t num_seqs) {
@@ -135,8 +156,8 @@ extern "C" size_t gdn_prefill_workspace_size(int64_t total_tokens, int64_t num_s
     return chunked_workspace_bytes(total_tokens, num_seqs);
 }
 
-extern "C" int gdn_prefill_launch(const GdnPrefillArgs* a, void* workspace, size_t workspace_bytes,
-                                  void* stream) {
+// Argument checks shared by the prefill entry points, then the kernel parameters.
+static int prefill_setup(const GdnPrefillArgs* a, PrefillParams& p, int hqk, int hv) {
     if (a == nullptr) return GDN_ERR_NULL_POINTER;
     if (a->total_tokens < 0 || a->num_seqs < 0) return GDN_ERR_BAD_SIZE;
     if (a->cu_seqlens_dtype != GDN_SEQLENS_INT32 && a->cu_seqlens_dtype != GDN_SEQLENS_INT64)
@@ -153,11 +174,6 @@ extern "C" int gdn_prefill_launch(const GdnPrefillArgs* a, void* workspace, size
         return GDN_ERR_MISALIGNED;
     if (a->state != nullptr && a->num_seqs > 0 && a->state == a->new_state) return GDN_ERR_BAD_SIZE;
     if (int rc = check_device()) return rc;
-    const size_t need = chunked_workspace_min_bytes(a->total_tokens, a->num_seqs);
-    if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 256)))
-        return GDN_ERR_WORKSPACE;
-
-    PrefillParams p;
     p.q = static_cast<const uint16_t*>(a->q);
     p.k = static_cast<const uint16_t*>(a->k);
     p.v = static_cast<const uint16_t*>(a->v);
@@ -174,11 +190,38 @@ extern "C" int gdn_prefill_launch(const GdnPrefillArgs* a, void* workspace, size
     p.out = static_cast<uint16_t*>(a->output);
     p.new_state = a->new_state;
     p.uniform_len = 0;
+    p.hqk = hqk;
+    p.hv = hv;
+    return GDN_OK;
+}
+
+extern "C" int gdn_prefill_launch(const GdnPrefillArgs* a, void* workspace, size_t workspace_bytes,
+                                  void* stream) {
+    PrefillParams p;
+    if (int rc = prefill_setup(a, p, kHQK, kHV)) return rc;
+    const size_t need = chunked_workspace_min_bytes(a->total_tokens, a->num_seqs);
+    if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 256)))
+        return GDN_ERR_WORKSPACE;
+
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (a->num_seqs == 0)  // every token is uncovered: zero output
         return a->total_tokens > 0 && launch_prefill_zero_uncovered(p, s) != cudaSuccess ? GDN_ERR_CUDA : GDN_OK;
     const cudaError_t e = launch_prefill(p, a->path, workspace, workspace_bytes, s);
     return e == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
+}
+
+// Other head counts: the token-recurrent prefill (no workspace; the chunked
+// kernels are built for 4 q/k and 8 v heads).
+extern "C" int gdn_prefill_launch_heads(const GdnPrefillArgs* a, int32_t num_qk_heads, int32_t num_v_heads,
+                                        void* stream) {
+    if (a == nullptr) return GDN_ERR_NULL_POINTER;
+    if (!heads_ok(num_qk_heads, num_v_heads)) return GDN_ERR_BAD_SIZE;
+    PrefillParams p;
+    if (int rc = prefill_setup(a, p, num_qk_heads, num_v_heads)) return rc;
+    if (a->num_seqs * num_v_heads * (kD / 16) > 0x7fffffffLL) return GDN_ERR_BAD_SIZE;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (launch_prefill_zero_uncovered(p, s) != cudaSuccess) return GDN_ERR_CUDA;
+    return a->num_seqs > 0 && launch_prefill_recurrent(p, s) != cudaSuccess ? GDN_ERR_CUDA : GDN_OK;
 }
 
 extern "C" int gdn_read_device_status(int* out, int clear, void* stream) {

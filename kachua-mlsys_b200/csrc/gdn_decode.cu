@@ -39,6 +39,7 @@ struct DecodeParams {
     float* new_state;
     int64_t batch;
     float scale;
+    int hqk, hv;  // q/k and v heads (4 / 8 in the reference; hv a multiple of hqk)
 };
 
 // BF16S: the state (in and out) is stored as bf16 instead of fp32; the
@@ -58,9 +59,9 @@ __global__ void __launch_bounds__(128) gdn_decode_kernel(const DecodeParams p) {
     const int64_t cta = blockIdx.x;
     const int64_t bh = cta / kTiles;  // b * 8 + h
     const int tile = static_cast<int>(cta - bh * kTiles);
-    const int64_t bi = bh / kHV;
-    const int h = static_cast<int>(bh - bi * kHV);
-    const int hq = h / kGva;
+    const int64_t bi = bh / p.hv;
+    const int h = static_cast<int>(bh - bi * p.hv);
+    const int hq = h / (p.hv / p.hqk);
     const int row0 = tile * kRowsPerCta + warp * RPW + grp;
 
     const float* src = p.state + bh * (kD * kD) + 4 * sub;
@@ -79,8 +80,8 @@ __global__ void __launch_bounds__(128) gdn_decode_kernel(const DecodeParams p) {
     }
 
     // 2. per-head vectors and gates (small, L2/L1 resident)
-    const uint16_t* qp = p.q + (bi * kHQK + hq) * kD + 4 * sub;
-    const uint16_t* kp = p.k + (bi * kHQK + hq) * kD + 4 * sub;
+    const uint16_t* qp = p.q + (bi * p.hqk + hq) * kD + 4 * sub;
+    const uint16_t* kp = p.k + (bi * p.hqk + hq) * kD + 4 * sub;
     float4 q4[4], k4[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -140,8 +141,7 @@ __global__ void __launch_bounds__(128) gdn_decode_kernel(const DecodeParams p) {
 }
 
 // Rows per warp: the largest tile that still yields >= 2 CTAs per SM.
-static int pick_rows_per_warp(int64_t batch) {
-    const int64_t heads = batch * kHV;
+static int pick_rows_per_warp(int64_t heads) {
     if (heads * (kD / 64) >= 2 * kSmCount) return 16;
     if (heads * (kD / 32) >= 2 * kSmCount) return 8;
     return 4;
@@ -159,8 +159,8 @@ static void launch_decode_rpw(int rpw, unsigned grid, const DecodeParams& p, cud
 // bf16_state: p.state / p.new_state point to bf16 [B, 8, 128, 128] arrays.
 cudaError_t launch_decode(const DecodeParams& p, cudaStream_t stream, bool bf16_state = false) {
     if (p.batch == 0) return cudaSuccess;
-    const int rpw = pick_rows_per_warp(p.batch);
-    const int64_t heads = p.batch * kHV;
+    const int64_t heads = p.batch * p.hv;
+    const int rpw = pick_rows_per_warp(heads);
     const int64_t grid = heads * (kD / (4 * rpw));
     if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
     if (bf16_state)

@@ -110,6 +110,8 @@ extern "C" int gdn_decode_launch_host_staged(const GdnDecodeArgs* host, const Gd
         p.new_state = reinterpret_cast<float*>(ds + lo * st);  // in place
         p.batch = hi - lo;
         p.scale = resolve_scale(host->scale);
+        p.hqk = kHQK;
+        p.hv = kHV;
         ok = ok && launch_decode(p, comp) == cudaSuccess;
         ok = ok && cudaEventRecord(c.done[i], comp) == cudaSuccess &&
              cudaStreamWaitEvent(down, c.done[i], 0) == cudaSuccess;

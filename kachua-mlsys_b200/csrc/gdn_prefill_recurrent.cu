@@ -34,6 +34,7 @@ struct PrefillParams {
     uint16_t* out;
     float* new_state;
     int64_t uniform_len;  // > 0: every sequence has this many tokens and cu_seqlens is unused
+    int hqk, hv;          // q/k and v heads; the chunked kernels take only 4 / 8
 };
 
 __device__ __forceinline__ int64_t load_cu(const PrefillParams& p, int64_t i) {
@@ -67,9 +68,9 @@ __global__ void __launch_bounds__(128) gdn_prefill_recurrent_kernel(const Prefil
     const int sub = lane & 7;
     const int64_t unit = blockIdx.x / kRecTiles;  // s * 8 + h
     const int tile = static_cast<int>(blockIdx.x - unit * kRecTiles);
-    const int64_t s = unit / kHV;
-    const int h = static_cast<int>(unit - s * kHV);
-    const int hq = h / kGva;
+    const int64_t s = unit / p.hv;
+    const int h = static_cast<int>(unit - s * p.hv);
+    const int hq = h / (p.hv / p.hqk);
     const int row = tile * kRecRowsPerCta + warp * 4 + grp;
 
     int64_t t0, t1;
@@ -109,7 +110,7 @@ __global__ void __launch_bounds__(128) gdn_prefill_recurrent_kernel(const Prefil
         // a warp stages one token's q and k per pass (32 x 4 dims) and reduces q.k
         for (int e = tid; e < nb * (kD / 4); e += 128) {
             const int i = e / (kD / 4), c = e % (kD / 4);
-            const int64_t base = ((tb + i) * kHQK + hq) * (kD / 4) + c;
+            const int64_t base = ((tb + i) * p.hqk + hq) * (kD / 4) + c;
             const uint2 qu = reinterpret_cast<const uint2*>(p.q)[base], ku = reinterpret_cast<const uint2*>(p.k)[base];
             s_q[i][c] = qu;
             s_k[i][c] = ku;
@@ -121,12 +122,12 @@ __global__ void __launch_bounds__(128) gdn_prefill_recurrent_kernel(const Prefil
         }
         for (int e = tid; e < nb * kRecRowsPerCta; e += 128) {
             const int i = e / kRecRowsPerCta, r = e % kRecRowsPerCta;
-            s_v[i][r] = p.v[((tb + i) * kHV + h) * kD + vrow0 + r];
+            s_v[i][r] = p.v[((tb + i) * p.hv + h) * kD + vrow0 + r];
         }
         if (tid < nb) {
             const int64_t t = tb + tid;
             float g, beta;
-            gdn_gates(A_log, dt_bias, bf16_bits_to_float(p.a[t * kHV + h]), bf16_bits_to_float(p.b[t * kHV + h]), g,
+            gdn_gates(A_log, dt_bias, bf16_bits_to_float(p.a[t * p.hv + h]), bf16_bits_to_float(p.b[t * p.hv + h]), g,
                       beta);
             s_g[tid] = g;
             s_b[tid] = beta;
@@ -161,7 +162,7 @@ __global__ void __launch_bounds__(128) gdn_prefill_recurrent_kernel(const Prefil
                 st[j].z = fmaf(g, st[j].z, delta * k4[j].z);
                 st[j].w = fmaf(g, st[j].w, delta * k4[j].w);
             }
-            if (sub == 0) out[(t * kHV + h) * kD + row] = __float2bfloat16_rn(p.scale * fmaf(g, qs, delta * qk));
+            if (sub == 0) out[(t * p.hv + h) * kD + row] = __float2bfloat16_rn(p.scale * fmaf(g, qs, delta * qk));
         }
     }
 #pragma unroll
@@ -176,7 +177,7 @@ __device__ __forceinline__ void zero_uncovered_rows(const PrefillParams& p) {
     int64_t lo = load_cu(p, 0), hi = load_cu(p, p.num_seqs);
     lo = lo < 0 ? 0 : (lo > p.total_tokens ? p.total_tokens : lo);
     hi = hi < lo ? lo : (hi > p.total_tokens ? p.total_tokens : hi);
-    const int64_t per_tok = kHV * kD / 8;  // uint4 per token
+    const int64_t per_tok = static_cast<int64_t>(p.hv) * kD / 8;  // uint4 per token
     const int64_t n_head = lo * per_tok, n_tail = (p.total_tokens - hi) * per_tok;
     uint4* o = reinterpret_cast<uint4*>(p.out);
     const uint4 z = make_uint4(0, 0, 0, 0);
@@ -189,7 +190,7 @@ __device__ __forceinline__ void zero_uncovered_rows(const PrefillParams& p) {
 __global__ void gdn_prefill_zero_uncovered_kernel(const PrefillParams p) { zero_uncovered_rows(p); }
 
 cudaError_t launch_prefill_recurrent(const PrefillParams& p, cudaStream_t stream) {
-    const int64_t grid = p.num_seqs * kHV * kRecTiles;
+    const int64_t grid = p.num_seqs * p.hv * kRecTiles;
     if (grid == 0) return cudaSuccess;
     if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
     gdn_prefill_recurrent_kernel<<<(unsigned)grid, 128, 0, stream>>>(p);

@@ -42,11 +42,14 @@ def validate(q, k, v, state, A_log, a, dt_bias, b, output, new_state, require_cu
     """Checks every argument; returns the batch size B.
 
     q is ``[B, T, 4, 128]`` with T tokens per sequence (T = 1 for a plain
-    decode step); k, v, a, b and output carry the same T.
+    decode step); k, v, a, b and output carry the same T.  Other head counts
+    (q ``[B, T, HQK, 128]``, v ``[B, T, HV, 128]``, HV a multiple of HQK) are
+    accepted for the head-count variant.
     ``require_cuda=False`` checks only shapes/dtypes/layout (host-side tests).
     """
     _need(isinstance(q, torch.Tensor) and q.dim() == 4, "q must be a [B, T, 4, 128] tensor")
     B, T = q.shape[0], q.shape[1]
+    HQK, HV = heads(q, v)
     _need(T >= 1 and tuple(q.shape) == (B, T, HQK, D), f"q must be [B, T, 4, 128], got {tuple(q.shape)}")
     dev = q.device
     _need(dev.type == "cuda" or not require_cuda, "q must be a CUDA tensor (there is no CPU path)")
@@ -63,9 +66,18 @@ def validate(q, k, v, state, A_log, a, dt_bias, b, output, new_state, require_cu
     _check(b, "b", torch.bfloat16, B * T * HV, dev)
     _check(output, "output", torch.bfloat16, B * T * HV * D, dev)
     _check(new_state, "new_state", sdt, B * HV * D * D, dev)
-    _need(tuple(state.shape) == (B, HV, D, D), f"state must be [B, 8, 128, 128], got {tuple(state.shape)}")
-    _need(tuple(new_state.shape) == (B, HV, D, D), "new_state must be [B, 8, 128, 128]")
+    _need(tuple(state.shape) == (B, HV, D, D), f"state must be [B, {HV}, 128, 128], got {tuple(state.shape)}")
+    _need(tuple(new_state.shape) == (B, HV, D, D), f"new_state must be [B, {HV}, 128, 128]")
     return B
+
+
+def heads(q, v) -> tuple[int, int]:
+    """(q/k heads, v heads) from the tensors: 4 / 8 in the reference."""
+    hqk = q.shape[-2] if isinstance(q, torch.Tensor) and q.dim() >= 2 else HQK
+    hv = v.shape[-2] if isinstance(v, torch.Tensor) and v.dim() >= 2 else HV
+    _need(hqk >= 1 and hv >= hqk and hv % hqk == 0,
+          f"v heads ({hv}) must be a multiple of q/k heads ({hqk})")
+    return hqk, hv
 
 
 def _ptr(t: torch.Tensor):
@@ -85,8 +97,9 @@ def launch_gdn(q, k, v, state, A_log, a, dt_bias, b, scale=None, output=None, ne
     """
     _need(isinstance(q, torch.Tensor) and q.dim() == 4, "q must be a [B, T, 4, 128] tensor")
     T = q.shape[1]
+    hqk, hv = heads(q, v)
     if output is None:
-        shape = (q.shape[0], HV, D) if T == 1 else (q.shape[0], T, HV, D)
+        shape = (q.shape[0], hv, D) if T == 1 else (q.shape[0], T, hv, D)
         output = torch.empty(shape, dtype=torch.bfloat16, device=q.device)
     if new_state is None:
         new_state = torch.empty_like(state)
@@ -97,7 +110,11 @@ def launch_gdn(q, k, v, state, A_log, a, dt_bias, b, scale=None, output=None, ne
         _ptr(output), _ptr(new_state), B, 0.0 if scale is None else float(scale))
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream
-        if state.dtype == torch.bfloat16:
+        if (hqk, hv) != (HQK, HV):
+            _capi.check(lib.gdn_decode_launch_heads(ctypes.byref(args), hqk, hv, T,
+                                                    int(state.dtype == torch.bfloat16), ctypes.c_void_p(stream)),
+                        "gdn_decode_launch_heads")
+        elif state.dtype == torch.bfloat16:
             _capi.check(lib.gdn_decode_launch_bf16_state(ctypes.byref(args), ctypes.c_void_p(stream)),
                         "gdn_decode_launch_bf16_state")
         elif T == 1:
@@ -120,6 +137,7 @@ class PreparedLaunch:
     def __init__(self, q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state):
         B = validate(q, k, v, state, A_log, a, dt_bias, b, output, new_state)
         _need(q.shape[1] == 1, "PreparedLaunch is for one token per sequence")
+        _need(heads(q, v) == (HQK, HV), "PreparedLaunch takes 4 q/k and 8 v heads")
         _need(state.dtype == torch.float32, "PreparedLaunch takes the fp32 state")
         self._keep = (q, k, v, state, A_log, a, dt_bias, b, output, new_state)
         self.device = q.device
@@ -185,6 +203,7 @@ class HostStager:
         B = validate(q, k, v, state, A_log, a, dt_bias, b, output, new_state, require_cuda=False)
         _need(B == self.batch, f"stager built for batch {self.batch}, got {B}")
         _need(q.shape[1] == 1, "HostStager is for one token per sequence")
+        _need(heads(q, v) == (HQK, HV), "HostStager takes 4 q/k and 8 v heads")
         _need(state.dtype == torch.float32, "HostStager takes the fp32 state")
         _need(q.device.type == "cpu", "HostStager takes host tensors")
         host = _capi.GdnDecodeArgs(

@@ -33,9 +33,9 @@ def _qk(gen: torch.Generator, shape) -> torch.Tensor:
     return x.to(torch.bfloat16)
 
 
-def _gate_params(gen: torch.Generator):
-    A_log = torch.log(torch.empty(NUM_V_HEADS, dtype=torch.float32).uniform_(1.0, 16.0, generator=gen))
-    dt_bias = torch.zeros(NUM_V_HEADS, dtype=torch.float32)
+def _gate_params(gen: torch.Generator, hv: int = NUM_V_HEADS):
+    A_log = torch.log(torch.empty(hv, dtype=torch.float32).uniform_(1.0, 16.0, generator=gen))
+    dt_bias = torch.zeros(hv, dtype=torch.float32)
     return A_log, dt_bias
 
 
@@ -89,17 +89,19 @@ class PrefillInputs:
         return self.q.shape[0]
 
 
-def make_decode_inputs(batch: int, seed: int = 0, tokens: int = 1) -> DecodeInputs:
+def make_decode_inputs(batch: int, seed: int = 0, tokens: int = 1, hqk: int = NUM_QK_HEADS,
+                       hv: int = NUM_V_HEADS) -> DecodeInputs:
     """Decode config 0/1/4a inputs: ``batch`` sequences, ``tokens`` tokens each
-    (1 for a plain decode step; more for speculative / multi-token decode)."""
+    (1 for a plain decode step; more for speculative / multi-token decode);
+    ``hqk`` / ``hv`` head counts (4 / 8 in the reference)."""
     gen = torch.Generator().manual_seed(seed)
-    q = _qk(gen, (batch, tokens, NUM_QK_HEADS, HEAD_DIM))
-    k = _qk(gen, (batch, tokens, NUM_QK_HEADS, HEAD_DIM))
-    v = torch.randn((batch, tokens, NUM_V_HEADS, HEAD_DIM), generator=gen).to(torch.bfloat16)
-    a = torch.randn((batch, tokens, NUM_V_HEADS), generator=gen).to(torch.bfloat16)
-    b = torch.randn((batch, tokens, NUM_V_HEADS), generator=gen).to(torch.bfloat16)
-    A_log, dt_bias = _gate_params(gen)
-    state = torch.randn((batch, NUM_V_HEADS, HEAD_DIM, HEAD_DIM), generator=gen) * 0.02
+    q = _qk(gen, (batch, tokens, hqk, HEAD_DIM))
+    k = _qk(gen, (batch, tokens, hqk, HEAD_DIM))
+    v = torch.randn((batch, tokens, hv, HEAD_DIM), generator=gen).to(torch.bfloat16)
+    a = torch.randn((batch, tokens, hv), generator=gen).to(torch.bfloat16)
+    b = torch.randn((batch, tokens, hv), generator=gen).to(torch.bfloat16)
+    A_log, dt_bias = _gate_params(gen, hv)
+    state = torch.randn((batch, hv, HEAD_DIM, HEAD_DIM), generator=gen) * 0.02
     return DecodeInputs(q, k, v, state, A_log, a, dt_bias, b)
 
 
@@ -116,20 +118,22 @@ def varlen_lengths(num_seqs: int, lo: int, hi: int, seed: int) -> list[int]:
     return torch.randint(lo, hi + 1, (num_seqs,), generator=gen).tolist()
 
 
-def make_prefill_inputs(lengths, seed: int = 0, with_state: bool = True) -> PrefillInputs:
-    """Prefill inputs for sequences of the given lengths, packed via cu_seqlens."""
+def make_prefill_inputs(lengths, seed: int = 0, with_state: bool = True, hqk: int = NUM_QK_HEADS,
+                        hv: int = NUM_V_HEADS) -> PrefillInputs:
+    """Prefill inputs for sequences of the given lengths, packed via cu_seqlens;
+    ``hqk`` / ``hv`` head counts (4 / 8 in the reference)."""
     gen = torch.Generator().manual_seed(seed)
     T = int(sum(lengths))
     N = len(lengths)
-    q = _qk(gen, (T, NUM_QK_HEADS, HEAD_DIM))
-    k = _qk(gen, (T, NUM_QK_HEADS, HEAD_DIM))
-    v = torch.randn((T, NUM_V_HEADS, HEAD_DIM), generator=gen).to(torch.bfloat16)
-    a = torch.randn((T, NUM_V_HEADS), generator=gen).to(torch.bfloat16)
-    b = torch.randn((T, NUM_V_HEADS), generator=gen).to(torch.bfloat16)
-    A_log, dt_bias = _gate_params(gen)
+    q = _qk(gen, (T, hqk, HEAD_DIM))
+    k = _qk(gen, (T, hqk, HEAD_DIM))
+    v = torch.randn((T, hv, HEAD_DIM), generator=gen).to(torch.bfloat16)
+    a = torch.randn((T, hv), generator=gen).to(torch.bfloat16)
+    b = torch.randn((T, hv), generator=gen).to(torch.bfloat16)
+    A_log, dt_bias = _gate_params(gen, hv)
     state = None
     if with_state:
-        state = torch.randn((N, NUM_V_HEADS, HEAD_DIM, HEAD_DIM), generator=gen) * 0.02
+        state = torch.randn((N, hv, HEAD_DIM, HEAD_DIM), generator=gen) * 0.02
     return PrefillInputs(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens_from_lengths(lengths))
 
 

@@ -49,6 +49,7 @@ def validate(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, output, new_state
     """
     _need(isinstance(q, torch.Tensor) and q.dim() == 3, "q must be a [T, 4, 128] tensor")
     T = q.shape[0]
+    HQK, HV = heads(q, v)
     dev = q.device
     _need(dev.type == "cuda" or not require_cuda, "q must be a CUDA tensor (there is no CPU path)")
     _need(isinstance(cu_seqlens, torch.Tensor) and cu_seqlens.dim() == 1 and cu_seqlens.numel() >= 1,
@@ -65,8 +66,8 @@ def validate(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, output, new_state
         _need(N == 0 or state.data_ptr() != new_state.data_ptr(), "state must not alias new_state")
     _check(A_log, "A_log", torch.float32, (HV,), dev)
     _check(dt_bias, "dt_bias", torch.float32, (HV,), dev)
-    _need(isinstance(a, torch.Tensor) and a.numel() == T * HV, "a must be [T, 8]")
-    _need(isinstance(b, torch.Tensor) and b.numel() == T * HV, "b must be [T, 8]")
+    _need(isinstance(a, torch.Tensor) and a.numel() == T * HV, f"a must be [T, {HV}]")
+    _need(isinstance(b, torch.Tensor) and b.numel() == T * HV, f"b must be [T, {HV}]")
     _check(a, "a", torch.bfloat16, a.shape, dev)
     _check(b, "b", torch.bfloat16, b.shape, dev)
     _check(output, "output", torch.bfloat16, (T, HV, D), dev)
@@ -77,6 +78,15 @@ def validate(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, output, new_state
         _need(bool((cu[1:] >= cu[:-1]).all()), "cu_seqlens must be non-decreasing")
         _need(int(cu[-1]) <= T, f"cu_seqlens[-1]={int(cu[-1])} exceeds total tokens {T}")
     return T, N
+
+
+def heads(q, v) -> tuple[int, int]:
+    """(q/k heads, v heads) from the tensors: 4 / 8 in the reference."""
+    hqk = q.shape[-2] if isinstance(q, torch.Tensor) and q.dim() >= 2 else HQK
+    hv = v.shape[-2] if isinstance(v, torch.Tensor) and v.dim() >= 2 else HV
+    _need(hqk >= 1 and hv >= hqk and hv % hqk == 0,
+          f"v heads ({hv}) must be a multiple of q/k heads ({hqk})")
+    return hqk, hv
 
 
 def workspace_bytes(total_tokens: int, num_seqs: int) -> int:
@@ -98,19 +108,35 @@ def launch_gdn(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None, out
     ``path`` selects the algorithm: ``"auto"`` (token-recurrent kernel for
     batches of short sequences, chunked tensor-core kernels otherwise),
     ``"recurrent"`` or ``"chunked"``.  ``workspace`` may be passed to reuse a
-    device buffer of at least ``workspace_bytes(T, N)`` bytes.
+    device buffer of at least ``workspace_bytes(T, N)`` bytes.  Head counts
+    other than 4 q/k / 8 v (q ``[T, HQK, 128]``, v ``[T, HV, 128]``) run the
+    token-recurrent kernel.
     """
     _need(path in PATHS, f"path must be one of {sorted(PATHS)}")
     _need(isinstance(q, torch.Tensor), "q must be a torch.Tensor")
     if isinstance(cu_seqlens, torch.Tensor) and cu_seqlens.device != q.device:
         cu_seqlens = cu_seqlens.to(q.device)
     N = cu_seqlens.numel() - 1
+    hqk, hv = heads(q, v)
+    _need((hqk, hv) == (HQK, HV) or path in ("auto", "recurrent"),
+          "head counts other than 4 / 8 run the token-recurrent kernel only (path auto or recurrent)")
     if output is None:
-        output = torch.empty((q.shape[0], HV, D), dtype=torch.bfloat16, device=q.device)
+        output = torch.empty((q.shape[0], hv, D), dtype=torch.bfloat16, device=q.device)
     if new_state is None:
-        new_state = torch.empty((N, HV, D, D), dtype=torch.float32, device=q.device)
+        new_state = torch.empty((N, hv, D, D), dtype=torch.float32, device=q.device)
     T, N = validate(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, output, new_state, check_seqlens)
     lib = _capi.load()
+    if (hqk, hv) != (HQK, HV):
+        args = _capi.GdnPrefillArgs(
+            _ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a), _ptr(dt_bias), _ptr(b),
+            _ptr(cu_seqlens),
+            _capi.GDN_SEQLENS_INT64 if cu_seqlens.dtype == torch.int64 else _capi.GDN_SEQLENS_INT32,
+            PATHS["recurrent"], T, N, 0.0 if scale is None else float(scale), _ptr(output), _ptr(new_state))
+        with torch.cuda.device(q.device):
+            stream = torch.cuda.current_stream(q.device).cuda_stream
+            _capi.check(lib.gdn_prefill_launch_heads(ctypes.byref(args), hqk, hv, ctypes.c_void_p(stream)),
+                        "gdn_prefill_launch_heads")
+        return output, new_state
     need = int(lib.gdn_prefill_workspace_size(T, N))
     if need > 0 and (workspace is None or workspace.numel() * workspace.element_size() < need
                      or workspace.device != q.device):

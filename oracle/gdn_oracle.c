@@ -22,6 +22,9 @@
  *   S        = old - k (x) old_v + k (x) new_v          (decode :63-65, prefill :77-87)
  *   o        = scale * q @ S                            (decode :67, prefill :89)
  * with q/k head = v head / 2 (repeat_interleave, decode :46-47, prefill :38-39).
+ * The *_heads entry points take other head counts (num_v_heads a multiple of
+ * num_qk_heads, q/k head = v head / (num_v_heads / num_qk_heads), the same
+ * repeat_interleave grouping); the plain ones are the reference's 4 / 8.
  * softplus follows torch.nn.functional.softplus (beta 1, threshold 20).
  * The state is stored k-last: S[v][k] (the reference transposes to [K,V]
  * and back, decode :57/:68, prefill :58/:91; the math is the same).
@@ -106,24 +109,26 @@ static void load_bf16_vec(const uint16_t* src, float* dst) {
  * A_log, dt_bias fp32 [8]; a, b bf16 [B,1,8]; output fp32 [B,8,128];
  * new_state fp32 [B,8,128,128].  scale == 0 selects 1/sqrt(128) (None maps to 0).
  */
-int oracle_gdn_decode(const uint16_t* q, const uint16_t* k, const uint16_t* v,
-                      const float* state, const float* A_log, const uint16_t* a,
-                      const float* dt_bias, const uint16_t* b, float scale,
-                      int64_t batch, float* output, float* new_state, int num_threads) {
+int oracle_gdn_decode_heads(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                            const float* state, const float* A_log, const uint16_t* a,
+                            const float* dt_bias, const uint16_t* b, float scale,
+                            int64_t batch, float* output, float* new_state, int num_threads,
+                            int hqk, int hv) {
+    if (hqk < 1 || hv < hqk || hv % hqk) return -1;
     if (scale == 0.0f) scale = 1.0f / sqrtf((float)ORC_D); /* `scale is None or scale == 0.0` */
-    const int64_t units = batch * ORC_HV;
+    const int64_t units = batch * hv;
 #pragma omp parallel for schedule(dynamic, 4) num_threads(num_threads)
     for (int64_t u = 0; u < units; ++u) {
-        const int64_t bi = u / ORC_HV;
-        const int h = (int)(u % ORC_HV);
-        const int hq = h / (ORC_HV / ORC_HQK);
+        const int64_t bi = u / hv;
+        const int h = (int)(u % hv);
+        const int hq = h / (hv / hqk);
         float qf[ORC_D], kf[ORC_D], vf[ORC_D];
-        load_bf16_vec(q + (bi * ORC_HQK + hq) * ORC_D, qf);
-        load_bf16_vec(k + (bi * ORC_HQK + hq) * ORC_D, kf);
-        load_bf16_vec(v + (bi * ORC_HV + h) * ORC_D, vf);
+        load_bf16_vec(q + (bi * hqk + hq) * ORC_D, qf);
+        load_bf16_vec(k + (bi * hqk + hq) * ORC_D, kf);
+        load_bf16_vec(v + (bi * hv + h) * ORC_D, vf);
         float g, beta;
-        gates(A_log[h], dt_bias[h], bf16_to_f32(a[bi * ORC_HV + h]),
-              bf16_to_f32(b[bi * ORC_HV + h]), &g, &beta);
+        gates(A_log[h], dt_bias[h], bf16_to_f32(a[bi * hv + h]),
+              bf16_to_f32(b[bi * hv + h]), &g, &beta);
         float* S = new_state + u * ORC_D * ORC_D;
         if (S != state + u * ORC_D * ORC_D) {
             memcpy(S, state + u * ORC_D * ORC_D, sizeof(float) * ORC_D * ORC_D);
@@ -133,25 +138,35 @@ int oracle_gdn_decode(const uint16_t* q, const uint16_t* k, const uint16_t* v,
     return 0;
 }
 
+int oracle_gdn_decode(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                      const float* state, const float* A_log, const uint16_t* a,
+                      const float* dt_bias, const uint16_t* b, float scale,
+                      int64_t batch, float* output, float* new_state, int num_threads) {
+    return oracle_gdn_decode_heads(q, k, v, state, A_log, a, dt_bias, b, scale, batch, output, new_state,
+                                   num_threads, ORC_HQK, ORC_HV);
+}
+
 /*
  * Prefill: q,k bf16 [T,4,128]; v bf16 [T,8,128]; state fp32 [N,8,128,128] or
  * NULL; a, b bf16 [T,8]; cu_seqlens int64 [N+1]; output bf16 [T,8,128];
  * new_state fp32 [N,8,128,128].  Tokens outside every sequence keep the
  * output zero (the reference allocates output with torch.zeros, prefill :41-45).
  */
-int oracle_gdn_prefill(const uint16_t* q, const uint16_t* k, const uint16_t* v,
-                       const float* state, const float* A_log, const uint16_t* a,
-                       const float* dt_bias, const uint16_t* b,
-                       const int64_t* cu_seqlens, int64_t num_seqs, int64_t total_tokens,
-                       float scale, uint16_t* output, float* new_state, int num_threads) {
+int oracle_gdn_prefill_heads(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                             const float* state, const float* A_log, const uint16_t* a,
+                             const float* dt_bias, const uint16_t* b,
+                             const int64_t* cu_seqlens, int64_t num_seqs, int64_t total_tokens,
+                             float scale, uint16_t* output, float* new_state, int num_threads,
+                             int hqk, int hv) {
+    if (hqk < 1 || hv < hqk || hv % hqk) return -1;
     if (scale == 0.0f) scale = 1.0f / sqrtf((float)ORC_D); /* `scale is None or scale == 0.0` */
-    memset(output, 0, sizeof(uint16_t) * (size_t)total_tokens * ORC_HV * ORC_D);
-    const int64_t units = num_seqs * ORC_HV;
+    memset(output, 0, sizeof(uint16_t) * (size_t)total_tokens * hv * ORC_D);
+    const int64_t units = num_seqs * hv;
 #pragma omp parallel for schedule(dynamic, 1) num_threads(num_threads)
     for (int64_t u = 0; u < units; ++u) {
-        const int64_t s = u / ORC_HV;
-        const int h = (int)(u % ORC_HV);
-        const int hq = h / (ORC_HV / ORC_HQK);
+        const int64_t s = u / hv;
+        const int h = (int)(u % hv);
+        const int hq = h / (hv / hqk);
         float* S = new_state + u * ORC_D * ORC_D;
         const int64_t t0 = cu_seqlens[s], t1 = cu_seqlens[s + 1];
         if (t1 <= t0) {
@@ -165,18 +180,27 @@ int oracle_gdn_prefill(const uint16_t* q, const uint16_t* k, const uint16_t* v,
         }
         float qf[ORC_D], kf[ORC_D], vf[ORC_D], of[ORC_D];
         for (int64_t t = t0; t < t1; ++t) {
-            load_bf16_vec(q + (t * ORC_HQK + hq) * ORC_D, qf);
-            load_bf16_vec(k + (t * ORC_HQK + hq) * ORC_D, kf);
-            load_bf16_vec(v + (t * ORC_HV + h) * ORC_D, vf);
+            load_bf16_vec(q + (t * hqk + hq) * ORC_D, qf);
+            load_bf16_vec(k + (t * hqk + hq) * ORC_D, kf);
+            load_bf16_vec(v + (t * hv + h) * ORC_D, vf);
             float g, beta;
-            gates(A_log[h], dt_bias[h], bf16_to_f32(a[t * ORC_HV + h]),
-                  bf16_to_f32(b[t * ORC_HV + h]), &g, &beta);
+            gates(A_log[h], dt_bias[h], bf16_to_f32(a[t * hv + h]),
+                  bf16_to_f32(b[t * hv + h]), &g, &beta);
             head_step(S, qf, kf, vf, g, beta, scale, of);
-            uint16_t* o = output + (t * ORC_HV + h) * ORC_D;
+            uint16_t* o = output + (t * hv + h) * ORC_D;
             for (int i = 0; i < ORC_D; ++i) o[i] = f32_to_bf16(of[i]);
         }
     }
     return 0;
 }
 
-int oracle_abi_version(void) { return 1; }
+int oracle_gdn_prefill(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                       const float* state, const float* A_log, const uint16_t* a,
+                       const float* dt_bias, const uint16_t* b,
+                       const int64_t* cu_seqlens, int64_t num_seqs, int64_t total_tokens,
+                       float scale, uint16_t* output, float* new_state, int num_threads) {
+    return oracle_gdn_prefill_heads(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs, total_tokens,
+                                    scale, output, new_state, num_threads, ORC_HQK, ORC_HV);
+}
+
+int oracle_abi_version(void) { return 2; }

@@ -11,6 +11,10 @@ reference arm may import this module.  The product path (the
 * prefill -> gdn_prefill_qk4_v8_d128_k_last/solution/reference_torch_impl.py:17-92,
   returns ``(output bf16 [T,8,128], new_state fp32 [N,8,128,128])``.
 
+Head counts come from the tensor shapes (q/k heads from ``q``, v heads from
+``v``): 4 / 8 is the reference; other counts with the same grouping check the
+head-count variants of the kernels.
+
 The arithmetic lives in ``gdn_oracle.c`` (built into ``oracle/_build``).
 """
 from __future__ import annotations
@@ -47,6 +51,10 @@ def _load():
         lib.oracle_gdn_prefill.argtypes = [P, P, P, P, P, P, P, P, P, ctypes.c_int64,
                                            ctypes.c_int64, ctypes.c_float, P, P, ctypes.c_int]
         lib.oracle_gdn_prefill.restype = ctypes.c_int
+        lib.oracle_gdn_decode_heads.argtypes = lib.oracle_gdn_decode.argtypes + [ctypes.c_int, ctypes.c_int]
+        lib.oracle_gdn_decode_heads.restype = ctypes.c_int
+        lib.oracle_gdn_prefill_heads.argtypes = lib.oracle_gdn_prefill.argtypes + [ctypes.c_int, ctypes.c_int]
+        lib.oracle_gdn_prefill_heads.restype = ctypes.c_int
         _lib = lib
     return _lib
 
@@ -75,12 +83,12 @@ def decode(q, k, v, state, A_log, a, dt_bias, b, scale=None, threads: int | None
     bf, f32 = torch.bfloat16, torch.float32
     q, k, v, a, b = (_cpu(x, bf) for x in (q, k, v, a, b))
     state, A_log, dt_bias = (_cpu(x, f32) for x in (state, A_log, dt_bias))
-    B = q.shape[0]
-    out = torch.empty((B, 8, 128), dtype=f32)
+    B, hqk, hv = q.shape[0], q.shape[-2], v.shape[-2]  # 4 / 8 in the reference; others for the heads variants
+    out = torch.empty((B, hv, 128), dtype=f32)
     new_state = torch.empty_like(state)
-    rc = lib.oracle_gdn_decode(_ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a),
-                               _ptr(dt_bias), _ptr(b), _scale(scale), B, _ptr(out),
-                               _ptr(new_state), threads or default_threads())
+    rc = lib.oracle_gdn_decode_heads(_ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a),
+                                     _ptr(dt_bias), _ptr(b), _scale(scale), B, _ptr(out),
+                                     _ptr(new_state), threads or default_threads(), hqk, hv)
     assert rc == 0
     return out, new_state
 
@@ -94,13 +102,13 @@ def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None,
     A_log, dt_bias = (_cpu(x, f32) for x in (A_log, dt_bias))
     cu = cu_seqlens.detach().to("cpu", torch.int64).contiguous()
     N = cu.numel() - 1
-    T = q.shape[0]
+    T, hqk, hv = q.shape[0], q.shape[-2], v.shape[-2]
     st = None if state is None else _cpu(state, f32)
-    out = torch.empty((T, 8, 128), dtype=bf)
-    new_state = torch.empty((N, 8, 128, 128), dtype=f32)
-    rc = lib.oracle_gdn_prefill(_ptr(q), _ptr(k), _ptr(v),
-                                None if st is None else _ptr(st), _ptr(A_log), _ptr(a),
-                                _ptr(dt_bias), _ptr(b), _ptr(cu), N, T, _scale(scale),
-                                _ptr(out), _ptr(new_state), threads or default_threads())
+    out = torch.empty((T, hv, 128), dtype=bf)
+    new_state = torch.empty((N, hv, 128, 128), dtype=f32)
+    rc = lib.oracle_gdn_prefill_heads(_ptr(q), _ptr(k), _ptr(v),
+                                      None if st is None else _ptr(st), _ptr(A_log), _ptr(a),
+                                      _ptr(dt_bias), _ptr(b), _ptr(cu), N, T, _scale(scale),
+                                      _ptr(out), _ptr(new_state), threads or default_threads(), hqk, hv)
     assert rc == 0
     return out, new_state

@@ -148,6 +148,37 @@ def test_decode_bf16_state(pkg, orc, cuda_dev, batch):
     assert torch.equal(out2, out) and torch.equal(st, ns)
 
 
+@pytest.mark.parametrize("hqk,hv", [(16, 32), (2, 8), (8, 8), (1, 4)])
+@pytest.mark.parametrize("tokens", [1, 3])
+def test_decode_other_head_counts(pkg, orc, cuda_dev, hqk, hv, tokens):
+    """Head counts other than 4 / 8 (e.g. the contest's 16 / 32), one and
+    three tokens per step, against the oracle with the same grouping."""
+    batch = 6
+    inp = pkg.inputs.make_decode_inputs(batch, seed=hqk * 100 + hv + tokens, tokens=tokens, hqk=hqk, hv=hv)
+    cu = torch.arange(0, (batch + 1) * tokens, tokens, dtype=torch.int64)
+    flat = lambda t: t.reshape(batch * tokens, *t.shape[2:])  # noqa: E731
+    ro, rs = orc.prefill(flat(inp.q), flat(inp.k), flat(inp.v), inp.state, inp.A_log, flat(inp.a),
+                         inp.dt_bias, flat(inp.b), cu, inp.scale)
+    g = inp.to(cuda_dev)
+    out, ns = pkg.decode.launch_gdn(*g.args())
+    torch.cuda.synchronize()
+    assert pkg.prefill.device_status(cuda_dev) == 0
+    torch.testing.assert_close(out.cpu().float().reshape(batch * tokens, hv, 128), ro.float(), atol=1e-2,
+                               rtol=1e-2)
+    assert state_rel_err(ns.cpu(), rs) < 1e-3
+
+
+def test_decode_other_head_counts_bf16_state(pkg, orc, cuda_dev):
+    inp = pkg.inputs.make_decode_inputs(5, seed=9, hqk=16, hv=32)
+    s16 = inp.state.to(torch.bfloat16)
+    ro, rs = orc.decode(inp.q, inp.k, inp.v, s16.float(), inp.A_log, inp.a, inp.dt_bias, inp.b, inp.scale)
+    g = inp.to(cuda_dev)
+    out, ns = pkg.decode.launch_gdn(g.q, g.k, g.v, s16.to(cuda_dev), g.A_log, g.a, g.dt_bias, g.b, g.scale)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(out.cpu().float(), ro.float(), atol=1e-2, rtol=1e-2)
+    assert state_rel_err(ns.cpu().float(), rs) < 2 ** -8
+
+
 @pytest.mark.parametrize("batch,slices", [(256, 16), (37, 8), (3, 16)])
 def test_host_stager_matches_device_call(pkg, cuda_dev, batch, slices):
     """HostStager (pinned host tensors in and out, state sliced over three

@@ -147,6 +147,15 @@ def test_prefill_segmented_auto(pkg, orc, cuda_dev, lengths):
            cuda_dev, path="auto")
 
 
+@pytest.mark.parametrize("hqk,hv", [(16, 32), (2, 4)])
+def test_prefill_other_head_counts(pkg, orc, cuda_dev, hqk, hv):
+    """Head counts other than 4 / 8 run the token-recurrent kernel."""
+    inp = pkg.inputs.make_prefill_inputs([33, 0, 70, 1], seed=hv, with_state=True, hqk=hqk, hv=hv)
+    _check(pkg, orc, inp, cuda_dev, path="auto")
+    with pytest.raises(ValueError, match="token-recurrent"):
+        pkg.prefill.launch_gdn(*inp.to(cuda_dev).args(), path="chunked")
+
+
 def test_segmented_matches_single_pass(pkg, cuda_dev):
     """Segmented and single-pass carries agree closely on the same batch."""
     inp = pkg.inputs.make_prefill_inputs([1500, 900], seed=48, with_state=True)
