@@ -37,7 +37,7 @@ static float resolve_scale(float s) { return s == 0.0f ? 1.0f / sqrtf((float)kD)
 
 using namespace gdn;
 
-extern "C" int gdn_abi_version(void) { return 6; }
+extern "C" int gdn_abi_version(void) { return 7; }
 
 extern "C" const char* gdn_status_string(int status) {
     switch (status) {
@@ -207,6 +207,32 @@ extern "C" int gdn_prefill_launch(const GdnPrefillArgs* a, void* workspace, size
     if (a->num_seqs == 0)  // every token is uncovered: zero output
         return a->total_tokens > 0 && launch_prefill_zero_uncovered(p, s) != cudaSuccess ? GDN_ERR_CUDA : GDN_OK;
     const cudaError_t e = launch_prefill(p, a->path, workspace, workspace_bytes, s);
+    return e == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
+}
+
+// Context parallelism (one batch of sequences split by token range over
+// `world` ranks; see launch_prefill_cp for the protocol).
+extern "C" size_t gdn_prefill_cp_workspace_size(int64_t local_tokens, int64_t num_seqs, int32_t world) {
+    if (local_tokens < 0 || num_seqs < 0 || world < 1 || world > 4096) return 0;
+    return static_cast<size_t>(cp_layout(local_tokens, num_seqs, world).total_seg);
+}
+
+extern "C" size_t gdn_prefill_cp_summary_offset(int64_t local_tokens, int64_t num_seqs) {
+    if (local_tokens < 0 || num_seqs < 0) return 0;
+    return static_cast<size_t>(ws_layout(local_tokens, num_seqs).total);
+}
+
+extern "C" int gdn_prefill_cp_launch(const GdnPrefillArgs* a, void* workspace, size_t workspace_bytes, int32_t rank,
+                                     int32_t world, int32_t phase, void* stream) {
+    if (a == nullptr) return GDN_ERR_NULL_POINTER;
+    if (world < 1 || world > 4096 || rank < 0 || rank >= world || (phase != 0 && phase != 1)) return GDN_ERR_BAD_SIZE;
+    PrefillParams p;
+    if (int rc = prefill_setup(a, p, kHQK, kHV)) return rc;
+    if (a->num_seqs == 0) return GDN_OK;
+    const size_t need = static_cast<size_t>(cp_layout(a->total_tokens, a->num_seqs, world).total_seg);
+    if (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 256)) return GDN_ERR_WORKSPACE;
+    const cudaError_t e =
+        launch_prefill_cp(p, workspace, workspace_bytes, rank, world, phase, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
 }
 

@@ -86,6 +86,7 @@ struct WsLayout {
     int64_t seg_slots;  // summary slots per chain (segments on a 148-SM part; 1: none)
     int64_t off_seg;    // segment summaries (0 without slots)
     int64_t total_seg;  // total + the summaries
+    int64_t cp_world;   // context parallel: ranks (seg_slots = segments per rank); 0 otherwise
 };
 
 __host__ __device__ inline WsLayout ws_layout(int64_t T, int64_t N) {
@@ -103,6 +104,7 @@ __host__ __device__ inline WsLayout ws_layout(int64_t T, int64_t N) {
     L.off_rec = o;
     o += L.R * kHV * kHeadRecBytes;
     L.total = align_up(o, 1024);
+    L.cp_world = 0;
     L.seg_slots = seg_segments(N, kSmCount);
     L.off_seg = L.seg_slots >= 2 ? L.total : 0;
     L.total_seg = L.total + (L.seg_slots >= 2 ? N * kHV * L.seg_slots * static_cast<int64_t>(kSegSlotBytes) : 0);
@@ -851,6 +853,13 @@ done:
 // U^T K' terms (T_s) and from 0 (Z_s); pass C (mode 2) rebuilds each
 // segment's initial state, S_{s+1} = S_s T_s + Z_s, and runs the segment with
 // outputs.  Mode 0 is the single pass over whole sequences.
+//
+// Context parallel (modes 4 and 5): rank r holds the r-th token range of
+// every sequence, cut into nP = seg_slots local segments; global segment
+// g = r nP + q.  Mode 4 is pass A over the rank's segments (rank 0 also
+// Sum0), writing every summary a later segment composes (an empty segment
+// writes T = I, Z = 0); the ranks all-gather the summaries; mode 5 is pass C
+// over the rank's segments, composing global segments 1 .. g-1.
 constexpr int kCarryThreads = 448;
 constexpr int kCaM = 0;                         // f16 M K-major [128 k][128 k'], 2 x 32 KiB
 constexpr int kCaKU = 65536;                    // K' [64 j][128 k] (MN-major) + U^T [128 v][64 j] (K-major), 3 x 32 KiB
@@ -897,6 +906,7 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     // this CTA's task
     int64_t unit;
     int seg = 0, role = kRoleMain, nP = 1;
+    int lseg = -1;  // context parallel: the segment within this rank's range (seg is global)
     if (mode == 0) {  // longest sequences first
         unit = static_cast<int64_t>(reinterpret_cast<const int*>(ws + L.off_order)[blockIdx.x / kHV]) * kHV +
                blockIdx.x % kHV;
@@ -904,6 +914,19 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
         nP = P;
         unit = blockIdx.x / P;
         seg = static_cast<int>(blockIdx.x % P);
+    } else if (mode == 4) {  // context parallel pass A on rank P: summaries of its nP local segments
+        nP = static_cast<int>(L.seg_slots);
+        const int per = P == 0 ? 2 * nP - 1 : 2 * nP;
+        unit = blockIdx.x / per;
+        const int r = static_cast<int>(blockIdx.x % per);
+        role = P == 0 && r == 0 ? kRoleSum0 : r < nP ? kRoleSumT : kRoleSumZ;
+        lseg = r < nP ? r : r - nP + (P == 0 ? 1 : 0);
+        seg = P * nP + lseg;
+    } else if (mode == 5) {  // context parallel pass C on rank P: compose global segments 1 .. seg-1, run
+        nP = static_cast<int>(L.seg_slots);
+        unit = blockIdx.x / nP;
+        lseg = static_cast<int>(blockIdx.x % nP);
+        seg = P * nP + lseg;
     } else {
         nP = P;
         const int per = 2 * P - 3;
@@ -928,7 +951,9 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     const int nch_all = (len_all + kC - 1) / kC;
     const int rec0_all = reinterpret_cast<const int*>(ws + L.off_base)[s];
     float* ns_head = p.new_state + unit * kD * kD;
+    const bool cp = mode >= 4;  // context parallel: every rank holds >= 1 chunk of every sequence
     if (nch_all == 0 || rec0_all + nch_all > L.R) {
+        if (cp && tid == 0) record_status(16);
         if (role == kRoleMain && seg == 0) {
             if (nch_all != 0 && tid == 0) record_status(16);
             // empty sequence: zero state (oracle prefill :53-55)
@@ -937,17 +962,58 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
         }
         return;
     }
+    if (lseg < 0) lseg = seg;
     const int Lseg = (nch_all + nP - 1) / nP;
-    const int cb = seg * Lseg < nch_all ? seg * Lseg : nch_all;
+    const int cb = lseg * Lseg < nch_all ? lseg * Lseg : nch_all;
     const int ce = cb + Lseg < nch_all ? cb + Lseg : nch_all;
-    if (cb >= ce) return;                             // empty segment of a short sequence
-    if (role != kRoleMain && ce >= nch_all) return;   // a summary nobody composes
+    // a summary nobody composes: one reaching the end of the sequence (context
+    // parallel: the end of the last rank's range)
+    if (role != kRoleMain && ce >= nch_all && (!cp || P + 1 == L.cp_world)) return;
     const bool last = ce == nch_all, outputs = role == kRoleMain, dpart = role != kRoleSumT;
     const int nch = ce - cb, rec0 = rec0_all + cb;
     t0 += static_cast<int64_t>(kC) * cb;
     const int len = len_all - kC * cb < kC * nch ? len_all - kC * cb : kC * nch;
     auto rec_ptr = [&](int c) { return ws + L.off_rec + (static_cast<int64_t>(rec0 + c) * kHV + h) * kHeadRecBytes; };
-    auto slot = [&](int sg) { return ws + L.off_seg + (unit * L.seg_slots + sg) * static_cast<int64_t>(kSegSlotBytes); };
+    // summaries: per unit and segment; context parallel: per global segment
+    // (rank-major) and unit, each rank's block contiguous as the all-gather
+    // lays them out
+    auto slot = [&](int sg) {
+        return ws + L.off_seg +
+               (cp ? static_cast<int64_t>(sg) * p.num_seqs * kHV + unit : unit * L.seg_slots + sg) *
+                   static_cast<int64_t>(kSegSlotBytes);
+    };
+    const int qw = warp & 3, hk = warp >> 2;  // state warps: sub-partition, k half
+    const int vrow = 32 * qw + lane;
+    // a segment summary from a state warp's registers (row vrow, k = 64 hk .. 64 hk + 63)
+    auto put_summary = [&](const float* a0, const float* a1) {
+        if (role == kRoleSumT) {  // T_seg as the f16 MN-major image [128 j][128 k]
+            uint8_t* img = slot(seg);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                *reinterpret_cast<uint4*>(img + h16(vrow, 64 * hk + 8 * e, kD)) = f16x8(a0 + 8 * e);
+                *reinterpret_cast<uint4*>(img + h16(vrow, 64 * hk + 32 + 8 * e, kD)) = f16x8(a1 + 8 * e);
+            }
+        } else {  // Z_seg (or S at the start of segment 1): fp32 rows
+            uint8_t* z = slot(role == kRoleSum0 ? 0 : seg) + 32768;
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                const float* a = e < 8 ? a0 + 4 * e : a1 + 4 * (e - 8);
+                *reinterpret_cast<float4*>(z + zrow_off(vrow, 16 * hk + e)) = make_float4(a[0], a[1], a[2], a[3]);
+            }
+        }
+    };
+    if (cb >= ce) {  // an empty segment of a short sequence
+        if (role != kRoleMain && warp < 8) {  // context parallel, composed by later ranks: T = I, Z = 0
+            float a0[32], a1[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+                a0[e] = role == kRoleSumT && 64 * hk + e == vrow ? 1.f : 0.f;
+                a1[e] = role == kRoleSumT && 64 * hk + 32 + e == vrow ? 1.f : 0.f;
+            }
+            put_summary(a0, a1);
+        }
+        return;
+    }
 
     const bool issuer = tid == 12 * 32, loader = tid == 13 * 32;
     int topM = -1, topKU = -1, topQt = -1;  // loader: highest chunk whose copy was issued
@@ -996,8 +1062,6 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     auto accS = [&](int b) { return tm + 128 * b; };
     auto sA = [&](int b) { return tm + 256 + 64 * b; };
     auto accO = [&](int b) { return tm + 384 + 64 * b; };
-    const int qw = warp & 3, hk = warp >> 2;  // state warps: sub-partition, k half
-    const int vrow = 32 * qw + lane;
 
     // initial state -> fp16 A operand 0 (state warps)
     if (warp < 8) {
@@ -1128,20 +1192,8 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
                             make_float4(a1[4 * e], a1[4 * e + 1], a1[4 * e + 2], a1[4 * e + 3]);
                     }
                 }
-            } else if (role == kRoleSumT) {  // T_seg as the f16 MN-major image [128 j][128 k]
-                uint8_t* img = slot(seg);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    *reinterpret_cast<uint4*>(img + h16(vrow, 64 * hk + 8 * e, kD)) = f16x8(a0 + 8 * e);
-                    *reinterpret_cast<uint4*>(img + h16(vrow, 64 * hk + 32 + 8 * e, kD)) = f16x8(a1 + 8 * e);
-                }
-            } else {  // Z_seg (or S at the start of segment 1): fp32 rows
-                uint8_t* z = slot(role == kRoleSum0 ? 0 : seg) + 32768;
-#pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const float* a = e < 8 ? a0 + 4 * e : a1 + 4 * (e - 8);
-                    *reinterpret_cast<float4*>(z + zrow_off(vrow, 16 * hk + e)) = make_float4(a[0], a[1], a[2], a[3]);
-                }
+            } else {
+                put_summary(a0, a1);
             }
         }
     } else if (warp < 12) {
@@ -1352,35 +1404,46 @@ static cudaError_t token_tensor_map(CUtensorMap* m, const void* base, int heads,
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-cudaError_t launch_prefill_chunked(const PrefillParams& p, void* workspace, size_t workspace_bytes, int path,
-                                   cudaStream_t stream) {
-    const WsLayout L = ws_layout(p.total_tokens, p.num_seqs);
-    uint8_t* ws = static_cast<uint8_t*>(workspace);
+// The chunk table and the operand records (table + prepare kernels); leaves
+// the output tensor map and the SM count for the carry.
+static cudaError_t chunk_records(const PrefillParams& p, uint8_t* ws, const WsLayout& L, CUtensorMap* tmO,
+                                 int* sms_out, cudaStream_t stream) {
     if (L.R * kHV > 0x7fffffffLL || p.total_tokens > 0x7fffffffLL) return cudaErrorInvalidValue;
-    CUtensorMap tmK, tmQ, tmV, tmO;
+    CUtensorMap tmK, tmQ, tmV;
     memset(&tmK, 0, sizeof(tmK));
     memset(&tmQ, 0, sizeof(tmQ));
     memset(&tmV, 0, sizeof(tmV));
-    memset(&tmO, 0, sizeof(tmO));
+    memset(tmO, 0, sizeof(*tmO));
     cudaError_t e;
     if (p.total_tokens > 0) {  // with no tokens there are no records and no loads
         if ((e = token_tensor_map(&tmK, p.k, kHQK, p.total_tokens)) != cudaSuccess) return e;
         if ((e = token_tensor_map(&tmQ, p.q, kHQK, p.total_tokens)) != cudaSuccess) return e;
         if ((e = token_tensor_map(&tmV, p.v, kHV, p.total_tokens)) != cudaSuccess) return e;
-        if ((e = token_tensor_map(&tmO, p.out, kHV, p.total_tokens)) != cudaSuccess) return e;
+        if ((e = token_tensor_map(tmO, p.out, kHV, p.total_tokens)) != cudaSuccess) return e;
     }
     gdn_chunk_table_kernel<<<kSmCount, 1024, 0, stream>>>(p, ws, L);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if ((e = set_smem(gdn_chunk_prepare_kernel, kPrSmem)) != cudaSuccess) return e;
     int dev = 0, sms = 148;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    *sms_out = sms;
     // persistent prepare: two CTAs per SM (or one per item when there are fewer)
     const int64_t items = L.R * kHV;
     if ((e = launch_dependent(gdn_chunk_prepare_kernel, static_cast<unsigned>(items < 2 * sms ? items : 2 * sms),
                               kPrepThreads, kPrSmem, stream, p, ws, L, tmK, tmQ, tmV)) != cudaSuccess)
         return e;
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    if ((e = set_smem(gdn_chunk_carry_kernel, kCaSmem)) != cudaSuccess) return e;
+    return set_smem(gdn_chunk_carry_kernel, kCaSmem);
+}
+
+cudaError_t launch_prefill_chunked(const PrefillParams& p, void* workspace, size_t workspace_bytes, int path,
+                                   cudaStream_t stream) {
+    const WsLayout L = ws_layout(p.total_tokens, p.num_seqs);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    CUtensorMap tmO;
+    int sms = 148;
+    cudaError_t e;
+    if ((e = chunk_records(p, ws, L, &tmO, &sms, stream)) != cudaSuccess) return e;
     const int64_t units = p.num_seqs * kHV;
     if (units > 0x7fffffffLL / (2 * kSegMaxP)) return cudaErrorInvalidValue;
     // Segmented carry: when sequences average 16 chunks or more and both
@@ -1404,6 +1467,60 @@ cudaError_t launch_prefill_chunked(const PrefillParams& p, void* workspace, size
     }
     return launch_dependent(gdn_chunk_carry_kernel, static_cast<unsigned>(units), kCarryThreads, kCaSmem, stream, p,
                             ws, L, 0, 1, tmO);
+}
+
+// Context parallelism: every sequence's tokens are split over `world` ranks in
+// consecutive ranges (every range at least one token; the composition is
+// exact for any split, whole chunks only keep the chunks full); rank r holds
+// range r of every sequence.  Phase 0 on
+// every rank builds its records and its carry summary (rank 0: its outputs,
+// final state and end state; rank r >= 1: the affine map (T_r, Z_r) of its
+// range), written at rank r's block of the summary region.  The caller then
+// all-gathers that region (world blocks of num_seqs x 8 x 96 KiB); phase 1 on
+// rank r >= 1 composes rank 0's end state through ranks 1 .. r-1 and runs its
+// range with outputs (its new_state: the state after its range).
+// Segments per rank for the context-parallel carry: every rank's pass A (2
+// CTAs per segment and unit) in one wave, and at most 16 segments over all
+// ranks (the last rank's CTAs compose up to world x segments - 2 summaries).
+// A function of (N, world) only, so that every rank lays out the same slots.
+static int cp_segments(int64_t N, int world) {
+    const int64_t units = N * kHV;
+    int q = 8;
+    while (q > 1 && (2 * units * q > kSmCount || static_cast<int64_t>(world) * q > 16)) --q;
+    return q;
+}
+
+WsLayout cp_layout(int64_t T, int64_t N, int world) {
+    WsLayout L = ws_layout(T, N);
+    L.cp_world = world;
+    L.seg_slots = cp_segments(N, world);
+    L.off_seg = L.total;
+    L.total_seg = L.total + static_cast<int64_t>(world) * L.seg_slots * N * kHV * kSegSlotBytes;
+    return L;
+}
+
+cudaError_t launch_prefill_cp(const PrefillParams& p, void* workspace, size_t workspace_bytes, int rank, int world,
+                              int phase, cudaStream_t stream) {
+    const WsLayout L = cp_layout(p.total_tokens, p.num_seqs, world);
+    if (workspace_bytes < static_cast<size_t>(L.total_seg)) return cudaErrorInvalidValue;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const int64_t units = p.num_seqs * kHV, q = L.seg_slots;
+    if (units == 0 || units > 0x7fffffffLL / (2 * q)) return units == 0 ? cudaSuccess : cudaErrorInvalidValue;
+    CUtensorMap tmO;
+    cudaError_t e;
+    if (phase == 0) {  // records, then pass A: Sum0 (rank 0), T and Z of the rank's segments
+        int sms = 148;
+        if ((e = chunk_records(p, ws, L, &tmO, &sms, stream)) != cudaSuccess) return e;
+        return launch_dependent(gdn_chunk_carry_kernel, static_cast<unsigned>(units * (rank == 0 ? 2 * q - 1 : 2 * q)),
+                                kCarryThreads, kCaSmem, stream, p, ws, L, 4, rank, tmO);
+    }
+    // pass C over the rank's segments, with outputs
+    memset(&tmO, 0, sizeof(tmO));
+    if (p.total_tokens > 0 && (e = token_tensor_map(&tmO, p.out, kHV, p.total_tokens)) != cudaSuccess) return e;
+    if ((e = set_smem(gdn_chunk_carry_kernel, kCaSmem)) != cudaSuccess) return e;
+    gdn_chunk_carry_kernel<<<static_cast<unsigned>(units * q), kCarryThreads, kCaSmem, stream>>>(p, ws, L, 5, rank,
+                                                                                                 tmO);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_prefill(const PrefillParams& p, int path, void* workspace, size_t workspace_bytes,

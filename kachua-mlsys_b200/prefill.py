@@ -159,3 +159,92 @@ def device_status(device=None, clear: bool = True) -> int:
     device = torch.device("cuda") if device is None else torch.device(device)
     with torch.cuda.device(device):
         return _capi.read_device_status(torch.cuda.current_stream(device).cuda_stream, clear)
+
+
+# ------------------------------------------------------ context parallelism --
+def cp_split(cu_seqlens, world: int) -> list[tuple[torch.Tensor, torch.Tensor]]:
+    """Token ranges of a batch for ``world`` context-parallel ranks: every
+    sequence's chunks (64 tokens) are split into ``world`` consecutive ranges
+    of whole chunks (the last may be partial).  Returns, per rank, the global
+    token indices it holds and its local cu_seqlens (int64, on the CPU).
+    Every sequence needs at least ``world`` chunks' worth of tokens beyond the
+    last rank's first token, i.e. ``64 * (world - 1) + 1`` tokens."""
+    cu = [int(x) for x in torch.as_tensor(cu_seqlens).to("cpu", torch.int64)]
+    out = []
+    for r in range(world):
+        idx, lens = [], []
+        for s in range(len(cu) - 1):
+            t0, t1 = cu[s], cu[s + 1]
+            nch = (t1 - t0 + 63) // 64
+            _need(t1 - t0 > 64 * (world - 1), f"sequence {s} ({t1 - t0} tokens) is too short for {world} ranks")
+            c0, c1 = nch * r // world, nch * (r + 1) // world
+            a, b = t0 + 64 * c0, min(t1, t0 + 64 * c1)
+            _need(b > a, f"sequence {s} leaves rank {r} no tokens")
+            idx.append(torch.arange(a, b))
+            lens.append(b - a)
+        loc = torch.zeros(len(lens) + 1, dtype=torch.int64)
+        if lens:
+            loc[1:] = torch.cumsum(torch.tensor(lens, dtype=torch.int64), 0)
+        out.append((torch.cat(idx) if idx else torch.zeros(0, dtype=torch.int64), loc))
+    return out
+
+
+def cp_workspace_bytes(local_tokens: int, num_seqs: int, world: int) -> int:
+    return int(_capi.load().gdn_prefill_cp_workspace_size(int(local_tokens), int(num_seqs), int(world)))
+
+
+def cp_summary_region(workspace: torch.Tensor, local_tokens: int, num_seqs: int, world: int) -> torch.Tensor:
+    """The uint8 view of the workspace that the ranks all-gather (world equal
+    blocks): its tail, from the summary offset to the workspace size."""
+    off = int(_capi.load().gdn_prefill_cp_summary_offset(int(local_tokens), int(num_seqs)))
+    return workspace[off: cp_workspace_bytes(local_tokens, num_seqs, world)]
+
+
+def cp_launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state, workspace,
+              rank: int, world: int, phase: int) -> None:
+    """One phase of the context-parallel prefill on this rank's local tokens
+    (``gdn_prefill_cp_launch``); the caller all-gathers ``cp_summary_region``
+    between phase 0 and phase 1."""
+    T, N = validate(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, output, new_state)
+    lib = _capi.load()
+    need = cp_workspace_bytes(T, N, world)
+    _need(workspace.numel() * workspace.element_size() >= need and workspace.device == q.device,
+          f"workspace must be >= {need} bytes on {q.device}")
+    args = _capi.GdnPrefillArgs(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a), _ptr(dt_bias), _ptr(b),
+        _ptr(cu_seqlens),
+        _capi.GDN_SEQLENS_INT64 if cu_seqlens.dtype == torch.int64 else _capi.GDN_SEQLENS_INT32,
+        PATHS["chunked"], T, N, 0.0 if scale is None else float(scale), _ptr(output), _ptr(new_state))
+    with torch.cuda.device(q.device):
+        stream = torch.cuda.current_stream(q.device).cuda_stream
+        _capi.check(lib.gdn_prefill_cp_launch(ctypes.byref(args), _ptr(workspace), need, rank, world, phase,
+                                              ctypes.c_void_p(stream)), "gdn_prefill_cp_launch")
+
+
+def launch_gdn_context_parallel(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None, output=None,
+                                new_state=None, group=None, workspace: torch.Tensor | None = None):
+    """Prefill with every sequence split by token range over the ranks of a
+    ``torch.distributed`` (NCCL) group, one GPU per rank: the tensors are this
+    rank's tokens (ranges as ``cp_split`` makes them) with its local
+    cu_seqlens; ``state`` is read on rank 0.  Returns ``(output, new_state)``:
+    this rank's outputs, and the state after its range (on the last rank, the
+    final state).  One all-gather carries the ranks' carry summaries (per rank,
+    num_seqs x 768 KiB per segment, up to 8 segments per rank)."""
+    import torch.distributed as dist
+
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    N = cu_seqlens.numel() - 1
+    if output is None:
+        output = torch.empty((q.shape[0], HV, D), dtype=torch.bfloat16, device=q.device)
+    if new_state is None:
+        new_state = torch.empty((N, HV, D, D), dtype=torch.float32, device=q.device)
+    need = cp_workspace_bytes(q.shape[0], N, world)
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    cp_launch(q, k, v, state if rank == 0 else None, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state,
+              workspace, rank, world, 0)
+    region = cp_summary_region(workspace, q.shape[0], N, world)
+    block = region.numel() // world
+    dist.all_gather_into_tensor(region, region[rank * block:(rank + 1) * block], group=group)
+    cp_launch(q, k, v, None, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state, workspace, rank, world, 1)
+    return output, new_state
