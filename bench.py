@@ -7,7 +7,9 @@ owns its own 256 sequences; sequences are independent, so there is no
 collective in the timed region).  Per-step microseconds are in
 ``ms_per_step``/``decode_us_per_step``.  Prefill tokens/s (configs 2 and 3 on
 one GPU; a config-4b shard of 8 x 8192 tokens per GPU for N > 1) ride along
-in ``prefill``.
+in ``prefill``; for N > 1 so does the context-parallel prefill of one
+131072-token sequence split by token range over the N GPUs (strong scaling,
+with the one-GPU time of the same sequence beside it).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...     (N > 1)
@@ -217,7 +219,7 @@ def cpu_prefill_baseline(pkg, budget_s: float):
             "sample": f"{n} x prefill of 8 sequences x 512 tokens through oracle/gdn_oracle.c"}
 
 
-def bench_prefill(pkg, device, lengths, seed, steps, warmup, ws, flush, with_state=True):
+def bench_prefill(pkg, device, lengths, seed, steps, warmup, ws, flush, with_state=True, gather=True):
     inp = pkg.inputs.make_prefill_inputs(lengths, seed=seed, with_state=with_state).to(device)
     T, N = inp.total_tokens, inp.num_seqs
     out = torch.empty((T, 8, 128), dtype=torch.bfloat16, device=device)
@@ -235,10 +237,39 @@ def bench_prefill(pkg, device, lengths, seed, steps, warmup, ws, flush, with_sta
     res = {"tokens": T, "seqs": N, "ms": ms, "tokens_per_s": T * ws / (ms * 1e-3),
            "algo_bytes": bytes_, "algo_flops": flops_per_tok * T,
            "hbm_gbs": bytes_ / (ms * 1e-3) / 1e9, "tflops": flops_per_tok * T / (ms * 1e-3) / 1e12}
-    if ws > 1:
+    if ws > 1 and gather:
         res.update(time_gather(pkg, out, ns, ws, device))
         res["tokens_per_s_with_gather"] = T * ws / ((ms + res["gather_ms"]) * 1e-3)
     return res
+
+
+def bench_prefill_cp(pkg, device, rank, ws, lengths, steps, warmup, flush):
+    """Context-parallel prefill (N > 1): the SAME batch split by token range
+    over the ranks (strong scaling), timed per call as max over ranks and
+    compared with one GPU running the whole batch."""
+    full = pkg.inputs.make_prefill_inputs(lengths, seed=7, with_state=True)
+    idx, loc = pkg.prefill.cp_split(full.cu_seqlens, ws)[rank]
+    pick = lambda t: t[idx].contiguous().to(device)  # noqa: E731
+    q, k, v, a, b = pick(full.q), pick(full.k), pick(full.v), pick(full.a), pick(full.b)
+    st, A_log, dt_bias, cu = (full.state.to(device), full.A_log.to(device), full.dt_bias.to(device),
+                              loc.to(device))
+    N = len(lengths)
+    out = torch.empty((q.shape[0], 8, 128), dtype=torch.bfloat16, device=device)
+    ns = torch.empty((N, 8, 128, 128), dtype=torch.float32, device=device)
+    wsb = torch.empty(pkg.prefill.cp_workspace_bytes(q.shape[0], N, ws), dtype=torch.uint8, device=device)
+
+    def step():
+        pkg.prefill.launch_gdn_context_parallel(q, k, v, st, A_log, a, dt_bias, b, cu, full.scale, out, ns,
+                                                workspace=wsb)
+
+    times, _ = time_steps(step, steps, warmup, ws, device, flush)
+    ms = max_over_ranks(sorted(times)[len(times) // 2], ws, device)
+    del q, k, v, a, b, out, wsb
+    one = bench_prefill(pkg, device, lengths, 7, steps, warmup, ws, flush, gather=False)  # every rank: all of it
+    T = int(full.cu_seqlens[-1])
+    return {"lengths": lengths, "tokens": T, "ms": ms, "tokens_per_s": T / (ms * 1e-3),
+            "one_gpu_ms": one["ms"], "speedup_vs_one_gpu": one["ms"] / ms,
+            "scaling": "strong (one batch over all ranks)"}
 
 
 def bench_decode_small(pkg, device, flush, batches=(1, 8, 16, 32, 64), steps=20):
@@ -509,6 +540,9 @@ def run_ours(args):
     if wl in ("all", "prefill4b") and (ws > 1 or wl == "prefill4b"):
         pf["config4b_shard_8x8192"] = bench_prefill(pkg, device, [8192] * 8, 2000 + rank, 3,
                                                     min(args.warmup, 3), ws, flush)
+    if wl in ("all", "prefill_cp") and ws > 1:
+        pf["context_parallel_1x131072"] = bench_prefill_cp(pkg, device, rank, ws, [131072], 5,
+                                                           min(args.warmup, 3), flush)
     if pf:
         line["prefill"] = pf
     if rank == 0 and ws == 1 and not args.skip_cpu and wl == "all":
@@ -568,7 +602,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds per CPU-baseline sample")
     ap.add_argument("--workload", default="all",
-                    choices=["all", "decode", "prefill2", "prefill3", "prefill4b"],
+                    choices=["all", "decode", "prefill2", "prefill3", "prefill4b", "prefill_cp"],
                     help="all = the JSON line the driver reads; the others time one workload")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline (profiling runs)")
     ap.add_argument("--skip-e2e", action="store_true", help="omit the host-buffer e2e leg")
