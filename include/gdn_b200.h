@@ -199,18 +199,18 @@ int gdn_prefill_launch_heads(const GdnPrefillArgs* args, int32_t num_qk_heads, i
  * chunks keep every chunk full); `args` describes the rank's local tokens
  * (local cu_seqlens).  args->state (the initial state) is read on rank 0 only.
  * Each rank cuts its range into up to 8 segments (the same count on every
- * rank, a function of num_seqs and world).
+ * rank, a function of num_seqs).
  *   1. gdn_prefill_cp_launch(args, ws, bytes, rank, world, 0, stream) on every
- *      rank: its chunk records and the carry summaries of its segments;
- *   2. all-gather the workspace's tail, from
- *      ws + gdn_prefill_cp_summary_offset(local_tokens, num_seqs) to
- *      ws + gdn_prefill_cp_workspace_size(local_tokens, num_seqs, world), as
- *      `world` equal blocks, rank r contributing block r (e.g. an in-place NCCL
- *      all-gather on `stream`);
+ *      rank: its chunk records, the carry summaries of its segments and their
+ *      composition, the rank's summary (rank 0: the state after its range);
+ *   2. all-gather world blocks of num_seqs x 8 x 98304 bytes at
+ *      ws + gdn_prefill_cp_summary_offset(local_tokens, num_seqs), rank r
+ *      contributing block r (e.g. an in-place NCCL all-gather on `stream`);
  *   3. gdn_prefill_cp_launch(..., 1, stream) on every rank: each segment
- *      composes the summaries of the segments before it (all ranks) into its
- *      start state and writes its outputs; new_state is the state after the
- *      rank's range (the last rank's is the batch's final state).
+ *      composes the rank summaries before it and the rank's own segments
+ *      before it into its start state and writes its outputs; new_state is
+ *      the state after the rank's range (the last rank's is the batch's final
+ *      state).
  * No reference counterpart (the reference prefill runs on one GPU,
  * triton/kernel.py:56-57); it lets one long sequence use several GPUs. */
 size_t gdn_prefill_cp_workspace_size(int64_t local_tokens, int64_t num_seqs, int32_t world);

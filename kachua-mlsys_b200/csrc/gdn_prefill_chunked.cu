@@ -87,6 +87,7 @@ struct WsLayout {
     int64_t off_seg;    // segment summaries (0 without slots)
     int64_t total_seg;  // total + the summaries
     int64_t cp_world;   // context parallel: ranks (seg_slots = segments per rank); 0 otherwise
+    int64_t off_gather; // context parallel: the all-gathered rank summaries (cp_world x N x 8 slots)
 };
 
 __host__ __device__ inline WsLayout ws_layout(int64_t T, int64_t N) {
@@ -105,6 +106,7 @@ __host__ __device__ inline WsLayout ws_layout(int64_t T, int64_t N) {
     o += L.R * kHV * kHeadRecBytes;
     L.total = align_up(o, 1024);
     L.cp_world = 0;
+    L.off_gather = 0;
     L.seg_slots = seg_segments(N, kSmCount);
     L.off_seg = L.seg_slots >= 2 ? L.total : 0;
     L.total_seg = L.total + (L.seg_slots >= 2 ? N * kHV * L.seg_slots * static_cast<int64_t>(kSegSlotBytes) : 0);
@@ -854,12 +856,14 @@ done:
 // segment's initial state, S_{s+1} = S_s T_s + Z_s, and runs the segment with
 // outputs.  Mode 0 is the single pass over whole sequences.
 //
-// Context parallel (modes 4 and 5): rank r holds the r-th token range of
-// every sequence, cut into nP = seg_slots local segments; global segment
-// g = r nP + q.  Mode 4 is pass A over the rank's segments (rank 0 also
-// Sum0), writing every summary a later segment composes (an empty segment
-// writes T = I, Z = 0); the ranks all-gather the summaries; mode 5 is pass C
-// over the rank's segments, composing global segments 1 .. g-1.
+// Context parallel (modes 4-6): rank r holds the r-th token range of every
+// sequence, cut into nP = seg_slots segments of its own.
+// Mode 4 is pass A over the rank's segments (rank 0's segment 0: Sum0),
+// writing every summary a later segment composes (an empty segment writes
+// T = I, Z = 0).  Mode 6 composes them into one summary per rank (rank 0:
+// its end state E_0); the ranks all-gather those; mode 5 is pass C, rank
+// r >= 1 starting from E_0 and composing ranks 1 .. r-1, then its own
+// segments before the CTA's.
 constexpr int kCarryThreads = 448;
 constexpr int kCaM = 0;                         // f16 M K-major [128 k][128 k'], 2 x 32 KiB
 constexpr int kCaKU = 65536;                    // K' [64 j][128 k] (MN-major) + U^T [128 v][64 j] (K-major), 3 x 32 KiB
@@ -906,7 +910,6 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     // this CTA's task
     int64_t unit;
     int seg = 0, role = kRoleMain, nP = 1;
-    int lseg = -1;  // context parallel: the segment within this rank's range (seg is global)
     if (mode == 0) {  // longest sequences first
         unit = static_cast<int64_t>(reinterpret_cast<const int*>(ws + L.off_order)[blockIdx.x / kHV]) * kHV +
                blockIdx.x % kHV;
@@ -914,19 +917,26 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
         nP = P;
         unit = blockIdx.x / P;
         seg = static_cast<int>(blockIdx.x % P);
-    } else if (mode == 4) {  // context parallel pass A on rank P: summaries of its nP local segments
+    } else if (mode == 4) {  // context parallel pass A on rank P: summaries of its nP segments
         nP = static_cast<int>(L.seg_slots);
         const int per = P == 0 ? 2 * nP - 1 : 2 * nP;
         unit = blockIdx.x / per;
         const int r = static_cast<int>(blockIdx.x % per);
         role = P == 0 && r == 0 ? kRoleSum0 : r < nP ? kRoleSumT : kRoleSumZ;
-        lseg = r < nP ? r : r - nP + (P == 0 ? 1 : 0);
-        seg = P * nP + lseg;
-    } else if (mode == 5) {  // context parallel pass C on rank P: compose global segments 1 .. seg-1, run
+        seg = r < nP ? r : r - nP + (P == 0 ? 1 : 0);
+    } else if (mode == 5) {  // context parallel pass C on rank P
         nP = static_cast<int>(L.seg_slots);
         unit = blockIdx.x / nP;
-        lseg = static_cast<int>(blockIdx.x % nP);
-        seg = P * nP + lseg;
+        seg = static_cast<int>(blockIdx.x % nP);
+    } else if (mode == 6) {  // context parallel rank summary (rank 0: the state at the end of its range)
+        nP = static_cast<int>(L.seg_slots);
+        if (P == 0) {
+            unit = blockIdx.x;
+            role = kRoleSum0;
+        } else {
+            unit = blockIdx.x / 2;
+            role = (blockIdx.x & 1) ? kRoleSumZ : kRoleSumT;
+        }
     } else {
         nP = P;
         const int per = 2 * P - 3;
@@ -962,47 +972,44 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
         }
         return;
     }
-    if (lseg < 0) lseg = seg;
+    const bool ranksum = mode == 6;  // composes the rank's segment summaries; no chunks
     const int Lseg = (nch_all + nP - 1) / nP;
-    const int cb = lseg * Lseg < nch_all ? lseg * Lseg : nch_all;
-    const int ce = cb + Lseg < nch_all ? cb + Lseg : nch_all;
+    const int cb = ranksum ? 0 : seg * Lseg < nch_all ? seg * Lseg : nch_all;
+    const int ce = ranksum ? 0 : cb + Lseg < nch_all ? cb + Lseg : nch_all;
     // a summary nobody composes: one reaching the end of the sequence (context
     // parallel: the end of the last rank's range)
-    if (role != kRoleMain && ce >= nch_all && (!cp || P + 1 == L.cp_world)) return;
-    const bool last = ce == nch_all, outputs = role == kRoleMain, dpart = role != kRoleSumT;
+    if (!ranksum && role != kRoleMain && ce >= nch_all && (!cp || P + 1 == L.cp_world)) return;
+    const bool last = !ranksum && ce == nch_all, outputs = role == kRoleMain;
+    const bool dpart = !ranksum && role != kRoleSumT;
     const int nch = ce - cb, rec0 = rec0_all + cb;
     t0 += static_cast<int64_t>(kC) * cb;
     const int len = len_all - kC * cb < kC * nch ? len_all - kC * cb : kC * nch;
     auto rec_ptr = [&](int c) { return ws + L.off_rec + (static_cast<int64_t>(rec0 + c) * kHV + h) * kHeadRecBytes; };
-    // summaries: per unit and segment; context parallel: per global segment
-    // (rank-major) and unit, each rank's block contiguous as the all-gather
-    // lays them out
+    // summaries (T at +0, Z at +32 KiB): per unit and segment; context
+    // parallel: the rank's own segments, and one all-gathered slot per rank
+    const int64_t units = p.num_seqs * kHV;
     auto slot = [&](int sg) {
-        return ws + L.off_seg +
-               (cp ? static_cast<int64_t>(sg) * p.num_seqs * kHV + unit : unit * L.seg_slots + sg) *
-                   static_cast<int64_t>(kSegSlotBytes);
+        return ws + L.off_seg + (cp ? sg * units + unit : unit * L.seg_slots + sg) * static_cast<int64_t>(kSegSlotBytes);
     };
+    auto gslot = [&](int r) { return ws + L.off_gather + (r * units + unit) * static_cast<int64_t>(kSegSlotBytes); };
+    auto sum_base_fn = [&]() { return ranksum || (cp && nP == 1) ? gslot(P) : slot(role == kRoleSum0 ? 0 : seg); };
     const int qw = warp & 3, hk = warp >> 2;  // state warps: sub-partition, k half
     const int vrow = 32 * qw + lane;
-    // a segment summary from a state warp's registers (row vrow, k = 64 hk .. 64 hk + 63)
-    auto put_summary = [&](const float* a0, const float* a1) {
-        if (role == kRoleSumT) {  // T_seg as the f16 MN-major image [128 j][128 k]
-            uint8_t* img = slot(seg);
+    // this CTA's summary from a state warp's registers: row vrow, k = 64 hk + 32 half + (0 .. 31)
+    auto put_half = [&](int half, const float* x) {
+        uint8_t* const sum_base = sum_base_fn();
+        if (role == kRoleSumT) {  // T as the f16 MN-major image [128 j][128 k]
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                *reinterpret_cast<uint4*>(img + h16(vrow, 64 * hk + 8 * e, kD)) = f16x8(a0 + 8 * e);
-                *reinterpret_cast<uint4*>(img + h16(vrow, 64 * hk + 32 + 8 * e, kD)) = f16x8(a1 + 8 * e);
-            }
-        } else {  // Z_seg (or S at the start of segment 1): fp32 rows
-            uint8_t* z = slot(role == kRoleSum0 ? 0 : seg) + 32768;
+            for (int e = 0; e < 4; ++e)
+                *reinterpret_cast<uint4*>(sum_base + h16(vrow, 64 * hk + 32 * half + 8 * e, kD)) = f16x8(x + 8 * e);
+        } else {  // Z (or a state): fp32 rows
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-                const float* a = e < 8 ? a0 + 4 * e : a1 + 4 * (e - 8);
-                *reinterpret_cast<float4*>(z + zrow_off(vrow, 16 * hk + e)) = make_float4(a[0], a[1], a[2], a[3]);
-            }
+            for (int e = 0; e < 8; ++e)
+                *reinterpret_cast<float4*>(sum_base + 32768 + zrow_off(vrow, 16 * hk + 8 * half + e)) =
+                    make_float4(x[4 * e], x[4 * e + 1], x[4 * e + 2], x[4 * e + 3]);
         }
     };
-    if (cb >= ce) {  // an empty segment of a short sequence
+    if (!ranksum && cb >= ce) {  // an empty segment of a short sequence
         if (role != kRoleMain && warp < 8) {  // context parallel, composed by later ranks: T = I, Z = 0
             float a0[32], a1[32];
 #pragma unroll
@@ -1010,7 +1017,8 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
                 a0[e] = role == kRoleSumT && 64 * hk + e == vrow ? 1.f : 0.f;
                 a1[e] = role == kRoleSumT && 64 * hk + 32 + e == vrow ? 1.f : 0.f;
             }
-            put_summary(a0, a1);
+            put_half(0, a0);
+            put_half(1, a1);
         }
         return;
     }
@@ -1063,11 +1071,32 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     auto sA = [&](int b) { return tm + 256 + 64 * b; };
     auto accO = [&](int b) { return tm + 384 + 64 * b; };
 
+    // The chain's start, and the summaries composed onto it before any chunk:
+    // segmented pass C starts at segment 1 (Sum0's state) and composes
+    // segments 1 .. seg-1; context parallel, rank P >= 1 starts at rank 0's
+    // end state and composes ranks 1 .. P-1, then its own segments
+    // 0 .. seg-1; a rank summary composes the rank's segments (rank 0: onto
+    // Sum0's state).
+    const bool cp_tail = cp && role == kRoleMain && P > 0;
+    const uint8_t* init_rows = nullptr;  // a state as fp32 rows (else p.state, I or 0)
+    if (cp_tail)
+        init_rows = gslot(0) + 32768;
+    else if ((role == kRoleMain && seg > 0) || (ranksum && role == kRoleSum0))
+        init_rows = slot(0) + 32768;
+    const int ncomp = cp_tail ? P - 1 + seg
+                      : role == kRoleMain ? (seg > 0 ? seg - 1 : 0)
+                      : ranksum ? (role == kRoleSum0 ? nP - 1 : nP)
+                                : 0;
+    const bool addZ = role != kRoleSumT;  // a T chain only multiplies
+    auto comp_slot = [&](int i) {
+        if (cp_tail) return i < P - 1 ? gslot(i + 1) : slot(i - (P - 1));
+        return ranksum && role != kRoleSum0 ? slot(i) : slot(i + 1);
+    };
     // initial state -> fp16 A operand 0 (state warps)
     if (warp < 8) {
         uint32_t w[32];
-        if (role == kRoleMain && seg > 0) {  // S at the start of segment 1 (pass A, segment 0)
-            const uint8_t* x1 = slot(0) + 32768;
+        if (init_rows != nullptr) {
+            const uint8_t* x1 = init_rows;
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
                 const float4 x = *reinterpret_cast<const float4*>(x1 + zrow_off(vrow, 16 * hk + e));
@@ -1096,23 +1125,25 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
         tc_fence_before();
     }
     __syncthreads();
-    // pass C: S_{j+1} = S_j T_j + Z_j for j = 1 .. seg-1 (in place in A operand 0).
-    // T_j (f16 MN-major [128 j][128 k]) goes to M buffer j & 1 and Z_j (fp32
+    // composition: S <- S T_i + Z_i for i < ncomp (in place in A operand 0).
+    // T_i (f16 MN-major [128 j][128 k]) goes to M buffer i & 1 and Z_i (fp32
     // rows) to a 64 KiB Z buffer over the [K' | U^T] and Qt^T space, both
-    // double-buffered and loaded one step ahead.
+    // double-buffered and loaded one step ahead.  A rank summary stores its
+    // last step's fp32 result.
     bool ok = true;
     const uint32_t aZ = aKU;  // 2 x 64 KiB (the [K' | U^T] and Qt^T buffers, 144 KiB)
-    auto issue_TZ = [&](int j) {
-        const int b = j & 1;
-        mbar_expect_tx(proLoad + 8 * b, 32768 + 65536);
-        bulk_g2s(aM + b * 32768, slot(j), 32768, proLoad + 8 * b);
-        bulk_g2s(aZ + b * 65536, slot(j) + 32768, 65536, proLoad + 8 * b);
+    auto issue_TZ = [&](int i) {
+        const int b = i & 1;
+        const uint8_t* src = comp_slot(i);
+        mbar_expect_tx(proLoad + 8 * b, addZ ? 32768 + 65536 : 32768);
+        bulk_g2s(aM + b * 32768, src, 32768, proLoad + 8 * b);
+        if (addZ) bulk_g2s(aZ + b * 65536, src + 32768, 65536, proLoad + 8 * b);
     };
-    if (loader && role == kRoleMain)
-        for (int j = 1; j < seg && j <= 2; ++j) issue_TZ(j);
-    for (int j = 1; role == kRoleMain && j < seg; ++j) {
+    if (loader)
+        for (int i = 0; i < ncomp && i < 2; ++i) issue_TZ(i);
+    for (int j = 0; j < ncomp; ++j) {
         const int b = j & 1;
-        const uint32_t ldbar = proLoad + 8 * b, ldpar = ((j - 1) >> 1) & 1;
+        const uint32_t ldbar = proLoad + 8 * b, ldpar = (j >> 1) & 1;
         if (issuer) {
             ok = mbar_wait(ldbar, ldpar) && ok;
             tc_fence_after();
@@ -1122,7 +1153,7 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
         if (warp < 8) {
             // Z_j arrived by TMA (observe its barrier) and S_j T_j is complete
             const bool okj =
-                __all_sync(0xffffffffu, mbar_wait(ldbar, ldpar) && mbar_wait(proMma, (j - 1) & 1));
+                __all_sync(0xffffffffu, mbar_wait(ldbar, ldpar) && mbar_wait(proMma, j & 1));
             tc_fence_after();
             uint32_t w[32];
 #pragma unroll
@@ -1132,10 +1163,17 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
                 tmem_wait_ld();
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
-                    const float4 z = Sm.ldf4(aZ + b * 65536 + zrow_off(vrow, 16 * hk + 8 * half + e));
-                    w[16 * half + 2 * e] = pack_half2(a[4 * e] + z.x, a[4 * e + 1] + z.y);
-                    w[16 * half + 2 * e + 1] = pack_half2(a[4 * e + 2] + z.z, a[4 * e + 3] + z.w);
+                    if (addZ) {
+                        const float4 z = Sm.ldf4(aZ + b * 65536 + zrow_off(vrow, 16 * hk + 8 * half + e));
+                        a[4 * e] += z.x;
+                        a[4 * e + 1] += z.y;
+                        a[4 * e + 2] += z.z;
+                        a[4 * e + 3] += z.w;
+                    }
+                    w[16 * half + 2 * e] = pack_half2(a[4 * e], a[4 * e + 1]);
+                    w[16 * half + 2 * e + 1] = pack_half2(a[4 * e + 2], a[4 * e + 3]);
                 }
+                if (ranksum && j + 1 == ncomp && okj) put_half(half, a);
             }
             tmem_st32(taddr(sA(0), 32 * qw, 32 * hk), w);
             tmem_wait_st();
@@ -1144,7 +1182,7 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
         }
         __syncthreads();
         tc_fence_after();
-        if (loader && j + 2 < seg) issue_TZ(j + 2);  // into the buffers step j just released
+        if (loader && j + 2 < ncomp) issue_TZ(j + 2);  // into the buffers step j just released
     }
     if (loader) {  // first copies of the segment's chunks
         for (int c = 0; c < 2 && c < nch; ++c) issue_M(c);
@@ -1193,7 +1231,8 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
                     }
                 }
             } else {
-                put_summary(a0, a1);
+                put_half(0, a0);
+                put_half(1, a1);
             }
         }
     } else if (warp < 12) {
@@ -1472,30 +1511,35 @@ cudaError_t launch_prefill_chunked(const PrefillParams& p, void* workspace, size
 // Context parallelism: every sequence's tokens are split over `world` ranks in
 // consecutive ranges (every range at least one token; the composition is
 // exact for any split, whole chunks only keep the chunks full); rank r holds
-// range r of every sequence.  Phase 0 on
-// every rank builds its records and its carry summary (rank 0: its outputs,
-// final state and end state; rank r >= 1: the affine map (T_r, Z_r) of its
-// range), written at rank r's block of the summary region.  The caller then
-// all-gathers that region (world blocks of num_seqs x 8 x 96 KiB); phase 1 on
-// rank r >= 1 composes rank 0's end state through ranks 1 .. r-1 and runs its
-// range with outputs (its new_state: the state after its range).
-// Segments per rank for the context-parallel carry: every rank's pass A (2
-// CTAs per segment and unit) in one wave, and at most 16 segments over all
-// ranks (the last rank's CTAs compose up to world x segments - 2 summaries).
-// A function of (N, world) only, so that every rank lays out the same slots.
-static int cp_segments(int64_t N, int world) {
+// range r of every sequence, cut into up to 8 segments.  Phase 0 on every
+// rank builds its records, its segments' summaries (pass A) and their
+// composition, the rank's carry summary (rank 0: the state at the end of its
+// range; rank r >= 1: the affine map (T_r, Z_r) of its range), written at
+// rank r's block of the summary region.  The caller then all-gathers that
+// region (world blocks of num_seqs x 8 x 96 KiB); phase 1 (pass C) runs every
+// segment with outputs from the composition of what precedes it (new_state:
+// the state after the rank's range).
+//
+// Segments per rank for the context-parallel carry: up to 8, with a rank's
+// pass A (2 CTAs per segment and unit) in one wave.  A function of N only,
+// so that every rank lays out the same slots.
+static int cp_segments(int64_t N) {
     const int64_t units = N * kHV;
     int q = 8;
-    while (q > 1 && (2 * units * q > kSmCount || static_cast<int64_t>(world) * q > 16)) --q;
+    while (q > 1 && 2 * units * q > kSmCount) --q;
     return q;
 }
 
+// Context-parallel workspace: the single-GPU records, then the all-gathered
+// rank summaries (world x N x 8 slots, at an offset that depends on the local
+// token count and N only), then the rank's own segment summaries.
 WsLayout cp_layout(int64_t T, int64_t N, int world) {
     WsLayout L = ws_layout(T, N);
     L.cp_world = world;
-    L.seg_slots = cp_segments(N, world);
-    L.off_seg = L.total;
-    L.total_seg = L.total + static_cast<int64_t>(world) * L.seg_slots * N * kHV * kSegSlotBytes;
+    L.seg_slots = cp_segments(N);
+    L.off_gather = L.total;
+    L.off_seg = L.off_gather + static_cast<int64_t>(world) * N * kHV * kSegSlotBytes;
+    L.total_seg = L.off_seg + L.seg_slots * N * kHV * kSegSlotBytes;
     return L;
 }
 
@@ -1508,11 +1552,17 @@ cudaError_t launch_prefill_cp(const PrefillParams& p, void* workspace, size_t wo
     if (units == 0 || units > 0x7fffffffLL / (2 * q)) return units == 0 ? cudaSuccess : cudaErrorInvalidValue;
     CUtensorMap tmO;
     cudaError_t e;
-    if (phase == 0) {  // records, then pass A: Sum0 (rank 0), T and Z of the rank's segments
+    if (phase == 0) {  // records; pass A: Sum0 (rank 0), T and Z of the rank's segments; the rank summary
         int sms = 148;
         if ((e = chunk_records(p, ws, L, &tmO, &sms, stream)) != cudaSuccess) return e;
-        return launch_dependent(gdn_chunk_carry_kernel, static_cast<unsigned>(units * (rank == 0 ? 2 * q - 1 : 2 * q)),
-                                kCarryThreads, kCaSmem, stream, p, ws, L, 4, rank, tmO);
+        if ((e = launch_dependent(gdn_chunk_carry_kernel,
+                                  static_cast<unsigned>(units * (rank == 0 ? 2 * q - 1 : 2 * q)), kCarryThreads,
+                                  kCaSmem, stream, p, ws, L, 4, rank, tmO)) != cudaSuccess)
+            return e;
+        // with one segment pass A wrote the rank summary itself; the last rank's is never read
+        if (q == 1 || rank + 1 == world) return cudaSuccess;
+        return launch_dependent(gdn_chunk_carry_kernel, static_cast<unsigned>(rank == 0 ? units : 2 * units),
+                                kCarryThreads, kCaSmem, stream, p, ws, L, 6, rank, tmO);
     }
     // pass C over the rank's segments, with outputs
     memset(&tmO, 0, sizeof(tmO));

@@ -194,10 +194,10 @@ def cp_workspace_bytes(local_tokens: int, num_seqs: int, world: int) -> int:
 
 
 def cp_summary_region(workspace: torch.Tensor, local_tokens: int, num_seqs: int, world: int) -> torch.Tensor:
-    """The uint8 view of the workspace that the ranks all-gather (world equal
-    blocks): its tail, from the summary offset to the workspace size."""
+    """The uint8 view of the workspace that the ranks all-gather: world blocks
+    of num_seqs x 8 x 98304 bytes (one carry summary per rank and unit)."""
     off = int(_capi.load().gdn_prefill_cp_summary_offset(int(local_tokens), int(num_seqs)))
-    return workspace[off: cp_workspace_bytes(local_tokens, num_seqs, world)]
+    return workspace[off: off + world * num_seqs * HV * 98304]
 
 
 def cp_launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state, workspace,
@@ -228,8 +228,8 @@ def launch_gdn_context_parallel(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens
     rank's tokens (ranges as ``cp_split`` makes them) with its local
     cu_seqlens; ``state`` is read on rank 0.  Returns ``(output, new_state)``:
     this rank's outputs, and the state after its range (on the last rank, the
-    final state).  One all-gather carries the ranks' carry summaries (per rank,
-    num_seqs x 768 KiB per segment, up to 8 segments per rank)."""
+    final state).  One all-gather of ``world x num_seqs x 768 KiB`` carries
+    the ranks' carry summaries."""
     import torch.distributed as dist
 
     rank, world = dist.get_rank(group), dist.get_world_size(group)

@@ -33,16 +33,17 @@ def test_cp_split_covers_every_token(pkg):
 
 @pytest.mark.parametrize("num_seqs,world", [(1, 1), (1, 2), (1, 8), (2, 2), (3, 4), (20, 2), (1, 64)])
 def test_cp_summary_region_layout(pkg, num_seqs, world):
-    """The all-gathered region is the workspace's tail: world equal blocks of
-    whole 98304-byte slots, 1 to 8 segments per rank, at most 16 in all."""
+    """The all-gathered region (world blocks of one 98304-byte slot per unit)
+    sits at an offset every rank computes alike, followed by the rank's own
+    1 to 8 segment slots per unit (one wave of pass A)."""
     for local_tokens in (1, 5000, 70000):
         need = pkg.prefill.cp_workspace_bytes(local_tokens, num_seqs, world)
         off = int(pkg._capi.load().gdn_prefill_cp_summary_offset(local_tokens, num_seqs))
-        slot_block = world * num_seqs * 8 * 98304
-        assert 0 < off < need and (need - off) % slot_block == 0
-        segs = (need - off) // slot_block
-        assert 1 <= segs <= 8 and (segs == 1 or world * segs <= 16)
-        assert 2 * num_seqs * 8 * segs <= 148 or segs == 1
+        units = num_seqs * 8
+        gathered = world * units * 98304
+        assert 0 < off and off + gathered < need and (need - off - gathered) % (units * 98304) == 0
+        segs = (need - off - gathered) // (units * 98304)
+        assert 1 <= segs <= 8 and (2 * units * segs <= 148 or segs == 1)
 
 
 def _local(inp, idx, loc, dev):
@@ -55,8 +56,9 @@ def _local(inp, idx, loc, dev):
 @pytest.mark.parametrize("world,lengths", [
     (2, [1000, 2048, 300]), (3, [5000]), (4, [700, 1500, 260, 4096]),
     (2, [130]),            # rank 0 holds one chunk: 7 of its 8 segments are empty (identity summaries)
-    (8, [9000]),           # 8 ranks x 2 segments: the last rank composes 14 summaries
+    (8, [9000]),           # 8 ranks x 8 segments of 2-3 chunks
     (2, [40000]),          # 8 segments of ~39 chunks per rank
+    (3, [3000] * 10),      # one segment per rank: pass A writes the rank summaries itself
 ])
 def test_cp_emulated_matches_single_gpu(pkg, cuda_dev, world, lengths):
     inp = pkg.inputs.make_prefill_inputs(lengths, seed=world * 17 + len(lengths), with_state=True)
