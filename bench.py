@@ -541,8 +541,11 @@ def run_ours(args):
         pf["config4b_shard_8x8192"] = bench_prefill(pkg, device, [8192] * 8, 2000 + rank, 3,
                                                     min(args.warmup, 3), ws, flush)
     if wl in ("all", "prefill_cp") and ws > 1:
-        pf["context_parallel_1x131072"] = bench_prefill_cp(pkg, device, rank, ws, [131072], 5,
-                                                           min(args.warmup, 3), flush)
+        try:  # a ride-along: an error (the same on every rank) is reported, not fatal to the line
+            pf["context_parallel_1x131072"] = bench_prefill_cp(pkg, device, rank, ws, [131072], 5,
+                                                               min(args.warmup, 3), flush)
+        except (ValueError, RuntimeError) as e:
+            pf["context_parallel_1x131072"] = {"error": str(e)[:300]}
     if pf:
         line["prefill"] = pf
     if rank == 0 and ws == 1 and not args.skip_cpu and wl == "all":
