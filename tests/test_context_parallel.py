@@ -46,6 +46,96 @@ def test_cp_summary_region_layout(pkg, num_seqs, world):
         assert 1 <= segs <= 8 and (2 * units * segs <= 148 or segs == 1)
 
 
+def _range_summary(inp, s, t0, t1):
+    """The affine carry map of tokens [t0, t1) of sequence s, per v-head, in
+    float64: S -> S T + Z on the k-last state, where each token applies
+    S -> g S (I - beta k k^T) + beta v k^T (oracle prefill: decay, then the
+    delta-rule update).  Returns (T, Z), each [8, 128, 128]."""
+    import math
+
+    A_log, dt_bias = inp.A_log.double(), inp.dt_bias.double()
+    T = torch.eye(128, dtype=torch.float64).repeat(8, 1, 1)
+    Z = torch.zeros(8, 128, 128, dtype=torch.float64)
+    for t in range(t0, t1):
+        for h in range(8):
+            x = float(inp.a[t, h]) + float(dt_bias[h])
+            sp = x if x > 20 else math.log1p(math.exp(x))
+            g = math.exp(-math.exp(float(A_log[h])) * sp)
+            beta = 1.0 / (1.0 + math.exp(-float(inp.b[t, h])))
+            kk = inp.k[t, h // 2].double()
+            for M, add in ((T[h], None), (Z[h], inp.v[t, h].double())):
+                M.copy_(g * (M - beta * torch.outer(M @ kk, kk)))
+                if add is not None:
+                    M.add_(beta * torch.outer(add, kk))
+    return T, Z
+
+
+def _gloo_cp_worker(rank, world, port, q):
+    """One context-parallel rank on the CPU: summary of its ranges, all-gather
+    over gloo, composition into its start states, the oracle over its tokens."""
+    import datetime
+
+    import torch.distributed as dist
+
+    sys.path.insert(0, str(REPO))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import __graft_entry__
+    from oracle import oracle
+
+    pkg = __graft_entry__.load_package()
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    try:
+        lengths = [150, 200]
+        inp = pkg.inputs.make_prefill_inputs(lengths, seed=91, with_state=True)
+        cu = [int(x) for x in inp.cu_seqlens]
+        parts = pkg.prefill.cp_split(inp.cu_seqlens, world)
+        idx, loc = parts[rank]
+        mine = torch.stack([torch.stack(_range_summary(inp, s, int(idx[loc[s]]), int(idx[loc[s + 1] - 1]) + 1))
+                            for s in range(len(lengths))])  # [N, 2, 8, 128, 128]
+        got = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(got, mine)
+        start = inp.state.double().clone()  # composition of ranks 0 .. rank-1 onto the initial state
+        for r in range(rank):
+            start = start @ got[r][:, 0] + got[r][:, 1]
+        pick = lambda t: t[idx]  # noqa: E731
+        out, ns = oracle.prefill(pick(inp.q), pick(inp.k), pick(inp.v), start.float(), inp.A_log, pick(inp.a),
+                                 inp.dt_bias, pick(inp.b), loc, inp.scale, threads=1)
+        ref_out, ref_ns = oracle.prefill(*inp.args(), threads=1)
+        err_o = (out.float() - ref_out[idx].float()).abs().max().item()
+        ok = err_o < 1e-2
+        if rank == world - 1:
+            ok = ok and state_rel_err(ns, ref_ns) < 1e-3
+        q.put(("ok", rank, ok, err_o, cu))
+    except Exception as e:  # reported to the test through the queue
+        q.put(("error", rank, f"{type(e).__name__}: {e}"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_cp_protocol_gloo_world2():
+    """The context-parallel decomposition over two gloo ranks on the CPU: per
+    rank affine summaries, an all-gather, composed start states, and each
+    rank's tokens run from its start state match one run over the whole
+    batch (outputs 1e-2, final state 1e-3)."""
+    import multiprocessing as mp
+    import socket
+
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_gloo_cp_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=240) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    assert all(r[0] == "ok" and r[2] for r in res), res
+
+
 def _local(inp, idx, loc, dev):
     pick = lambda t: t[idx].contiguous().to(dev)  # noqa: E731
     return (pick(inp.q), pick(inp.k), pick(inp.v), inp.A_log.to(dev), pick(inp.a), inp.dt_bias.to(dev),
