@@ -149,7 +149,7 @@ def _local(inp, idx, loc, dev):
     (8, [9000]),           # 8 ranks x 8 segments of 2-3 chunks
     (2, [40000]),          # 8 segments of ~39 chunks per rank
     (3, [3000] * 10),      # one segment per rank: pass A writes the rank summaries itself
-])
+], ids=["w2-ragged3", "w3-5000", "w4-ragged4", "w2-130", "w8-9000", "w2-40000", "w3-10x3000"])
 def test_cp_emulated_matches_single_gpu(pkg, cuda_dev, world, lengths):
     inp = pkg.inputs.make_prefill_inputs(lengths, seed=world * 17 + len(lengths), with_state=True)
     ref_out, ref_ns = pkg.prefill.launch_gdn(*inp.to(cuda_dev).args())
