@@ -62,7 +62,8 @@ __host__ __device__ inline int64_t align_up(int64_t x, int64_t a) { return (x + 
 // Workspace: header, per-sequence record bases, the chunk table and the
 // per-record, per-head operand arrays (every array 1024-byte aligned).
 // Segmented carry summaries (few-sequence problems only): per sequence, v-head
-// and segment, T (f16 image, 32 KiB) and Z (fp32 rows, 64 KiB).
+// and segment, T (f16 image, 32 KiB) and Z (f16 rows, 32 KiB), or a state
+// (Sum0's, or a rank's end state: fp32 rows, 64 KiB) at the Z offset.
 constexpr int kSegMaxP = 8;
 constexpr int kSegSlotBytes = 98304;
 
@@ -883,6 +884,9 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
 // fp32 [128 v][128 k] matrices of the segment summaries: row v is 512 bytes,
 // its 16-byte chunk c (k = 4c .. 4c+3) stored at position c ^ (v & 31)
 __device__ __forceinline__ uint32_t zrow_off(int v, int c) { return v * 512 + ((c ^ (v & 31)) << 4); }
+// f16 [128 v][128 k] segment Z summaries: row v is 256 bytes, its 16-byte
+// chunk c (k = 8c .. 8c+7) stored at position c ^ (v & 15)
+__device__ __forceinline__ uint32_t zh_off(int v, int c) { return v * 256 + ((c ^ (v & 15)) << 4); }
 
 __global__ void __launch_bounds__(kCarryThreads, 1)
     gdn_chunk_carry_kernel(const PrefillParams p, uint8_t* __restrict__ ws, const WsLayout L, const int mode,
@@ -902,7 +906,9 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     const uint32_t imgReady = bar0 + 88;
     auto oFree = [&](int b) { return bar0 + 96 + 8 * b; };    // 2
     const uint32_t drain = bar0 + 112;
-    const uint32_t proLoad = bar0 + 136, proMma = bar0 + 152;  // pass C's composition steps (proLoad x 2)
+    // composition steps: three load barriers (bar0 + 136, + 144, + 160) and the MMA's
+    auto proLoad = [&](int b) { return b == 2 ? bar0 + 160 : bar0 + 136 + 8 * b; };
+    const uint32_t proMma = bar0 + 152;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kCaSmall + 128);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1002,7 +1008,11 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
 #pragma unroll
             for (int e = 0; e < 4; ++e)
                 *reinterpret_cast<uint4*>(sum_base + h16(vrow, 64 * hk + 32 * half + 8 * e, kD)) = f16x8(x + 8 * e);
-        } else {  // Z (or a state): fp32 rows
+        } else if (role == kRoleSumZ) {  // Z as f16 rows
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                *reinterpret_cast<uint4*>(sum_base + 32768 + zh_off(vrow, 8 * hk + 4 * half + e)) = f16x8(x + 8 * e);
+        } else {  // a state (Sum0; a rank's end state): fp32 rows
 #pragma unroll
             for (int e = 0; e < 8; ++e)
                 *reinterpret_cast<float4*>(sum_base + 32768 + zrow_off(vrow, 16 * hk + 8 * half + e)) =
@@ -1053,8 +1063,7 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
         mbar_init(imgReady, 8);
         for (int b = 0; b < 2; ++b) mbar_init(oFree(b), 4);
         mbar_init(drain, 1);
-        mbar_init(proLoad, 1);
-        mbar_init(proLoad + 8, 1);
+        for (int b = 0; b < 3; ++b) mbar_init(proLoad(b), 1);
         mbar_init(proMma, 1);
         fence_mbar_init();
     }
@@ -1126,28 +1135,29 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     }
     __syncthreads();
     // composition: S <- S T_i + Z_i for i < ncomp (in place in A operand 0).
-    // T_i (f16 MN-major [128 j][128 k]) goes to M buffer i & 1 and Z_i (fp32
-    // rows) to a 64 KiB Z buffer over the [K' | U^T] and Qt^T space, both
-    // double-buffered and loaded one step ahead.  A rank summary stores its
+    // T_i (f16 MN-major [128 j][128 k]) and Z_i (f16 rows) go to 32 KiB
+    // buffers i % 3 over the chunk operand space (T at 0 / 32 / 64 KiB, Z at
+    // 96 / 128 / 160 KiB), loaded two steps ahead.  A rank summary stores its
     // last step's fp32 result.
     bool ok = true;
-    const uint32_t aZ = aKU;  // 2 x 64 KiB (the [K' | U^T] and Qt^T buffers, 144 KiB)
+    auto aT = [&](int b) { return aM + b * 32768; };
+    auto aZ = [&](int b) { return aM + 98304 + b * 32768; };
     auto issue_TZ = [&](int i) {
-        const int b = i & 1;
+        const int b = i % 3;
         const uint8_t* src = comp_slot(i);
-        mbar_expect_tx(proLoad + 8 * b, addZ ? 32768 + 65536 : 32768);
-        bulk_g2s(aM + b * 32768, src, 32768, proLoad + 8 * b);
-        if (addZ) bulk_g2s(aZ + b * 65536, src + 32768, 65536, proLoad + 8 * b);
+        mbar_expect_tx(proLoad(b), addZ ? 65536 : 32768);
+        bulk_g2s(aT(b), src, 32768, proLoad(b));
+        if (addZ) bulk_g2s(aZ(b), src + 32768, 32768, proLoad(b));
     };
     if (loader)
-        for (int i = 0; i < ncomp && i < 2; ++i) issue_TZ(i);
+        for (int i = 0; i < ncomp && i < 3; ++i) issue_TZ(i);
     for (int j = 0; j < ncomp; ++j) {
-        const int b = j & 1;
-        const uint32_t ldbar = proLoad + 8 * b, ldpar = (j >> 1) & 1;
+        const int b = j % 3;
+        const uint32_t ldbar = proLoad(b), ldpar = (j / 3) & 1;
         if (issuer) {
             ok = mbar_wait(ldbar, ldpar) && ok;
             tc_fence_after();
-            mma_ct_ta<kF16, true, kD, kD, kD>(accS(0), sA(0), aM + b * 32768, false);
+            mma_ct_ta<kF16, true, kD, kD, kD>(accS(0), sA(0), aT(b), false);
             mma_commit(proMma);
         }
         if (warp < 8) {
@@ -1161,15 +1171,17 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
                 float a[32];
                 tmem_ld32(taddr(accS(0), 32 * qw, 64 * hk + 32 * half), a);
                 tmem_wait_ld();
+                if (addZ) {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        float z[8];
+                        h16x8_to_f32(Sm.ld16(aZ(b) + zh_off(vrow, 8 * hk + 4 * half + e)), z);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) a[8 * e + i] += z[i];
+                    }
+                }
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
-                    if (addZ) {
-                        const float4 z = Sm.ldf4(aZ + b * 65536 + zrow_off(vrow, 16 * hk + 8 * half + e));
-                        a[4 * e] += z.x;
-                        a[4 * e + 1] += z.y;
-                        a[4 * e + 2] += z.z;
-                        a[4 * e + 3] += z.w;
-                    }
                     w[16 * half + 2 * e] = pack_half2(a[4 * e], a[4 * e + 1]);
                     w[16 * half + 2 * e + 1] = pack_half2(a[4 * e + 2], a[4 * e + 3]);
                 }
@@ -1182,7 +1194,7 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
         }
         __syncthreads();
         tc_fence_after();
-        if (loader && j + 2 < ncomp) issue_TZ(j + 2);  // into the buffers step j just released
+        if (loader && j + 3 < ncomp) issue_TZ(j + 3);  // into the buffers step j just released
     }
     if (loader) {  // first copies of the segment's chunks
         for (int c = 0; c < 2 && c < nch; ++c) issue_M(c);
