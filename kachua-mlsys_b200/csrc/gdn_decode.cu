@@ -22,6 +22,7 @@
 //   * the new state is written once with streaming (evict-first) stores.
 // Each thread reads all of its state elements before writing any of them and
 // no other thread touches them, so state == new_state (in place) is safe.
+#include <type_traits>
 #include "gdn_common.cuh"
 
 namespace gdn {
@@ -69,14 +70,19 @@ __global__ void __launch_bounds__(128) gdn_decode_kernel(const DecodeParams p) {
     const uint16_t* src16 = reinterpret_cast<const uint16_t*>(p.state) + bh * (kD * kD) + 4 * sub;
     uint16_t* dst16 = reinterpret_cast<uint16_t*>(p.new_state) + bh * (kD * kD) + 4 * sub;
 
-    // 1. issue every state load first (kPasses x 4 x 16 B per thread; 8 B with a bf16 state)
-    float4 s[kPasses][4];
+    // 1. issue every state load first (kPasses x 4 x 16 B per thread; 8 B with a
+    // bf16 state, kept as raw bf16 words until its row is processed)
+    using Raw = typename std::conditional<BF16S, uint2, float4>::type;
+    Raw raw[kPasses][4];
 #pragma unroll
     for (int ps = 0; ps < kPasses; ++ps) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-            s[ps][j] = BF16S ? bf16x4_to_float4(ld_stream_u2(src16 + (row0 + 4 * ps) * kD + 32 * j))
-                             : ld_stream_f4(src + (row0 + 4 * ps) * kD + 32 * j);
+        for (int j = 0; j < 4; ++j) {
+            if constexpr (BF16S)
+                raw[ps][j] = ld_stream_u2(src16 + (row0 + 4 * ps) * kD + 32 * j);
+            else
+                raw[ps][j] = ld_stream_f4(src + (row0 + 4 * ps) * kD + 32 * j);
+        }
     }
 
     // 2. per-head vectors and gates (small, L2/L1 resident)
@@ -107,13 +113,19 @@ __global__ void __launch_bounds__(128) gdn_decode_kernel(const DecodeParams p) {
     // 3. per row: two dot products, the rank-1 update, the output
 #pragma unroll
     for (int ps = 0; ps < kPasses; ++ps) {
+        float4 s[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            if constexpr (BF16S)
+                s[j] = bf16x4_to_float4(raw[ps][j]);
+            else
+                s[j] = raw[ps][j];
+        }
         float ks = 0.f, qs = 0.f;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            ks += s[ps][j].x * k4[j].x + s[ps][j].y * k4[j].y + s[ps][j].z * k4[j].z +
-                  s[ps][j].w * k4[j].w;
-            qs += s[ps][j].x * q4[j].x + s[ps][j].y * q4[j].y + s[ps][j].z * q4[j].z +
-                  s[ps][j].w * q4[j].w;
+            ks += s[j].x * k4[j].x + s[j].y * k4[j].y + s[j].z * k4[j].z + s[j].w * k4[j].w;
+            qs += s[j].x * q4[j].x + s[j].y * q4[j].y + s[j].z * q4[j].z + s[j].w * q4[j].w;
         }
 #pragma unroll
         for (int off = 1; off < 8; off <<= 1) {
@@ -124,10 +136,10 @@ __global__ void __launch_bounds__(128) gdn_decode_kernel(const DecodeParams p) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             float4 o;
-            o.x = fmaf(g, s[ps][j].x, delta * k4[j].x);
-            o.y = fmaf(g, s[ps][j].y, delta * k4[j].y);
-            o.z = fmaf(g, s[ps][j].z, delta * k4[j].z);
-            o.w = fmaf(g, s[ps][j].w, delta * k4[j].w);
+            o.x = fmaf(g, s[j].x, delta * k4[j].x);
+            o.y = fmaf(g, s[j].y, delta * k4[j].y);
+            o.z = fmaf(g, s[j].z, delta * k4[j].z);
+            o.w = fmaf(g, s[j].w, delta * k4[j].w);
             if (BF16S)
                 st_stream_u2(dst16 + (row0 + 4 * ps) * kD + 32 * j, float4_to_bf16x4(o));
             else
@@ -141,7 +153,9 @@ __global__ void __launch_bounds__(128) gdn_decode_kernel(const DecodeParams p) {
 }
 
 // Rows per warp: the largest tile that still yields >= 2 CTAs per SM.
-static int pick_rows_per_warp(int64_t heads) {
+static int pick_rows_per_warp(int64_t heads, bool bf16_state) {
+    // a bf16 row is half as many bytes: 32 rows keep the fp32 kernel's 256 B of loads in flight per thread
+    if (bf16_state && heads >= 2 * kSmCount) return 32;
     if (heads * (kD / 64) >= 2 * kSmCount) return 16;
     if (heads * (kD / 32) >= 2 * kSmCount) return 8;
     return 4;
@@ -150,6 +164,9 @@ static int pick_rows_per_warp(int64_t heads) {
 template <bool BF16S>
 static void launch_decode_rpw(int rpw, unsigned grid, const DecodeParams& p, cudaStream_t stream) {
     switch (rpw) {
+        case 32:  // bf16 state only
+            if constexpr (BF16S) gdn_decode_kernel<32, true><<<grid, 128, 0, stream>>>(p);
+            break;
         case 16: gdn_decode_kernel<16, BF16S><<<grid, 128, 0, stream>>>(p); break;
         case 8: gdn_decode_kernel<8, BF16S><<<grid, 128, 0, stream>>>(p); break;
         default: gdn_decode_kernel<4, BF16S><<<grid, 128, 0, stream>>>(p); break;
@@ -160,7 +177,7 @@ static void launch_decode_rpw(int rpw, unsigned grid, const DecodeParams& p, cud
 cudaError_t launch_decode(const DecodeParams& p, cudaStream_t stream, bool bf16_state = false) {
     if (p.batch == 0) return cudaSuccess;
     const int64_t heads = p.batch * p.hv;
-    const int rpw = pick_rows_per_warp(heads);
+    const int rpw = pick_rows_per_warp(heads, bf16_state);
     const int64_t grid = heads * (kD / (4 * rpw));
     if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
     if (bf16_state)
