@@ -48,11 +48,20 @@ STATE_BYTES_PER_SEQ = 8 * 128 * 128 * 4
 # q, k, v, a, b, output (bf16), plus A_log/dt_bias once per launch
 DECODE_BYTES_PER_SEQ = 2 * STATE_BYTES_PER_SEQ + 1024 + 1024 + 2048 + 16 + 16 + 2048
 DECODE_BYTES_FIXED = 64
+# prefill algorithmic bytes per token (q, k, v, a, b read; output written) and
+# the fixed chunked-WY FLOP count per token at C = 64 over 8 v-heads
+PREFILL_BYTES_PER_TOKEN = 1024 + 1024 + 2048 + 16 + 16 + 2048
+PREFILL_FLOPS_PER_TOKEN = 1452715.0
+# ncu DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one prefill
+# call, summed over its kernels, per leg; filled from the captures summarised
+# under profiles/ (None: not captured for the current kernels)
+PREFILL_NCU_TRAFFIC: dict = {}
 L2_FLUSH_BYTES = 256 << 20
 SLEEP_CYCLES = 200_000  # ~100 us GPU spin before each timed step (outside the events)
-# dram__bytes_read.sum + dram__bytes_write.sum of one gdn_decode_kernel launch at
-# B=256, from one ncu capture (profiles/gdn_decode_kernel_B256.md)
-DECODE_NCU_TRAFFIC = 214475264
+# dram__bytes_read.sum + dram__bytes_write.sum per gdn_decode_kernel launch at
+# B=256 in steady state: the mean over launches 21-23 of this file's own
+# back-to-back decode loop under ncu --cache-control none (profiles/)
+DECODE_NCU_TRAFFIC = 265710763
 
 
 def load_peaks():
@@ -219,7 +228,8 @@ def cpu_prefill_baseline(pkg, budget_s: float):
             "sample": f"{n} x prefill of 8 sequences x 512 tokens through oracle/gdn_oracle.c"}
 
 
-def bench_prefill(pkg, device, lengths, seed, steps, warmup, ws, flush, with_state=True, gather=True):
+def bench_prefill(pkg, device, lengths, seed, steps, warmup, ws, flush, peaks, with_state=True,
+                  traffic=None):
     inp = pkg.inputs.make_prefill_inputs(lengths, seed=seed, with_state=with_state).to(device)
     T, N = inp.total_tokens, inp.num_seqs
     out = torch.empty((T, 8, 128), dtype=torch.bfloat16, device=device)
@@ -232,18 +242,39 @@ def bench_prefill(pkg, device, lengths, seed, steps, warmup, ws, flush, with_sta
 
     times, _ = time_steps(step, steps, warmup, ws, device, flush)
     ms = max_over_ranks(sorted(times)[len(times) // 2], ws, device)  # median of the per-call times
-    flops_per_tok = 1452715.0  # fixed chunked-WY count at C=64, 8 heads
-    bytes_ = 6176 * T + 524288 * N * (2 if with_state else 1)
+    bytes_ = PREFILL_BYTES_PER_TOKEN * T + STATE_BYTES_PER_SEQ * N * (2 if with_state else 1)
     res = {"tokens": T, "seqs": N, "ms": ms, "tokens_per_s": T * ws / (ms * 1e-3),
-           "algo_bytes": bytes_, "algo_flops": flops_per_tok * T,
-           "hbm_gbs": bytes_ / (ms * 1e-3) / 1e9, "tflops": flops_per_tok * T / (ms * 1e-3) / 1e12}
-    if ws > 1 and gather:
-        res.update(time_gather(pkg, out, ns, ws, device))
-        res["tokens_per_s_with_gather"] = T * ws / ((ms + res["gather_ms"]) * 1e-3)
+           "algo_bytes": bytes_, "algo_flops": PREFILL_FLOPS_PER_TOKEN * T,
+           "hbm_gbs": bytes_ / (ms * 1e-3) / 1e9, "tflops": PREFILL_FLOPS_PER_TOKEN * T / (ms * 1e-3) / 1e12,
+           "roofline": prefill_roofline(bytes_, PREFILL_FLOPS_PER_TOKEN * T, ms, peaks, traffic)}
     return res
 
 
-def bench_prefill_cp(pkg, device, rank, ws, lengths, steps, warmup, flush):
+def prefill_roofline(algo_bytes: float, algo_flops: float, ms: float, peaks: dict, traffic=None) -> dict:
+    """Roofline of one prefill call: the bound is whichever of the HBM floor
+    (algorithmic bytes / measured copy bandwidth) and the tensor floor
+    (algorithmic FLOPs / measured bf16 burst GEMM rate) is longer; both
+    fractions are given.  ``traffic``: ncu DRAM bytes of one call (summed over
+    its kernels), or None where no capture covers the leg."""
+    t_hbm = algo_bytes / (peaks["hbm_gbs"] * 1e9)
+    t_tc = algo_flops / (peaks["bf16_tflops"] * 1e12)
+    hbm_gbs = algo_bytes / (ms * 1e-3) / 1e9
+    tflops = algo_flops / (ms * 1e-3) / 1e12
+    if t_hbm >= t_tc:
+        r = {"bound": "hbm", "achieved": round(hbm_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+             "frac": round(hbm_gbs / peaks["hbm_gbs"], 4)}
+    else:
+        r = {"bound": "tensor", "achieved": round(tflops, 1), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+             "frac": round(tflops / peaks["bf16_tflops"], 4)}
+    r.update({"hbm_frac": round(hbm_gbs / peaks["hbm_gbs"], 4),
+              "tensor_frac": round(tflops / peaks["bf16_tflops"], 4),
+              "floor_us": round(max(t_hbm, t_tc) * 1e6, 2), "traffic": traffic,
+              "algo": "bytes = 6176 x tokens + 512 KiB x seqs x (1 + initial state); "
+                      "flops = 1,452,715 x tokens (chunked WY at C = 64, 8 v-heads)"})
+    return r
+
+
+def bench_prefill_cp(pkg, device, rank, ws, lengths, steps, warmup, flush, peaks):
     """Context-parallel prefill (N > 1): the SAME batch split by token range
     over the ranks (strong scaling), timed per call as max over ranks and
     compared with one GPU running the whole batch."""
@@ -265,7 +296,7 @@ def bench_prefill_cp(pkg, device, rank, ws, lengths, steps, warmup, flush):
     times, _ = time_steps(step, steps, warmup, ws, device, flush)
     ms = max_over_ranks(sorted(times)[len(times) // 2], ws, device)
     del q, k, v, a, b, out, wsb
-    one = bench_prefill(pkg, device, lengths, 7, steps, warmup, ws, flush, gather=False)  # every rank: all of it
+    one = bench_prefill(pkg, device, lengths, 7, steps, warmup, ws, flush, peaks)  # every rank: all of it
     T = int(full.cu_seqlens[-1])
     return {"lengths": lengths, "tokens": T, "ms": ms, "tokens_per_s": T / (ms * 1e-3),
             "one_gpu_ms": one["ms"], "speedup_vs_one_gpu": one["ms"] / ms,
@@ -343,23 +374,256 @@ def bench_decode_heads(pkg, device, flush, batch=64, hqk=16, hv=32, steps=20):
             "state_gbs": round(state_bytes / (ms * 1e-3) / 1e9, 1)}
 
 
-def time_gather(pkg, out, ns, ws, device):
+def device_decode_inputs(pkg, batch: int, seed: int, device):
+    """Config-0 distributions drawn directly on the GPU (fast at 2 GiB of
+    state; the timing does not depend on the values)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def qk(shape):
+        x = torch.randn(shape, generator=g, device=device)
+        return (x / x.norm(dim=-1, keepdim=True).clamp_min(1e-6)).to(torch.bfloat16)
+
+    q, k = qk((batch, 1, 4, 128)), qk((batch, 1, 4, 128))
+    v = torch.randn((batch, 1, 8, 128), generator=g, device=device).to(torch.bfloat16)
+    a = torch.randn((batch, 1, 8), generator=g, device=device).to(torch.bfloat16)
+    b = torch.randn((batch, 1, 8), generator=g, device=device).to(torch.bfloat16)
+    A_log = torch.log(torch.empty(8, device=device).uniform_(1.0, 16.0, generator=g))
+    dt_bias = torch.zeros(8, device=device)
+    state = torch.randn((batch, 8, 128, 128), generator=g, device=device) * 0.02
+    return pkg.inputs.DecodeInputs(q, k, v, state, A_log, a, dt_bias, b)
+
+
+def device_prefill_inputs(pkg, lengths, seed: int, device, with_state=True):
+    """Config-2 distributions for packed sequences, drawn on the GPU."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    T, N = int(sum(lengths)), len(lengths)
+
+    def qk(shape):
+        x = torch.randn(shape, generator=g, device=device)
+        return (x / x.norm(dim=-1, keepdim=True).clamp_min(1e-6)).to(torch.bfloat16)
+
+    q, k = qk((T, 4, 128)), qk((T, 4, 128))
+    v = torch.randn((T, 8, 128), generator=g, device=device).to(torch.bfloat16)
+    a = torch.randn((T, 8), generator=g, device=device).to(torch.bfloat16)
+    b = torch.randn((T, 8), generator=g, device=device).to(torch.bfloat16)
+    A_log = torch.log(torch.empty(8, device=device).uniform_(1.0, 16.0, generator=g))
+    dt_bias = torch.zeros(8, device=device)
+    state = torch.randn((N, 8, 128, 128), generator=g, device=device) * 0.02 if with_state else None
+    cu = pkg.inputs.cu_seqlens_from_lengths(lengths).to(device)
+    return pkg.inputs.PrefillInputs(q, k, v, state, A_log, a, dt_bias, b, cu)
+
+
+def time_gather_median(pkg, tensors, shapes, ws, device, reps=3):
     """The final gather of every rank's outputs and states to rank 0 (NCCL
-    point-to-point over NVLink), timed on the device, max over ranks."""
+    point-to-point, every peer's transfers concurrent), device time of the
+    median of ``reps`` gathers, max over ranks."""
     rank = int(os.environ.get("RANK", "0"))
-    shapes = [[tuple(out.shape), tuple(ns.shape)]] * ws  # equal shards in this bench
+    if ws == 1:
+        return {"gather_ms": 0.0, "gather_bytes": 0}
     stream = torch.cuda.current_stream(device)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    pkg.shard.gather_to_rank0([out, ns], shapes, rank, ws)  # warm the P2P paths
+    pkg.shard.gather_to_rank0(tensors, shapes, rank, ws)  # warm the P2P paths
     torch.cuda.synchronize(device)
-    barrier(ws)
-    e0.record(stream)
-    pkg.shard.gather_to_rank0([out, ns], shapes, rank, ws)
-    e1.record(stream)
-    torch.cuda.synchronize(device)
-    ms = max_over_ranks(e0.elapsed_time(e1), ws, device)
-    moved = (ws - 1) * (out.numel() * 2 + ns.numel() * 4)
+    times = []
+    for _ in range(reps):
+        barrier(ws)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        got = pkg.shard.gather_to_rank0(tensors, shapes, rank, ws)
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        del got
+        times.append(e0.elapsed_time(e1))
+    ms = max_over_ranks(sorted(times)[len(times) // 2], ws, device)
+    moved = sum(math.prod(s) * t.element_size() for r in range(1, ws) for s, t in zip(shapes[r], tensors))
     return {"gather_ms": ms, "gather_bytes": moved, "gather_gbs_into_rank0": moved / (ms * 1e-3) / 1e9}
+
+
+def bench_config4a(pkg, device, rank, ws, steps, warmup, peaks):
+    """BASELINE config 4a: decode of B = 4096 sequences (2 GiB of fp32 state)
+    split by sequence over the ranks -- the FIXED global problem (strong
+    scaling).  Steps run back to back over two state buffers (read one, write
+    the other; each rank's slice is larger than L2 up to N = 8), max over
+    ranks; then the gather of outputs and states to rank 0."""
+    B = 4096
+    lo, hi = pkg.shard.decode_slice(B, ws, rank)
+    inp = device_decode_inputs(pkg, hi - lo, 4000 + rank, device)
+    out = torch.empty((hi - lo, 8, 128), dtype=torch.bfloat16, device=device)
+    st = [inp.state, torch.empty_like(inp.state)]
+    launches = [pkg.decode.PreparedLaunch(inp.q, inp.k, inp.v, st[i], inp.A_log, inp.a, inp.dt_bias, inp.b,
+                                          inp.scale, out, st[1 - i]) for i in range(2)]
+    it = [0]
+
+    def step():
+        launches[it[0] % 2]()
+        it[0] += 1
+
+    ms_local, _ = time_back_to_back(step, steps, warmup, ws, device)
+    ms = max_over_ranks(ms_local, ws, device)
+    shapes = [[(pkg.shard.decode_slice(B, ws, r)[1] - pkg.shard.decode_slice(B, ws, r)[0], 8, 128),
+               (pkg.shard.decode_slice(B, ws, r)[1] - pkg.shard.decode_slice(B, ws, r)[0], 8, 128, 128)]
+              for r in range(ws)]
+    gat = time_gather_median(pkg, [out, st[it[0] % 2]], shapes, ws, device)
+    state_bytes = 2 * B * STATE_BYTES_PER_SEQ
+    algo_local = DECODE_BYTES_PER_SEQ * (hi - lo) + DECODE_BYTES_FIXED
+    achieved = algo_local / (ms_local * 1e-3) / 1e9
+    res = {"batch": B, "per_rank": hi - lo, "ms": ms, "us_per_step": round(ms * 1e3, 2),
+           "state_gbs": state_bytes / (ms * 1e-3) / 1e9,
+           "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                        "frac": round(achieved / peaks["hbm_gbs"], 4), "per": "rank (rank-local step time)"},
+           **gat}
+    res["ms_with_gather"] = ms + res["gather_ms"]
+    res["state_gbs_with_gather"] = state_bytes / (res["ms_with_gather"] * 1e-3) / 1e9
+    return res
+
+
+def bench_config4b(pkg, device, rank, ws, steps, warmup, flush, peaks):
+    """BASELINE config 4b: prefill of 64 sequences x 8192 tokens (524,288
+    tokens) split by sequence over the ranks (LPT plan) -- the FIXED global
+    problem (strong scaling).  Per-call device time with the L2 flushed
+    before each call, median, max over ranks; then the gather of outputs and
+    states to rank 0."""
+    lengths = [8192] * 64
+    plan = pkg.shard.plan_prefill(lengths, ws)
+    mine = [lengths[s] for s in plan[rank]]
+    res = {"seqs": 64, "tokens": sum(lengths), "per_rank_seqs": len(mine)}
+    if mine:
+        inp = device_prefill_inputs(pkg, mine, 5000 + rank, device)
+        T, N = inp.total_tokens, inp.num_seqs
+        out = torch.empty((T, 8, 128), dtype=torch.bfloat16, device=device)
+        ns = torch.empty((N, 8, 128, 128), dtype=torch.float32, device=device)
+        wsb = torch.empty(max(pkg.prefill.workspace_bytes(T, N), 1), dtype=torch.uint8, device=device)
+
+        def step():
+            pkg.prefill.launch_gdn(*inp.args(), output=out, new_state=ns, workspace=wsb)
+    else:  # more ranks than sequences: this rank idles but joins every collective
+        out = torch.empty((0, 8, 128), dtype=torch.bfloat16, device=device)
+        ns = torch.empty((0, 8, 128, 128), dtype=torch.float32, device=device)
+
+        def step():
+            pass
+    times, _ = time_steps(step, steps, warmup, ws, device, flush)
+    ms_local = sorted(times)[len(times) // 2]
+    ms = max_over_ranks(ms_local, ws, device)
+    shapes = [[(sum(lengths[s] for s in plan[r]), 8, 128), (len(plan[r]), 8, 128, 128)] for r in range(ws)]
+    gat = time_gather_median(pkg, [out, ns], shapes, ws, device)
+    T_all = sum(lengths)
+    tok_local = sum(mine)
+    flops = PREFILL_FLOPS_PER_TOKEN * tok_local
+    bytes_ = PREFILL_BYTES_PER_TOKEN * tok_local + STATE_BYTES_PER_SEQ * len(mine) * 2
+    roof = prefill_roofline(bytes_, flops, ms_local, peaks, PREFILL_NCU_TRAFFIC.get("config4b_rank8x8192")
+                            if len(mine) == 8 else None) if mine else None
+    if roof:
+        roof["per"] = "rank (its shard's bytes and FLOPs over its own call time)"
+    res.update({"ms": ms, "tokens_per_s": T_all / (ms * 1e-3), "roofline": roof, **gat})
+    res["ms_with_gather"] = ms + res["gather_ms"]
+    res["tokens_per_s_with_gather"] = T_all / (res["ms_with_gather"] * 1e-3)
+    return res
+
+
+def split_total(total: int, parts: int, seed: int) -> list[int]:
+    """``parts`` positive lengths summing to ``total`` (seeded random cut points):
+    the published prefill shapes give only T and N."""
+    gen = torch.Generator().manual_seed(seed)
+    cuts = sorted(torch.randperm(total - 1, generator=gen)[: parts - 1].add(1).tolist())
+    edges = [0] + cuts + [total]
+    return [edges[i + 1] - edges[i] for i in range(parts)]
+
+
+# Prefill shapes timed against the reference's Triton kernel: BASELINE configs 2
+# and 3, a config-4b shard, and the reference's published shapes (T, N) from
+# its experiment log (lengths within a batch are not published: seeded split).
+REF_PREFILL_SHAPES = {
+    "config2_T4096_N1": ([4096], False),
+    "config3_32seq": (None, True),
+    "pub_T1377_N1": ([1377], True),
+    "pub_T2107_N1": ([2107], True),
+    "pub_T5709_N2": (split_total(5709, 2, 5709), True),
+    "pub_T8192_N34": (split_total(8192, 34, 8192), True),
+    "config4b_shard_8x8192": ([8192] * 8, True),
+}
+REF_DECODE_BATCHES = (1, 8, 16, 32, 64, 256)
+
+
+def agreement(ro, rns, out, ns) -> dict:
+    """How the reference kernel's output and state compare with this project's
+    (which the GPU tests hold to the oracle): max abs output difference, the
+    norm-wise state difference, and whether both are within the reference
+    harness's own tolerance (allclose atol = rtol = 1e-2, bench_fi_timing.py:241-242)."""
+    od = float((ro.float() - out.float()).abs().max())
+    sd = float((rns - ns).abs().max() / ns.abs().max().clamp_min(1e-30))
+    ok = bool(torch.allclose(ro.float(), out.float(), atol=1e-2, rtol=1e-2)) and sd <= 1e-2
+    return {"out_max_abs_diff": od, "state_rel_diff": sd, "ref_within_tolerance": ok}
+
+
+def bench_reference_gpu(pkg, device, flush, steps=20):
+    """The reference's own GPU kernels beside this project's, same box, same
+    run, same timing (per-call CUDA events, L2 flushed by a 256 MiB read
+    before every call, median): the reference decode extension
+    (``kernel.cu::launch_gdn``) at the contest's batch sizes and config 1, and
+    the reference Triton prefill (``kernel.py::launch_gdn``) on configs 2/3 and
+    its published shapes.  Each reference output is compared with this
+    project's output for the same inputs (this project's is oracle-checked by
+    the GPU tests)."""
+    sys.path.insert(0, str(REPO / "baseline"))
+    import reference_gpu as rg
+
+    why = rg.missing()
+    if why:
+        return {"unavailable": why}
+    res = {"how": "median per-call device time (CUDA events), L2 flushed before each call; "
+                  "ratio = reference time / this project's time (>1: this project is faster)"}
+    dec = {}
+    ext = rg.decode_ext()
+    for B in REF_DECODE_BATCHES:
+        inp = pkg.inputs.make_decode_inputs(B, seed=500 + B).to(device)
+        out, ns = torch.empty((B, 8, 128), dtype=torch.bfloat16, device=device), torch.empty_like(inp.state)
+        ro, rns = torch.empty_like(out), torch.empty_like(inp.state)
+        ours = pkg.decode.PreparedLaunch(inp.q, inp.k, inp.v, inp.state, inp.A_log, inp.a, inp.dt_bias, inp.b,
+                                         inp.scale, out, ns)
+
+        def ref():
+            ext.launch_gdn(inp.q, inp.k, inp.v, inp.state, inp.A_log, inp.a, inp.dt_bias, inp.b, inp.scale, ro, rns)
+
+        t_ref, _ = time_steps(ref, steps, 3, 1, device, flush)
+        t_our, _ = time_steps(ours, steps, 3, 1, device, flush)
+        mr, mo = sorted(t_ref)[steps // 2] * 1e3, sorted(t_our)[steps // 2] * 1e3
+        dec[str(B)] = {"ref_us": round(mr, 2), "ours_us": round(mo, 2), "ratio": round(mr / mo, 3),
+                       **agreement(ro, rns, out, ns)}
+    res["decode_vs_reference_cuda"] = dec
+    pre = {}
+    try:
+        mod = rg.prefill_module()
+    except Exception as e:  # noqa: BLE001  (reported in the line, not fatal)
+        res["prefill_vs_reference_triton"] = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+        return res
+    for name, (lengths, with_state) in REF_PREFILL_SHAPES.items():
+        lengths = lengths if lengths is not None else pkg.inputs.config3_lengths(0)
+        inp = pkg.inputs.make_prefill_inputs(lengths, seed=len(lengths) * 7 + 1, with_state=with_state).to(device)
+        T, N = inp.total_tokens, inp.num_seqs
+        out = torch.empty((T, 8, 128), dtype=torch.bfloat16, device=device)
+        ns = torch.empty((N, 8, 128, 128), dtype=torch.float32, device=device)
+        ro, rns = torch.empty_like(out), torch.empty_like(ns)
+        wsb = torch.empty(max(pkg.prefill.workspace_bytes(T, N), 1), dtype=torch.uint8, device=device)
+
+        def ours():
+            pkg.prefill.launch_gdn(*inp.args(), output=out, new_state=ns, workspace=wsb)
+
+        def ref():
+            mod.launch_gdn(inp.q, inp.k, inp.v, inp.state, inp.A_log, inp.a, inp.dt_bias, inp.b, inp.cu_seqlens,
+                           inp.scale, ro, rns)
+
+        try:
+            t_ref, _ = time_steps(ref, steps, 3, 1, device, flush)
+        except Exception as e:  # noqa: BLE001
+            pre[name] = {"tokens": T, "seqs": N, "error": f"{type(e).__name__}: {str(e)[:200]}"}
+            continue
+        t_our, _ = time_steps(ours, steps, 3, 1, device, flush)
+        mr, mo = sorted(t_ref)[steps // 2] * 1e3, sorted(t_our)[steps // 2] * 1e3
+        pre[name] = {"tokens": T, "seqs": N, "ref_us": round(mr, 1), "ours_us": round(mo, 1),
+                     "ref_mtok_s": round(T / mr, 2), "ours_mtok_s": round(T / mo, 2), "ratio": round(mr / mo, 3),
+                     **agreement(ro, rns, out, ns)}
+    res["prefill_vs_reference_triton"] = pre
+    return res
 
 
 def soak(step, seconds: float, device, flush):
@@ -427,7 +691,8 @@ def bench_decode(pkg, args, device, ws, rank, flush, peaks, peaks_kind):
                                      else "fallback 6650 GB/s"),
                      "traffic": DECODE_NCU_TRAFFIC, "algo_bytes_per_launch": algo_bytes,
                      "kernel": "gdn_decode_kernel<16>",
-                     "traffic_source": "profiles/gdn_decode_kernel_B256.md (ncu dram bytes, one launch)"},
+                     "traffic_source": "ncu dram bytes read + write, steady state: mean of launches 21-23 of "
+                                       "--workload decode (profiles/gdn_decode_kernel_B256.md)"},
     }
     if not args.skip_e2e:
         stager = pkg.decode.HostStager(B, device)
@@ -532,22 +797,31 @@ def run_ours(args):
     psteps = max(3, args.steps // 2)
     if ws == 1:
         if wl in ("all", "prefill2"):
-            pf["config2_T4096_N1"] = bench_prefill(pkg, device, [4096], 0, psteps, args.warmup, ws, flush,
-                                                   with_state=False)
+            pf["config2_T4096_N1"] = bench_prefill(pkg, device, [4096], 0, psteps, args.warmup, ws, flush, peaks,
+                                                   with_state=False, traffic=PREFILL_NCU_TRAFFIC.get("config2"))
         if wl in ("all", "prefill3"):
             pf["config3_32seq"] = bench_prefill(pkg, device, pkg.inputs.config3_lengths(0), 0, psteps,
-                                                args.warmup, ws, flush)
-    if wl in ("all", "prefill4b") and (ws > 1 or wl == "prefill4b"):
-        pf["config4b_shard_8x8192"] = bench_prefill(pkg, device, [8192] * 8, 2000 + rank, 3,
-                                                    min(args.warmup, 3), ws, flush)
+                                                args.warmup, ws, flush, peaks, traffic=PREFILL_NCU_TRAFFIC.get("config3"))
     if wl in ("all", "prefill_cp") and ws > 1:
         try:  # a ride-along: an error (the same on every rank) is reported, not fatal to the line
             pf["context_parallel_1x131072"] = bench_prefill_cp(pkg, device, rank, ws, [131072], 5,
-                                                               min(args.warmup, 3), flush)
+                                                               min(args.warmup, 3), flush, peaks)
         except (ValueError, RuntimeError) as e:
             pf["context_parallel_1x131072"] = {"error": str(e)[:300]}
     if pf:
         line["prefill"] = pf
+    if wl in ("all", "config4"):
+        # BASELINE config 4 as written: the fixed global problem split over the N ranks
+        line["config4a"] = bench_config4a(pkg, device, rank, ws, args.steps, args.warmup, peaks)
+        torch.cuda.empty_cache()
+        line["config4b"] = bench_config4b(pkg, device, rank, ws, max(3, args.steps // 2), min(args.warmup, 3),
+                                          flush, peaks)
+        torch.cuda.empty_cache()
+    if ws == 1 and wl in ("all", "reference_gpu") and not args.skip_ref_gpu:
+        try:  # a ride-along: an error is reported in the line, not fatal to it
+            line["reference_gpu"] = bench_reference_gpu(pkg, device, flush)
+        except Exception as e:  # noqa: BLE001
+            line["reference_gpu"] = {"error": f"{type(e).__name__}: {str(e)[:300]}"}
     if rank == 0 and ws == 1 and not args.skip_cpu and wl == "all":
         line["cpu_baseline"] = cpu_decode_baseline(pkg, args.cpu_budget)
         line["cpu_baseline_prefill"] = cpu_prefill_baseline(pkg, args.cpu_budget)
@@ -605,10 +879,12 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds per CPU-baseline sample")
     ap.add_argument("--workload", default="all",
-                    choices=["all", "decode", "prefill2", "prefill3", "prefill4b", "prefill_cp"],
+                    choices=["all", "decode", "prefill2", "prefill3", "config4", "prefill_cp", "reference_gpu"],
                     help="all = the JSON line the driver reads; the others time one workload")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline (profiling runs)")
     ap.add_argument("--skip-e2e", action="store_true", help="omit the host-buffer e2e leg")
+    ap.add_argument("--skip-ref-gpu", action="store_true",
+                    help="omit the reference's own GPU kernels (baseline/_ref) timed beside ours")
     ap.add_argument("--soak", type=float, default=1.0,
                     help="seconds of untimed steps under the clock sampler before timing")
     args = ap.parse_args()

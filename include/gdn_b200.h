@@ -230,10 +230,17 @@ int gdn_prefill_cp_launch(const GdnPrefillArgs* args, void* workspace, size_t wo
  * Same arguments and results as gdn_prefill_launch, but the scratch is a
  * fixed array of GDN_NOALLOC_SCRATCH_BYTES inside this library, held on every
  * GPU that loads the library until the process exits; nothing is allocated.
- * Limit: unless args->path is GDN_PREFILL_PATH_RECURRENT, problems with
- * gdn_prefill_workspace_size(T, N) > GDN_NOALLOC_SCRATCH_BYTES are rejected
- * with GDN_ERR_WORKSPACE before anything runs (about 2,600 tokens for one
- * sequence with the current workspace layout).  The first call on each device
+ * Limit: problems that run on the token-recurrent kernel (args->path
+ * GDN_PREFILL_PATH_RECURRENT, or AUTO with total_tokens / num_seqs <= 24)
+ * need no scratch and are always accepted.  Every other problem needs the
+ * chunked kernels' per-chunk operand records in the array -- the minimum
+ * workspace that gdn_prefill_launch also accepts, (ceil(T / 64) + N) x
+ * 768 KiB plus small tables -- and is rejected with GDN_ERR_WORKSPACE before
+ * anything runs when that exceeds GDN_NOALLOC_SCRATCH_BYTES (about 2,600
+ * tokens of one sequence).  The segmented carry for few long sequences also
+ * needs its summaries and runs only when the whole
+ * gdn_prefill_workspace_size(T, N) fits; otherwise the single-pass carry
+ * gives the same results more slowly.  The first call on each device
  * looks up the array's device address; make it before any stream capture.
  * All calls on a device share the array: calls whose kernels overlap on the
  * GPU (different streams or host threads) race and must be serialised. */

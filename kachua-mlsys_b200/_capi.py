@@ -38,7 +38,7 @@ EXPORTED_SYMBOLS = (
     "gdn_prefill_cp_summary_offset",
     "gdn_prefill_cp_launch",
 )
-ABI_VERSION = 7
+ABI_VERSION = 8
 PATH_AUTO, PATH_RECURRENT, PATH_CHUNKED, PATH_SEGMENTED = 0, 1, 2, 3
 MMA_KIND_BF16, MMA_KIND_TF32, MMA_KIND_F16 = 1, 2, 3
 MMA_A_MN, MMA_B_MN, MMA_D_LANE16, MMA_A_TMEM = 1, 2, 4, 8

@@ -37,7 +37,7 @@ static float resolve_scale(float s) { return s == 0.0f ? 1.0f / sqrtf((float)kD)
 
 using namespace gdn;
 
-extern "C" int gdn_abi_version(void) { return 7; }
+extern "C" int gdn_abi_version(void) { return 8; }
 
 extern "C" const char* gdn_status_string(int status) {
     switch (status) {
@@ -199,7 +199,10 @@ extern "C" int gdn_prefill_launch(const GdnPrefillArgs* a, void* workspace, size
                                   void* stream) {
     PrefillParams p;
     if (int rc = prefill_setup(a, p, kHQK, kHV)) return rc;
-    const size_t need = chunked_workspace_min_bytes(a->total_tokens, a->num_seqs);
+    // the token-recurrent path needs no workspace; the chunked paths need the records
+    const size_t need = prefill_path_is_recurrent(a->path, a->total_tokens, a->num_seqs)
+                            ? 0
+                            : chunked_workspace_min_bytes(a->total_tokens, a->num_seqs);
     if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 256)))
         return GDN_ERR_WORKSPACE;
 

@@ -1585,11 +1585,16 @@ cudaError_t launch_prefill_cp(const PrefillParams& p, void* workspace, size_t wo
     return cudaGetLastError();
 }
 
+// True when `path` resolves to the token-recurrent kernel for this problem
+// (which needs no workspace): asked for, or AUTO with a short mean length.
+bool prefill_path_is_recurrent(int path, int64_t total_tokens, int64_t num_seqs) {
+    const int64_t avg = total_tokens / (num_seqs > 0 ? num_seqs : 1);
+    return path == kPathRecurrent || (path == kPathAuto && avg <= kRecurrentMaxAvgLen);
+}
+
 cudaError_t launch_prefill(const PrefillParams& p, int path, void* workspace, size_t workspace_bytes,
                            cudaStream_t stream) {
-    const int64_t avg = p.total_tokens / (p.num_seqs > 0 ? p.num_seqs : 1);
-    const bool recurrent = path == kPathRecurrent || (path == kPathAuto && avg <= kRecurrentMaxAvgLen);
-    if (recurrent) {
+    if (prefill_path_is_recurrent(path, p.total_tokens, p.num_seqs)) {
         cudaError_t e = launch_prefill_zero_uncovered(p, stream);
         return e != cudaSuccess ? e : launch_prefill_recurrent(p, stream);
     }

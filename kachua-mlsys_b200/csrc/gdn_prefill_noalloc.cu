@@ -51,8 +51,11 @@ static int noalloc_scratch(void** out) {
 extern "C" int gdn_prefill_launch_noalloc(const GdnPrefillArgs* args, void* stream) {
     if (args == nullptr) return GDN_ERR_NULL_POINTER;
     if (args->total_tokens < 0 || args->num_seqs < 0) return GDN_ERR_BAD_SIZE;
-    // the token-recurrent path needs no scratch; every other path must fit the array
-    if (args->path != GDN_PREFILL_PATH_RECURRENT &&
+    // The token-recurrent path (asked for, or chosen by AUTO for short mean
+    // lengths) needs no scratch; the chunked paths need at least their operand
+    // records in the array.  The segmented carry also needs its summaries and
+    // runs only when gdn_prefill_workspace_size(T, N) fits as a whole.
+    if (!gdn::prefill_path_is_recurrent(args->path, args->total_tokens, args->num_seqs) &&
         gdn::chunked_workspace_min_bytes(args->total_tokens, args->num_seqs) > gdn::kNoAllocScratchBytes)
         return GDN_ERR_WORKSPACE;
     void* scratch = nullptr;

@@ -87,9 +87,10 @@ def plan_prefill_shards(cu_seqlens: torch.Tensor, world: int) -> list[PrefillSha
 
 
 def shard_prefill_inputs(inp: PrefillInputs, shard: PrefillShard) -> PrefillInputs:
-    """The packed inputs of one shard (host tensors; copy to the rank's GPU)."""
-    ti = shard.token_index
-    sidx = torch.tensor(shard.seqs, dtype=torch.int64)
+    """The packed inputs of one shard, on the device of ``inp`` (host tensors
+    are then copied to the rank's GPU; device tensors are gathered in place)."""
+    ti = shard.token_index.to(inp.q.device)
+    sidx = torch.tensor(shard.seqs, dtype=torch.int64, device=inp.q.device)
     state = None if inp.state is None else inp.state.index_select(0, sidx)
     return PrefillInputs(inp.q.index_select(0, ti), inp.k.index_select(0, ti), inp.v.index_select(0, ti),
                          state, inp.A_log, inp.a.index_select(0, ti), inp.dt_bias,
@@ -117,23 +118,33 @@ def gather_to_rank0(tensors: list[torch.Tensor], shapes_per_rank: list[list[tupl
     ``shapes_per_rank[r]`` lists the shapes rank r contributes (known to every
     rank from the shared plan, so no size exchange is needed).  Returns, on
     rank 0, a list over ranks of the received tensor lists; elsewhere None.
-    Every rank issues the same collective sequence (sends pair with rank 0's
-    receives in rank order).
+
+    Rank 0 posts the receives from every peer at once and the peers their
+    sends, as one batch (``batch_isend_irecv``: one NCCL group), so the
+    transfers from all peers run concurrently over NVLink into rank 0 rather
+    than one peer and one tensor at a time.  Empty tensors are skipped on both
+    sides (their shapes are known everywhere).  The call returns once this
+    rank's transfers are complete on its current stream.
     """
     import torch.distributed as dist
 
+    ops = []
+    got = None
     if rank != 0:
         for t in tensors:
             if t.numel():
-                dist.send(t.contiguous(), dst=0, group=group)
-        return None
-    got = [list(tensors)]
-    for r in range(1, world):
-        recv = []
-        for shp, like in zip(shapes_per_rank[r], tensors):
-            buf = torch.empty(shp, dtype=like.dtype, device=like.device)
-            if buf.numel():
-                dist.recv(buf, src=r, group=group)
-            recv.append(buf)
-        got.append(recv)
+                ops.append(dist.P2POp(dist.isend, t.contiguous(), 0, group))
+    else:
+        got = [list(tensors)]
+        for r in range(1, world):
+            recv = []
+            for shp, like in zip(shapes_per_rank[r], tensors):
+                buf = torch.empty(shp, dtype=like.dtype, device=like.device)
+                if buf.numel():
+                    ops.append(dist.P2POp(dist.irecv, buf, r, group))
+                recv.append(buf)
+            got.append(recv)
+    if ops:
+        for w in dist.batch_isend_irecv(ops):
+            w.wait()
     return got

@@ -99,11 +99,11 @@ def _worker(rank, world, port, mode, q):
                 pass
 
 
-def _run_world(mode):
+def _run_world(mode, world=2):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, mode, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -114,8 +114,11 @@ def _run_world(mode):
     return [q.get(timeout=5) for _ in range(q.qsize())] if not q.empty() else []
 
 
-def test_gloo_gather_world2_matches_unsharded():
-    res = _run_world("ok")
+@pytest.mark.parametrize("world", [2, 3])
+def test_gloo_gather_matches_unsharded(world):
+    """Rank 0 receives every peer's outputs and states in one batch of
+    concurrent receives and merges them into the unsharded result."""
+    res = _run_world("ok", world)
     assert ("ok", True) in res, res
 
 
