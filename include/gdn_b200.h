@@ -270,6 +270,9 @@ int gdn_abi_version(void);
 #define GDN_MMA_B_MN_MAJOR 2  /* B operand image stored MN-major */
 #define GDN_MMA_D_LANE16 4    /* accumulator at TMEM lane 16 (M = 64 only) */
 #define GDN_MMA_A_TMEM 8      /* A operand read from TMEM (16-bit kinds, M = 128, K-major) */
+#define GDN_MMA_NO_COMPLETION 16  /* diagnostic: issue no MMA and never signal its completion barrier, so the
+                                     kernel's bounded wait expires: it records GDN_ERR_DEVICE_TIMEOUT in the
+                                     device status word, releases its TMEM and returns; D is not written */
 
 /* D[M x N] = A[M x K] . B[N x K]^T on one CTA through the same shared-memory
  * operand images, tcgen05 descriptors and TMEM read-back the prefill kernels
@@ -277,8 +280,9 @@ int gdn_abi_version(void);
  * row-major in global memory (bf16 for BF16, fp16 for F16, fp32 for TF32 --
  * rounded to tf32); D fp32 row-major.  M in {64, 128}; N a multiple of 16 in [16, 256];
  * K in {64, 128}; an MN-major operand's M (or N) must fill whole 128-byte
- * rows (multiples of 64 bf16 / 32 tf32).  No reference counterpart: a
- * self-test of the tensor-core layer. */
+ * rows (multiples of 64 bf16 / 32 tf32).  With GDN_MMA_NO_COMPLETION the call
+ * exercises the device-side timeout instead (about 10 ms of GPU time).  No
+ * reference counterpart: a self-test of the tensor-core layer. */
 int gdn_mma_selftest(int kind, int flags, int M, int N, int K, const void* A, const void* B, float* D,
                      void* stream);
 

@@ -41,7 +41,7 @@ EXPORTED_SYMBOLS = (
 ABI_VERSION = 8
 PATH_AUTO, PATH_RECURRENT, PATH_CHUNKED, PATH_SEGMENTED = 0, 1, 2, 3
 MMA_KIND_BF16, MMA_KIND_TF32, MMA_KIND_F16 = 1, 2, 3
-MMA_A_MN, MMA_B_MN, MMA_D_LANE16, MMA_A_TMEM = 1, 2, 4, 8
+MMA_A_MN, MMA_B_MN, MMA_D_LANE16, MMA_A_TMEM, MMA_NO_COMPLETION = 1, 2, 4, 8, 16
 
 
 class GdnDecodeArgs(ctypes.Structure):

@@ -97,16 +97,16 @@ extern "C" int gdn_decode_launch_bf16_state(const GdnDecodeArgs* a, void* stream
     return decode_launch(a, stream, true);
 }
 
-// T tokens per sequence (speculative or multi-token decode): the recurrence
-// runs token by token on the state rows held in registers, so the state is
-// read and written once per call, as in a single-token step.  This is the
-// token-recurrent prefill kernel with every sequence T tokens long.
+// T tokens per sequence (speculative or multi-token decode): the state rows
+// stay in registers for all T updates, so the state is read and written once
+// per call, as in a single-token step (gdn_decode_tokens_kernel).
 static int decode_tokens(const GdnDecodeArgs* a, int64_t tokens, void* stream, int hqk, int hv) {
     if (a == nullptr) return GDN_ERR_NULL_POINTER;
     if (tokens < 1 || a->batch < 0) return GDN_ERR_BAD_SIZE;
     if (tokens == 1) return decode_launch(a, stream, false, hqk, hv);
     if (a->batch == 0) return GDN_OK;
-    if (a->batch > (int64_t(1) << 40) / tokens || a->batch * hv * (kD / 16) > 0x7fffffffLL) return GDN_ERR_BAD_SIZE;
+    if (tokens > 0x7fffffffLL || a->batch > (int64_t(1) << 40) / tokens || a->batch * hv * (kD / 16) > 0x7fffffffLL)
+        return GDN_ERR_BAD_SIZE;
     if (!a->q || !a->k || !a->v || !a->state || !a->A_log || !a->a || !a->dt_bias || !a->b || !a->output ||
         !a->new_state)
         return GDN_ERR_NULL_POINTER;
@@ -115,26 +115,24 @@ static int decode_tokens(const GdnDecodeArgs* a, int64_t tokens, void* stream, i
         !aligned(a->A_log, 4) || !aligned(a->dt_bias, 4))
         return GDN_ERR_MISALIGNED;
     if (int rc = check_device()) return rc;
-    PrefillParams p;
+    DecodeParams p;
     p.q = static_cast<const uint16_t*>(a->q);
     p.k = static_cast<const uint16_t*>(a->k);
     p.v = static_cast<const uint16_t*>(a->v);
-    p.state = a->state;  // may equal new_state: each CTA reads its rows before writing them
+    p.state = a->state;  // may equal new_state: every tile is read before it is written, by one CTA
     p.A_log = a->A_log;
     p.a = static_cast<const uint16_t*>(a->a);
     p.dt_bias = a->dt_bias;
     p.b = static_cast<const uint16_t*>(a->b);
-    p.cu_seqlens = nullptr;
-    p.cu_is_int64 = 0;
-    p.total_tokens = a->batch * tokens;
-    p.num_seqs = a->batch;
-    p.scale = resolve_scale(a->scale);
     p.out = static_cast<uint16_t*>(a->output);
     p.new_state = a->new_state;
-    p.uniform_len = tokens;
+    p.batch = a->batch;
+    p.scale = resolve_scale(a->scale);
     p.hqk = hqk;
     p.hv = hv;
-    return launch_prefill_recurrent(p, static_cast<cudaStream_t>(stream)) == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
+    return launch_decode_tokens(p, static_cast<int>(tokens), static_cast<cudaStream_t>(stream)) == cudaSuccess
+               ? GDN_OK
+               : GDN_ERR_CUDA;
 }
 
 extern "C" int gdn_decode_launch_tokens(const GdnDecodeArgs* a, int64_t tokens, void* stream) {
@@ -271,7 +269,7 @@ extern "C" int gdn_mma_selftest(int kind, int flags, int M, int N, int K, const 
     if (!A || !B || !D) return GDN_ERR_NULL_POINTER;
     if ((kind != GDN_MMA_KIND_BF16 && kind != GDN_MMA_KIND_TF32 && kind != GDN_MMA_KIND_F16) || (M != 64 && M != 128) ||
         N < 16 ||
-        N > 256 || N % 16 != 0 || (K != 64 && K != 128) || (flags & ~15) != 0 || ((flags & 4) && M != 64) ||
+        N > 256 || N % 16 != 0 || (K != 64 && K != 128) || (flags & ~31) != 0 || ((flags & 4) && M != 64) ||
         ((flags & 8) && (M != 128 || kind == GDN_MMA_KIND_TF32 || (flags & 1))))
         return GDN_ERR_BAD_SIZE;
     // an MN-major image fills whole 128-byte rows: its M (or N) extent must be too

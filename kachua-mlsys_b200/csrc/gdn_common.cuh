@@ -11,7 +11,11 @@ constexpr int kHQK = 4;        // q/k heads
 constexpr int kHV = 8;         // v heads
 constexpr int kGva = kHV / kHQK;
 constexpr int kD = 128;        // head dim (K and V)
-constexpr int kSmCount = 148;  // B200
+// SM count of a B200.  Only layouts that must not depend on the device (the
+// prefill workspace's segment slots, the context-parallel segment count that
+// every rank must agree on) use this constant; launch shapes use
+// device_sm_count().
+constexpr int kSmCount = 148;
 
 // Per-device status word (OR of GDN_ERR_DEVICE_* bits); one copy per device
 // that loads the library.  The library is a single translation unit
@@ -19,6 +23,21 @@ constexpr int kSmCount = 148;  // B200
 __device__ int g_status = 0;
 
 __device__ __forceinline__ void record_status(int bits) { atomicOr(&g_status, bits); }
+
+// Multiprocessor count of the current device, queried once per device (falls
+// back to kSmCount if the query fails).
+static int device_sm_count() {
+    static int cached[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return kSmCount;
+    if (cached[dev] == 0) {
+        int n = 0;
+        cached[dev] = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0
+                          ? n
+                          : kSmCount;
+    }
+    return cached[dev];
+}
 
 __device__ __forceinline__ float bf16_bits_to_float(uint16_t h) {
     return __uint_as_float(static_cast<uint32_t>(h) << 16);

@@ -1472,7 +1472,7 @@ static cudaError_t chunk_records(const PrefillParams& p, uint8_t* ws, const WsLa
         if ((e = token_tensor_map(&tmV, p.v, kHV, p.total_tokens)) != cudaSuccess) return e;
         if ((e = token_tensor_map(tmO, p.out, kHV, p.total_tokens)) != cudaSuccess) return e;
     }
-    gdn_chunk_table_kernel<<<kSmCount, 1024, 0, stream>>>(p, ws, L);
+    gdn_chunk_table_kernel<<<device_sm_count(), 1024, 0, stream>>>(p, ws, L);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if ((e = set_smem(gdn_chunk_prepare_kernel, kPrSmem)) != cudaSuccess) return e;
     int dev = 0, sms = 148;
@@ -1683,7 +1683,10 @@ __global__ void __launch_bounds__(128, 1)
         __syncthreads();
         tc_fence_after();
     }
-    if (tid == 0 && a_tmem) {
+    if (flags & 16) {
+        // diagnostic: nothing is issued and nothing signals `bar`, so the
+        // bounded wait below expires and the kernel unwinds (status bit, TMEM freed)
+    } else if (tid == 0 && a_tmem) {
         const uint32_t id = idesc(kind == kBF16 ? kBF16 : kF16, 128, N, false, b_mn);
         const uint32_t b = smem_u32(sB);
         for (int s = 0; s < K / 16; ++s) {

@@ -198,7 +198,7 @@ cudaError_t launch_prefill_recurrent(const PrefillParams& p, cudaStream_t stream
 }
 
 cudaError_t launch_prefill_zero_uncovered(const PrefillParams& p, cudaStream_t stream) {
-    gdn_prefill_zero_uncovered_kernel<<<kSmCount, 256, 0, stream>>>(p);
+    gdn_prefill_zero_uncovered_kernel<<<device_sm_count(), 256, 0, stream>>>(p);
     return cudaGetLastError();
 }
 

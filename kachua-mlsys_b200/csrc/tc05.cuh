@@ -73,13 +73,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait: gives up after `limit` polls (each poll may itself block for a
-// hardware-defined slice) and returns false; callers record a status bit and
-// unwind instead of hanging the GPU.
-constexpr uint32_t kWaitLimit = 1u << 24;
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait: gives up once kWaitLimitNs of wall time (the %globaltimer
+// clock) have passed since the first unsuccessful poll, or after
+// kWaitMaxPolls polls, whichever comes first, and returns false; callers
+// record GDN_ERR_DEVICE_TIMEOUT and unwind instead of hanging the GPU.  Every
+// wait in this library is on an mbarrier of the waiting CTA, completed by
+// that CTA's own copies or MMAs (never by another CTA or GPU), which take
+// microseconds; 10 ms is far above any legitimate wait.
+constexpr uint64_t kWaitLimitNs = 10ull * 1000 * 1000;
+constexpr uint32_t kWaitMaxPolls = 1u << 26;
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-    for (uint32_t i = 0; i < kWaitLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 0; i < kWaitMaxPolls; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 15) == 15 && globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    }
     return false;
 }
 

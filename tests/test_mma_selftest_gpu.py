@@ -92,3 +92,34 @@ def test_mma_selftest_rejects_partial_mn_rows(pkg, cuda_dev):
     buf = torch.zeros(64 * 128, device=cuda_dev)
     p = ctypes.c_void_p(buf.data_ptr())
     assert lib.gdn_mma_selftest(pkg._capi.MMA_KIND_BF16, 2, 64, 32, 128, p, p, p, None) == 2
+
+
+def test_bounded_wait_expires_and_unwinds(pkg, cuda_dev):
+    """A wait that nothing completes: the self-test kernel issues no MMA and
+    never signals its barrier (GDN_MMA_NO_COMPLETION).  The kernel's bounded
+    wait gives up after its time limit (10 ms), the device status word reports
+    GDN_ERR_DEVICE_TIMEOUT, D stays unwritten, and the kernel releases its TMEM:
+    the context stays usable and the next tensor-core kernel runs normally."""
+    import time
+
+    C = pkg._capi
+    lib = C.load()
+    pkg.prefill.device_status(cuda_dev)  # clear
+    A = torch.randn(128, 64).to(torch.bfloat16).to(cuda_dev)
+    B = torch.randn(64, 64).to(torch.bfloat16).to(cuda_dev)
+    D = torch.full((128, 64), float("nan"), device=cuda_dev)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    t0 = time.perf_counter()
+    assert lib.gdn_mma_selftest(C.MMA_KIND_BF16, C.MMA_NO_COMPLETION, 128, 64, 64, P(A), P(B), P(D), stream) == 0
+    torch.cuda.synchronize()
+    took = time.perf_counter() - t0
+    assert pkg.prefill.device_status(cuda_dev) == C.GDN_ERR_DEVICE_TIMEOUT
+    assert torch.isnan(D).all()
+    assert took < 2.0, f"the expired wait took {took:.3f} s"
+    # TMEM was released: the same kernel allocates it again and completes normally
+    assert lib.gdn_mma_selftest(C.MMA_KIND_BF16, 0, 128, 64, 64, P(A), P(B), P(D), stream) == 0
+    torch.cuda.synchronize()
+    assert pkg.prefill.device_status(cuda_dev) == 0
+    ref = A.double().cpu() @ B.double().cpu().T
+    assert (D.double().cpu() - ref).abs().max().item() < 1e-3 * ref.abs().max().item()
