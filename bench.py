@@ -229,12 +229,12 @@ def cpu_prefill_baseline(pkg, budget_s: float):
 
 
 def bench_prefill(pkg, device, lengths, seed, steps, warmup, ws, flush, peaks, with_state=True,
-                  traffic=None):
-    inp = pkg.inputs.make_prefill_inputs(lengths, seed=seed, with_state=with_state).to(device)
+                  traffic=None, hqk=4, hv=8):
+    inp = pkg.inputs.make_prefill_inputs(lengths, seed=seed, with_state=with_state, hqk=hqk, hv=hv).to(device)
     T, N = inp.total_tokens, inp.num_seqs
-    out = torch.empty((T, 8, 128), dtype=torch.bfloat16, device=device)
-    ns = torch.empty((N, 8, 128, 128), dtype=torch.float32, device=device)
-    ws_bytes = pkg.prefill.workspace_bytes(T, N)
+    out = torch.empty((T, hv, 128), dtype=torch.bfloat16, device=device)
+    ns = torch.empty((N, hv, 128, 128), dtype=torch.float32, device=device)
+    ws_bytes = pkg.prefill.workspace_bytes(T, N, hv)
     wsb = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=device)
 
     def step():
@@ -242,11 +242,16 @@ def bench_prefill(pkg, device, lengths, seed, steps, warmup, ws, flush, peaks, w
 
     times, _ = time_steps(step, steps, warmup, ws, device, flush)
     ms = max_over_ranks(sorted(times)[len(times) // 2], ws, device)  # median of the per-call times
-    bytes_ = PREFILL_BYTES_PER_TOKEN * T + STATE_BYTES_PER_SEQ * N * (2 if with_state else 1)
+    # per token: q, k (hqk heads) and v, a, b, output (hv heads); states hv x 64 KiB per sequence
+    per_tok = 2 * hqk * 256 + hv * (256 + 2 + 2 + 256)
+    bytes_ = per_tok * T + (hv // 8) * STATE_BYTES_PER_SEQ * N * (2 if with_state else 1)
+    flops = PREFILL_FLOPS_PER_TOKEN * (hv / 8) * T
     res = {"tokens": T, "seqs": N, "ms": ms, "tokens_per_s": T * ws / (ms * 1e-3),
-           "algo_bytes": bytes_, "algo_flops": PREFILL_FLOPS_PER_TOKEN * T,
-           "hbm_gbs": bytes_ / (ms * 1e-3) / 1e9, "tflops": PREFILL_FLOPS_PER_TOKEN * T / (ms * 1e-3) / 1e12,
-           "roofline": prefill_roofline(bytes_, PREFILL_FLOPS_PER_TOKEN * T, ms, peaks, traffic)}
+           "algo_bytes": bytes_, "algo_flops": flops,
+           "hbm_gbs": bytes_ / (ms * 1e-3) / 1e9, "tflops": flops / (ms * 1e-3) / 1e12,
+           "roofline": prefill_roofline(bytes_, flops, ms, peaks, traffic)}
+    if (hqk, hv) != (4, 8):
+        res["heads"] = [hqk, hv]
     return res
 
 
@@ -802,6 +807,12 @@ def run_ours(args):
         if wl in ("all", "prefill3"):
             pf["config3_32seq"] = bench_prefill(pkg, device, pkg.inputs.config3_lengths(0), 0, psteps,
                                                 args.warmup, ws, flush, peaks, traffic=PREFILL_NCU_TRAFFIC.get("config3"))
+        if wl in ("all", "prefill_heads"):
+            # the contest's other head layout (16 q/k, 32 v heads) on config 2's and config 3's shapes
+            pf["qk16_v32_T4096_N1"] = bench_prefill(pkg, device, [4096], 0, psteps, args.warmup, ws, flush, peaks,
+                                                    with_state=False, hqk=16, hv=32)
+            pf["qk16_v32_config3_lengths"] = bench_prefill(pkg, device, pkg.inputs.config3_lengths(0), 0, psteps,
+                                                           args.warmup, ws, flush, peaks, hqk=16, hv=32)
     if wl in ("all", "prefill_cp") and ws > 1:
         try:  # a ride-along: an error (the same on every rank) is reported, not fatal to the line
             pf["context_parallel_1x131072"] = bench_prefill_cp(pkg, device, rank, ws, [131072], 5,
@@ -879,7 +890,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds per CPU-baseline sample")
     ap.add_argument("--workload", default="all",
-                    choices=["all", "decode", "prefill2", "prefill3", "config4", "prefill_cp", "reference_gpu"],
+                    choices=["all", "decode", "prefill2", "prefill3", "prefill_heads", "config4", "prefill_cp",
+                             "reference_gpu"],
                     help="all = the JSON line the driver reads; the others time one workload")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline (profiling runs)")
     ap.add_argument("--skip-e2e", action="store_true", help="omit the host-buffer e2e leg")

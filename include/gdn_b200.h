@@ -187,11 +187,20 @@ size_t gdn_prefill_workspace_size(int64_t total_tokens, int64_t num_seqs);
 int gdn_prefill_launch(const GdnPrefillArgs* args, void* workspace, size_t workspace_bytes,
                        void* stream);
 
-/* gdn_prefill_launch for head counts other than 4 / 8 (rules as
- * gdn_decode_launch_heads): runs the token-recurrent kernel whatever
- * args->path says and needs no workspace.  The chunked tensor-core kernels
- * exist for 4 q/k and 8 v heads only. */
-int gdn_prefill_launch_heads(const GdnPrefillArgs* args, int32_t num_qk_heads, int32_t num_v_heads, void* stream);
+/* gdn_prefill_launch for other head counts (rules as gdn_decode_launch_heads;
+ * e.g. the contest's 16 q/k / 32 v heads): every tensor's head axis has the
+ * given count, new_state is [N, num_v_heads, 128, 128].  args->path selects
+ * the algorithm as for gdn_prefill_launch -- the chunked tensor-core kernels
+ * take the head counts at run time -- and the workspace rules are the same
+ * with gdn_prefill_workspace_size_heads(T, N, num_v_heads) in place of
+ * gdn_prefill_workspace_size (a smaller workspace that holds the operand
+ * records, (ceil(T / 64) + N) x num_v_heads x 96 KiB plus tables, runs the
+ * single-pass carry; the token-recurrent path needs none and accepts NULL).
+ * Reference: the reference kernels are fixed at 4 / 8 heads
+ * (triton/kernel.py:30-33); its definition's head axes (FAQ.md:109-111). */
+size_t gdn_prefill_workspace_size_heads(int64_t total_tokens, int64_t num_seqs, int32_t num_v_heads);
+int gdn_prefill_launch_heads(const GdnPrefillArgs* args, int32_t num_qk_heads, int32_t num_v_heads,
+                             void* workspace, size_t workspace_bytes, void* stream);
 
 /* Context parallelism: one batch of long sequences split by token range over
  * `world` GPUs (one process each).  Rank r holds the r-th consecutive range

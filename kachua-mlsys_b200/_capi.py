@@ -34,11 +34,12 @@ EXPORTED_SYMBOLS = (
     "gdn_decode_launch_bf16_state",
     "gdn_decode_launch_heads",
     "gdn_prefill_launch_heads",
+    "gdn_prefill_workspace_size_heads",
     "gdn_prefill_cp_workspace_size",
     "gdn_prefill_cp_summary_offset",
     "gdn_prefill_cp_launch",
 )
-ABI_VERSION = 8
+ABI_VERSION = 9
 PATH_AUTO, PATH_RECURRENT, PATH_CHUNKED, PATH_SEGMENTED = 0, 1, 2, 3
 MMA_KIND_BF16, MMA_KIND_TF32, MMA_KIND_F16 = 1, 2, 3
 MMA_A_MN, MMA_B_MN, MMA_D_LANE16, MMA_A_TMEM, MMA_NO_COMPLETION = 1, 2, 4, 8, 16
@@ -118,8 +119,11 @@ def load(build_if_needed: bool = True) -> ctypes.CDLL:
         lib.gdn_decode_launch_heads.argtypes = [ctypes.POINTER(GdnDecodeArgs), ctypes.c_int32, ctypes.c_int32,
                                                 ctypes.c_int64, ctypes.c_int32, P]
         lib.gdn_decode_launch_heads.restype = ctypes.c_int
-        lib.gdn_prefill_launch_heads.argtypes = [ctypes.POINTER(GdnPrefillArgs), ctypes.c_int32, ctypes.c_int32, P]
+        lib.gdn_prefill_launch_heads.argtypes = [ctypes.POINTER(GdnPrefillArgs), ctypes.c_int32, ctypes.c_int32, P,
+                                                 ctypes.c_size_t, P]
         lib.gdn_prefill_launch_heads.restype = ctypes.c_int
+        lib.gdn_prefill_workspace_size_heads.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32]
+        lib.gdn_prefill_workspace_size_heads.restype = ctypes.c_size_t
         lib.gdn_prefill_cp_workspace_size.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32]
         lib.gdn_prefill_cp_workspace_size.restype = ctypes.c_size_t
         lib.gdn_prefill_cp_summary_offset.argtypes = [ctypes.c_int64, ctypes.c_int64]

@@ -37,7 +37,7 @@ static float resolve_scale(float s) { return s == 0.0f ? 1.0f / sqrtf((float)kD)
 
 using namespace gdn;
 
-extern "C" int gdn_abi_version(void) { return 8; }
+extern "C" int gdn_abi_version(void) { return 9; }
 
 extern "C" const char* gdn_status_string(int status) {
     switch (status) {
@@ -237,18 +237,30 @@ extern "C" int gdn_prefill_cp_launch(const GdnPrefillArgs* a, void* workspace, s
     return e == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
 }
 
-// Other head counts: the token-recurrent prefill (no workspace; the chunked
-// kernels are built for 4 q/k and 8 v heads).
+// Other head counts: the same paths as gdn_prefill_launch (the chunked
+// kernels take the head counts from the parameters); the token-recurrent
+// path needs no workspace.
+extern "C" size_t gdn_prefill_workspace_size_heads(int64_t total_tokens, int64_t num_seqs, int32_t num_v_heads) {
+    if (total_tokens < 0 || num_seqs < 0 || num_v_heads < 1 || num_v_heads > 4096) return 0;
+    return chunked_workspace_bytes(total_tokens, num_seqs, num_v_heads);
+}
+
 extern "C" int gdn_prefill_launch_heads(const GdnPrefillArgs* a, int32_t num_qk_heads, int32_t num_v_heads,
-                                        void* stream) {
+                                        void* workspace, size_t workspace_bytes, void* stream) {
     if (a == nullptr) return GDN_ERR_NULL_POINTER;
     if (!heads_ok(num_qk_heads, num_v_heads)) return GDN_ERR_BAD_SIZE;
     PrefillParams p;
     if (int rc = prefill_setup(a, p, num_qk_heads, num_v_heads)) return rc;
     if (a->num_seqs * num_v_heads * (kD / 16) > 0x7fffffffLL) return GDN_ERR_BAD_SIZE;
+    const size_t need = prefill_path_is_recurrent(a->path, a->total_tokens, a->num_seqs)
+                            ? 0
+                            : chunked_workspace_min_bytes(a->total_tokens, a->num_seqs, num_v_heads);
+    if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 256)))
+        return GDN_ERR_WORKSPACE;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (launch_prefill_zero_uncovered(p, s) != cudaSuccess) return GDN_ERR_CUDA;
-    return a->num_seqs > 0 && launch_prefill_recurrent(p, s) != cudaSuccess ? GDN_ERR_CUDA : GDN_OK;
+    if (a->num_seqs == 0)  // every token is uncovered: zero output
+        return a->total_tokens > 0 && launch_prefill_zero_uncovered(p, s) != cudaSuccess ? GDN_ERR_CUDA : GDN_OK;
+    return launch_prefill(p, a->path, workspace, workspace_bytes, s) == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
 }
 
 extern "C" int gdn_read_device_status(int* out, int clear, void* stream) {

@@ -73,10 +73,10 @@ constexpr int kSegSlotBytes = 98304;
 // thirds of the SMs, N x 8 x P <= 2 sms / 3: more concurrent chains than that
 // saturate HBM (about 70 GB/s each) and the split costs more than it saves.
 // Two segments were measured to gain nothing; 1 = no segmented carry.
-__host__ __device__ inline int seg_segments(int64_t N, int sms) {
+__host__ __device__ inline int seg_segments(int64_t N, int sms, int hv = kHV) {
     int best = 1;
     for (int P = 3; P <= kSegMaxP; ++P)
-        if (N > 0 && N * kHV * (P > 2 * P - 3 ? P : 2 * P - 3) <= sms && 3 * N * kHV * P <= 2 * sms) best = P;
+        if (N > 0 && N * hv * (P > 2 * P - 3 ? P : 2 * P - 3) <= sms && 3 * N * hv * P <= 2 * sms) best = P;
     return best;
 }
 
@@ -89,10 +89,12 @@ struct WsLayout {
     int64_t total_seg;  // total + the summaries
     int64_t cp_world;   // context parallel: ranks (seg_slots = segments per rank); 0 otherwise
     int64_t off_gather; // context parallel: the all-gathered rank summaries (cp_world x N x 8 slots)
+    int64_t hv;         // v-heads (records per chunk; carry chains per sequence)
 };
 
-__host__ __device__ inline WsLayout ws_layout(int64_t T, int64_t N) {
+__host__ __device__ inline WsLayout ws_layout(int64_t T, int64_t N, int hv = kHV) {
     WsLayout L;
+    L.hv = hv;
     L.R = (T + kC - 1) / kC + N;
     int64_t o = 0;
     L.off_hdr = o;
@@ -104,23 +106,23 @@ __host__ __device__ inline WsLayout ws_layout(int64_t T, int64_t N) {
     L.off_table = o;
     o = align_up(o + 16 * L.R, 1024);
     L.off_rec = o;
-    o += L.R * kHV * kHeadRecBytes;
+    o += L.R * hv * kHeadRecBytes;
     L.total = align_up(o, 1024);
     L.cp_world = 0;
     L.off_gather = 0;
-    L.seg_slots = seg_segments(N, kSmCount);
+    L.seg_slots = seg_segments(N, kSmCount, hv);
     L.off_seg = L.seg_slots >= 2 ? L.total : 0;
-    L.total_seg = L.total + (L.seg_slots >= 2 ? N * kHV * L.seg_slots * static_cast<int64_t>(kSegSlotBytes) : 0);
+    L.total_seg = L.total + (L.seg_slots >= 2 ? N * hv * L.seg_slots * static_cast<int64_t>(kSegSlotBytes) : 0);
     return L;
 }
 
 // Workspace for the fastest dispatch (with room for the segmented carry when
 // it may apply) and the minimum every chunked launch needs.
-size_t chunked_workspace_bytes(int64_t total_tokens, int64_t num_seqs) {
-    return static_cast<size_t>(ws_layout(total_tokens, num_seqs).total_seg);
+size_t chunked_workspace_bytes(int64_t total_tokens, int64_t num_seqs, int hv = kHV) {
+    return static_cast<size_t>(ws_layout(total_tokens, num_seqs, hv).total_seg);
 }
-size_t chunked_workspace_min_bytes(int64_t total_tokens, int64_t num_seqs) {
-    return static_cast<size_t>(ws_layout(total_tokens, num_seqs).total);
+size_t chunked_workspace_min_bytes(int64_t total_tokens, int64_t num_seqs, int hv = kHV) {
+    return static_cast<size_t>(ws_layout(total_tokens, num_seqs, hv).total);
 }
 
 // ------------------------------------------------------------ chunk table --
@@ -399,7 +401,8 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
     griddep_launch_dependents();  // the carry may start its prologue on freed SMs
     griddep_wait();               // the chunk table is complete
     const int nrec = reinterpret_cast<const int*>(ws + L.off_hdr)[0];
-    const int64_t nitems = static_cast<int64_t>(nrec) * kHV;
+    const int hv = p.hv, gva = p.hv / p.hqk;
+    const int64_t nitems = static_cast<int64_t>(nrec) * hv;
     if (static_cast<int64_t>(blockIdx.x) >= nitems) return;
     const int4* table = reinterpret_cast<const int4*>(ws + L.off_table);
 
@@ -429,24 +432,24 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
     // a chunk run side by side (their K and Q loads share L2 lines).  The next
     // item's table entry and gate inputs are read, and its K, Q and V prefetched
     // into L2, while the current one is processed.
-    int4 te = table[blockIdx.x / kHV];
+    int4 te = table[blockIdx.x / hv];
     uint16_t ga = 0, gb = 0;  // raw bf16 gate inputs a, b of token tid of the item (tid < 64)
     if (tid < te.z) {
         const int64_t t = static_cast<int64_t>(te.y) + tid;
-        ga = p.a[t * kHV + blockIdx.x % kHV];
-        gb = p.b[t * kHV + blockIdx.x % kHV];
+        ga = p.a[t * hv + blockIdx.x % hv];
+        gb = p.b[t * hv + blockIdx.x % hv];
     }
     bool stop = false;
     int it = 0;
     for (int64_t item = blockIdx.x; item < nitems && !stop; item += gridDim.x, ++it) {
-        const int64_t rec = item / kHV;
-        const int h = static_cast<int>(item % kHV), hq = h / kGva;
+        const int64_t rec = item / hv;
+        const int h = static_cast<int>(item % hv), hq = h / gva;
         const uint32_t pl = static_cast<uint32_t>(it) & 1u;  // parity of the item's barL and first barM phase
         const int t0 = te.y;  // first token (T < 2^31, checked on the host)
         const int n = te.z;   // tokens in this chunk (1..64)
-        uint8_t* out_rec = ws + L.off_rec + (rec * kHV + h) * kHeadRecBytes;
+        uint8_t* out_rec = ws + L.off_rec + (rec * hv + h) * kHeadRecBytes;
         const int64_t nitem = item + gridDim.x;
-        const int4 te_next = nitem < nitems ? table[nitem / kHV] : te;  // used after the Gram issue
+        const int4 te_next = nitem < nitems ? table[nitem / hv] : te;  // used after the Gram issue
         uint16_t ga_next = 0, gb_next = 0;
         if (tid == 0) {
             mbar_expect_tx(barL, 6 * 8192);
@@ -498,19 +501,19 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
         }
         __syncthreads();  // the row scales are visible
         if (nitem < nitems && tid < kC) {  // the next item: gate inputs, and its K, Q and V into L2
-            const int nh = static_cast<int>(nitem % kHV);
+            const int nh = static_cast<int>(nitem % hv);
             if (tid < te_next.z) {
                 const int64_t t = static_cast<int64_t>(te_next.y) + tid;
-                ga_next = p.a[t * kHV + nh];
-                gb_next = p.b[t * kHV + nh];
+                ga_next = p.a[t * hv + nh];
+                gb_next = p.b[t * hv + nh];
             }
             if (tid == 32) {
                 const int nt0 = te_next.y;
-                if ((nh & 1) == 0) {
-                    tma_prefetch_3d(&tmK, 0, nh / kGva, nt0);
-                    tma_prefetch_3d(&tmK, 64, nh / kGva, nt0);
-                    tma_prefetch_3d(&tmQ, 0, nh / kGva, nt0);
-                    tma_prefetch_3d(&tmQ, 64, nh / kGva, nt0);
+                if (nh % gva == 0) {
+                    tma_prefetch_3d(&tmK, 0, nh / gva, nt0);
+                    tma_prefetch_3d(&tmK, 64, nh / gva, nt0);
+                    tma_prefetch_3d(&tmQ, 0, nh / gva, nt0);
+                    tma_prefetch_3d(&tmQ, 64, nh / gva, nt0);
                 }
                 tma_prefetch_3d(&tmV, 0, nh, nt0);
                 tma_prefetch_3d(&tmV, 64, nh, nt0);
@@ -917,8 +920,8 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     int64_t unit;
     int seg = 0, role = kRoleMain, nP = 1;
     if (mode == 0) {  // longest sequences first
-        unit = static_cast<int64_t>(reinterpret_cast<const int*>(ws + L.off_order)[blockIdx.x / kHV]) * kHV +
-               blockIdx.x % kHV;
+        unit = static_cast<int64_t>(reinterpret_cast<const int*>(ws + L.off_order)[blockIdx.x / p.hv]) * p.hv +
+               blockIdx.x % p.hv;
     } else if (mode == 2) {
         nP = P;
         unit = blockIdx.x / P;
@@ -958,8 +961,8 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
             role = kRoleSumZ;
         }
     }
-    const int64_t s = unit / kHV;
-    const int h = static_cast<int>(unit - s * kHV);
+    const int64_t s = unit / p.hv;
+    const int h = static_cast<int>(unit - s * p.hv);
 
     int64_t t0, t1;
     seq_bounds(p, s, t0, t1);
@@ -990,10 +993,10 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     const int nch = ce - cb, rec0 = rec0_all + cb;
     t0 += static_cast<int64_t>(kC) * cb;
     const int len = len_all - kC * cb < kC * nch ? len_all - kC * cb : kC * nch;
-    auto rec_ptr = [&](int c) { return ws + L.off_rec + (static_cast<int64_t>(rec0 + c) * kHV + h) * kHeadRecBytes; };
+    auto rec_ptr = [&](int c) { return ws + L.off_rec + (static_cast<int64_t>(rec0 + c) * p.hv + h) * kHeadRecBytes; };
     // summaries (T at +0, Z at +32 KiB): per unit and segment; context
     // parallel: the rank's own segments, and one all-gathered slot per rank
-    const int64_t units = p.num_seqs * kHV;
+    const int64_t units = p.num_seqs * p.hv;
     auto slot = [&](int sg) {
         return ws + L.off_seg + (cp ? sg * units + unit : unit * L.seg_slots + sg) * static_cast<int64_t>(kSegSlotBytes);
     };
@@ -1316,11 +1319,11 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
                     bulk_commit();
                 }
             } else {
-                uint16_t* dst = p.out + ((t0 + static_cast<int64_t>(kC) * c) * kHV + h) * kD + v;
+                uint16_t* dst = p.out + ((t0 + static_cast<int64_t>(kC) * c) * p.hv + h) * kD + v;
 #pragma unroll
                 for (int i = 0; i < kC; ++i)
                     if (i < rows)
-                        dst[static_cast<int64_t>(i) * (kHV * kD)] =
+                        dst[static_cast<int64_t>(i) * (p.hv * kD)] =
                             static_cast<uint16_t>((i & 1) ? pk[i >> 1] >> 16 : pk[i >> 1] & 0xffffu);
             }
         }
@@ -1459,7 +1462,7 @@ static cudaError_t token_tensor_map(CUtensorMap* m, const void* base, int heads,
 // the output tensor map and the SM count for the carry.
 static cudaError_t chunk_records(const PrefillParams& p, uint8_t* ws, const WsLayout& L, CUtensorMap* tmO,
                                  int* sms_out, cudaStream_t stream) {
-    if (L.R * kHV > 0x7fffffffLL || p.total_tokens > 0x7fffffffLL) return cudaErrorInvalidValue;
+    if (L.R * p.hv > 0x7fffffffLL || p.total_tokens > 0x7fffffffLL) return cudaErrorInvalidValue;
     CUtensorMap tmK, tmQ, tmV;
     memset(&tmK, 0, sizeof(tmK));
     memset(&tmQ, 0, sizeof(tmQ));
@@ -1467,10 +1470,10 @@ static cudaError_t chunk_records(const PrefillParams& p, uint8_t* ws, const WsLa
     memset(tmO, 0, sizeof(*tmO));
     cudaError_t e;
     if (p.total_tokens > 0) {  // with no tokens there are no records and no loads
-        if ((e = token_tensor_map(&tmK, p.k, kHQK, p.total_tokens)) != cudaSuccess) return e;
-        if ((e = token_tensor_map(&tmQ, p.q, kHQK, p.total_tokens)) != cudaSuccess) return e;
-        if ((e = token_tensor_map(&tmV, p.v, kHV, p.total_tokens)) != cudaSuccess) return e;
-        if ((e = token_tensor_map(tmO, p.out, kHV, p.total_tokens)) != cudaSuccess) return e;
+        if ((e = token_tensor_map(&tmK, p.k, p.hqk, p.total_tokens)) != cudaSuccess) return e;
+        if ((e = token_tensor_map(&tmQ, p.q, p.hqk, p.total_tokens)) != cudaSuccess) return e;
+        if ((e = token_tensor_map(&tmV, p.v, p.hv, p.total_tokens)) != cudaSuccess) return e;
+        if ((e = token_tensor_map(tmO, p.out, p.hv, p.total_tokens)) != cudaSuccess) return e;
     }
     gdn_chunk_table_kernel<<<device_sm_count(), 1024, 0, stream>>>(p, ws, L);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
@@ -1479,7 +1482,7 @@ static cudaError_t chunk_records(const PrefillParams& p, uint8_t* ws, const WsLa
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     *sms_out = sms;
     // persistent prepare: two CTAs per SM (or one per item when there are fewer)
-    const int64_t items = L.R * kHV;
+    const int64_t items = L.R * p.hv;
     if ((e = launch_dependent(gdn_chunk_prepare_kernel, static_cast<unsigned>(items < 2 * sms ? items : 2 * sms),
                               kPrepThreads, kPrSmem, stream, p, ws, L, tmK, tmQ, tmV)) != cudaSuccess)
         return e;
@@ -1489,13 +1492,13 @@ static cudaError_t chunk_records(const PrefillParams& p, uint8_t* ws, const WsLa
 
 cudaError_t launch_prefill_chunked(const PrefillParams& p, void* workspace, size_t workspace_bytes, int path,
                                    cudaStream_t stream) {
-    const WsLayout L = ws_layout(p.total_tokens, p.num_seqs);
+    const WsLayout L = ws_layout(p.total_tokens, p.num_seqs, p.hv);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     CUtensorMap tmO;
     int sms = 148;
     cudaError_t e;
     if ((e = chunk_records(p, ws, L, &tmO, &sms, stream)) != cudaSuccess) return e;
-    const int64_t units = p.num_seqs * kHV;
+    const int64_t units = p.num_seqs * p.hv;
     if (units > 0x7fffffffLL / (2 * kSegMaxP)) return cudaErrorInvalidValue;
     // Segmented carry: when sequences average 16 chunks or more and both
     // passes fit one wave with P >= 2 segments per chain (or when asked for:
@@ -1503,7 +1506,7 @@ cudaError_t launch_prefill_chunked(const PrefillParams& p, void* workspace, size
     // segments (pass A, then pass C).
     int P = 1;
     if (L.off_seg > 0 && workspace_bytes >= static_cast<size_t>(L.total_seg)) {
-        const int fit = seg_segments(p.num_seqs, sms);
+        const int fit = seg_segments(p.num_seqs, sms, p.hv);
         if (path == kPathSegmented)
             P = L.seg_slots < 4 ? static_cast<int>(L.seg_slots) : 4;
         else if (p.total_tokens >= p.num_seqs * 16 * kC)
@@ -1560,7 +1563,7 @@ cudaError_t launch_prefill_cp(const PrefillParams& p, void* workspace, size_t wo
     const WsLayout L = cp_layout(p.total_tokens, p.num_seqs, world);
     if (workspace_bytes < static_cast<size_t>(L.total_seg)) return cudaErrorInvalidValue;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
-    const int64_t units = p.num_seqs * kHV, q = L.seg_slots;
+    const int64_t units = p.num_seqs * p.hv, q = L.seg_slots;
     if (units == 0 || units > 0x7fffffffLL / (2 * q)) return units == 0 ? cudaSuccess : cudaErrorInvalidValue;
     CUtensorMap tmO;
     cudaError_t e;
@@ -1578,7 +1581,7 @@ cudaError_t launch_prefill_cp(const PrefillParams& p, void* workspace, size_t wo
     }
     // pass C over the rank's segments, with outputs
     memset(&tmO, 0, sizeof(tmO));
-    if (p.total_tokens > 0 && (e = token_tensor_map(&tmO, p.out, kHV, p.total_tokens)) != cudaSuccess) return e;
+    if (p.total_tokens > 0 && (e = token_tensor_map(&tmO, p.out, p.hv, p.total_tokens)) != cudaSuccess) return e;
     if ((e = set_smem(gdn_chunk_carry_kernel, kCaSmem)) != cudaSuccess) return e;
     gdn_chunk_carry_kernel<<<static_cast<unsigned>(units * q), kCarryThreads, kCaSmem, stream>>>(p, ws, L, 5, rank,
                                                                                                  tmO);
@@ -1598,7 +1601,7 @@ cudaError_t launch_prefill(const PrefillParams& p, int path, void* workspace, si
         cudaError_t e = launch_prefill_zero_uncovered(p, stream);
         return e != cudaSuccess ? e : launch_prefill_recurrent(p, stream);
     }
-    if (workspace == nullptr || workspace_bytes < chunked_workspace_min_bytes(p.total_tokens, p.num_seqs))
+    if (workspace == nullptr || workspace_bytes < chunked_workspace_min_bytes(p.total_tokens, p.num_seqs, p.hv))
         return cudaErrorInvalidValue;
     return launch_prefill_chunked(p, workspace, workspace_bytes, path, stream);
 }

@@ -89,8 +89,12 @@ def heads(q, v) -> tuple[int, int]:
     return hqk, hv
 
 
-def workspace_bytes(total_tokens: int, num_seqs: int) -> int:
-    return int(_capi.load().gdn_prefill_workspace_size(int(total_tokens), int(num_seqs)))
+def workspace_bytes(total_tokens: int, num_seqs: int, num_v_heads: int = HV) -> int:
+    """Workspace bytes for ``launch_gdn`` (gdn_prefill_workspace_size[_heads])."""
+    lib = _capi.load()
+    if num_v_heads == HV:
+        return int(lib.gdn_prefill_workspace_size(int(total_tokens), int(num_seqs)))
+    return int(lib.gdn_prefill_workspace_size_heads(int(total_tokens), int(num_seqs), int(num_v_heads)))
 
 
 def _ptr(t):
@@ -108,9 +112,10 @@ def launch_gdn(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None, out
     ``path`` selects the algorithm: ``"auto"`` (token-recurrent kernel for
     batches of short sequences, chunked tensor-core kernels otherwise),
     ``"recurrent"`` or ``"chunked"``.  ``workspace`` may be passed to reuse a
-    device buffer of at least ``workspace_bytes(T, N)`` bytes.  Head counts
-    other than 4 q/k / 8 v (q ``[T, HQK, 128]``, v ``[T, HV, 128]``) run the
-    token-recurrent kernel.
+    device buffer of at least ``workspace_bytes(T, N)`` bytes (other head
+    counts: ``workspace_bytes(T, N, hv)``).  Head counts other than 4 q/k /
+    8 v (q ``[T, HQK, 128]``, v ``[T, HV, 128]``, HV a multiple of HQK) take
+    the same paths.
     """
     _need(path in PATHS, f"path must be one of {sorted(PATHS)}")
     _need(isinstance(q, torch.Tensor), "q must be a torch.Tensor")
@@ -118,26 +123,14 @@ def launch_gdn(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None, out
         cu_seqlens = cu_seqlens.to(q.device)
     N = cu_seqlens.numel() - 1
     hqk, hv = heads(q, v)
-    _need((hqk, hv) == (HQK, HV) or path in ("auto", "recurrent"),
-          "head counts other than 4 / 8 run the token-recurrent kernel only (path auto or recurrent)")
     if output is None:
         output = torch.empty((q.shape[0], hv, D), dtype=torch.bfloat16, device=q.device)
     if new_state is None:
         new_state = torch.empty((N, hv, D, D), dtype=torch.float32, device=q.device)
     T, N = validate(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, output, new_state, check_seqlens)
     lib = _capi.load()
-    if (hqk, hv) != (HQK, HV):
-        args = _capi.GdnPrefillArgs(
-            _ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a), _ptr(dt_bias), _ptr(b),
-            _ptr(cu_seqlens),
-            _capi.GDN_SEQLENS_INT64 if cu_seqlens.dtype == torch.int64 else _capi.GDN_SEQLENS_INT32,
-            PATHS["recurrent"], T, N, 0.0 if scale is None else float(scale), _ptr(output), _ptr(new_state))
-        with torch.cuda.device(q.device):
-            stream = torch.cuda.current_stream(q.device).cuda_stream
-            _capi.check(lib.gdn_prefill_launch_heads(ctypes.byref(args), hqk, hv, ctypes.c_void_p(stream)),
-                        "gdn_prefill_launch_heads")
-        return output, new_state
-    need = int(lib.gdn_prefill_workspace_size(T, N))
+    other_heads = (hqk, hv) != (HQK, HV)
+    need = workspace_bytes(T, N, hv)
     if need > 0 and (workspace is None or workspace.numel() * workspace.element_size() < need
                      or workspace.device != q.device):
         workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
@@ -149,8 +142,12 @@ def launch_gdn(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None, out
     ws_ptr = _ptr(workspace) if need > 0 else ctypes.c_void_p(None)
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream
-        _capi.check(lib.gdn_prefill_launch(ctypes.byref(args), ws_ptr, need, ctypes.c_void_p(stream)),
-                    "gdn_prefill_launch")
+        if other_heads:
+            _capi.check(lib.gdn_prefill_launch_heads(ctypes.byref(args), hqk, hv, ws_ptr, need,
+                                                     ctypes.c_void_p(stream)), "gdn_prefill_launch_heads")
+        else:
+            _capi.check(lib.gdn_prefill_launch(ctypes.byref(args), ws_ptr, need, ctypes.c_void_p(stream)),
+                        "gdn_prefill_launch")
     return output, new_state
 
 

@@ -77,10 +77,14 @@ def test_heads_validation(pkg):
     assert lib.gdn_decode_launch_heads(ctypes.byref(d), 3, 8, 1, 0, None) == 2   # 8 not a multiple of 3
     assert lib.gdn_decode_launch_heads(ctypes.byref(d), 16, 32, 2, 1, None) == 2  # bf16 state: one token
     assert lib.gdn_decode_launch_heads(ctypes.byref(d), 16, 32, 1, 0, None) == 1  # NULL pointers
-    assert lib.gdn_prefill_launch_heads(ctypes.byref(p), 0, 8, None) == 2
+    assert lib.gdn_prefill_launch_heads(ctypes.byref(p), 0, 8, None, 0, None) == 2
     p.total_tokens, p.num_seqs = 16, 1
     p.cu_seqlens_dtype = C.GDN_SEQLENS_INT64
-    assert lib.gdn_prefill_launch_heads(ctypes.byref(p), 16, 32, None) == 1
+    assert lib.gdn_prefill_launch_heads(ctypes.byref(p), 16, 32, None, 0, None) == 1
+    # the chunked paths size their workspace by the v-head count
+    assert lib.gdn_prefill_workspace_size_heads(4096, 1, 32) > 3 * lib.gdn_prefill_workspace_size(4096, 1)
+    assert lib.gdn_prefill_workspace_size_heads(4096, 1, 8) == lib.gdn_prefill_workspace_size(4096, 1)
+    assert lib.gdn_prefill_workspace_size_heads(-1, 1, 8) == 0 and lib.gdn_prefill_workspace_size_heads(1, 1, 0) == 0
 
 
 def test_decode_host_staged_validation(pkg):

@@ -147,13 +147,22 @@ def test_prefill_segmented_auto(pkg, orc, cuda_dev, lengths):
            cuda_dev, path="auto")
 
 
-@pytest.mark.parametrize("hqk,hv", [(16, 32), (2, 4)])
-def test_prefill_other_head_counts(pkg, orc, cuda_dev, hqk, hv):
-    """Head counts other than 4 / 8 run the token-recurrent kernel."""
-    inp = pkg.inputs.make_prefill_inputs([33, 0, 70, 1], seed=hv, with_state=True, hqk=hqk, hv=hv)
-    _check(pkg, orc, inp, cuda_dev, path="auto")
-    with pytest.raises(ValueError, match="token-recurrent"):
-        pkg.prefill.launch_gdn(*inp.to(cuda_dev).args(), path="chunked")
+@pytest.mark.parametrize("hqk,hv", [(16, 32), (2, 4), (1, 2), (4, 4)])
+@pytest.mark.parametrize("hpath", ["recurrent", "chunked", "auto"])
+def test_prefill_other_head_counts(pkg, orc, cuda_dev, hqk, hv, hpath):
+    """Head counts other than 4 / 8 (the contest's 16 / 32, other grouping
+    ratios, one v-head per q/k head) on every path: the chunked tensor-core
+    kernels take the counts at run time."""
+    inp = pkg.inputs.make_prefill_inputs([33, 0, 70, 1, 130], seed=hv + hqk, with_state=True, hqk=hqk, hv=hv)
+    _check(pkg, orc, inp, cuda_dev, path=hpath)
+
+
+@pytest.mark.parametrize("lengths,hpath", [([2048], "chunked"), ([4096], "auto"), ([700, 1500, 64], "chunked")])
+def test_prefill_qk16_v32_long(pkg, orc, cuda_dev, lengths, hpath):
+    """The contest's 16 / 32 head layout on long sequences through the chunked
+    tensor-core path (single pass, and the automatic choice)."""
+    inp = pkg.inputs.make_prefill_inputs(lengths, seed=sum(lengths), with_state=True, hqk=16, hv=32)
+    _check(pkg, orc, inp, cuda_dev, path=hpath)
 
 
 def test_segmented_matches_single_pass(pkg, cuda_dev):
