@@ -73,7 +73,7 @@ def _worker(rank, world, port, mode, q):
 
     pkg = __graft_entry__.load_package()
     dist.init_process_group("gloo", rank=rank, world_size=world,
-                            timeout=datetime.timedelta(seconds=4))
+                            timeout=datetime.timedelta(seconds=15))
     try:
         inp = pkg.inputs.make_prefill_inputs([33, 70, 1, 0, 20], seed=73, with_state=True)
         shards = pkg.shard.plan_prefill_shards(inp.cu_seqlens, world)
