@@ -65,6 +65,21 @@ __device__ __forceinline__ void gdn_gates(float A_log, float dt_bias, float a, f
     beta = 1.0f / (1.0f + expf(-b));
 }
 
+// The same gates on the special-function unit (__expf, __logf, __fdividef):
+// a shorter dependent chain between the gate inputs' arrival and the state
+// update, which a single decode step at small batch waits on.  softplus is
+// formed as max(x, 0) + log(1 + exp(-|x|)) (no cancellation), torch's
+// threshold kept; g's relative error stays near 1e-6 (the intrinsics' few
+// ulp, times exp(A_log) <= 16 for |softplus| errors ~1e-7), far inside the
+// 1e-3 state tolerance.  The reference CUDA decode used the same intrinsics
+// (kernel.cu:579-582, 655-657).
+__device__ __forceinline__ void gdn_gates_fast(float A_log, float dt_bias, float a, float b, float& g, float& beta) {
+    const float x = a + dt_bias;
+    const float sp = x > 20.0f ? x : fmaxf(x, 0.0f) + __logf(1.0f + __expf(-fabsf(x)));
+    g = __expf(-__expf(A_log) * sp);
+    beta = __fdividef(1.0f, 1.0f + __expf(-b));
+}
+
 // log2 of the decay, for the chunked path: log2 g = -exp(A_log) * softplus(x) / ln 2.
 __device__ __forceinline__ float gdn_log2_decay(float A_log, float dt_bias, float a) {
     return -expf(A_log) * softplus_f(a + dt_bias) * 1.4426950408889634f;

@@ -45,11 +45,11 @@ struct DecodeParams {
 
 // BF16S: the state (in and out) is stored as bf16 instead of fp32; the
 // arithmetic is the same fp32, the new state rounded to bf16 once.
-template <int RPW, bool BF16S>
-__global__ void __launch_bounds__(128) gdn_decode_kernel(const DecodeParams p) {
+template <int RPW, bool BF16S, int WARPS = 4>
+__global__ void __launch_bounds__(32 * WARPS) gdn_decode_kernel(const DecodeParams p) {
     static_assert(RPW % 4 == 0, "rows per warp must be a multiple of 4");
     constexpr int kPasses = RPW / 4;
-    constexpr int kRowsPerCta = 4 * RPW;
+    constexpr int kRowsPerCta = WARPS * RPW;
     constexpr int kTiles = kD / kRowsPerCta;
 
     const int warp = threadIdx.x >> 5;
@@ -99,8 +99,8 @@ __global__ void __launch_bounds__(128) gdn_decode_kernel(const DecodeParams p) {
     for (int ps = 0; ps < kPasses; ++ps)
         vrow[ps] = bf16_bits_to_float(p.v[bh * kD + row0 + 4 * ps]);
     float g, beta;
-    gdn_gates(p.A_log[h], p.dt_bias[h], bf16_bits_to_float(p.a[bh]), bf16_bits_to_float(p.b[bh]), g,
-              beta);
+    gdn_gates_fast(p.A_log[h], p.dt_bias[h], bf16_bits_to_float(p.a[bh]), bf16_bits_to_float(p.b[bh]), g,
+                   beta);
 
     float qk = 0.f;
 #pragma unroll
@@ -297,14 +297,19 @@ cudaError_t launch_decode_tokens(const DecodeParams& p, int T, cudaStream_t stre
     return cudaGetLastError();
 }
 
-// Rows per warp: the largest tile that still yields >= 2 CTAs per SM.
+// Rows per warp (per CTA of 4 warps: 4 x RPW rows).  Measured per launch
+// (ncu, caches flushed, fp32 state): up to 128 heads (B <= 16 at 8 v-heads)
+// the smallest tile is fastest (the step is one round trip of latency and
+// more CTAs spread it over more SMs: B = 16 4.96 us at 4 rows vs 5.60 at 8);
+// from there to 2048 heads 8 rows (B = 64 10.9 us, B = 128 18.1 us); beyond,
+// 16 rows, which also won the back-to-back config-1 steady state.
 static int pick_rows_per_warp(int64_t heads, bool bf16_state) {
     const int sms = device_sm_count();
     // a bf16 row is half as many bytes: 32 rows keep the fp32 kernel's 256 B of loads in flight per thread
     if (bf16_state && heads >= 2 * sms) return 32;
-    if (heads * (kD / 64) >= 2 * sms) return 16;
-    if (heads * (kD / 32) >= 2 * sms) return 8;
-    return 4;
+    if (heads <= 128) return 4;
+    if (heads < 2048) return 8;
+    return 16;
 }
 
 template <bool BF16S>

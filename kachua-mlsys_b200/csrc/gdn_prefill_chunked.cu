@@ -1,12 +1,13 @@
 // gdn_prefill_chunked.cu -- chunked-WY varlen GDN prefill on tcgen05 tensor cores.
 //
 // Replaces the reference's three Triton paths (Direct-v2 kernel.py:886-993,
-// Split-WY :379-540, Flat-WY :576-863) with one design in two kernels.
+// Split-WY :379-540, Flat-WY :576-863) with one design: a per-chunk prepare
+// kernel and a carry kernel.
 //
 // Algebra for one chunk of C = 64 tokens of one v-head (state S is [V][K]):
 //   G_i   = prod_{m<=i} g_m (kept as log2 G),  Gam_ij = G_i / G_j = exp2(lG_i - lG_j), j <= i
 //   N_ij  = beta_i Gam_ij (k_i . k_j)          for j < i     (strictly lower)
-//   A     = I + N,   Ainv = (I - N)(I + N^2)(I + N^4)...(I + N^32)   (Neumann doubling)
+//   A     = I + N,   Ainv = A^-1 (the reference: Neumann doubling (I - N)(I + N^2)...(I + N^32))
 //   W     = Ainv (beta G (.) K),   U = Ainv (beta (.) V)
 //   Delta = U - W S0^T                          (rows delta_i of the update)
 //   P_ij  = Gam_ij (q_i . k_j)                  for j <= i
@@ -23,21 +24,39 @@
 // -- the same identities with Delta expanded, so the chunk-to-chunk chain is
 // one matrix product and everything else is per-chunk, parallel work.
 //
-// Kernel 1, gdn_chunk_prepare (one CTA per chunk x q/k head, both v-heads):
-//   [K;Q] K^T on bf16 tcgen05 (M=128, N=64, K=128); per v-head the gates,
-//   N and P; Ainv by Neumann doubling on fp16 tcgen05 64x64x64 products (both
-//   v-heads packed into one M=64 accumulator pair); [W | U] = Ainv [bGK | bV]
-//   (M=64, N=256); then P [W | U] and K'^T [W | U] (M=128, N=256), whose
-//   epilogues write Qt, Ut, M and D to the workspace.
-// Kernel 2, gdn_chunk_carry (one CTA per sequence x v-head x 64 value rows):
-//   four state warps keep the fp32 state in registers and run the chain
-//   S <- S M^T + D^T with one M=128, N=64, K=128 fp16 MMA per chunk; four
-//   output warps finish O = scale (Qt S^T + Ut) from a second MMA on the same
-//   state image, overlapped with the next chunk.  Operands arrive by bulk
-//   copies issued two chunks ahead.
+// The inverse.  Ainv is the inverse of a unit lower-triangular 64 x 64
+// matrix; instead of the reference's Neumann doubling (log2 C squarings and
+// products, each a dependent tensor-core round trip) it is formed blocked
+// 2 x 2: the two 32 x 32 diagonal blocks by fp32 forward substitution (one
+// column per thread), the off-diagonal block X21 = -X22 (N21 X11) by two
+// tcgen05 products -- three dependent steps instead of ten, and the diagonal
+// blocks exact in fp32.
+//
+// Kernels (one prefill call = table + prepare + carry, chained by
+// programmatic dependent launch):
+//   gdn_chunk_table   one block: chunk records (sequence, first token,
+//                     length) for every 64-token chunk of every sequence,
+//                     per-sequence record bases, sequences ordered longest
+//                     first; zeroes output rows no sequence covers.
+//   gdn_chunk_prepare persistent, two 256-thread CTAs per SM, one item =
+//                     (chunk record, v-head): TMA loads of K, Q, V into SW128
+//                     images; Gram [K;Q] K^T (bf16); N, P and the decay
+//                     ratios; Ainv as above; [W | U]^T, Qt^T, Ut^T and
+//                     K'^T W as M = 128 fp16 tcgen05 products; 96 KiB of fp16
+//                     operand images per item bulk-stored to the workspace.
+//   gdn_chunk_carry   one 448-thread CTA per sequence x v-head (per segment
+//                     of one in the segmented and context-parallel modes):
+//                     the state lives in TMEM, transposed, and is the A
+//                     operand of its own next product; per chunk one
+//                     128 x 128 x 128 state MMA S M^T (plus U^T K' issued a
+//                     chunk early) and one output MMA S Qt^T, operands by
+//                     bulk copies two chunks ahead, bf16 output tiles by TMA.
+// Any q/k and v head counts (v a multiple of q/k): items, records and carry
+// chains are per v-head, and v-head h reads q/k head h / (hv / hqk).
 // Precision: tensor-core operands are fp16 (round-to-nearest, 11-bit
-// significand like tf32) with fp32 accumulation; the state and D stay fp32
-// between chunks, and only the MMA's copy of the state is rounded.
+// significand) or bf16 (the Gram of the bf16 inputs) with fp32
+// accumulation; the carried state is fp32 in TMEM and rounded to fp16 only
+// as the operand of the next product.
 #include <cudaTypedefs.h>  // PFN_cuTensorMapEncodeTiled
 #include <string.h>
 
