@@ -1,4 +1,4 @@
-"""The reference's own GPU kernels, loaded from ``baseline/_ref`` for timing.
+"""The reference's own kernels and PyTorch code, loaded from ``baseline/_ref`` for timing.
 
 ``install_ref.py`` puts the unmodified reference solutions there.  This module
 only loads them, the way the reference's harness does:
@@ -70,3 +70,19 @@ def prefill_module():
             tvm_ffi.register_global_func = orig
         _cache["prefill"] = mod
     return _cache["prefill"]
+
+
+def torch_reference(definition: str):
+    """``run`` of the reference's own PyTorch implementation of ``definition``
+    (``solution/reference_torch_impl.py``, decode ``:12``, prefill ``:17``):
+    the reference's CPU algorithm, timed on the host cores beside the GPU kernels."""
+    key = "torch_" + definition
+    if key not in _cache:
+        path = REF / definition / "solution" / "reference_torch_impl.py"
+        name = f"kachua_ref_torch_{definition}"
+        spec = importlib.util.spec_from_file_location(name, path)
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules[name] = mod
+        spec.loader.exec_module(mod)
+        _cache[key] = mod.run
+    return _cache[key]

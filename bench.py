@@ -212,6 +212,49 @@ def cpu_decode_baseline(pkg, budget_s: float):
             "sample": f"{n} full decode steps of config 1 (B=256) through oracle/gdn_oracle.c"}
 
 
+def cpu_torch_reference(pkg, budget_s: float):
+    """The reference's own PyTorch implementation (reference_torch_impl.run,
+    unmodified, from baseline/_ref) on the host CPU with every host thread:
+    decode config 0 (B = 8) and one config-1 step (B = 256), and prefill of 8
+    sequences x 512 tokens -- bounded samples of about ``budget_s`` each."""
+    sys.path.insert(0, str(REPO / "baseline"))
+    import reference_gpu as rg
+
+    if rg.missing():
+        return {"unavailable": rg.missing()}
+    threads = cpu_threads()
+    prev = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    try:
+        dec = rg.torch_reference("gdn_decode_qk4_v8_d128_k_last")
+        pre = rg.torch_reference("gdn_prefill_qk4_v8_d128_k_last")
+        res = {"cores": threads, "kind": "reference (reference_torch_impl.run, PyTorch on the host CPU)"}
+        for B in (8, DECODE_BATCH):
+            inp = pkg.inputs.make_decode_inputs(B, seed=B)
+            dec(*inp.args())  # warm
+            n, t0 = 0, time.perf_counter()
+            while True:
+                dec(*inp.args())
+                n += 1
+                el = time.perf_counter() - t0
+                if el >= budget_s / 2 or n >= 50:
+                    break
+            res[f"decode_B{B}"] = {"ms_per_step": round(el / n * 1e3, 2), "steps": n,
+                                   "state_gbs": round(B * STATE_BYTES_PER_SEQ * 2 / (el / n) / 1e9, 3)}
+        inp = pkg.inputs.make_prefill_inputs([512] * 8, seed=0, with_state=True)
+        n, t0 = 0, time.perf_counter()
+        while True:
+            pre(*inp.args())
+            n += 1
+            el = time.perf_counter() - t0
+            if el >= budget_s or n >= 20:
+                break
+        res["prefill_8x512"] = {"tokens_per_s": round(n * inp.total_tokens / el, 1), "calls": n}
+        return res
+    finally:
+        torch.set_num_threads(prev)
+
+
 def cpu_prefill_baseline(pkg, budget_s: float):
     from oracle import oracle
 
@@ -836,6 +879,10 @@ def run_ours(args):
     if rank == 0 and ws == 1 and not args.skip_cpu and wl == "all":
         line["cpu_baseline"] = cpu_decode_baseline(pkg, args.cpu_budget)
         line["cpu_baseline_prefill"] = cpu_prefill_baseline(pkg, args.cpu_budget)
+        try:  # the reference's own PyTorch code on the host CPU (ride-along; the C port is the baseline proper)
+            line["cpu_reference_torch"] = cpu_torch_reference(pkg, args.cpu_budget)
+        except Exception as e:  # noqa: BLE001
+            line["cpu_reference_torch"] = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
     if ws > 1:
         import torch.distributed as dist
 
