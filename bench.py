@@ -53,9 +53,11 @@ DECODE_BYTES_FIXED = 64
 PREFILL_BYTES_PER_TOKEN = 1024 + 1024 + 2048 + 16 + 16 + 2048
 PREFILL_FLOPS_PER_TOKEN = 1452715.0
 # ncu DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one prefill
-# call, summed over its kernels, per leg; filled from the captures summarised
-# under profiles/ (None: not captured for the current kernels)
-PREFILL_NCU_TRAFFIC: dict = {}
+# call, summed over its kernels (table, prepare, carry), per leg, from one
+# capture of this file's own --workload prefill2 / prefill3 runs
+# (profiles/prefill_call_traffic_config2_config3.md); legs without a capture
+# report None
+PREFILL_NCU_TRAFFIC = {"config2": 28573184, "config3": 1083683584}
 L2_FLUSH_BYTES = 256 << 20
 SLEEP_CYCLES = 200_000  # ~100 us GPU spin before each timed step (outside the events)
 # dram__bytes_read.sum + dram__bytes_write.sum per gdn_decode_kernel launch at
