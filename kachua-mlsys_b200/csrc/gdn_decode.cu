@@ -297,19 +297,20 @@ cudaError_t launch_decode_tokens(const DecodeParams& p, int T, cudaStream_t stre
     return cudaGetLastError();
 }
 
-// Rows per warp (per CTA of 4 warps: 4 x RPW rows).  Measured per launch
-// (ncu, caches flushed, fp32 state): up to 128 heads (B <= 16 at 8 v-heads)
-// the smallest tile is fastest (the step is one round trip of latency and
-// more CTAs spread it over more SMs: B = 16 4.96 us at 4 rows vs 5.60 at 8);
-// from there to 2048 heads 8 rows (B = 64 10.9 us, B = 128 18.1 us); beyond,
-// 16 rows, which also won the back-to-back config-1 steady state.
+// Rows per warp (per CTA of 4 warps: 4 x RPW rows).  Up to 128 heads (B <= 16
+// at 8 v-heads) the smallest tile: the step is one round trip of latency and
+// more CTAs spread it over more SMs (ncu, caches flushed: B = 16 4.96 us at 4
+// rows vs 5.60 at 8).  Beyond, the largest tile that still gives >= 2 CTAs
+// per SM (per-call event timing: B = 32 / 64 10.2 / 14.3 us at 16 rows vs
+// 10.9 / 15.2 at 8).
 static int pick_rows_per_warp(int64_t heads, bool bf16_state) {
     const int sms = device_sm_count();
     // a bf16 row is half as many bytes: 32 rows keep the fp32 kernel's 256 B of loads in flight per thread
     if (bf16_state && heads >= 2 * sms) return 32;
     if (heads <= 128) return 4;
-    if (heads < 2048) return 8;
-    return 16;
+    if (heads * (kD / 64) >= 2 * sms) return 16;
+    if (heads * (kD / 32) >= 2 * sms) return 8;
+    return 4;
 }
 
 template <bool BF16S>
