@@ -187,16 +187,7 @@ __global__ void __launch_bounds__(1024) gdn_chunk_table_kernel(const PrefillPara
             const long long excl = carry_s + (warp > 0 ? warp_tot[warp - 1] : 0) + (x - nch);
             if (s < p.num_seqs) {
                 base[s] = static_cast<int>(excl < L.R ? excl : L.R);
-                for (int j = 0; j < nch; ++j) {
-                    const long long rec = excl + j;
-                    if (rec >= L.R) {
-                        record_status(16 /* GDN_ERR_DEVICE_BAD_SEQLENS */);
-                        break;
-                    }
-                    const int64_t ts = t0 + static_cast<int64_t>(j) * kC;
-                    const int64_t len = t1 - ts < kC ? t1 - ts : kC;
-                    table[rec] = make_int4(static_cast<int>(s), static_cast<int>(ts), static_cast<int>(len), 0);
-                }
+                if (excl + nch > L.R) record_status(16 /* GDN_ERR_DEVICE_BAD_SEQLENS */);  // records dropped
             }
             __syncthreads();
             if (tid == 0) carry_s += warp_tot[31];
@@ -207,7 +198,28 @@ __global__ void __launch_bounds__(1024) gdn_chunk_table_kernel(const PrefillPara
             base[p.num_seqs] = static_cast<int>(tot < L.R ? tot : L.R);
             reinterpret_cast<int*>(ws + L.off_hdr)[0] = static_cast<int>(tot < L.R ? tot : L.R);
         }
+        __syncthreads();  // base[] is complete (global writes of this block, visible after the barrier)
         {
+            // the records, one per thread: record r belongs to the last sequence s
+            // with base[s] <= r (binary search; empty sequences share a base)
+            const int nrec = base[p.num_seqs];
+            const int N = static_cast<int>(p.num_seqs);
+            for (int r = tid; r < nrec; r += 1024) {
+                int lo = 0, hi = N - 1;  // base[lo] <= r < base[N]
+                while (lo < hi) {
+                    const int mid = (lo + hi + 1) >> 1;
+                    if (base[mid] <= r) lo = mid; else hi = mid - 1;
+                }
+                int64_t t0, t1;
+                seq_bounds(p, lo, t0, t1);
+                const int64_t ts = t0 + static_cast<int64_t>(r - base[lo]) * kC;
+                const int64_t len = t1 - ts < kC ? t1 - ts : kC;
+                table[r] = make_int4(lo, static_cast<int>(ts), static_cast<int>(len), 0);
+            }
+        }
+        if (p.num_seqs == 1) {
+            if (tid == 0) reinterpret_cast<int*>(ws + L.off_order)[0] = 0;
+        } else {
             // Sequences in order of decreasing chunk count (counting sort, counts
             // above 1023 share the first bin): the single-pass carry starts the
             // longest chains first, so that short ones fill in behind them.
