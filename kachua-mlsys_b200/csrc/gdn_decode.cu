@@ -162,14 +162,32 @@ __global__ void __launch_bounds__(32 * WARPS) gdn_decode_kernel(const DecodePara
 // token), their loads in flight together with the state's.
 // q/k/v/a/b/out are [B, T, heads, ...].
 //
-// Measured at B = 256 (T = 2 / 4 / 8: 55 / 66 / 92 us, against 72 / 88 / 129
+// Measured at B = 256 (T = 2 / 4 / 8: 53 / 63 / 86 us, against 72 / 88 / 129
 // for the token-recurrent prefill kernel it replaces): the state stream alone
-// takes ~41 us and each token adds ~5.5 us of fp32 FMA and shuffle work per
-// SM that this load -> compute -> store order does not overlap with HBM.  A
+// takes ~41 us and each token adds ~5 us of fp32 FMA and shuffle work per SM
+// that this load -> compute -> store order does not overlap with HBM.  The
+// per-token dot products reduce by a transposed 8-lane reduction (12 shuffles
+// per token and thread at 16 rows per warp instead of 24: 55 / 66 / 90 us
+// before).  A
 // persistent variant that double- (and 3- and 4-) buffered 16-32 KiB state
 // tiles in shared memory with bulk async copies was slower at every T (T = 2
 // / 8: 64-82 / 114-143 us) and was not kept.
 constexpr int kTokBlk = 16;
+
+// One level of the transposed reduction over the lanes `bit` apart: a lane
+// whose `bit` is set keeps the upper half of its CNT values and sends the
+// lower half to its partner (and the other way round), adding what it
+// receives; the first CNT / 2 entries then hold the kept half's partial sums.
+template <int CNT, int N>
+__device__ __forceinline__ void transpose_reduce_step(float (&v)[N], int sub, int bit) {
+    const bool upper = (sub & bit) != 0;
+#pragma unroll
+    for (int e = 0; e < CNT / 2; ++e) {
+        const float keep = upper ? v[CNT / 2 + e] : v[e];
+        const float send = upper ? v[e] : v[CNT / 2 + e];
+        v[e] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
+    }
+}
 
 template <int RPW>
 __global__ void __launch_bounds__(128) gdn_decode_tokens_kernel(const DecodeParams p, int T) {
@@ -246,6 +264,13 @@ __global__ void __launch_bounds__(128) gdn_decode_tokens_kernel(const DecodePara
             }
             const float g = s_g[i], beta = s_b[i], qk = s_qk[i];
             const int64_t orow = ((bi * T + tb + i) * p.hv + h) * kD + row0;
+            // the 2 x kPasses partial dot products of this lane (k.S and q.S of each
+            // of its rows), then a transposed reduction over the 8 lanes of the row
+            // group: each xor level hands half of the remaining values to the
+            // partner lane, so 2P values take 2P - 1 shuffles instead of 3 x 2P;
+            // afterwards lane sub holds the total of value sub / (8 / 2P)
+            constexpr int kVals = 2 * kPasses;
+            float vals[kVals];
 #pragma unroll
             for (int ps = 0; ps < kPasses; ++ps) {
                 float ks = 0.f, qs = 0.f;
@@ -255,12 +280,36 @@ __global__ void __launch_bounds__(128) gdn_decode_tokens_kernel(const DecodePara
                     ks += s.x * k4[j].x + s.y * k4[j].y + s.z * k4[j].z + s.w * k4[j].w;
                     qs += s.x * q4[j].x + s.y * q4[j].y + s.z * q4[j].z + s.w * q4[j].w;
                 }
+                vals[ps] = ks;
+                vals[kPasses + ps] = qs;
+            }
+            if constexpr (kVals == 8) {
+                transpose_reduce_step<8>(vals, sub, 4);
+                transpose_reduce_step<4>(vals, sub, 2);
+                transpose_reduce_step<2>(vals, sub, 1);
+            } else if constexpr (kVals == 4) {
+                transpose_reduce_step<4>(vals, sub, 4);
+                transpose_reduce_step<2>(vals, sub, 2);
+                vals[0] += __shfl_xor_sync(0xffffffffu, vals[0], 1);
+            } else {
+                transpose_reduce_step<2>(vals, sub, 4);
+                vals[0] += __shfl_xor_sync(0xffffffffu, vals[0], 2);
+                vals[0] += __shfl_xor_sync(0xffffffffu, vals[0], 1);
+            }
+            constexpr int kSpan = 8 / kVals;  // lanes holding each total
+            const int vidx = sub / kSpan;
+            const bool holds_ks = vidx < kPasses;
+            const int own = holds_ks ? vidx : vidx - kPasses;  // the pass of the held total
+            const float dl =
+                holds_ks ? beta * (bf16_bits_to_float(s_v[i][lrow0 + 4 * own]) - g * vals[0]) : 0.f;
+            const int gbase = lane & ~7;
+            // the output row of a q.S holder needs its pass's delta
+            const float dq = __shfl_sync(0xffffffffu, dl, gbase + own * kSpan);
+            if (!holds_ks && sub % kSpan == 0)
+                out[orow + 4 * own] = __float2bfloat16_rn(p.scale * fmaf(g, vals[0], dq * qk));
 #pragma unroll
-                for (int off = 1; off < 8; off <<= 1) {
-                    ks += __shfl_xor_sync(0xffffffffu, ks, off);
-                    qs += __shfl_xor_sync(0xffffffffu, qs, off);
-                }
-                const float delta = beta * (bf16_bits_to_float(s_v[i][lrow0 + 4 * ps]) - g * ks);
+            for (int ps = 0; ps < kPasses; ++ps) {
+                const float delta = __shfl_sync(0xffffffffu, dl, gbase + ps * kSpan);
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     st[ps][j].x = fmaf(g, st[ps][j].x, delta * k4[j].x);
@@ -268,7 +317,6 @@ __global__ void __launch_bounds__(128) gdn_decode_tokens_kernel(const DecodePara
                     st[ps][j].z = fmaf(g, st[ps][j].z, delta * k4[j].z);
                     st[ps][j].w = fmaf(g, st[ps][j].w, delta * k4[j].w);
                 }
-                if (sub == 0) out[orow + 4 * ps] = __float2bfloat16_rn(p.scale * fmaf(g, qs, delta * qk));
             }
         }
     }
