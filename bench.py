@@ -866,6 +866,9 @@ def run_ours(args):
             pf["context_parallel_1x131072"] = {"error": str(e)[:300]}
     if pf:
         line["prefill"] = pf
+        # flat summary of the legs: tokens/s and the roofline fraction of its bound
+        line["prefill_tokens_per_s"] = {k: round(v["tokens_per_s"], 1) for k, v in pf.items() if "tokens_per_s" in v}
+        line["prefill_roofline_frac"] = {k: v["roofline"]["frac"] for k, v in pf.items() if v.get("roofline")}
     if wl in ("all", "config4"):
         # BASELINE config 4 as written: the fixed global problem split over the N ranks
         line["config4a"] = bench_config4a(pkg, device, rank, ws, args.steps, args.warmup, peaks)
