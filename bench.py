@@ -5,11 +5,18 @@ one token each, fp32 k-last state [256, 8, 128, 128] -- reported as the
 state-stream HBM throughput in GB/s summed over GPUs (weak scaling: every GPU
 owns its own 256 sequences; sequences are independent, so there is no
 collective in the timed region).  Per-step microseconds are in
-``ms_per_step``/``decode_us_per_step``.  Prefill tokens/s (configs 2 and 3 on
-one GPU; a config-4b shard of 8 x 8192 tokens per GPU for N > 1) ride along
-in ``prefill``; for N > 1 so does the context-parallel prefill of one
-131072-token sequence split by token range over the N GPUs (strong scaling,
-with the one-GPU time of the same sequence beside it).
+``ms_per_step``/``decode_us_per_step``; ``roofline`` relates the step to the
+measured copy peak, ``e2e`` times it through the public API with the state in
+pinned host memory.
+
+Ride-alongs in the same line: prefill configs 2 and 3 and the 16 / 32-head
+layout (one GPU), each with its roofline; ``config4a`` / ``config4b``, BASELINE
+config 4 as written (the fixed global problem split over the N ranks, with
+and without the final gather to rank 0); for N > 1 the context-parallel
+prefill of one 131072-token sequence split by token range over the N GPUs;
+on one GPU the reference's own decode and prefill kernels timed beside these
+(``reference_gpu``) and the CPU baselines (``cpu_baseline``: the C port;
+``cpu_reference_torch``: the reference's PyTorch code).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...     (N > 1)
@@ -18,9 +25,10 @@ Timing: W untimed warm-up steps, then exactly K steps between a barrier and
 a device synchronize, timed with CUDA events on the launching stream; the
 reported time is the max over ranks.  Decode steps run back to back over three
 rotating 128 MiB state buffers (inputs larger than L2, each step pays for its
-own write-backs).  Prefill steps are timed one by one with an L2 flush (a
-256 MiB read) between them, outside the events.  ``--impl reference`` times the reference's own
-algorithm on the host CPU (the oracle port in oracle/, all host threads).
+own write-backs).  Other legs are timed call by call with an L2 flush (a
+256 MiB read) before each, outside the events.  ``--impl reference`` times the
+reference's own algorithm on the host CPU (the oracle port in oracle/, all
+host threads).
 """
 from __future__ import annotations
 
