@@ -613,7 +613,7 @@ def agreement(ro, rns, out, ns) -> dict:
     return {"out_max_abs_diff": od, "state_rel_diff": sd, "ref_within_tolerance": ok}
 
 
-def bench_reference_gpu(pkg, device, flush, steps=20):
+def bench_reference_gpu(pkg, device, flush, steps=20, prefill=True):
     """The reference's own GPU kernels beside this project's, same box, same
     run, same timing (per-call CUDA events, L2 flushed by a 256 MiB read
     before every call, median): the reference decode extension
@@ -648,6 +648,8 @@ def bench_reference_gpu(pkg, device, flush, steps=20):
         dec[str(B)] = {"ref_us": round(mr, 2), "ours_us": round(mo, 2), "ratio": round(mr / mo, 3),
                        **agreement(ro, rns, out, ns)}
     res["decode_vs_reference_cuda"] = dec
+    if not prefill:
+        return res
     pre = {}
     try:
         mod = rg.prefill_module()
@@ -884,9 +886,10 @@ def run_ours(args):
         line["config4b"] = bench_config4b(pkg, device, rank, ws, max(3, args.steps // 2), min(args.warmup, 3),
                                           flush, peaks)
         torch.cuda.empty_cache()
-    if ws == 1 and wl in ("all", "reference_gpu") and not args.skip_ref_gpu:
+    if ws == 1 and wl in ("all", "reference_gpu", "reference_gpu_decode") and not args.skip_ref_gpu:
         try:  # a ride-along: an error is reported in the line, not fatal to it
-            line["reference_gpu"] = bench_reference_gpu(pkg, device, flush)
+            line["reference_gpu"] = bench_reference_gpu(pkg, device, flush,
+                                                         prefill=wl != "reference_gpu_decode")
         except Exception as e:  # noqa: BLE001
             line["reference_gpu"] = {"error": f"{type(e).__name__}: {str(e)[:300]}"}
     if rank == 0 and ws == 1 and not args.skip_cpu and wl == "all":
@@ -951,7 +954,7 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds per CPU-baseline sample")
     ap.add_argument("--workload", default="all",
                     choices=["all", "decode", "prefill2", "prefill3", "prefill_heads", "config4", "prefill_cp",
-                             "reference_gpu"],
+                             "reference_gpu", "reference_gpu_decode"],
                     help="all = the JSON line the driver reads; the others time one workload")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline (profiling runs)")
     ap.add_argument("--skip-e2e", action="store_true", help="omit the host-buffer e2e leg")
