@@ -15,9 +15,10 @@
 //   * 8 lanes own one state row; lane `sub` holds floats 4*sub + 32*j
 //     (j = 0..3) -- every float4 load/store instruction of the 8 lanes covers
 //     128 contiguous bytes, a warp covers 4 rows per pass;
-//   * a CTA is 4 warps x RPW rows per warp; every load of a thread's rows is
-//     issued before any arithmetic, so a 128-thread CTA keeps 16*RPW*128 bytes
-//     in flight;
+//   * a CTA is WARPS warps x RPW rows per warp (fp32 state: 4 rows, 2 or 4
+//     warps; the choice is measured, see pick_decode_shape); every load of a
+//     thread's rows is issued before any arithmetic, so a thread keeps
+//     16 * RPW bytes in flight;
 //   * both dot products reduce with 3 xor-shuffles inside the 8-lane group;
 //   * the new state is written once with streaming (evict-first) stores.
 // Each thread reads all of its state elements before writing any of them and
@@ -345,45 +346,56 @@ cudaError_t launch_decode_tokens(const DecodeParams& p, int T, cudaStream_t stre
     return cudaGetLastError();
 }
 
-// Rows per warp (per CTA of 4 warps: 4 x RPW rows).  Up to 128 heads (B <= 16
-// at 8 v-heads) the smallest tile: the step is one round trip of latency and
-// more CTAs spread it over more SMs (ncu, caches flushed: B = 16 4.96 us at 4
-// rows vs 5.60 at 8).  Beyond, the largest tile that still gives >= 2 CTAs
-// per SM (per-call event timing: B = 32 / 64 10.2 / 14.3 us at 16 rows vs
-// 10.9 / 15.2 at 8).
-static int pick_rows_per_warp(int64_t heads, bool bf16_state) {
+// CTA shape: rows per warp x warps per CTA.
+//
+// fp32 state: 4 rows per warp at every batch (16 rows per CTA of 4 warps; 2
+// warps from 9 to 128 heads).  Kernel times from one ncu pass with the caches
+// flushed before every launch, the reference's CUDA decode kernel in the same
+// capture (4 rows x 4 warps / 2 warps / the earlier 16 rows x 4 warps /
+// reference, us): B = 8: 4.35 / 4.10 / - / 4.22; B = 16: 5.25 / 4.90 / - /
+// 5.12; B = 32: 6.66 / 7.17 / 7.94 / 7.10; B = 64: 10.62 / 10.40 / 12.03 /
+// 10.46; B = 256: 36.61 / 36.93 / 38.59 / 36.48; B = 4096: 618.7 / - / 622.1 /
+// 620.1.  Many small CTAs start and finish out of step, which keeps more of
+// the stream in flight at every moment than a few large ones; back to back
+// (three rotating state buffers) B = 256 takes 42.98 us at 4 rows against
+// 43.86 at 16.
+// bf16 state: half as many bytes per row, so 32 rows per warp keep the fp32
+// kernel's 256 B of loads in flight per thread at large batch; 4 rows up to
+// 128 heads, then the largest tile that still gives >= 2 CTAs per SM.
+struct DecodeShape {
+    int rpw, warps;
+};
+static DecodeShape pick_decode_shape(int64_t heads, bool bf16_state) {
+    if (!bf16_state) return {4, heads > 8 && heads <= 128 ? 2 : 4};
     const int sms = device_sm_count();
-    // a bf16 row is half as many bytes: 32 rows keep the fp32 kernel's 256 B of loads in flight per thread
-    if (bf16_state && heads >= 2 * sms) return 32;
-    if (heads <= 128) return 4;
-    if (heads * (kD / 64) >= 2 * sms) return 16;
-    if (heads * (kD / 32) >= 2 * sms) return 8;
-    return 4;
-}
-
-template <bool BF16S>
-static void launch_decode_rpw(int rpw, unsigned grid, const DecodeParams& p, cudaStream_t stream) {
-    switch (rpw) {
-        case 32:  // bf16 state only
-            if constexpr (BF16S) gdn_decode_kernel<32, true><<<grid, 128, 0, stream>>>(p);
-            break;
-        case 16: gdn_decode_kernel<16, BF16S><<<grid, 128, 0, stream>>>(p); break;
-        case 8: gdn_decode_kernel<8, BF16S><<<grid, 128, 0, stream>>>(p); break;
-        default: gdn_decode_kernel<4, BF16S><<<grid, 128, 0, stream>>>(p); break;
-    }
+    if (heads >= 2 * sms) return {32, 4};
+    if (heads <= 128) return {4, 4};
+    if (heads * (kD / 64) >= 2 * sms) return {16, 4};
+    if (heads * (kD / 32) >= 2 * sms) return {8, 4};
+    return {4, 4};
 }
 
 // bf16_state: p.state / p.new_state point to bf16 [B, 8, 128, 128] arrays.
 cudaError_t launch_decode(const DecodeParams& p, cudaStream_t stream, bool bf16_state = false) {
     if (p.batch == 0) return cudaSuccess;
     const int64_t heads = p.batch * p.hv;
-    const int rpw = pick_rows_per_warp(heads, bf16_state);
-    const int64_t grid = heads * (kD / (4 * rpw));
+    const DecodeShape sh = pick_decode_shape(heads, bf16_state);
+    const int64_t grid = heads * (kD / (sh.warps * sh.rpw));
     if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
-    if (bf16_state)
-        launch_decode_rpw<true>(rpw, static_cast<unsigned>(grid), p, stream);
-    else
-        launch_decode_rpw<false>(rpw, static_cast<unsigned>(grid), p, stream);
+    const unsigned g = static_cast<unsigned>(grid);
+    if (!bf16_state) {
+        if (sh.warps == 2)
+            gdn_decode_kernel<4, false, 2><<<g, 64, 0, stream>>>(p);
+        else
+            gdn_decode_kernel<4, false, 4><<<g, 128, 0, stream>>>(p);
+    } else {
+        switch (sh.rpw) {
+            case 32: gdn_decode_kernel<32, true><<<g, 128, 0, stream>>>(p); break;
+            case 16: gdn_decode_kernel<16, true><<<g, 128, 0, stream>>>(p); break;
+            case 8: gdn_decode_kernel<8, true><<<g, 128, 0, stream>>>(p); break;
+            default: gdn_decode_kernel<4, true><<<g, 128, 0, stream>>>(p); break;
+        }
+    }
     return cudaGetLastError();
 }
 
