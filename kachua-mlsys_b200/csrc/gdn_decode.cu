@@ -359,16 +359,16 @@ cudaError_t launch_decode_tokens(const DecodeParams& p, int T, cudaStream_t stre
 // the stream in flight at every moment than a few large ones; back to back
 // (three rotating state buffers) B = 256 takes 42.98 us at 4 rows against
 // 43.86 at 16.
-// bf16 state: half as many bytes per row, so 32 rows per warp keep the fp32
-// kernel's 256 B of loads in flight per thread at large batch; 4 rows up to
-// 128 heads, then the largest tile that still gives >= 2 CTAs per SM.
+// bf16 state: 4 rows up to 128 heads, then the largest tile up to 16 rows
+// that still gives >= 2 CTAs per SM (back to back / L2 flushed per call, B =
+// 256: 24.67 / 26.44 us at 16 rows against 26.72 / 28.64 at 32 and 30.83 /
+// 35.02 at 4; B = 64: 8.36 / 12.28 at 16 against 8.77 / 14.24 at 32).
 struct DecodeShape {
     int rpw, warps;
 };
 static DecodeShape pick_decode_shape(int64_t heads, bool bf16_state) {
     if (!bf16_state) return {4, heads > 8 && heads <= 128 ? 2 : 4};
     const int sms = device_sm_count();
-    if (heads >= 2 * sms) return {32, 4};
     if (heads <= 128) return {4, 4};
     if (heads * (kD / 64) >= 2 * sms) return {16, 4};
     if (heads * (kD / 32) >= 2 * sms) return {8, 4};
@@ -390,7 +390,6 @@ cudaError_t launch_decode(const DecodeParams& p, cudaStream_t stream, bool bf16_
             gdn_decode_kernel<4, false, 4><<<g, 128, 0, stream>>>(p);
     } else {
         switch (sh.rpw) {
-            case 32: gdn_decode_kernel<32, true><<<g, 128, 0, stream>>>(p); break;
             case 16: gdn_decode_kernel<16, true><<<g, 128, 0, stream>>>(p); break;
             case 8: gdn_decode_kernel<8, true><<<g, 128, 0, stream>>>(p); break;
             default: gdn_decode_kernel<4, true><<<g, 128, 0, stream>>>(p); break;

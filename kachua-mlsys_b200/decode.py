@@ -131,14 +131,19 @@ class PreparedLaunch:
 
     For serving loops that call the same buffers every step (and for CUDA
     graph capture): arguments are checked once here; ``__call__`` launches on
-    the current stream of the tensors' device.
+    the current stream of the tensors' device.  Every form ``launch_gdn``
+    takes is accepted: T >= 1 tokens per sequence, an fp32 or (one token) a
+    bf16 state, any supported head counts; all go through
+    ``gdn_decode_launch_heads``, which routes the reference's 4 / 8 heads to
+    the same kernels as ``gdn_decode_launch``.
     """
 
     def __init__(self, q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state):
+        _need(isinstance(q, torch.Tensor) and q.dim() == 4, "q must be a [B, T, 4, 128] tensor")
         B = validate(q, k, v, state, A_log, a, dt_bias, b, output, new_state)
-        _need(q.shape[1] == 1, "PreparedLaunch is for one token per sequence")
-        _need(heads(q, v) == (HQK, HV), "PreparedLaunch takes 4 q/k and 8 v heads")
-        _need(state.dtype == torch.float32, "PreparedLaunch takes the fp32 state")
+        self.tokens = int(q.shape[1])
+        self.hqk, self.hv = heads(q, v)
+        self.bf16_state = int(state.dtype == torch.bfloat16)
         self._keep = (q, k, v, state, A_log, a, dt_bias, b, output, new_state)
         self.device = q.device
         self.lib = _capi.load()
@@ -152,9 +157,10 @@ class PreparedLaunch:
             raise RuntimeError(f"PreparedLaunch for {self.device} called with cuda:"
                                f"{torch.cuda.current_device()} current")
         stream = torch.cuda.current_stream(self.device).cuda_stream
-        rc = self.lib.gdn_decode_launch(self._ref, ctypes.c_void_p(stream))
+        rc = self.lib.gdn_decode_launch_heads(self._ref, self.hqk, self.hv, self.tokens, self.bf16_state,
+                                              ctypes.c_void_p(stream))
         if rc:
-            _capi.check(rc, "gdn_decode_launch")
+            _capi.check(rc, "gdn_decode_launch_heads")
 
 
 def kernel(q, k, v, state, A_log, a, dt_bias, b, scale=None):

@@ -128,7 +128,7 @@ def test_decode_multi_token_matches_steps_and_in_place(pkg, cuda_dev):
     assert torch.equal(out2, out) and torch.equal(inplace, ns)
 
 
-@pytest.mark.parametrize("batch", [1, 8, 64, 300])
+@pytest.mark.parametrize("batch", [1, 8, 17, 64, 300])
 def test_decode_bf16_state(pkg, orc, cuda_dev, batch):
     """The bf16-state variant equals the oracle run on the bf16 state (read
     as fp32), its new state within bf16 rounding (norm-wise 2^-8), also in
@@ -177,6 +177,33 @@ def test_decode_other_head_counts_bf16_state(pkg, orc, cuda_dev):
     torch.cuda.synchronize()
     torch.testing.assert_close(out.cpu().float(), ro.float(), atol=1e-2, rtol=1e-2)
     assert state_rel_err(ns.cpu().float(), rs) < 2 ** -8
+
+
+@pytest.mark.parametrize("batch,tokens,hqk,hv,bf16", [
+    (256, 1, 4, 8, False), (12, 1, 4, 8, False), (64, 3, 4, 8, False), (40, 1, 4, 8, True), (6, 2, 16, 32, False),
+    (5, 1, 16, 32, True),
+])
+def test_prepared_launch_every_form(pkg, cuda_dev, batch, tokens, hqk, hv, bf16):
+    """PreparedLaunch (the bench's back-to-back step, one ctypes call per
+    launch) computes exactly what launch_gdn computes, for every decode form."""
+    inp = pkg.inputs.make_decode_inputs(batch, seed=batch + tokens, tokens=tokens, hqk=hqk, hv=hv).to(cuda_dev)
+    st = inp.state.to(torch.bfloat16) if bf16 else inp.state
+    ref_out, ref_ns = pkg.decode.launch_gdn(inp.q, inp.k, inp.v, st, inp.A_log, inp.a, inp.dt_bias, inp.b, inp.scale)
+    out, ns = torch.empty_like(ref_out), torch.empty_like(ref_ns)
+    launch = pkg.decode.PreparedLaunch(inp.q, inp.k, inp.v, st, inp.A_log, inp.a, inp.dt_bias, inp.b, inp.scale,
+                                       out, ns)
+    launch()
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref_out) and torch.equal(ns, ref_ns)
+
+
+def test_prepared_launch_rejects_bf16_state_with_tokens(pkg, cuda_dev):
+    inp = pkg.inputs.make_decode_inputs(2, seed=1, tokens=2).to(cuda_dev)
+    s16 = inp.state.to(torch.bfloat16)
+    out = torch.empty((2, 2, 8, 128), dtype=torch.bfloat16, device=cuda_dev)
+    with pytest.raises(ValueError):
+        pkg.decode.PreparedLaunch(inp.q, inp.k, inp.v, s16, inp.A_log, inp.a, inp.dt_bias, inp.b, inp.scale, out,
+                                  torch.empty_like(s16))
 
 
 @pytest.mark.parametrize("batch,slices", [(256, 16), (37, 8), (3, 16)])
