@@ -120,4 +120,33 @@ __device__ __forceinline__ uint2 float4_to_bf16x4(float4 f) {
     return make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
 }
 
+// --------------------------------------------- programmatic dependent launch --
+// In a kernel launched with programmatic stream serialization: wait until the
+// preceding kernel in the stream has completed and its memory is visible (a
+// no-op in a kernel launched normally).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Let the next kernel (if launched with programmatic serialization) begin
+// launching once every CTA of this grid has executed this or exited.
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Launch `kernel` so that it may begin (prologue up to griddep_wait) while the
+// previous kernel in the stream finishes (programmatic dependent launch).
+template <typename... Params, typename... Args>
+static cudaError_t launch_dependent(void (*kernel)(Params...), unsigned grid, unsigned block, size_t smem,
+                                    cudaStream_t stream, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);
+}
+
 }  // namespace gdn

@@ -53,6 +53,12 @@ __global__ void __launch_bounds__(32 * WARPS) gdn_decode_kernel(const DecodePara
     constexpr int kRowsPerCta = WARPS * RPW;
     constexpr int kTiles = kD / kRowsPerCta;
 
+    // Launched as a programmatic dependent of the previous kernel in the
+    // stream (back-to-back decode steps: this step's state is the previous
+    // step's output): the CTAs become resident while that kernel drains and
+    // wait here, before any global access, until it has completed.
+    griddep_launch_dependents();
+    griddep_wait();
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int grp = lane >> 3;  // row within a pass
@@ -197,6 +203,8 @@ __global__ void __launch_bounds__(128) gdn_decode_tokens_kernel(const DecodePara
     constexpr int kRowsPerCta = 4 * RPW;
     constexpr int kTiles = kD / kRowsPerCta;
 
+    griddep_launch_dependents();  // as in gdn_decode_kernel
+    griddep_wait();
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
     const int lane = tid & 31;
@@ -337,13 +345,9 @@ cudaError_t launch_decode_tokens(const DecodeParams& p, int T, cudaStream_t stre
     const int64_t grid = heads * (kD / (4 * rpw));
     if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
     const unsigned g = static_cast<unsigned>(grid);
-    if (rpw == 16)
-        gdn_decode_tokens_kernel<16><<<g, 128, 0, stream>>>(p, T);
-    else if (rpw == 8)
-        gdn_decode_tokens_kernel<8><<<g, 128, 0, stream>>>(p, T);
-    else
-        gdn_decode_tokens_kernel<4><<<g, 128, 0, stream>>>(p, T);
-    return cudaGetLastError();
+    if (rpw == 16) return launch_dependent(gdn_decode_tokens_kernel<16>, g, 128, 0, stream, p, T);
+    if (rpw == 8) return launch_dependent(gdn_decode_tokens_kernel<8>, g, 128, 0, stream, p, T);
+    return launch_dependent(gdn_decode_tokens_kernel<4>, g, 128, 0, stream, p, T);
 }
 
 // CTA shape: rows per warp x warps per CTA.
@@ -375,8 +379,23 @@ static DecodeShape pick_decode_shape(int64_t heads, bool bf16_state) {
     return {4, 4};
 }
 
+// A decode kernel launch: as a programmatic dependent of the previous kernel
+// in the stream (pdl), or normally.
+template <typename... Params, typename... Args>
+static cudaError_t launch_decode_kernel(bool pdl, void (*kernel)(Params...), unsigned grid, unsigned block,
+                                        cudaStream_t stream, Args... args) {
+    if (pdl) return launch_dependent(kernel, grid, block, 0, stream, args...);
+    kernel<<<grid, block, 0, stream>>>(static_cast<Params>(args)...);
+    return cudaGetLastError();
+}
+
 // bf16_state: p.state / p.new_state point to bf16 [B, 8, 128, 128] arrays.
-cudaError_t launch_decode(const DecodeParams& p, cudaStream_t stream, bool bf16_state = false) {
+// pdl: launch as a programmatic dependent of the previous kernel in the
+// stream (consecutive steps overlap one kernel's drain with the next one's
+// launch; every global access of the next still follows the previous
+// kernel's completion).  Off where other stream work -- a copy or an event
+// wait -- sits between the two kernels.
+cudaError_t launch_decode(const DecodeParams& p, cudaStream_t stream, bool bf16_state = false, bool pdl = true) {
     if (p.batch == 0) return cudaSuccess;
     const int64_t heads = p.batch * p.hv;
     const DecodeShape sh = pick_decode_shape(heads, bf16_state);
@@ -384,18 +403,14 @@ cudaError_t launch_decode(const DecodeParams& p, cudaStream_t stream, bool bf16_
     if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
     const unsigned g = static_cast<unsigned>(grid);
     if (!bf16_state) {
-        if (sh.warps == 2)
-            gdn_decode_kernel<4, false, 2><<<g, 64, 0, stream>>>(p);
-        else
-            gdn_decode_kernel<4, false, 4><<<g, 128, 0, stream>>>(p);
-    } else {
-        switch (sh.rpw) {
-            case 16: gdn_decode_kernel<16, true><<<g, 128, 0, stream>>>(p); break;
-            case 8: gdn_decode_kernel<8, true><<<g, 128, 0, stream>>>(p); break;
-            default: gdn_decode_kernel<4, true><<<g, 128, 0, stream>>>(p); break;
-        }
+        if (sh.warps == 2) return launch_decode_kernel(pdl, gdn_decode_kernel<4, false, 2>, g, 64, stream, p);
+        return launch_decode_kernel(pdl, gdn_decode_kernel<4, false, 4>, g, 128, stream, p);
     }
-    return cudaGetLastError();
+    switch (sh.rpw) {
+        case 16: return launch_decode_kernel(pdl, gdn_decode_kernel<16, true>, g, 128, stream, p);
+        case 8: return launch_decode_kernel(pdl, gdn_decode_kernel<8, true>, g, 128, stream, p);
+        default: return launch_decode_kernel(pdl, gdn_decode_kernel<4, true>, g, 128, stream, p);
+    }
 }
 
 }  // namespace gdn

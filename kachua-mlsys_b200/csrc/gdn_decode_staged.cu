@@ -112,7 +112,7 @@ extern "C" int gdn_decode_launch_host_staged(const GdnDecodeArgs* host, const Gd
         p.scale = resolve_scale(host->scale);
         p.hqk = kHQK;
         p.hv = kHV;
-        ok = ok && launch_decode(p, comp) == cudaSuccess;
+        ok = ok && launch_decode(p, comp, false, /*pdl=*/false) == cudaSuccess;  // follows an event wait
         ok = ok && cudaEventRecord(c.done[i], comp) == cudaSuccess &&
              cudaStreamWaitEvent(down, c.done[i], 0) == cudaSuccess;
         down_copy(hns + lo * st, ds + lo * st, (hi - lo) * st);

@@ -1440,23 +1440,6 @@ constexpr int kPathAuto = 0, kPathRecurrent = 1, kPathChunked = 2, kPathSegmente
 // tokens, chunked at 32).
 constexpr int64_t kRecurrentMaxAvgLen = 24;
 
-// Launch `kernel` so that it may begin (prologue up to griddep_wait) while the
-// previous kernel in the stream finishes (programmatic dependent launch).
-template <typename... Params, typename... Args>
-static cudaError_t launch_dependent(void (*kernel)(Params...), unsigned grid, unsigned block, size_t smem,
-                                    cudaStream_t stream, Args... args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(block);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);
-}
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link
 // against libcuda); looked up once per process.

@@ -97,16 +97,6 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     return false;
 }
 
-// --------------------------------------------- programmatic dependent launch --
-// In a kernel launched with programmatic stream serialization: wait until the
-// preceding kernel in the stream has completed and its memory is visible.
-__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-// Let the next kernel (if launched with programmatic serialization) begin
-// launching once every CTA of this grid has executed this or exited.
-__device__ __forceinline__ void griddep_launch_dependents() {
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-
 // ------------------------------------------------------------ bulk copies --
 __device__ __forceinline__ void bulk_g2s(uint32_t dst_smem, const void* src, uint32_t bytes, uint32_t bar) {
     asm volatile(

@@ -206,6 +206,40 @@ def test_prepared_launch_rejects_bf16_state_with_tokens(pkg, cuda_dev):
                                   torch.empty_like(s16))
 
 
+def test_decode_steps_back_to_back_with_copies_between(pkg, cuda_dev):
+    """Decode kernels launch as programmatic dependents of the previous kernel
+    in the stream.  Consecutive steps (each reading the state the previous one
+    wrote) and steps whose token inputs were just copied up from pinned host
+    memory in the same stream, with no synchronisation in between, give the
+    bits of the same steps run one at a time."""
+    B, steps = 64, 6
+    inps = [pkg.inputs.make_decode_inputs(B, seed=300 + i) for i in range(steps)]
+    h_tok = [[t.pin_memory() for t in (x.q, x.k, x.v, x.a, x.b)] for x in inps]
+    d_tok = [torch.empty_like(t, device=cuda_dev) for t in h_tok[0]]
+    A_log, dt_bias = inps[0].A_log.to(cuda_dev), inps[0].dt_bias.to(cuda_dev)
+    state0 = inps[0].state.to(cuda_dev)
+    # one at a time
+    ref_outs, st = [], state0
+    for i in range(steps):
+        q, k, v, a, b = (t.to(cuda_dev) for t in h_tok[i])
+        out, st = pkg.decode.launch_gdn(q, k, v, st, A_log, a, dt_bias, b, inps[0].scale)
+        torch.cuda.synchronize()
+        ref_outs.append(out.clone())
+    ref_state = st.clone()
+    # back to back: copy up, decode, next copy, next decode ... one sync at the end
+    outs = [torch.empty_like(ref_outs[0]) for _ in range(steps)]
+    states = [state0, torch.empty_like(state0), torch.empty_like(state0)]
+    for i in range(steps):
+        for d, h in zip(d_tok, h_tok[i]):
+            d.copy_(h, non_blocking=True)
+        pkg.decode.launch_gdn(d_tok[0], d_tok[1], d_tok[2], states[i % 3], A_log, d_tok[3], dt_bias, d_tok[4],
+                              inps[0].scale, output=outs[i], new_state=states[(i + 1) % 3])
+    torch.cuda.synchronize()
+    for i in range(steps):
+        assert torch.equal(outs[i], ref_outs[i]), i
+    assert torch.equal(states[steps % 3], ref_state)
+
+
 @pytest.mark.parametrize("batch,slices", [(256, 16), (37, 8), (3, 16)])
 def test_host_stager_matches_device_call(pkg, cuda_dev, batch, slices):
     """HostStager (pinned host tensors in and out, state sliced over three
