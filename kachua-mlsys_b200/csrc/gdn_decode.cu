@@ -335,6 +335,24 @@ __global__ void __launch_bounds__(128) gdn_decode_tokens_kernel(const DecodePara
         for (int j = 0; j < 4; ++j) st_stream_f4(dst + (row0 + 4 * ps) * kD + 32 * j, st[ps][j]);
 }
 
+// A decode kernel launch: as a programmatic dependent of the previous kernel
+// in the stream (pdl), or normally.
+template <typename... Params, typename... Args>
+static cudaError_t launch_decode_kernel(bool pdl, void (*kernel)(Params...), unsigned grid, unsigned block,
+                                        cudaStream_t stream, Args... args) {
+    if (pdl) return launch_dependent(kernel, grid, block, 0, stream, args...);
+    kernel<<<grid, block, 0, stream>>>(static_cast<Params>(args)...);
+    return cudaGetLastError();
+}
+
+// Programmatic dependent launch from 65 heads up (B >= 9 at 8 v-heads).  Back
+// to back inside a CUDA graph (per step, normal launch / dependent launch):
+// B = 16 3.46 / 3.40 us, B = 64 8.88 / 8.52, B = 256 41.18 / 40.70; issued
+// one by one from the host, B = 256 43.1 / 41.1.  At B = 8 the dependent
+// launch was slower in the graph (2.48 / 3.08 us), at B = 1 level.  Per call
+// after an idle GPU it makes no difference.
+static bool decode_pdl(int64_t heads) { return heads > 64; }
+
 // Rows per warp of the multi-token kernel: 16 (the fastest at every T
 // measured) while that still gives >= 2 CTAs per SM, else 8, else 4.
 cudaError_t launch_decode_tokens(const DecodeParams& p, int T, cudaStream_t stream) {
@@ -345,9 +363,10 @@ cudaError_t launch_decode_tokens(const DecodeParams& p, int T, cudaStream_t stre
     const int64_t grid = heads * (kD / (4 * rpw));
     if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
     const unsigned g = static_cast<unsigned>(grid);
-    if (rpw == 16) return launch_dependent(gdn_decode_tokens_kernel<16>, g, 128, 0, stream, p, T);
-    if (rpw == 8) return launch_dependent(gdn_decode_tokens_kernel<8>, g, 128, 0, stream, p, T);
-    return launch_dependent(gdn_decode_tokens_kernel<4>, g, 128, 0, stream, p, T);
+    const bool pdl = decode_pdl(heads);
+    if (rpw == 16) return launch_decode_kernel(pdl, gdn_decode_tokens_kernel<16>, g, 128, stream, p, T);
+    if (rpw == 8) return launch_decode_kernel(pdl, gdn_decode_tokens_kernel<8>, g, 128, stream, p, T);
+    return launch_decode_kernel(pdl, gdn_decode_tokens_kernel<4>, g, 128, stream, p, T);
 }
 
 // CTA shape: rows per warp x warps per CTA.
@@ -379,22 +398,12 @@ static DecodeShape pick_decode_shape(int64_t heads, bool bf16_state) {
     return {4, 4};
 }
 
-// A decode kernel launch: as a programmatic dependent of the previous kernel
-// in the stream (pdl), or normally.
-template <typename... Params, typename... Args>
-static cudaError_t launch_decode_kernel(bool pdl, void (*kernel)(Params...), unsigned grid, unsigned block,
-                                        cudaStream_t stream, Args... args) {
-    if (pdl) return launch_dependent(kernel, grid, block, 0, stream, args...);
-    kernel<<<grid, block, 0, stream>>>(static_cast<Params>(args)...);
-    return cudaGetLastError();
-}
-
 // bf16_state: p.state / p.new_state point to bf16 [B, 8, 128, 128] arrays.
 // pdl: launch as a programmatic dependent of the previous kernel in the
-// stream (consecutive steps overlap one kernel's drain with the next one's
-// launch; every global access of the next still follows the previous
-// kernel's completion).  Off where other stream work -- a copy or an event
-// wait -- sits between the two kernels.
+// stream (decode_pdl decides by size): consecutive steps overlap one
+// kernel's drain with the next one's launch, and every global access of the
+// next still follows the previous kernel's completion.  The host-staged path
+// launches normally: its kernels follow waits on events of other streams.
 cudaError_t launch_decode(const DecodeParams& p, cudaStream_t stream, bool bf16_state = false, bool pdl = true) {
     if (p.batch == 0) return cudaSuccess;
     const int64_t heads = p.batch * p.hv;
@@ -402,6 +411,7 @@ cudaError_t launch_decode(const DecodeParams& p, cudaStream_t stream, bool bf16_
     const int64_t grid = heads * (kD / (sh.warps * sh.rpw));
     if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
     const unsigned g = static_cast<unsigned>(grid);
+    pdl = pdl && decode_pdl(heads);
     if (!bf16_state) {
         if (sh.warps == 2) return launch_decode_kernel(pdl, gdn_decode_kernel<4, false, 2>, g, 64, stream, p);
         return launch_decode_kernel(pdl, gdn_decode_kernel<4, false, 4>, g, 128, stream, p);
