@@ -169,16 +169,18 @@ __global__ void __launch_bounds__(32 * WARPS) gdn_decode_kernel(const DecodePara
 // token), their loads in flight together with the state's.
 // q/k/v/a/b/out are [B, T, heads, ...].
 //
-// Measured at B = 256 (T = 2 / 4 / 8: 53 / 63 / 86 us, against 72 / 88 / 129
-// for the token-recurrent prefill kernel it replaces): the state stream alone
-// takes ~41 us and each token adds ~5 us of fp32 FMA and shuffle work per SM
-// that this load -> compute -> store order does not overlap with HBM.  The
-// per-token dot products reduce by a transposed 8-lane reduction (12 shuffles
-// per token and thread at 16 rows per warp instead of 24: 55 / 66 / 90 us
-// before).  A
-// persistent variant that double- (and 3- and 4-) buffered 16-32 KiB state
-// tiles in shared memory with bulk async copies was slower at every T (T = 2
-// / 8: 64-82 / 114-143 us) and was not kept.
+// Measured at B = 256, per call with the L2 flushed (T = 2 / 4 / 8: 53 / 63 /
+// 86 us, against 72 / 88 / 129 for the token-recurrent prefill kernel it
+// replaces; back to back over rotating state buffers 45 / 53 / 77 us): the
+// state stream alone takes ~41 us and each token adds ~5 us of fp32 FMA and
+// shuffle work per SM that this load -> compute -> store order does not
+// overlap with HBM.  The per-token dot products reduce by a transposed 8-lane
+// reduction (12 shuffles per token and thread at 16 rows per warp instead of
+// 24: 55 / 66 / 90 us before).  A persistent variant that double- (and 3- and
+// 4-) buffered 16-32 KiB state tiles in shared memory with bulk async copies
+// was slower at every T (T = 2 / 8: 64-82 / 114-143 us) and was not kept;
+// so were 1- and 2-warp CTAs and 8 rows per warp (no faster at T = 2-4,
+// slower at T = 8).
 constexpr int kTokBlk = 16;
 
 // One level of the transposed reduction over the lanes `bit` apart: a lane
