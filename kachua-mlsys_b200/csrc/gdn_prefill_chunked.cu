@@ -69,10 +69,10 @@ using namespace tc05;
 constexpr int kC = 64;
 // Per (chunk record, v-head) the prepare kernel leaves 96 KiB of f16 operand
 // images for the carry, at these offsets:
-constexpr int kRecM = 0;          // M = G_C I - K'^T W   [128 k][128 k']  K-major SW128        32 KiB
-constexpr int kRecKb = 32768;     // K' = tail (.) K      [64 j][128 k]    MN-major (2 kblocks) 16 KiB
-constexpr int kRecUT = 49152;     // U^T                  [128 v][64 j]    K-major SW128        16 KiB
-constexpr int kRecQt = 65536;     // Qt^T = (G (.) Q - P W)^T [128 k][64 i] MN-major SW128      16 KiB
+constexpr int kRecM = 0;          // M = G_C I - K'^T W   [128 k][128 k']  MN-major SW128 (row k: M[k'][k]) 32 KiB
+constexpr int kRecQt = 32768;     // Qt^T = (G (.) Q - P W)^T [128 k][64 i] MN-major SW128 16 KiB (with M: one B operand)
+constexpr int kRecKb = 49152;     // K' = tail (.) K      [64 j][128 k]    MN-major (2 kblocks) 16 KiB
+constexpr int kRecUT = 65536;     // U^T                  [128 v][64 j]    K-major SW128        16 KiB
 constexpr int kRecUt = 81920;     // Ut^T = (P U)^T       [128 v][64 i]    SW128 rows           16 KiB
 constexpr int kHeadRecBytes = 98304;
 
@@ -266,10 +266,10 @@ __global__ void __launch_bounds__(1024) gdn_chunk_table_kernel(const PrefillPara
 // SM, take items blockIdx.x, + gridDim.x, ...): everything the carry's chain
 // does not need, finished per chunk in fp16 operand images (fp32
 // accumulation) and bulk-stored to the workspace:
-//   M    = G_C I - K'^T W     [k][k']  K-major    (B of the state MMA S M^T)
+//   M    = G_C I - K'^T W     [k][k']  MN-major   (row k holds M[k'][k])     } B of the carry's one
+//   Qt^T = (G (.) Q - P W)^T  [k][i]   MN-major                              } product S [M^T | Qt^T]
 //   K'   = tail (.) K         [j][k]   MN-major   (B of the carry's U^T K')
 //   U^T                       [v][j]   K-major    (A of the carry's U^T K')
-//   Qt^T = (G (.) Q - P W)^T  [k][i]   MN-major   (B of the output MMA S Qt^T)
 //   Ut^T = (P U)^T            [v][i]   SW128 rows (added by the output epilogue)
 // K, Q and V arrive by tiled TMA loads straight into SW128 images (rows past
 // the chunk hold the next tokens or zeros; every use masks them).  A^-1 of
@@ -278,7 +278,8 @@ __global__ void __launch_bounds__(1024) gdn_chunk_table_kernel(const PrefillPara
 // off-diagonal block X21 = -X22 (N21 X11) by two tcgen05 products.  The
 // remaining products are computed transposed (M = 128 = k or v rows, all TMEM
 // lanes busy): [W | U]^T = [bGK | bV]^T A^-T, Qt^T = Q^T diag(G) + W^T (-P)^T,
-// Ut^T = -(U^T (-P)^T) and K'^T W.
+// Ut^T = -(U^T (-P)^T) and W^T K' (the transpose of K'^T W, so that lane k
+// holds column k of M and M is written MN-major, beside Qt^T).
 constexpr int kPrepThreads = 256;
 constexpr int kPrKQ = 0;        // bf16 [K;Q] K-major, kblock b at b*16K (rows 0-63 K, 64-127 Q); K rows -> K' in place
 constexpr int kPrN = 32768;     // fp32 diagonal blocks of N (8K) | f16 NL (8K); later TB | diag(G); then Qt^T staging
@@ -766,12 +767,12 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
         if (__syncthreads_or(!ok)) goto abort;
         if (tid == 0) {
             // 7. Qt^T = Q^T diag(G) + W^T (-P)^T -> columns 0-63; -(Ut^T) = U^T (-P)^T -> 64-127;
-            //    K'^T W -> 128-255 (all M=128)
+            //    W^T K' = (K'^T W)^T -> 128-255 (all M=128)
             tc_fence_after();
             mma_ct<kF16, true, false, 64, 128, 64, 128, 64>(tm, aKQ + 8192, aNL, false);
             mma_ct<kF16, false, false, 64, 128, 64, 128, 64>(tm, aRHS, aPO, true);
             mma_ct<kF16, false, false, 64, 128, 64, 128, 64>(tm + 64, aRHS + 16384, aPO, false);
-            mma_ct<kF16, true, false, 64, 128, 128, 128, 128>(tm + 128, aKQ, aRHS, false);
+            mma_ct<kF16, false, true, 64, 128, 128, 128, 128>(tm + 128, aRHS, aKQ, false);
             mma_commit(barW);
             bulk_s2g(out_rec + kRecUT, aRHS + 16384, 16384);  // U^T
             bulk_s2g(out_rec + kRecKb, aKQ, 8192);            // K': two 8 KiB kblocks
@@ -818,7 +819,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
             __syncthreads();  // [K;Q] is free
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
-                const int col0 = 64 * hc + 32 * c;  // M column k'
+                const int col0 = 64 * hc + 32 * c;  // image column k' of row r = k: M[k'][k]
 #pragma unroll
                 for (int e0 = 0; e0 < 32; e0 += 8) {
                     float f[8];
@@ -868,18 +869,22 @@ done:
 // its own MMA operand:
 //   chain   S_{c+1}^T <- U_c^T K'_c + S_c M_c^T     [v][k], fp32 accumulator
 //   output  O_c^T      = S_c Qt_c^T                  [v][i]
-// (U^T K' is issued one chunk early into the second accumulator; S M^T and
-// S Qt^T read S from TMEM as fp16 -- the A operand -- so no shared-memory
-// state image exists).  Warp roles:
+// as ONE product per chunk, S_c [M_c^T | Qt_c^T] (M = 128, N = 192, K = 128;
+// B = [M | Qt^T] MN-major, three 16 KiB N blocks), into the 192 accumulator
+// columns [S | O] of the chunk's parity: U^T K' is issued one chunk early
+// into the S columns, the O columns were cleared by the output warps.  One
+// N = 192 product holds the tensor pipe for 8 x ~96 cycles where an N = 128
+// and an N = 64 product took 8 x (64 + 45).  S is read from TMEM as fp16 --
+// the A operand -- so no shared-memory state image exists.  Warp roles:
 //   warps 0-7   state epilogue: warp w owns lanes 32 (w & 3).. and k columns
 //               64 (w >> 2)..: fp32 accumulator -> fp16 A operand of the next
 //               chunk, and the fp32 final state;
-//   warps 8-11  output epilogue: lane = v, 64 columns = tokens; adds Ut and
-//               writes bf16 rows (coalesced over v);
+//   warps 8-11  output epilogue: lane = v, 64 columns = tokens; reads and
+//               clears the O columns, adds Ut, writes bf16 rows;
 //   warp 12     one thread issues every MMA;
 //   warp 13     one thread issues the bulk copies (refills follow the state
 //               MMA's completion, off the MMA issuer's path).
-// M is double-buffered, [K' | U^T] and Qt^T triple-buffered, each refilled
+// [M | Qt^T] is double-buffered, [K' | U^T] triple-buffered, each refilled
 // when the MMA that read it is known complete, two chunks before use.
 //
 // Segmented carry (few, long sequences): the chunks of a sequence are split
@@ -900,13 +905,15 @@ done:
 // r >= 1 starting from E_0 and composing ranks 1 .. r-1, then its own
 // segments before the CTA's.
 constexpr int kCarryThreads = 448;
-constexpr int kCaM = 0;                         // f16 M K-major [128 k][128 k'], 2 x 32 KiB
-constexpr int kCaKU = 65536;                    // K' [64 j][128 k] (MN-major) + U^T [128 v][64 j] (K-major), 3 x 32 KiB
-constexpr int kCaQt = kCaKU + 3 * 32768;        // f16 Qt^T MN-major [128 k][64 i], 3 x 16 KiB
-constexpr int kCaSmall = kCaQt + 3 * 16384;
+// [M | Qt^T] MN-major [128 k][128 k' | 64 i] (three 16 KiB N blocks), 2 x 48 KiB
+constexpr int kCaM = 0;
+constexpr int kCaMQBytes = 49152;
+constexpr int kCaKU = 2 * kCaMQBytes;           // K' [64 j][128 k] (MN-major) + U^T [128 v][64 j] (K-major), 3 x 32 KiB
+constexpr int kCaSmall = kCaKU + 3 * 32768;     // (the composition steps' T and Z buffers span [0, kCaSmall))
 constexpr int kCaOut = kCaSmall + 1024;         // bf16 output tile [64 i][128 v]: two SW128 images (v 0-63, 64-127)
 constexpr int kCaSmem = kCaOut + 16384 + 1024;
-constexpr int kCaTmemCols = 512;  // accS x 2 [0, 256), fp16 S x 2 [256, 384), accO x 2 [384, 512)
+// per chunk parity b: [accS | accO] at 192 b (the product's N = 192 columns), fp16 S x 2 at [384, 512)
+constexpr int kCaTmemCols = 512;
 
 enum CarryRole { kRoleMain = 0, kRoleSum0 = 1, kRoleSumT = 2, kRoleSumZ = 3 };
 
@@ -928,15 +935,13 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = smem_align1024(smem_raw);
     const Smem Sm{sm, smem_u32(sm)};
-    const uint32_t aM = smem_u32(sm + kCaM), aKU = smem_u32(sm + kCaKU), aQt = smem_u32(sm + kCaQt);
+    const uint32_t aM = smem_u32(sm + kCaM), aKU = smem_u32(sm + kCaKU);
     const uint32_t bar0 = smem_u32(sm + kCaSmall);
-    auto fullM = [&](int b) { return bar0 + 8 * b; };         // 2
+    auto fullM = [&](int b) { return bar0 + 8 * b; };         // 2 ([M | Qt^T])
     auto fullKU = [&](int b) { return bar0 + 16 + 8 * b; };   // 3
-    auto fullQt = [&](int b) { return bar0 + 40 + 8 * b; };   // 3
-    // state MMA done, alternating by chunk parity so that a late waiter never
-    // sees the same barrier complete twice
+    // the chunk's product done (next state and output), alternating by chunk
+    // parity so that a late waiter never sees the same barrier complete twice
     auto mmaS = [&](int c) { return (c & 1) ? bar0 + 120 : bar0 + 64; };
-    auto mmaO = [&](int b) { return bar0 + 72 + 8 * b; };     // 2
     const uint32_t imgReady = bar0 + 88;
     auto oFree = [&](int b) { return bar0 + 96 + 8 * b; };    // 2
     const uint32_t drain = bar0 + 112;
@@ -1068,11 +1073,12 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     }
 
     const bool issuer = tid == 12 * 32, loader = tid == 13 * 32;
-    int topM = -1, topKU = -1, topQt = -1;  // loader: highest chunk whose copy was issued
-    auto issue_M = [&](int c) {
+    int topM = -1, topKU = -1;  // loader: highest chunk whose copy was issued
+    auto issue_M = [&](int c) {  // M and Qt^T are adjacent in the record: [M | Qt^T]
         const int b = c & 1;
-        mbar_expect_tx(fullM(b), 32768);
-        bulk_g2s(aM + b * 32768, rec_ptr(c) + kRecM, 32768, fullM(b));
+        const uint32_t bytes = outputs ? kCaMQBytes : 32768;
+        mbar_expect_tx(fullM(b), bytes);
+        bulk_g2s(aM + b * kCaMQBytes, rec_ptr(c) + kRecM, bytes, fullM(b));
         topM = c;
     };
     auto issue_KU = [&](int c) {  // K' and U^T are adjacent in the record
@@ -1081,19 +1087,11 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
         bulk_g2s(aKU + b * 32768, rec_ptr(c) + kRecKb, 32768, fullKU(b));
         topKU = c;
     };
-    auto issue_Qt = [&](int c) {
-        const int b = c % 3;
-        mbar_expect_tx(fullQt(b), 16384);
-        bulk_g2s(aQt + b * 16384, rec_ptr(c) + kRecQt, 16384, fullQt(b));
-        topQt = c;
-    };
     if (issuer) {
         for (int b = 0; b < 2; ++b) mbar_init(fullM(b), 1);
         for (int b = 0; b < 3; ++b) mbar_init(fullKU(b), 1);
-        for (int b = 0; b < 3; ++b) mbar_init(fullQt(b), 1);
         mbar_init(mmaS(0), 1);
         mbar_init(mmaS(1), 1);
-        for (int b = 0; b < 2; ++b) mbar_init(mmaO(b), 1);
         mbar_init(imgReady, 8);
         for (int b = 0; b < 2; ++b) mbar_init(oFree(b), 4);
         mbar_init(drain, 1);
@@ -1110,9 +1108,18 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
     tc_fence_after();
     griddep_wait();  // the operand images / segment summaries of the preceding kernel are complete
     const uint32_t tm = *tmem_slot;
-    auto accS = [&](int b) { return tm + 128 * b; };
-    auto sA = [&](int b) { return tm + 256 + 64 * b; };
-    auto accO = [&](int b) { return tm + 384 + 64 * b; };
+    auto accS = [&](int b) { return tm + 192 * b; };
+    auto accO = [&](int b) { return tm + 192 * b + 128; };
+    auto sA = [&](int b) { return tm + 384 + 64 * b; };
+    if (outputs && warp >= 8 && warp < 12) {
+        // the output columns start cleared: each chunk's product accumulates S Qt^T
+        // onto them, and the output warps clear them again once read
+        const uint32_t z[32] = {};
+        for (int b = 0; b < 2; ++b)
+            for (int half = 0; half < 2; ++half) tmem_st32(taddr(accO(b), 32 * (warp - 8), 32 * half), z);
+        tmem_wait_st();
+        tc_fence_before();
+    }
 
     // The chain's start, and the summaries composed onto it before any chunk:
     // segmented pass C starts at segment 1 (Sum0's state) and composes
@@ -1234,8 +1241,6 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
         for (int c = 0; c < 2 && c < nch; ++c) issue_M(c);
         if (dpart)
             for (int c = 0; c < 3 && c < nch; ++c) issue_KU(c);
-        if (outputs)
-            for (int c = 0; c < 2 && c < nch; ++c) issue_Qt(c);
         if (outputs)  // Ut^T is read by the output warps straight from global memory
             for (int c = 0; c < 2 && c < nch; ++c) bulk_prefetch_l2(rec_ptr(c) + kRecUt, 16384);
     }
@@ -1303,7 +1308,7 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
         for (int c = 0; outputs && c < nch; ++c) {
             const int rows = len - kC * c < kC ? len - kC * c : kC;
             // one verdict for the four warps (they meet at named barriers below)
-            const bool okc = named_sync_and(1, 128, mbar_wait(mmaO(c & 1), (c >> 1) & 1));
+            const bool okc = named_sync_and(1, 128, mbar_wait(mmaS(c), (c >> 1) & 1));
             tc_fence_after();
             if (!okc) {
                 if (lane == 0) record_status(32);
@@ -1316,7 +1321,11 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
                 float o[32];
                 tmem_ld32(taddr(accO(c & 1), 32 * q, 32 * half), o);
                 tmem_wait_ld();
-                if (half == 1) {  // the accumulator is read: release it before the stores
+                if (half == 1) {  // read: clear the columns for chunk c + 2 and release them before the stores
+                    const uint32_t z[32] = {};
+                    tmem_st32(taddr(accO(c & 1), 32 * q, 0), z);
+                    tmem_st32(taddr(accO(c & 1), 32 * q, 32), z);
+                    tmem_wait_st();
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(oFree(c & 1));
@@ -1367,11 +1376,16 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
             mma_ct<kF16, false, true, 64, 128, 64, 128, 128>(accS(0), aKU + 16384, aKU, false);
         }
         for (int c = 0; c < nch && ok; ++c) {
-            ok = mbar_wait(imgReady, c & 1) && mbar_wait(fullM(c & 1), (c >> 1) & 1);
+            // the output columns of this parity were read and cleared for chunk c - 2
+            ok = mbar_wait(imgReady, c & 1) && mbar_wait(fullM(c & 1), (c >> 1) & 1) &&
+                 (!outputs || c < 2 || mbar_wait(oFree(c & 1), ((c - 2) >> 1) & 1));
             if (!ok) break;
             tc_fence_after();
-            // S_c M_c^T, accumulated onto U_c^T K'_c (B = M K-major [128 k][128 k'])
-            mma_ct_ta<kF16, false, kD, 128, 128>(accS(c & 1), sA(c & 1), aM + (c & 1) * 32768, dpart);
+            const uint32_t bMQ = aM + (c & 1) * kCaMQBytes;
+            if (outputs)  // S_c [M_c^T | Qt_c^T] (N = 192): the next state onto U_c^T K'_c, O_c^T onto zeros
+                mma_ct_ta<kF16, true, kD, 128, 192>(accS(c & 1), sA(c & 1), bMQ, true);
+            else  // S_c M_c^T (onto U_c^T K'_c, or alone for a T chain)
+                mma_ct_ta<kF16, true, kD, 128, 128>(accS(c & 1), sA(c & 1), bMQ, dpart);
             mma_commit(mmaS(c));
             if (dpart && c + 1 < nch) {  // next chunk's U^T K' into the other accumulator (its reader is done)
                 const int b = (c + 1) % 3;
@@ -1380,14 +1394,6 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
                 mma_ct<kF16, false, true, 64, 128, 64, 128, 128>(accS((c + 1) & 1), aKU + b * 32768 + 16384,
                                                                 aKU + b * 32768, false);
             }
-            if (outputs) {
-                ok = mbar_wait(fullQt(c % 3), (c / 3) & 1) && (c < 2 || mbar_wait(oFree(c & 1), ((c - 2) >> 1) & 1));
-                if (!ok) break;
-                tc_fence_after();
-                // O_c^T = S_c Qt_c^T (B = Qt^T MN-major [128 k][64 i])
-                mma_ct_ta<kF16, true, kD, kD, 64>(accO(c & 1), sA(c & 1), aQt + (c % 3) * 16384, false);
-                mma_commit(mmaO(c & 1));
-            }
         }
         if (!ok) {
             record_status(32 /* GDN_ERR_DEVICE_TIMEOUT */);
@@ -1395,17 +1401,14 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
             mbar_wait(drain, 0);
         }
     } else if (loader) {
-        // S_c M_c^T complete => so is everything issued before it (U^T K' of c,
-        // S_{c-1} Qt_{c-1}^T): refill those buffers two chunks ahead
+        // chunk c's product complete => so is everything issued before it (U^T K'
+        // of c): refill those buffers two (three) chunks ahead
         for (int c = 0; c < nch && ok; ++c) {
             ok = mbar_wait(mmaS(c), (c >> 1) & 1);
             if (!ok) break;
             if (c + 2 < nch) {
                 issue_M(c + 2);
-                if (outputs) {
-                    issue_Qt(c + 2);
-                    bulk_prefetch_l2(rec_ptr(c + 2) + kRecUt, 16384);
-                }
+                if (outputs) bulk_prefetch_l2(rec_ptr(c + 2) + kRecUt, 16384);
             }
             if (dpart && c + 3 < nch) issue_KU(c + 3);
         }
@@ -1414,7 +1417,6 @@ __global__ void __launch_bounds__(kCarryThreads, 1)
             // wait (bounded) for the copies in flight: per buffer, its latest chunk
             for (int c = topM > 1 ? topM - 1 : 0; c <= topM; ++c) mbar_wait(fullM(c & 1), (c >> 1) & 1);
             for (int c = topKU > 2 ? topKU - 2 : 0; c <= topKU; ++c) mbar_wait(fullKU(c % 3), (c / 3) & 1);
-            for (int c = topQt > 2 ? topQt - 2 : 0; c <= topQt; ++c) mbar_wait(fullQt(c % 3), (c / 3) & 1);
         }
     }
     tc_fence_before();
