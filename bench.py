@@ -65,7 +65,7 @@ PREFILL_FLOPS_PER_TOKEN = 1452715.0
 # capture of this file's own --workload prefill2 / prefill3 runs
 # (profiles/prefill_call_traffic_config2_config3.md); legs without a capture
 # report None
-PREFILL_NCU_TRAFFIC = {"config2": 28573184, "config3": 1083683584}
+PREFILL_NCU_TRAFFIC = {"config2": 28218112, "config3": 1075082752}
 L2_FLUSH_BYTES = 256 << 20
 SLEEP_CYCLES = 200_000  # ~100 us GPU spin before each timed step (outside the events)
 # dram__bytes_read.sum + dram__bytes_write.sum per gdn_decode_kernel launch at
@@ -898,6 +898,9 @@ def run_ours(args):
         if wl in ("all", "prefill3"):
             pf["config3_32seq"] = bench_prefill(pkg, device, pkg.inputs.config3_lengths(0), 0, psteps,
                                                 args.warmup, ws, flush, peaks, traffic=PREFILL_NCU_TRAFFIC.get("config3"))
+        if wl == "prefill4b_shard":  # one rank's share of config 4b at N = 8, alone (for per-kernel captures)
+            pf["config4b_shard_8x8192"] = bench_prefill(pkg, device, [8192] * 8, 5, psteps, args.warmup, ws, flush,
+                                                        peaks)
         if wl in ("all", "prefill_heads"):
             # the contest's other head layout (16 q/k, 32 v heads) on config 2's and config 3's shapes
             pf["qk16_v32_T4096_N1"] = bench_prefill(pkg, device, [4096], 0, psteps, args.warmup, ws, flush, peaks,
@@ -989,8 +992,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds per CPU-baseline sample")
     ap.add_argument("--workload", default="all",
-                    choices=["all", "decode", "prefill2", "prefill3", "prefill_heads", "config4", "prefill_cp",
-                             "reference_gpu", "reference_gpu_decode"],
+                    choices=["all", "decode", "prefill2", "prefill3", "prefill_heads", "prefill4b_shard", "config4",
+                             "prefill_cp", "reference_gpu", "reference_gpu_decode"],
                     help="all = the JSON line the driver reads; the others time one workload")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline (profiling runs)")
     ap.add_argument("--skip-e2e", action="store_true", help="omit the host-buffer e2e leg")
