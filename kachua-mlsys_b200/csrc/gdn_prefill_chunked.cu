@@ -42,15 +42,17 @@
 //                     (chunk record, v-head): TMA loads of K, Q, V into SW128
 //                     images; Gram [K;Q] K^T (bf16); N, P and the decay
 //                     ratios; Ainv as above; [W | U]^T, Qt^T, Ut^T and
-//                     K'^T W as M = 128 fp16 tcgen05 products; 96 KiB of fp16
-//                     operand images per item bulk-stored to the workspace.
+//                     W^T K' (= (K'^T W)^T) as M = 128 fp16 tcgen05
+//                     products; 96 KiB of fp16 operand images per item
+//                     bulk-stored to the workspace.
 //   gdn_chunk_carry   one 448-thread CTA per sequence x v-head (per segment
 //                     of one in the segmented and context-parallel modes):
 //                     the state lives in TMEM, transposed, and is the A
 //                     operand of its own next product; per chunk one
-//                     128 x 128 x 128 state MMA S M^T (plus U^T K' issued a
-//                     chunk early) and one output MMA S Qt^T, operands by
-//                     bulk copies two chunks ahead, bf16 output tiles by TMA.
+//                     product S [M^T | Qt^T] (M = 128, N = 192, K = 128)
+//                     giving the next state and the chunk's output at once
+//                     (plus U^T K' issued a chunk early), operands by bulk
+//                     copies two chunks ahead, bf16 output tiles by TMA.
 // Any q/k and v head counts (v a multiple of q/k): items, records and carry
 // chains are per v-head, and v-head h reads q/k head h / (hv / hqk).
 // Precision: tensor-core operands are fp16 (round-to-nearest, 11-bit
